@@ -1,0 +1,348 @@
+"""Benchmark of the product-key memory (PKM) layer on B200: tokens/s of fwd + bwd + optimizer step.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl cuda|reference] [--rows-per-half 4096]
+
+Workload (BASELINE metric "PKM layer tokens/s (fwd+bwd+opt) at 16.8M rows"): one PKM layer with 4096 sub-keys
+per half (16,777,216 value rows x 384, fp32 table, fp32 Adam moments), H=4 heads x knn=32 reads per token,
+k_dim 256, d_model 384, no BatchNorm / swilu (the config-1 layer), 32,768 tokens per GPU per step, x ~ N(0, 1)
+and upstream gradient ~ N(0, 1), seeded synthetic data. One step = forward under bf16 autocast (query
+projection, sub-key scoring, selection, value bag), backward (value bag -> row store, selection -> scores ->
+keys / query), value clipping, LazyRowAdam on the table + fused AdamW on the dense parameters. All through the
+public API (smlm_b200.pkm.ProductKeyMemory, smlm_b200.sparse_values).
+
+`value` is device-timed with the inputs resident (CUDA events on the launching stream, barrier + synchronize
+around exactly K steps, max over ranks). `e2e` repeats the K steps with each step's inputs copied from pinned
+host memory and a scalar read back inside the timed region. `roofline` is the dominant kernel (the lazy Adam
+step) against the measured HBM copy bandwidth. `cpu_baseline` times the reference's PyTorch CPU path (a
+restatement under oracle/, the only oracle use in this file) on a bounded sample.
+
+--impl reference times the reference's PyTorch path on the host cores instead (rank 0 only under torchrun).
+With --gpus N > 1 each rank runs its own full layer (replicas, weak scaling) until the row-sharded layer lands.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "sparse-memory-lm_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "PKM layer tokens/s (fwd+bwd+opt) at 16.8M rows"
+D_MODEL, HEADS, KNN, K_DIM = 384, 4, 32, 256
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--rows-per-half", type=int, default=4096, help="sub-keys per half (rows = this squared)")
+    ap.add_argument("--tokens", type=int, default=32768, help="tokens per GPU per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-rows-per-half", type=int, default=1024)
+    ap.add_argument("--cpu-tokens", type=int, default=4096)
+    return ap.parse_args()
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampling of SM clocks / throttle reasons during a timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        try:
+            rows = [ln.split(",") for ln in open(self.file.name).read().strip().splitlines() if ln.strip()]
+            os.unlink(self.file.name)
+        except OSError:
+            rows = []
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows if len(r) >= 9 for n, v in zip(names, r[5:9]) if "Active" in v
+                          and "Not" not in v})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------ layer
+def build_layer(n_keys, device):
+    from smlm_b200.pkm import ProductKeyMemory
+    from smlm_b200.sparse_values import LazyRowAdam, OptimizerSet
+    torch.manual_seed(0)
+    with torch.device(device):
+        mem = ProductKeyMemory(D_MODEL, D_MODEL, n_keys=n_keys, heads=HEADS, knn=KNN, k_dim=K_DIM,
+                               query_norm="none", swilu=False, value_grad="row_sparse")
+        # config-1 initialisation: query N(0, 0.02), bias 0, sub-keys N(0, 1/128), values N(0, 384^-0.5)
+        with torch.no_grad():
+            mem.query_proj.weight.normal_(0, 0.02)
+            mem.keys.normal_(0, (K_DIM // 2) ** -0.5)
+    table = mem.values.weight
+    dense = [p for p in mem.parameters() if p is not table]
+    opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True),
+                       LazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98), eps=1e-8))
+    return mem, opt
+
+
+def train_step(mem, opt, x, g):
+    from smlm_b200.sparse_values import clip_row_sparse
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = mem(x)
+    out.backward(g)
+    vnorm = clip_row_sparse([mem.values.weight], 1.0)
+    torch.nn.utils.clip_grad_norm_([p for p in mem.parameters() if p.grad is not None], 1.0, foreach=True)
+    opt.step()
+    opt.zero_grad(set_to_none=True)
+    return vnorm
+
+
+def timed_loop(fn, steps, world):
+    barrier(world)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return s.elapsed_time(e)
+
+
+def run_cuda(args, world, rank, local):
+    from smlm_b200 import _lib as L
+    dev = torch.device("cuda", local)
+    N, n_keys = args.tokens, args.rows_per_half
+    rows = n_keys ** 2
+    mem, opt = build_layer(n_keys, dev)
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    n_batches = 4
+    xs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(n_batches)]
+    gs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(n_batches)]
+    for i in range(args.warmup):
+        train_step(mem, opt, xs[i % n_batches], gs[i % n_batches])
+    torch.cuda.synchronize()
+
+    # unique rows per step (U) for the algorithmic byte counts: measured on untimed steps
+    from smlm_b200.sparse_values import row_store
+    st = row_store(mem.values.weight)
+    uniq = []
+    for i in range(2):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = mem(xs[i])
+        out.backward(gs[i])
+        uniq.append(int(st.touched.sum()))
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+    U = sum(uniq) / len(uniq)
+
+    L.PROFILE = []
+    with Clocks(local) as clocks:
+        ms = timed_loop(lambda i: train_step(mem, opt, xs[i % n_batches], gs[i % n_batches]), args.steps, world)
+    prof, L.PROFILE = L.PROFILE, None
+    ms = max_over_ranks(ms, world)
+    ms_step = ms / args.steps
+    tokens_per_s = N * world / (ms_step / 1e3)
+    per_kernel = {}
+    launches = 0
+    for name, s, e, nl in prof:
+        per_kernel.setdefault(name, []).append(s.elapsed_time(e))
+        launches += nl
+
+    # end to end: inputs from pinned host memory, a scalar read back, every step
+    hx = [x.cpu().pin_memory() for x in xs]
+    hg = [g.cpu().pin_memory() for g in gs]
+    out_host = torch.empty(n_batches, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        x = hx[i % n_batches].to(dev, non_blocking=True)
+        g = hg[i % n_batches].to(dev, non_blocking=True)
+        v = train_step(mem, opt, x, g)
+        out_host[i % n_batches].copy_(v, non_blocking=True)
+    ms_e2e = max_over_ranks(timed_loop(e2e_step, args.steps, world), world)
+    e2e_tok_s = N * world / (ms_e2e / args.steps / 1e3)
+
+    # roofline of the dominant kernel: lazy Adam over the U touched rows of a (rows, 384) fp32 table
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm = peaks.get("hbm_gbs")
+    peak_src = "measured" if hbm else "fallback"
+    hbm = hbm or 6650.0
+    adam_ms = statistics.mean(per_kernel["lazy_adam_step"])
+    adam_bytes = rows * 1 + U * (4 + 4 + 1) + U * D_MODEL * 4 * 8    # mask scan, row list, p/m/v/acc r+w
+    roof = {"kernel": "lazy_adam_step", "bound": "hbm", "achieved": adam_bytes / (adam_ms / 1e3) / 1e9,
+            "peak": hbm, "peak_source": peak_src, "unit": "GB/s", "traffic": None,
+            "algorithmic_bytes": adam_bytes, "unique_rows": U}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    M = N * HEADS * KNN
+    kernel_bytes = {
+        "bag_forward": M * (D_MODEL * 4 + 12) + N * D_MODEL * 4,
+        "bag_backward_rows": U * D_MODEL * 4 * 3 + M * (8 * 4 + 4 + 4) + N * D_MODEL * 4,
+        "lazy_adam_step": adam_bytes,
+    }
+    breakdown = {}
+    for name, t in sorted(per_kernel.items()):
+        entry = {"ms": round(statistics.mean(t), 4), "calls_per_step": len(t) / args.steps}
+        if name in kernel_bytes:
+            gbs = kernel_bytes[name] / (statistics.mean(t) / 1e3) / 1e9
+            entry.update({"GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3)})
+        breakdown[name] = entry
+
+    line = {"metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "pkm-layer-b16m" if n_keys == 4096 else f"pkm-layer-{rows}rows",
+                       "rows": rows, "rows_per_half": n_keys, "v_dim": D_MODEL, "heads": HEADS, "knn": KNN,
+                       "k_dim": K_DIM, "tokens_per_gpu": N, "global_tokens": N * world,
+                       "scoring": "bf16 autocast (bf16 operands, fp32 accumulate)", "values": "fp32 table",
+                       "optimizer": "LazyRowAdam fp32 moments + fused AdamW (dense)",
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "working set > L2: each step gathers ~6.4 GB of table rows and updates ~U rows of "
+                             "table + moments (77 GB resident), inputs cycle over 4 batches",
+                       "unique_rows_per_step": round(U)},
+            "e2e": {"value": round(e2e_tok_s, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 2 * N * D_MODEL * 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": launches, "roofline": roof, "kernels": breakdown, "clocks": clocks.summary()}
+    return line
+
+
+# ----------------------------------------------------------------------------------------- CPU reference
+def cpu_reference(n_keys, N, steps, warmup):
+    """The reference's PyTorch path (oracle/torch_path.py) on the host cores: fwd + bwd + clip + lazy Adam
+    (the reference's full-table fp32 Adam with unread rows restored) + AdamW on the dense parameters."""
+    from oracle import torch_path as TP
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    mem = TP.TorchPKM(D_MODEL, D_MODEL, n_keys=n_keys, heads=HEADS, knn=KNN, k_dim=K_DIM, query_norm="none",
+                      swilu=False, canonical=False)
+    TP.init_like_reference(mem, 0)
+    table = mem.values.weight
+    dense = [p for p in mem.parameters() if p is not table]
+    adamw = torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0)
+    lazy = TP.TorchLazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98))
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(N, D_MODEL, generator=gen)
+    g = torch.randn(N, D_MODEL, generator=gen)
+
+    def step():
+        out = mem(x)
+        out.backward(g)
+        TP.clip_row_sparse([table], 1.0)
+        torch.nn.utils.clip_grad_norm_(dense, 1.0)
+        adamw.step()
+        lazy.step()
+        adamw.zero_grad(set_to_none=True)
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    try:
+        cpu = [ln.split(":", 1)[1].strip() for ln in open("/proc/cpuinfo") if ln.startswith("model name")][0]
+    except (OSError, IndexError):
+        cpu = "unknown"
+    return {"value": round(N / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"reference PyTorch path (oracle/torch_path.py) on {cpu}: one PKM layer with "
+                      f"{n_keys}^2 = {n_keys ** 2} rows (the 16.8M-row table scaled down to fit host RAM; the "
+                      f"reference's full-table Adam makes larger tables slower), {N} tokens per step, "
+                      f"{steps} timed steps after {warmup} warm-up, {threads} threads",
+            "ms_per_step": round(dt * 1e3, 2)}
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        if rank == 0:
+            base = cpu_reference(args.cpu_rows_per_half, args.cpu_tokens, max(1, min(args.steps, 3)),
+                                 min(args.warmup, 1))
+            line = {"metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": world,
+                    "steps": max(1, min(args.steps, 3)), "warmup": min(args.warmup, 1),
+                    "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                    "config": {"workload": "pkm-layer-b16m", "rows": args.cpu_rows_per_half ** 2,
+                               "tokens_per_step": args.cpu_tokens, "note": "CPU sample, see cpu_baseline.sample"},
+                    "cpu_baseline": base,
+                    "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                            "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    line = run_cuda(args, world, rank, local)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference(args.cpu_rows_per_half, args.cpu_tokens, 2, 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

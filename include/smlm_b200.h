@@ -1,0 +1,168 @@
+/*
+ * C ABI of the B200 product-key-memory (PKM) kernels: libsmlm_b200.so.
+ *
+ * Each entry point replaces one function of the reference's kernel layer (smlm/kernels.py of
+ * re133/sparse-memory-lm) or one torch-op sequence of its PyTorch path; the comment above each declaration
+ * names the reference interface (file:line) it stands in for. The Python shims in smlm_b200/kernels.py keep
+ * the reference's Python signatures and call these through ctypes.
+ *
+ * Conventions shared by all entry points:
+ *   - All tensor pointers are device pointers (CUDA global memory); sizes are element counts.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default stream) and is asynchronous:
+ *     no entry point synchronizes the device or the stream, none allocates device memory.
+ *   - Scratch memory comes in through `workspace` / `workspace_bytes`; the matching *_workspace() query
+ *     returns the number of bytes needed (a pure host computation).
+ *   - Return value: SMLM_OK, or an error code; smlm_last_error() describes the error (thread-local).
+ *     SMLM_ERR_INVALID is raised before any launch (shape / dtype / range checks on the host).
+ *   - Index range violations found on the device (a row outside [0, rows)) never trap: the lookup is skipped
+ *     and SMLM_FLAG_INDEX_RANGE is OR-ed into *status (if status is not NULL).
+ *   - Layouts are row-major and contiguous.
+ */
+#ifndef SMLM_B200_H
+#define SMLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define SMLM_API __attribute__((visibility("default")))
+#else
+#define SMLM_API
+#endif
+
+/* return codes */
+#define SMLM_OK 0
+#define SMLM_ERR_INVALID 1   /* bad argument, detected on the host before launch */
+#define SMLM_ERR_CUDA 2      /* a CUDA runtime call or launch failed */
+#define SMLM_ERR_WORKSPACE 3 /* workspace_bytes smaller than the size query's answer */
+
+/* element types */
+#define SMLM_F32 0
+#define SMLM_BF16 1
+#define SMLM_F16 2
+#define SMLM_Q4 3 /* packed 4-bit rows (d/2 bytes) + one fp16 scale per row, see smlm_quantize_q4 */
+
+/* device status word bits */
+#define SMLM_FLAG_INDEX_RANGE 1
+
+/* row-wise optimizer kinds (smlm/row_optim.py:21 KINDS) */
+#define SMLM_ROWRMS 0
+#define SMLM_ROWADAGRAD 1
+
+/* score modes of the fused scoring + selection (smlm_score_select) */
+#define SMLM_SCORE_F32_EXACT 0 /* fp32 sub-key scores, sequential fmaf over the half dimension */
+#define SMLM_SCORE_BF16 1      /* bf16 operands, fp32 accumulate, scores rounded to bf16 (autocast path) */
+
+/* Library version (major * 10000 + minor * 100 + patch) and the last error of this thread. */
+SMLM_API int smlm_version(void);
+SMLM_API const char *smlm_last_error(void);
+
+/* ----------------------------------------------------------------------------------- value bag (gather) */
+
+/* out[n, :] = sum_j weights[n, j] * table[indices[n, j], :], fp32 accumulation in j order.
+ * Replaces kernels.py:229 bag_forward (and the aten _embedding_bag forward of sparse_values.py:78).
+ * weights: F32 or BF16 (n, k); table: F32 or BF16 (rows, d); out: F32 or BF16 (n, d). */
+SMLM_API int smlm_bag_forward(const int64_t *indices, const void *weights, int weights_dtype, const void *table,
+                     int table_dtype, int64_t n, int64_t k, int64_t rows, int64_t d, void *out, int out_dtype,
+                     int *status, void *stream);
+
+/* Inference bag on an fp32 / bf16 / q4 table with the swilu product fused:
+ *   a = sum_j weights[n, j] * table[indices[n, j]]   (q4: codes * per-row fp16 scale)
+ *   if pre: a = a * bf16(silu(pre[n]))               (pre: BF16 or F32 (n, d))
+ *   out = a (F32) or bf16(a) (BF16).
+ * Replaces kernels.py:364 bag_infer. For q4, table is uint8 (rows, d/2) and scales is fp16 (rows,). */
+SMLM_API int smlm_bag_infer(const int64_t *indices, const void *weights, int weights_dtype, const void *table,
+                   int table_dtype, const void *scales, const void *pre, int pre_dtype, int64_t n, int64_t k,
+                   int64_t rows, int64_t d, void *out, int out_dtype, int *status, void *stream);
+
+/* 4-bit row quantisation: per row s = half(w[argmax|w|] / -8) (1 if zero), codes clamp(round(w / s), -8, 7) + 8,
+ * byte i of a row = code(col i) | code(col i + d/2) << 4. Replaces kernels.py:280 quantize_q4. d must be even. */
+SMLM_API int smlm_quantize_q4(const float *table, int64_t rows, int64_t d, uint8_t *packed, void *scales_f16,
+                     void *stream);
+
+/* ------------------------------------------------------------------------ value bag backward (row-sparse) */
+
+SMLM_API size_t smlm_bag_backward_workspace(int64_t n, int64_t k, int64_t rows, int64_t d);
+
+/* Row-sparse backward of the value bag:
+ *   gw[n, j] = <grad_out[n], table[indices[n, j]]>
+ *   acc[r] += sum over (n, j) with indices[n, j] == r of weights[n, j] * grad_out[n]   (in place)
+ *   touched[indices[n, j]] = 1                                                          (in place)
+ * The (row, position) pairs are radix-sorted (stable) and each row's run is summed in position order;
+ * runs that cross a work chunk are completed by a second pass in chunk order. No float atomics:
+ * results are bit-identical from run to run.
+ * Replaces kernels.py:73 bag_backward_rows (and sparse_values.py:97-103, the aten per-sample-weight
+ * backward + index_put_ accumulation). grad_out: F32 (n, d); weights F32/BF16; table F32/BF16; acc F32.
+ * acc == NULL (and touched == NULL): only gw is computed (frozen table, sparse_values.py:118-120). */
+SMLM_API int smlm_bag_backward_rows(const float *grad_out, const int64_t *indices, const void *weights,
+                           int weights_dtype, const void *table, int table_dtype, float *acc, uint8_t *touched,
+                           float *gw, int64_t n, int64_t k, int64_t rows, int64_t d, void *workspace,
+                           size_t workspace_bytes, int *status, void *stream);
+
+/* ------------------------------------------------------------------------------- row-sparse optimizers */
+
+SMLM_API size_t smlm_touched_workspace(int64_t rows);
+
+/* Lazy Adam on the rows with touched[r] != 0 (the only rows loaded): with g = acc[r] * scale,
+ *   m = m + (1 - b1) (g - m);  v = v b2 + (1 - b2) g g;  p = p + neg_step_size * (m / (sqrt(v) / bc2_sqrt + eps))
+ * then acc[r] = 0 and touched[r] = 0. Operation order and fp32 rounding follow the reference's C loop
+ * (smlm/host_rows.c:63-80, no contraction into FMA), so results are bit-identical to it.
+ * scale = *grad_scale_dev if grad_scale_dev is not NULL, else grad_scale.
+ * value_copy (optional, copy_dtype BF16 or F32, (rows, d)): the updated rows are also written there.
+ * Replaces kernels.py:417 lazy_adam_step (and LazyRowAdam.step's torch path, sparse_values.py:270-305). */
+SMLM_API int smlm_lazy_adam_step(float *param, float *exp_avg, float *exp_avg_sq, float *acc, uint8_t *touched,
+                        const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
+                        float one_minus_b1, float b2, float one_minus_b2, float bc2_sqrt, float eps,
+                        float neg_step_size, void *value_copy, int copy_dtype, void *workspace,
+                        size_t workspace_bytes, void *stream);
+
+/* Row-wise optimizer on the touched rows (smlm/row_optim.py; formulas of host_rows.c:84-117):
+ *   q = mean over the row of g^2 (summed in double), g = acc[r] * scale
+ *   SMLM_ROWRMS:     v[r] = b2 v[r] + (1 - b2) q;  count[r] += 1;  denom = sqrt(v[r] / (1 - b2^count[r])) + eps
+ *   SMLM_ROWADAGRAD: v[r] += q;                                      denom = sqrt(v[r]) + eps
+ *   p[r] -= (lr / denom) * g;  acc[r] = 0;  touched[r] = 0.
+ * count may be NULL for SMLM_ROWADAGRAD. Replaces RowWiseOptimizer._masked (row_optim.py:179-201). */
+SMLM_API int smlm_rowwise_step(float *param, float *acc, uint8_t *touched, float *v, int32_t *count,
+                      const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d, int kind, float b2,
+                      float eps, float lr, void *workspace, size_t workspace_bytes, void *stream);
+
+/* L2 norm of the accumulator over the touched rows, written to *norm_out (device fp32). Rows that were not
+ * touched hold zeros in a RowStore (the backward only adds to touched rows, the step zeroes them), so this is
+ * the reference's acc.norm() (sparse_values.py:143) without reading the untouched rows. Deterministic. */
+SMLM_API int smlm_touched_norm(const float *acc, const uint8_t *touched, int64_t rows, int64_t d, float *norm_out,
+                      void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------- product-key scoring / select */
+
+/* Product-key selection on given sub-key scores s1, s2 (n, h, nk), F32 or BF16:
+ * per (n, h): top-knn of each half by (score desc, index asc); the knn x knn pair sums (rounded to the
+ * score type, as `s1 + s2` in PyTorch); top-knn of those by (score desc, full index asc), full index
+ * = i1 * nk + i2; softmax in fp32. Outputs scores (n, h, knn) in the score type, indices int64, weights F32,
+ * in (score desc, index asc) order. 1 <= knn <= 32, knn <= nk <= 65536.
+ * Replaces kernels.py:214 pk_select and pkm.py:125-136 get_indices + pkm.py:205-208 softmax. */
+SMLM_API int smlm_pk_select(const void *s1, const void *s2, int score_dtype, int64_t n, int64_t h, int64_t nk,
+                   int64_t knn, void *scores, int64_t *indices, float *weights, void *stream);
+
+/* Backward of the selection, dense form: dl = w (g_w - sum(w g_w)) + g_scores; ds = dl rounded to the score
+ * type; ds1[n, h, i1] = sum of ds over the selected pairs with that i1 (fp32, in selection order, then
+ * rounded), ds2 likewise; all other entries zero. grad_w / grad_scores may be NULL.
+ * Replaces kernels.py:253-266 PKSelect.backward. */
+SMLM_API int smlm_select_backward(const int64_t *indices, const float *weights, const float *grad_w,
+                         const void *grad_scores, int score_dtype, int64_t n, int64_t h, int64_t nk, int64_t knn,
+                         void *ds1, void *ds2, void *stream);
+
+/* Exact fp32 sub-key scores: s1[n, h, j] = sum_t q[n, h, t] k[h, 0, j, t] and s2 with the second halves,
+ * each a sequential fmaf chain over t = 0 .. half-1 (the order a C loop reproduces bit for bit).
+ * q: (n, h, 2 half), keys: (h, 2, nk, half). Replaces pkm.py:117-123 subkey_scores in fp32. */
+SMLM_API int smlm_subkey_scores_f32(const float *q, const float *keys, int64_t n, int64_t h, int64_t nk, int64_t half,
+                           float *s1, float *s2, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMLM_B200_H */

@@ -1,0 +1,317 @@
+// Row-sparse optimizer steps over the touched rows only: lazy Adam (fp32 moments), the row-wise rowrms /
+// rowadagrad variant, and the accumulator norm used for clipping.
+//
+// Each entry first compacts the touched mask into an ascending list of row ids plus its length, both in the
+// workspace (cub::DeviceSelect::Flagged; ordered, deterministic); the update kernels are persistent grids that
+// read the length from device memory, so nothing syncs with the host. One warp per row, 16-byte vectors.
+#include <cub/device/device_select.cuh>
+#include <cub/iterator/counting_input_iterator.cuh>
+
+#include "common.cuh"
+
+namespace smlm {
+
+struct TouchedBufs {
+    int32_t* list;
+    int32_t* count;
+    void* tmp;
+    size_t tmp_bytes;
+    double* partials;
+};
+
+constexpr int PARTIALS = 4096;  // per-warp partial sums of the norm kernel (fixed: deterministic order)
+
+static size_t select_tmp_bytes(int64_t rows) {
+    size_t bytes = 0;
+    cub::DeviceSelect::Flagged(nullptr, bytes, cub::CountingInputIterator<int32_t>(0), (const uint8_t*)nullptr,
+                               (int32_t*)nullptr, (int32_t*)nullptr, (int)std::max<int64_t>(rows, 1));
+    return bytes;
+}
+
+static size_t layout_touched(int64_t rows, void* base, TouchedBufs* b) {
+    size_t off = 0;
+    char* c = static_cast<char*>(base);
+    auto take = [&](size_t bytes) -> void* {
+        off = (off + 255) & ~size_t(255);
+        void* ptr = c ? c + off : nullptr;
+        off += bytes;
+        return ptr;
+    };
+    b->list = static_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(rows, 1)));
+    b->count = static_cast<int32_t*>(take(sizeof(int32_t) * 4));
+    b->tmp_bytes = select_tmp_bytes(rows);
+    b->tmp = take(b->tmp_bytes);
+    b->partials = static_cast<double*>(take(sizeof(double) * PARTIALS));
+    return off;
+}
+
+static int compact_touched(const uint8_t* touched, int64_t rows, void* workspace, size_t workspace_bytes,
+                           TouchedBufs* b, cudaStream_t st) {
+    const size_t need = layout_touched(rows, nullptr, b);
+    if (workspace == nullptr || workspace_bytes < need) {
+        set_error("touched-row workspace too small (%zu < %zu)", workspace_bytes, need);
+        return SMLM_ERR_WORKSPACE;
+    }
+    layout_touched(rows, workspace, b);
+    size_t tmp = b->tmp_bytes;
+    SMLM_CUDA(cub::DeviceSelect::Flagged(b->tmp, tmp, cub::CountingInputIterator<int32_t>(0), touched, b->list,
+                                         b->count, (int)rows, st));
+    return SMLM_OK;
+}
+
+static int persistent_blocks(int warps_per_block, int per_sm) {
+    (void)warps_per_block;
+    return sm_count() * per_sm;
+}
+
+// ------------------------------------------------------------------------------------------------ lazy Adam
+struct AdamArgs {
+    float *p, *m, *v, *acc;
+    uint8_t* touched;
+    const int32_t* list;
+    const int32_t* count;
+    const float* scale_dev;
+    float scale;
+    int d;
+    float one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step;
+    void* copy;
+    int copy_dtype;
+};
+
+// Element update in the reference C loop's order (host_rows.c:69-76), every operation rounded on its own.
+__device__ __forceinline__ void adam_elem(const AdamArgs& a, float scale, float& p, float& m, float& v, float g) {
+    const float gk = __fmul_rn(g, scale);
+    const float mk = __fadd_rn(m, __fmul_rn(a.one_minus_b1, __fsub_rn(gk, m)));
+    const float vk = __fadd_rn(__fmul_rn(v, a.b2), __fmul_rn(__fmul_rn(a.one_minus_b2, gk), gk));
+    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vk), a.bc2_sqrt), a.eps);
+    p = __fadd_rn(p, __fmul_rn(a.neg_step, __fdiv_rn(mk, denom)));
+    m = mk;
+    v = vk;
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(256) lazy_adam_kernel(AdamArgs a) {
+    const int lane = lane_id();
+    const int n = *a.count;
+    const float scale = a.scale_dev ? *a.scale_dev : a.scale;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
+        const int64_t r = a.list[i];
+        const int64_t base = r * a.d;
+        if constexpr (VEC == 4) {
+#pragma unroll 3
+            for (int c = lane * 4; c < a.d; c += 128) {
+                float4 p = *reinterpret_cast<float4*>(a.p + base + c);
+                float4 m = *reinterpret_cast<float4*>(a.m + base + c);
+                float4 v = *reinterpret_cast<float4*>(a.v + base + c);
+                const float4 g = *reinterpret_cast<float4*>(a.acc + base + c);
+                adam_elem(a, scale, p.x, m.x, v.x, g.x);
+                adam_elem(a, scale, p.y, m.y, v.y, g.y);
+                adam_elem(a, scale, p.z, m.z, v.z, g.z);
+                adam_elem(a, scale, p.w, m.w, v.w, g.w);
+                *reinterpret_cast<float4*>(a.p + base + c) = p;
+                *reinterpret_cast<float4*>(a.m + base + c) = m;
+                *reinterpret_cast<float4*>(a.v + base + c) = v;
+                *reinterpret_cast<float4*>(a.acc + base + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (a.copy) {
+                    if (a.copy_dtype == SMLM_BF16) {
+                        uint2 o;
+                        o.x = f32_to_bf16_bits(p.x) | (f32_to_bf16_bits(p.y) << 16);
+                        o.y = f32_to_bf16_bits(p.z) | (f32_to_bf16_bits(p.w) << 16);
+                        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.copy) + base + c) = o;
+                    } else {
+                        *reinterpret_cast<float4*>(static_cast<float*>(a.copy) + base + c) = p;
+                    }
+                }
+            }
+        } else {
+            for (int c = lane; c < a.d; c += 32) {
+                float p = a.p[base + c], m = a.m[base + c], v = a.v[base + c];
+                adam_elem(a, scale, p, m, v, a.acc[base + c]);
+                a.p[base + c] = p;
+                a.m[base + c] = m;
+                a.v[base + c] = v;
+                a.acc[base + c] = 0.f;
+                if (a.copy) {
+                    if (a.copy_dtype == SMLM_BF16) static_cast<uint16_t*>(a.copy)[base + c] = (uint16_t)f32_to_bf16_bits(p);
+                    else static_cast<float*>(a.copy)[base + c] = p;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) a.touched[r] = 0;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ row-wise
+struct RowArgs {
+    float *p, *acc, *v;
+    int32_t* count_state;
+    uint8_t* touched;
+    const int32_t* list;
+    const int32_t* count;
+    const float* scale_dev;
+    float scale;
+    int d, kind;
+    float b2, eps, lr;
+};
+
+// Formulas and rounding of the reference C loop (host_rows.c:84-117): q summed in double, row state in fp32.
+template <int VEC>
+__global__ void __launch_bounds__(256) rowwise_kernel(RowArgs a) {
+    const int lane = lane_id();
+    const int n = *a.count;
+    const float scale = a.scale_dev ? *a.scale_dev : a.scale;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    const float one_minus_b2 = __fsub_rn(1.0f, a.b2);
+    for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
+        const int64_t r = a.list[i];
+        const int64_t base = r * a.d;
+        double q = 0.0;
+        for (int c = lane * VEC; c < a.d; c += 32 * VEC) {
+#pragma unroll
+            for (int t = 0; t < VEC; t++) {
+                const float gk = __fmul_rn(a.acc[base + c + t], scale);
+                q = fma((double)gk, (double)gk, q);
+            }
+        }
+        q = warp_sum_d(q) / (double)a.d;
+        float denom;
+        if (a.kind == SMLM_ROWRMS) {
+            const float vr = __fadd_rn(__fmul_rn(a.b2, a.v[r]), __fmul_rn(one_minus_b2, (float)q));
+            const int32_t cnt = a.count_state[r] + 1;
+            denom = __fadd_rn(__fsqrt_rn((float)((double)vr / (1.0 - pow((double)a.b2, (double)cnt)))), a.eps);
+            __syncwarp();
+            if (lane == 0) {
+                a.v[r] = vr;
+                a.count_state[r] = cnt;
+            }
+        } else {
+            const float vr = __fadd_rn(a.v[r], (float)q);
+            denom = __fadd_rn(__fsqrt_rn(vr), a.eps);
+            __syncwarp();
+            if (lane == 0) a.v[r] = vr;
+        }
+        const float step = __fdiv_rn(a.lr, denom);
+        for (int c = lane * VEC; c < a.d; c += 32 * VEC) {
+#pragma unroll
+            for (int t = 0; t < VEC; t++) {
+                const float gk = __fmul_rn(a.acc[base + c + t], scale);
+                a.p[base + c + t] = __fsub_rn(a.p[base + c + t], __fmul_rn(step, gk));
+                a.acc[base + c + t] = 0.f;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) a.touched[r] = 0;
+    }
+}
+
+// --------------------------------------------------------------------------------------------------- norm
+// Pass 1: warp w sums the squares of rows list[w], list[w + W], ... (double); W = PARTIALS fixed, so the
+// summation order does not depend on the device. Pass 2: one warp adds the PARTIALS in a fixed tree.
+__global__ void __launch_bounds__(256) touched_sq_kernel(const float* acc, const int32_t* list, const int32_t* count,
+                                                         int d, double* partials) {
+    const int lane = lane_id();
+    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (w >= PARTIALS) return;
+    const int n = *count;
+    double s = 0.0;
+    for (int i = w; i < n; i += PARTIALS) {
+        const int64_t base = (int64_t)list[i] * d;
+        for (int c = lane; c < d; c += 32) {
+            const double x = acc[base + c];
+            s = fma(x, x, s);
+        }
+    }
+    s = warp_sum_d(s);
+    if (lane == 0) partials[w] = s;
+}
+
+__global__ void norm_finish_kernel(const double* partials, float* out) {
+    const int lane = lane_id();
+    double s = 0.0;
+    for (int i = lane; i < PARTIALS; i += 32) s += partials[i];
+    s = warp_sum_d(s);
+    if (lane == 0) *out = (float)sqrt(s);
+}
+
+}  // namespace smlm
+
+using namespace smlm;
+
+extern "C" size_t smlm_touched_workspace(int64_t rows) {
+    TouchedBufs b;
+    return layout_touched(std::max<int64_t>(rows, 0), nullptr, &b);
+}
+
+extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_sq, float* acc, uint8_t* touched,
+                                   const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
+                                   float one_minus_b1, float b2, float one_minus_b2, float bc2_sqrt, float eps,
+                                   float neg_step_size, void* value_copy, int copy_dtype, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    SMLM_CHECK_ARG(rows >= 0 && d >= 0, "lazy_adam_step: negative size");
+    SMLM_CHECK_ARG(rows < (int64_t)0x7fffffff, "lazy_adam_step: rows must be below 2^31");
+    SMLM_CHECK_ARG(d < (1 << 30), "lazy_adam_step: d too large");
+    SMLM_CHECK_ARG(value_copy == nullptr || copy_dtype == SMLM_F32 || copy_dtype == SMLM_BF16,
+                   "lazy_adam_step: value copy must be fp32 or bf16");
+    if (rows == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(param && exp_avg && exp_avg_sq && acc && touched, "lazy_adam_step: null pointer");
+    cudaStream_t st = as_stream(stream);
+    TouchedBufs b;
+    int rc = compact_touched(touched, rows, workspace, workspace_bytes, &b, st);
+    if (rc != SMLM_OK) return rc;
+    AdamArgs a{param, exp_avg, exp_avg_sq, acc, touched, b.list, b.count, grad_scale_dev, grad_scale, (int)d,
+               one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step_size, value_copy, copy_dtype};
+    const bool vec = d % 4 == 0 && reinterpret_cast<uintptr_t>(param) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(exp_avg) % 16 == 0 && reinterpret_cast<uintptr_t>(exp_avg_sq) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(acc) % 16 == 0 &&
+                     (value_copy == nullptr || reinterpret_cast<uintptr_t>(value_copy) % 16 == 0);
+    const int blocks = persistent_blocks(8, 8);
+    if (vec) lazy_adam_kernel<4><<<blocks, 256, 0, st>>>(a);
+    else lazy_adam_kernel<1><<<blocks, 256, 0, st>>>(a);
+    SMLM_LAUNCHED("lazy_adam_kernel");
+    return SMLM_OK;
+}
+
+extern "C" int smlm_rowwise_step(float* param, float* acc, uint8_t* touched, float* v, int32_t* count,
+                                 const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d, int kind,
+                                 float b2, float eps, float lr, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    SMLM_CHECK_ARG(rows >= 0 && d > 0, "rowwise_step: rows must be >= 0 and the width > 0");
+    SMLM_CHECK_ARG(rows < (int64_t)0x7fffffff && d < (1 << 30), "rowwise_step: size too large");
+    SMLM_CHECK_ARG(kind == SMLM_ROWRMS || kind == SMLM_ROWADAGRAD, "rowwise_step: unknown kind %d", kind);
+    SMLM_CHECK_ARG(kind != SMLM_ROWRMS || count != nullptr, "rowwise_step: rowrms needs the per-row count");
+    if (rows == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(param && acc && touched && v, "rowwise_step: null pointer");
+    cudaStream_t st = as_stream(stream);
+    TouchedBufs b;
+    int rc = compact_touched(touched, rows, workspace, workspace_bytes, &b, st);
+    if (rc != SMLM_OK) return rc;
+    RowArgs a{param, acc, v, count, touched, b.list, b.count, grad_scale_dev, grad_scale, (int)d, kind, b2, eps, lr};
+    const int blocks = persistent_blocks(8, 8);
+    if (d % 4 == 0) rowwise_kernel<4><<<blocks, 256, 0, st>>>(a);
+    else rowwise_kernel<1><<<blocks, 256, 0, st>>>(a);
+    SMLM_LAUNCHED("rowwise_kernel");
+    return SMLM_OK;
+}
+
+extern "C" int smlm_touched_norm(const float* acc, const uint8_t* touched, int64_t rows, int64_t d, float* norm_out,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+    SMLM_CHECK_ARG(rows >= 0 && d >= 0, "touched_norm: negative size");
+    SMLM_CHECK_ARG(rows < (int64_t)0x7fffffff && d < (1 << 30), "touched_norm: size too large");
+    SMLM_CHECK_ARG(norm_out != nullptr, "touched_norm: null output");
+    cudaStream_t st = as_stream(stream);
+    if (rows == 0 || d == 0) {
+        SMLM_CUDA(cudaMemsetAsync(norm_out, 0, sizeof(float), st));
+        return SMLM_OK;
+    }
+    SMLM_CHECK_ARG(acc && touched, "touched_norm: null pointer");
+    TouchedBufs b;
+    int rc = compact_touched(touched, rows, workspace, workspace_bytes, &b, st);
+    if (rc != SMLM_OK) return rc;
+    touched_sq_kernel<<<PARTIALS / 8, 256, 0, st>>>(acc, b.list, b.count, (int)d, b.partials);
+    SMLM_LAUNCHED("touched_sq_kernel");
+    norm_finish_kernel<<<1, 32, 0, st>>>(b.partials, norm_out);
+    SMLM_LAUNCHED("norm_finish_kernel");
+    return SMLM_OK;
+}

@@ -1,0 +1,694 @@
+// Weighted value bag: forward gather, inference bag (fp32 / bf16 / q4 table, fused swilu), q4 quantisation,
+// and the row-sparse backward (stable radix sort of (row, position) + deterministic segment sums).
+//
+// Layout: table (rows, d) row-major; indices / weights (n, k) row-major; one warp per (token, column block).
+// Row loads are 16-byte (fp32) or 8-byte (bf16) vectors, one vector per lane per slot, so a warp reads a
+// contiguous 512 B / 256 B stretch of a row per instruction.
+#include <cub/device/device_radix_sort.cuh>
+
+#include "common.cuh"
+
+namespace smlm {
+
+// ------------------------------------------------------------------------------------------- vector loads
+template <typename T>
+struct Elt;
+template <>
+struct Elt<float> {
+    template <int VEC>
+    __device__ __forceinline__ static void load(const float* p, float (&v)[VEC]) {
+        if constexpr (VEC == 4) {
+            float4 x = __ldg(reinterpret_cast<const float4*>(p));
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; i++) v[i] = __ldg(p + i);
+        }
+    }
+};
+template <>
+struct Elt<__nv_bfloat16> {
+    template <int VEC>
+    __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&v)[VEC]) {
+        if constexpr (VEC == 4) {
+            uint2 x = __ldg(reinterpret_cast<const uint2*>(p));
+            v[0] = bf16_bits_to_f32(x.x & 0xffffu);
+            v[1] = bf16_bits_to_f32(x.x >> 16);
+            v[2] = bf16_bits_to_f32(x.y & 0xffffu);
+            v[3] = bf16_bits_to_f32(x.y >> 16);
+        } else {
+            const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+#pragma unroll
+            for (int i = 0; i < VEC; i++) v[i] = bf16_bits_to_f32(__ldg(q + i));
+        }
+    }
+};
+
+__device__ __forceinline__ float load_weight(const void* w, int dtype, int64_t i) {
+    if (dtype == SMLM_F32) return __ldg(static_cast<const float*>(w) + i);
+    return bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(w) + i));
+}
+
+template <int VEC>
+__device__ __forceinline__ void store_out(void* out, int dtype, int64_t off, const float (&v)[VEC]) {
+    if (dtype == SMLM_F32) {
+        float* o = static_cast<float*>(out) + off;
+        if constexpr (VEC == 4) {
+            *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; i++) o[i] = v[i];
+        }
+    } else {
+        uint16_t* o = static_cast<uint16_t*>(out) + off;
+#pragma unroll
+        for (int i = 0; i < VEC; i++) o[i] = (uint16_t)f32_to_bf16_bits(v[i]);
+    }
+}
+
+__device__ __forceinline__ float silu_bf16(float p) { return round_bf16(p / (1.0f + expf(-p))); }
+
+// ---------------------------------------------------------------------------------------------- bag gather
+struct BagArgs {
+    const int64_t* idx;
+    const void* w;
+    int w_dtype;
+    const void* table;
+    const void* pre;  // swilu pre-activation or NULL
+    int pre_dtype;
+    void* out;
+    int out_dtype;
+    int64_t n, rows;
+    int k, d;
+    int col_block;  // columns per warp task = 32 * VEC * NS
+    int* status;
+};
+
+// One warp per (token, column block); j-loop over the token's k lookups in chunks of 32 (lane j holds the
+// j-th index / weight of the chunk and broadcasts it), four rows in flight per step. The accumulation is a
+// sequential fmaf chain over j for every column.
+template <typename TT, int VEC, int NS>
+__global__ void __launch_bounds__(256) bag_gather_kernel(BagArgs a) {
+    const int lane = lane_id();
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int nblk = (a.d + a.col_block - 1) / a.col_block;
+    const TT* table = static_cast<const TT*>(a.table);
+    for (int64_t task = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < a.n * nblk;
+         task += warps) {
+        const int64_t n = task / nblk;
+        const int c0 = (int)(task % nblk) * a.col_block;
+        float acc[NS][VEC];
+#pragma unroll
+        for (int s = 0; s < NS; s++)
+#pragma unroll
+            for (int i = 0; i < VEC; i++) acc[s][i] = 0.f;
+        for (int j0 = 0; j0 < a.k; j0 += 32) {
+            const int cnt = min(32, a.k - j0);
+            int64_t my_r = 0;
+            float my_w = 0.f;
+            if (lane < cnt) {
+                my_r = __ldg(a.idx + n * a.k + j0 + lane);
+                my_w = load_weight(a.w, a.w_dtype, n * a.k + j0 + lane);
+                if (my_r < 0 || my_r >= a.rows) {
+                    flag(a.status, SMLM_FLAG_INDEX_RANGE);
+                    my_r = -1;
+                }
+            }
+            for (int jj = 0; jj < cnt; jj += 4) {
+                int64_t r[4];
+                float wv[4];
+                float v[4][NS][VEC];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    r[u] = __shfl_sync(FULL, my_r, (jj + u) & 31);
+                    wv[u] = __shfl_sync(FULL, my_w, (jj + u) & 31);
+                    const bool ok = (jj + u < cnt) && r[u] >= 0;
+#pragma unroll
+                    for (int s = 0; s < NS; s++) {
+                        const int col = c0 + (lane + 32 * s) * VEC;
+                        if (ok && col < a.d) {
+                            Elt<TT>::template load<VEC>(table + r[u] * a.d + col, v[u][s]);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < VEC; i++) v[u][s][i] = 0.f;
+                        }
+                    }
+                    if (!ok) wv[u] = 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+#pragma unroll
+                    for (int s = 0; s < NS; s++)
+#pragma unroll
+                        for (int i = 0; i < VEC; i++)
+                            if (jj + u < cnt) acc[s][i] = fmaf(wv[u], v[u][s][i], acc[s][i]);
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = c0 + (lane + 32 * s) * VEC;
+            if (col < a.d) {
+                if (a.pre) {
+#pragma unroll
+                    for (int i = 0; i < VEC; i++) {
+                        const int64_t off = n * a.d + col + i;
+                        const float p = a.pre_dtype == SMLM_F32
+                                            ? __ldg(static_cast<const float*>(a.pre) + off)
+                                            : bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(a.pre) + off));
+                        acc[s][i] = acc[s][i] * silu_bf16(p);
+                    }
+                }
+                store_out<VEC>(a.out, a.out_dtype, n * a.d + col, acc[s]);
+            }
+        }
+    }
+}
+
+template <typename TT, int VEC>
+static int launch_bag_vec(BagArgs a, cudaStream_t st) {
+    const int slots = (a.d + VEC - 1) / VEC;
+    const int ns = (slots + 31) / 32;
+    int blocks_needed;
+    auto go = [&](auto NSc) {
+        constexpr int NS = decltype(NSc)::value;
+        a.col_block = 32 * VEC * NS;
+        const int64_t tasks = a.n * ((a.d + a.col_block - 1) / a.col_block);
+        const int64_t want = (tasks + 7) / 8;
+        blocks_needed = (int)std::min<int64_t>(want, (int64_t)sm_count() * 16);
+        if (blocks_needed < 1) blocks_needed = 1;
+        bag_gather_kernel<TT, VEC, NS><<<blocks_needed, 256, 0, st>>>(a);
+    };
+    if (ns <= 1) go(std::integral_constant<int, 1>{});
+    else if (ns == 2) go(std::integral_constant<int, 2>{});
+    else if (ns == 3) go(std::integral_constant<int, 3>{});
+    else go(std::integral_constant<int, 4>{});
+    SMLM_LAUNCHED("bag_gather_kernel");
+    return SMLM_OK;
+}
+
+static int launch_bag(BagArgs a, int table_dtype, cudaStream_t st) {
+    if (a.n == 0 || a.d == 0) return SMLM_OK;
+    const uintptr_t tp = reinterpret_cast<uintptr_t>(a.table);
+    const uintptr_t op = reinterpret_cast<uintptr_t>(a.out);
+    const bool out_vec_ok = a.out_dtype != SMLM_F32 || (op % 16 == 0);
+    if (table_dtype == SMLM_F32) {
+        if (a.d % 4 == 0 && tp % 16 == 0 && out_vec_ok) return launch_bag_vec<float, 4>(a, st);
+        return launch_bag_vec<float, 1>(a, st);
+    }
+    if (a.d % 4 == 0 && tp % 8 == 0 && out_vec_ok) return launch_bag_vec<__nv_bfloat16, 4>(a, st);
+    return launch_bag_vec<__nv_bfloat16, 1>(a, st);
+}
+
+// ------------------------------------------------------------------------------------------------------ q4
+// Row r: d/2 bytes, byte i = (code of column i) | (code of column i + d/2) << 4, code = c + 8, value = c * s_r.
+struct Q4Args {
+    const int64_t* idx;
+    const void* w;
+    int w_dtype;
+    const uint8_t* table;
+    const uint16_t* scales;  // fp16 bits
+    const void* pre;
+    int pre_dtype;
+    void* out;
+    int out_dtype;
+    int64_t n, rows;
+    int k, d;
+    int* status;
+};
+
+// One warp per token; lane s handles bytes [8 s, 8 s + 8) of the row (columns 8s.. and d/2 + 8s..), so one
+// 8-byte load per lane per row; tokens with d/2 > 256 loop over byte blocks.
+template <int VEC>
+__global__ void __launch_bounds__(256) bag_q4_kernel(Q4Args a) {
+    const int lane = lane_id();
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int dh = a.d / 2;
+    const int blk = 32 * VEC;
+    const int nblk = (dh + blk - 1) / blk;
+    for (int64_t task = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < a.n * nblk;
+         task += warps) {
+        const int64_t n = task / nblk;
+        const int b0 = (int)(task % nblk) * blk + lane * VEC;
+        float lo[VEC], hi[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; i++) lo[i] = hi[i] = 0.f;
+        for (int j0 = 0; j0 < a.k; j0 += 32) {
+            const int cnt = min(32, a.k - j0);
+            int64_t my_r = -1;
+            float my_w = 0.f;
+            if (lane < cnt) {
+                my_r = __ldg(a.idx + n * a.k + j0 + lane);
+                my_w = load_weight(a.w, a.w_dtype, n * a.k + j0 + lane);
+                if (my_r < 0 || my_r >= a.rows) {
+                    flag(a.status, SMLM_FLAG_INDEX_RANGE);
+                    my_r = -1;
+                } else {
+                    my_w = my_w * __half2float(__ushort_as_half(__ldg(a.scales + my_r)));
+                }
+            }
+            for (int jj = 0; jj < cnt; jj++) {
+                const int64_t r = __shfl_sync(FULL, my_r, jj);
+                const float ws = __shfl_sync(FULL, my_w, jj);
+                if (r < 0 || b0 >= dh) continue;
+                uint8_t bytes[VEC];
+                if constexpr (VEC == 8) {
+                    uint2 x = __ldg(reinterpret_cast<const uint2*>(a.table + r * dh + b0));
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        bytes[i] = (x.x >> (8 * i)) & 0xff;
+                        bytes[4 + i] = (x.y >> (8 * i)) & 0xff;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < VEC; i++) bytes[i] = b0 + i < dh ? __ldg(a.table + r * dh + b0 + i) : 8;
+                }
+#pragma unroll
+                for (int i = 0; i < VEC; i++) {
+                    lo[i] = fmaf(ws, (float)((int)(bytes[i] & 15) - 8), lo[i]);
+                    hi[i] = fmaf(ws, (float)((int)(bytes[i] >> 4) - 8), hi[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+#pragma unroll
+            for (int i = 0; i < VEC; i++) {
+                if (b0 + i >= dh) continue;
+                const int col = b0 + i + half * dh;
+                float v = half ? hi[i] : lo[i];
+                const int64_t off = n * a.d + col;
+                if (a.pre) {
+                    const float p = a.pre_dtype == SMLM_F32
+                                        ? __ldg(static_cast<const float*>(a.pre) + off)
+                                        : bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(a.pre) + off));
+                    v = v * silu_bf16(p);
+                }
+                if (a.out_dtype == SMLM_F32) static_cast<float*>(a.out)[off] = v;
+                else static_cast<uint16_t*>(a.out)[off] = (uint16_t)f32_to_bf16_bits(v);
+            }
+        }
+    }
+}
+
+// One warp per row: scale from the element of largest |w| (first such column), then codes.
+__global__ void __launch_bounds__(256) quantize_q4_kernel(const float* table, int64_t rows, int d,
+                                                          uint8_t* packed, uint16_t* scales) {
+    const int lane = lane_id();
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int dh = d / 2;
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const float* row = table + r * d;
+        float best = -1.f;
+        int best_col = 0x7fffffff;
+        for (int c = lane; c < d; c += 32) {
+            const float a = fabsf(row[c]);
+            if (a > best) { best = a; best_col = c; }  // first column of this lane's largest |w|
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(FULL, best, o);
+            const int oc = __shfl_xor_sync(FULL, best_col, o);
+            if (ob > best || (ob == best && oc < best_col)) { best = ob; best_col = oc; }
+        }
+        if (best_col >= d) best_col = 0;  // all-NaN row
+        const float m = row[best_col];
+        __half dh16 = __float2half_rn(m / -8.0f);
+        if (__half2float(dh16) == 0.f) dh16 = __float2half_rn(1.0f);
+        const float s = __half2float(dh16);
+        for (int c = lane; c < dh; c += 32) {
+            const float q0 = fminf(fmaxf(rintf(row[c] / s), -8.f), 7.f) + 8.f;
+            const float q1 = fminf(fmaxf(rintf(row[c + dh] / s), -8.f), 7.f) + 8.f;
+            packed[r * dh + c] = (uint8_t)((int)q0 | ((int)q1 << 4));
+        }
+        if (lane == 0) scales[r] = __half_as_ushort(dh16);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------- backward
+constexpr uint32_t NO_ROW = 0xffffffffu;
+constexpr int FLAG_TAIL = 1;  // chunk's last run continues into the next chunk; partial in carry_tail
+constexpr int FLAG_MID = 2;   // the whole chunk is one run that started before and continues after
+
+static int chunk_positions(int64_t m) { return m >= (1 << 20) ? 256 : 64; }
+
+static int bit_width_u32(uint64_t x) {
+    int b = 0;
+    while (x) { b++; x >>= 1; }
+    return b;
+}
+
+__global__ void bb_keys_kernel(const int64_t* idx, int64_t m, int64_t rows, uint32_t* keys, uint32_t* pos,
+                               int* status) {
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < m; p += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = idx[p];
+        uint32_t key = (uint32_t)r;
+        if (r < 0 || r >= rows) {
+            flag(status, SMLM_FLAG_INDEX_RANGE);
+            key = (uint32_t)rows;  // sorts after every valid row; skipped by the segment pass
+        }
+        keys[p] = key;
+        pos[p] = (uint32_t)p;
+    }
+}
+
+struct SegArgs {
+    const uint32_t* keys;  // sorted rows
+    const uint32_t* pos;   // positions (n * k + j), ascending within a row
+    const float* g;        // grad_out (n, d)
+    const void* w;
+    int w_dtype;
+    const void* table;
+    float* acc;
+    uint8_t* touched;
+    float* gw;
+    float* carry_head;  // (chunks, d)
+    float* carry_tail;  // (chunks, d)
+    int* chunk_flags;   // (chunks,)
+    int64_t m, rows;
+    int k, d, P;
+    int64_t chunks;
+};
+
+// One warp per chunk of P sorted positions. Each run of equal rows is summed in position order; runs that
+// lie inside the chunk go straight into acc (they belong to this chunk alone: no atomics), the run that
+// enters from the previous chunk goes to carry_head, the run that leaves to carry_tail (see fixup).
+template <typename TT, int VEC, int NS>
+__global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
+    const int lane = lane_id();
+    const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (c >= a.chunks) return;
+    const TT* table = static_cast<const TT*>(a.table);
+    const int64_t start = c * a.P;
+    const int64_t end = min(start + (int64_t)a.P, a.m);
+    const uint32_t valid_lim = (uint32_t)a.rows;
+    const uint32_t first_row = a.keys[start];
+    const uint32_t last_row = a.keys[end - 1];
+    const uint32_t prev_row = start > 0 ? a.keys[start - 1] : NO_ROW;
+    const uint32_t next_row = end < a.m ? a.keys[end] : NO_ROW;
+    const bool head_cross = first_row < valid_lim && prev_row == first_row;
+    const bool tail_cross = last_row < valid_lim && next_row == last_row;
+    const bool mid = head_cross && tail_cross && first_row == last_row;
+    int cflags = 0;
+
+    uint32_t cur = NO_ROW;
+    float sum[NS][VEC], trow[NS][VEC];
+#pragma unroll
+    for (int s = 0; s < NS; s++)
+#pragma unroll
+        for (int i = 0; i < VEC; i++) sum[s][i] = trow[s][i] = 0.f;
+
+    auto flush = [&]() {
+        if (cur == NO_ROW || a.acc == nullptr) return;  // acc == NULL: per-sample-weight gradient only
+        float* dst = nullptr;
+        bool direct = false;
+        if (mid) {
+            dst = a.carry_head + c * a.d;
+            cflags |= FLAG_MID;
+        } else if (head_cross && cur == first_row) {
+            dst = a.carry_head + c * a.d;
+        } else if (tail_cross && cur == last_row) {
+            dst = a.carry_tail + c * a.d;
+            cflags |= FLAG_TAIL;
+        } else {
+            dst = a.acc + (int64_t)cur * a.d;
+            direct = true;
+        }
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = (lane + 32 * s) * VEC;
+            if (col < a.d) {
+                if constexpr (VEC == 4) {
+                    float4* q = reinterpret_cast<float4*>(dst + col);
+                    float4 x = direct ? *q : make_float4(0.f, 0.f, 0.f, 0.f);
+                    x.x = x.x + sum[s][0]; x.y = x.y + sum[s][1]; x.z = x.z + sum[s][2]; x.w = x.w + sum[s][3];
+                    *q = x;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < VEC; i++) dst[col + i] = (direct ? dst[col + i] : 0.f) + sum[s][i];
+                }
+            }
+        }
+        if (direct && lane == 0 && a.touched) a.touched[cur] = 1;
+    };
+
+    for (int64_t b = start; b < end; b += 32) {
+        const int cnt = (int)min((int64_t)32, end - b);
+        uint32_t my_key = NO_ROW, my_pos = 0;
+        if (lane < cnt) {
+            my_key = a.keys[b + lane];
+            my_pos = a.pos[b + lane];
+        }
+        for (int t = 0; t < cnt; t++) {
+            const uint32_t row = __shfl_sync(FULL, my_key, t);
+            const uint32_t p = __shfl_sync(FULL, my_pos, t);
+            if (row >= valid_lim) {  // out-of-range lookup (flagged when the keys were built)
+                if (lane == 0) a.gw[p] = 0.f;
+                continue;
+            }
+            if (row != cur) {
+                flush();
+                cur = row;
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    const int col = (lane + 32 * s) * VEC;
+#pragma unroll
+                    for (int i = 0; i < VEC; i++) sum[s][i] = 0.f;
+                    if (col < a.d) Elt<TT>::template load<VEC>(table + (int64_t)row * a.d + col, trow[s]);
+                }
+            }
+            const int64_t tok = p / a.k;
+            const float wv = load_weight(a.w, a.w_dtype, p);
+            float dot = 0.f;
+#pragma unroll
+            for (int s = 0; s < NS; s++) {
+                const int col = (lane + 32 * s) * VEC;
+                if (col < a.d) {
+                    float gv[VEC];
+                    Elt<float>::template load<VEC>(a.g + tok * a.d + col, gv);
+#pragma unroll
+                    for (int i = 0; i < VEC; i++) {
+                        sum[s][i] = fmaf(wv, gv[i], sum[s][i]);
+                        dot = fmaf(gv[i], trow[s][i], dot);
+                    }
+                }
+            }
+            dot = warp_sum(dot);
+            if (lane == 0) a.gw[p] = dot;
+        }
+    }
+    flush();
+    if (lane == 0) a.chunk_flags[c] = cflags;
+}
+
+// Completes the runs that cross chunk borders, in chunk order: tail of the run's first chunk, the full
+// chunks it covers, then the head of the chunk where it ends.
+template <int VEC>
+__global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a) {
+    const int lane = lane_id();
+    const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (c >= a.chunks || a.acc == nullptr) return;
+    if (!(a.chunk_flags[c] & FLAG_TAIL)) return;
+    const int64_t end = min((c + 1) * a.P, a.m);
+    const uint32_t row = a.keys[end - 1];
+    for (int col0 = lane * VEC; col0 < a.d; col0 += 32 * VEC) {
+        float tot[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; i++) tot[i] = a.carry_tail[c * a.d + col0 + i];
+        int64_t c2 = c + 1;
+        while (c2 < a.chunks && (a.chunk_flags[c2] & FLAG_MID)) {
+#pragma unroll
+            for (int i = 0; i < VEC; i++) tot[i] = tot[i] + a.carry_head[c2 * a.d + col0 + i];
+            c2++;
+        }
+        if (c2 < a.chunks) {
+#pragma unroll
+            for (int i = 0; i < VEC; i++) tot[i] = tot[i] + a.carry_head[c2 * a.d + col0 + i];
+        }
+        float* dst = a.acc + (int64_t)row * a.d + col0;
+#pragma unroll
+        for (int i = 0; i < VEC; i++) dst[i] = dst[i] + tot[i];
+    }
+    if (lane == 0 && a.touched) a.touched[row] = 1;
+}
+
+template <typename TT, int VEC>
+static int launch_segment(SegArgs a, cudaStream_t st) {
+    const int slots = (a.d + VEC - 1) / VEC;
+    const int ns = (slots + 31) / 32;
+    const int blocks = (int)((a.chunks + 7) / 8);
+    if (ns <= 1) bb_segment_kernel<TT, VEC, 1><<<blocks, 256, 0, st>>>(a);
+    else if (ns == 2) bb_segment_kernel<TT, VEC, 2><<<blocks, 256, 0, st>>>(a);
+    else if (ns == 3) bb_segment_kernel<TT, VEC, 3><<<blocks, 256, 0, st>>>(a);
+    else bb_segment_kernel<TT, VEC, 4><<<blocks, 256, 0, st>>>(a);
+    SMLM_LAUNCHED("bb_segment_kernel");
+    bb_fixup_kernel<VEC><<<blocks, 256, 0, st>>>(a);
+    SMLM_LAUNCHED("bb_fixup_kernel");
+    return SMLM_OK;
+}
+
+struct BackwardPlan {
+    int64_t m;
+    int P;
+    int64_t chunks;
+    int end_bit;
+    size_t sort_bytes;
+};
+
+static BackwardPlan plan_backward(int64_t n, int64_t k, int64_t rows) {
+    BackwardPlan p;
+    p.m = n * k;
+    p.P = chunk_positions(p.m);
+    p.chunks = (p.m + p.P - 1) / p.P;
+    p.end_bit = bit_width_u32((uint64_t)rows);
+    p.sort_bytes = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, p.sort_bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                    (const uint32_t*)nullptr, (uint32_t*)nullptr, (int)std::max<int64_t>(p.m, 1),
+                                    0, std::max(p.end_bit, 1));
+    return p;
+}
+
+struct BackwardBufs {
+    uint32_t *keys_in, *keys_out, *pos_in, *pos_out;
+    void* sort_tmp;
+    float *carry_head, *carry_tail;
+    int* flags;
+};
+
+// Carves the workspace (base == nullptr: only computes the size, returned).
+static size_t layout_backward(const BackwardPlan& p, int64_t d, void* base, BackwardBufs* b) {
+    size_t off = 0;
+    char* c = static_cast<char*>(base);
+    auto take = [&](size_t bytes) -> void* {
+        off = (off + 255) & ~size_t(255);
+        void* ptr = c ? c + off : nullptr;
+        off += bytes;
+        return ptr;
+    };
+    b->keys_in = static_cast<uint32_t*>(take(sizeof(uint32_t) * p.m));
+    b->keys_out = static_cast<uint32_t*>(take(sizeof(uint32_t) * p.m));
+    b->pos_in = static_cast<uint32_t*>(take(sizeof(uint32_t) * p.m));
+    b->pos_out = static_cast<uint32_t*>(take(sizeof(uint32_t) * p.m));
+    b->sort_tmp = take(p.sort_bytes);
+    b->carry_head = static_cast<float*>(take(sizeof(float) * p.chunks * d));
+    b->carry_tail = static_cast<float*>(take(sizeof(float) * p.chunks * d));
+    b->flags = static_cast<int*>(take(sizeof(int) * p.chunks));
+    return off;
+}
+
+}  // namespace smlm
+
+using namespace smlm;
+
+extern "C" int smlm_bag_forward(const int64_t* indices, const void* weights, int weights_dtype, const void* table,
+                                int table_dtype, int64_t n, int64_t k, int64_t rows, int64_t d, void* out,
+                                int out_dtype, int* status, void* stream) {
+    SMLM_CHECK_ARG(n >= 0 && k >= 0 && rows >= 0 && d >= 0, "bag_forward: negative size");
+    SMLM_CHECK_ARG(table_dtype == SMLM_F32 || table_dtype == SMLM_BF16, "bag_forward: table must be fp32 or bf16");
+    SMLM_CHECK_ARG(weights_dtype == SMLM_F32 || weights_dtype == SMLM_BF16, "bag_forward: weights must be fp32 or bf16");
+    SMLM_CHECK_ARG(out_dtype == SMLM_F32 || out_dtype == SMLM_BF16, "bag_forward: out must be fp32 or bf16");
+    SMLM_CHECK_ARG(d < (1 << 30) && k < (1 << 30), "bag_forward: d or k too large");
+    if (n == 0 || d == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(indices && table && out && (k == 0 || weights), "bag_forward: null pointer");
+    BagArgs a{indices, weights, weights_dtype, table, nullptr, SMLM_F32, out, out_dtype, n, rows, (int)k, (int)d,
+              0, status};
+    return launch_bag(a, table_dtype, as_stream(stream));
+}
+
+extern "C" int smlm_bag_infer(const int64_t* indices, const void* weights, int weights_dtype, const void* table,
+                              int table_dtype, const void* scales, const void* pre, int pre_dtype, int64_t n,
+                              int64_t k, int64_t rows, int64_t d, void* out, int out_dtype, int* status,
+                              void* stream) {
+    SMLM_CHECK_ARG(n >= 0 && k >= 0 && rows >= 0 && d >= 0, "bag_infer: negative size");
+    SMLM_CHECK_ARG(table_dtype == SMLM_F32 || table_dtype == SMLM_BF16 || table_dtype == SMLM_Q4,
+                   "bag_infer: table must be fp32, bf16 or q4");
+    SMLM_CHECK_ARG(weights_dtype == SMLM_F32 || weights_dtype == SMLM_BF16, "bag_infer: weights must be fp32 or bf16");
+    SMLM_CHECK_ARG(out_dtype == SMLM_F32 || out_dtype == SMLM_BF16, "bag_infer: out must be fp32 or bf16");
+    SMLM_CHECK_ARG(pre == nullptr || pre_dtype == SMLM_F32 || pre_dtype == SMLM_BF16, "bag_infer: pre must be fp32 or bf16");
+    SMLM_CHECK_ARG(table_dtype != SMLM_Q4 || (d % 2 == 0 && scales != nullptr), "bag_infer: q4 needs an even width and scales");
+    SMLM_CHECK_ARG(d < (1 << 30) && k < (1 << 30), "bag_infer: d or k too large");
+    if (n == 0 || d == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(indices && table && out && (k == 0 || weights), "bag_infer: null pointer");
+    cudaStream_t st = as_stream(stream);
+    if (table_dtype == SMLM_Q4) {
+        Q4Args a{indices, weights, weights_dtype, static_cast<const uint8_t*>(table),
+                 static_cast<const uint16_t*>(scales), pre, pre_dtype, out, out_dtype, n, rows, (int)k, (int)d,
+                 status};
+        const int dh = (int)(d / 2);
+        const bool vec = dh % 8 == 0 && reinterpret_cast<uintptr_t>(table) % 8 == 0;
+        const int blk = 32 * (vec ? 8 : 1);
+        const int64_t tasks = n * ((dh + blk - 1) / blk);
+        const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((tasks + 7) / 8, (int64_t)sm_count() * 16));
+        if (vec) bag_q4_kernel<8><<<blocks, 256, 0, st>>>(a);
+        else bag_q4_kernel<1><<<blocks, 256, 0, st>>>(a);
+        SMLM_LAUNCHED("bag_q4_kernel");
+        return SMLM_OK;
+    }
+    BagArgs a{indices, weights, weights_dtype, table, pre, pre_dtype, out, out_dtype, n, rows, (int)k, (int)d, 0,
+              status};
+    return launch_bag(a, table_dtype, st);
+}
+
+extern "C" int smlm_quantize_q4(const float* table, int64_t rows, int64_t d, uint8_t* packed, void* scales_f16,
+                                void* stream) {
+    SMLM_CHECK_ARG(rows >= 0 && d >= 0 && d % 2 == 0 && d < (1 << 30), "quantize_q4: width must be even");
+    if (rows == 0 || d == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(table && packed && scales_f16, "quantize_q4: null pointer");
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16));
+    quantize_q4_kernel<<<blocks, 256, 0, as_stream(stream)>>>(table, rows, (int)d, packed,
+                                                              static_cast<uint16_t*>(scales_f16));
+    SMLM_LAUNCHED("quantize_q4_kernel");
+    return SMLM_OK;
+}
+
+extern "C" size_t smlm_bag_backward_workspace(int64_t n, int64_t k, int64_t rows, int64_t d) {
+    if (n <= 0 || k <= 0) return 0;
+    BackwardPlan p = plan_backward(n, k, rows);
+    BackwardBufs b;
+    return layout_backward(p, d, nullptr, &b);
+}
+
+extern "C" int smlm_bag_backward_rows(const float* grad_out, const int64_t* indices, const void* weights,
+                                      int weights_dtype, const void* table, int table_dtype, float* acc,
+                                      uint8_t* touched, float* gw, int64_t n, int64_t k, int64_t rows, int64_t d,
+                                      void* workspace, size_t workspace_bytes, int* status, void* stream) {
+    SMLM_CHECK_ARG(n >= 0 && k >= 0 && rows >= 0 && d >= 0, "bag_backward_rows: negative size");
+    SMLM_CHECK_ARG(table_dtype == SMLM_F32 || table_dtype == SMLM_BF16, "bag_backward_rows: table must be fp32 or bf16");
+    SMLM_CHECK_ARG(weights_dtype == SMLM_F32 || weights_dtype == SMLM_BF16, "bag_backward_rows: weights must be fp32 or bf16");
+    SMLM_CHECK_ARG(n * k < (int64_t)0x7fffffff, "bag_backward_rows: n * k must be below 2^31");
+    SMLM_CHECK_ARG(rows < (int64_t)0xffffffff, "bag_backward_rows: rows must be below 2^32 - 1");
+    SMLM_CHECK_ARG(d < (1 << 30), "bag_backward_rows: d too large");
+    if (n == 0 || k == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(grad_out && indices && weights && table && gw, "bag_backward_rows: null pointer");
+    if (d == 0) {
+        SMLM_CUDA(cudaMemsetAsync(gw, 0, sizeof(float) * n * k, as_stream(stream)));
+    }
+    BackwardPlan p = plan_backward(n, k, rows);
+    BackwardBufs bb;
+    const size_t need = layout_backward(p, d, nullptr, &bb);
+    if (workspace == nullptr || workspace_bytes < need) {
+        set_error("bag_backward_rows: workspace too small (%zu < %zu)", workspace_bytes, need);
+        return SMLM_ERR_WORKSPACE;
+    }
+    layout_backward(p, d, workspace, &bb);
+    uint32_t *keys_in = bb.keys_in, *keys_out = bb.keys_out, *pos_in = bb.pos_in, *pos_out = bb.pos_out;
+    void* sort_tmp = bb.sort_tmp;
+    float *carry_head = bb.carry_head, *carry_tail = bb.carry_tail;
+    int* flags = bb.flags;
+    cudaStream_t st = as_stream(stream);
+    const int kb = (int)std::max<int64_t>(1, std::min<int64_t>((p.m + 255) / 256, (int64_t)sm_count() * 8));
+    bb_keys_kernel<<<kb, 256, 0, st>>>(indices, p.m, rows, keys_in, pos_in, status);
+    SMLM_LAUNCHED("bb_keys_kernel");
+    size_t sort_bytes = p.sort_bytes;
+    SMLM_CUDA(cub::DeviceRadixSort::SortPairs(sort_tmp, sort_bytes, keys_in, keys_out, pos_in, pos_out, (int)p.m, 0,
+                                              std::max(p.end_bit, 1), st));
+    if (d == 0) return SMLM_OK;
+    SegArgs a{keys_out, pos_out, grad_out, weights, weights_dtype, table, acc, touched, gw, carry_head,
+              carry_tail, flags, p.m, rows, (int)k, (int)d, p.P, p.chunks};
+    const uintptr_t tp = reinterpret_cast<uintptr_t>(table);
+    const uintptr_t gp = reinterpret_cast<uintptr_t>(grad_out);
+    const uintptr_t ap = reinterpret_cast<uintptr_t>(acc);
+    const bool vec = d % 4 == 0 && gp % 16 == 0 && ap % 16 == 0 &&
+                     tp % (table_dtype == SMLM_F32 ? 16 : 8) == 0;
+    if (table_dtype == SMLM_F32) return vec ? launch_segment<float, 4>(a, st) : launch_segment<float, 1>(a, st);
+    return vec ? launch_segment<__nv_bfloat16, 4>(a, st) : launch_segment<__nv_bfloat16, 1>(a, st);
+}

@@ -1,0 +1,130 @@
+// Shared device/host helpers for the PKM layer kernels (sm_100a only).
+//
+// Every kernel in this library is launched on the caller's stream, allocates nothing (scratch comes in
+// through a workspace pointer whose size the matching *_workspace query returns), and never traps: index
+// range violations set a bit in a caller-provided device status word and the offending lookup is skipped.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "../../include/smlm_b200.h"
+
+#if !defined(__CUDA_ARCH__) || __CUDA_ARCH__ >= 1000
+#else
+#error "this library is built for sm_100a only"
+#endif
+
+namespace smlm {
+
+// ------------------------------------------------------------------------------------------------ host side
+// Thread-local last-error message, read through smlm_last_error().
+void set_error(const char* fmt, ...);
+int cuda_status(cudaError_t e, const char* what);
+
+#define SMLM_CHECK_ARG(cond, ...)                 \
+    do {                                          \
+        if (!(cond)) {                            \
+            ::smlm::set_error(__VA_ARGS__);       \
+            return SMLM_ERR_INVALID;              \
+        }                                         \
+    } while (0)
+
+#define SMLM_CUDA(call)                                              \
+    do {                                                             \
+        cudaError_t _e = (call);                                     \
+        if (_e != cudaSuccess) return ::smlm::cuda_status(_e, #call); \
+    } while (0)
+
+#define SMLM_LAUNCHED(what)                                          \
+    do {                                                             \
+        cudaError_t _e = cudaGetLastError();                         \
+        if (_e != cudaSuccess) return ::smlm::cuda_status(_e, what); \
+    } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Bump allocator over a caller-provided workspace; every slice is 256-byte aligned.
+struct Workspace {
+    char* base;
+    size_t size;
+    size_t used = 0;
+    Workspace(void* b, size_t s) : base(static_cast<char*>(b)), size(s) {}
+    template <typename T>
+    T* take(size_t count) {
+        size_t off = (used + 255) & ~size_t(255);
+        used = off + count * sizeof(T);
+        return reinterpret_cast<T*>(base + off);
+    }
+    bool ok() const { return used <= size; }
+};
+// The same carve-up without a base pointer, for the size queries.
+struct WorkspaceSize {
+    size_t used = 0;
+    template <typename T>
+    void take(size_t count) { used = ((used + 255) & ~size_t(255)) + count * sizeof(T); }
+};
+
+// ---------------------------------------------------------------------------------------------- device side
+constexpr unsigned FULL = 0xffffffffu;
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
+
+// fp32 -> bf16 bits, round to nearest even (PyTorch's c10::BFloat16 rounding for finite values).
+__device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0u;  // NaN
+    return (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
+}
+__device__ __forceinline__ float round_bf16(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+
+// Order-preserving unsigned codes: a larger code means a larger value; -0 is mapped onto +0 so that the two
+// zeros tie (and the tie goes to the lower index, as for any other equal scores).
+__device__ __forceinline__ uint32_t order_code16(uint32_t b) {
+    b &= 0xffffu;
+    if (b == 0x8000u) b = 0;
+    return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+}
+__device__ __forceinline__ uint32_t decode_code16(uint32_t c) {
+    return (c & 0x8000u) ? (c ^ 0x8000u) : (~c & 0xffffu);
+}
+__device__ __forceinline__ uint32_t order_code32(uint32_t u) {
+    if (u == 0x80000000u) u = 0;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ uint32_t decode_code32(uint32_t c) {
+    return (c & 0x80000000u) ? (c ^ 0x80000000u) : ~c;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+__device__ __forceinline__ void flag(int* status, int bit) {
+    if (status) atomicOr(status, bit);
+}
+
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+}  // namespace smlm

@@ -1,0 +1,289 @@
+"""sm_100a kernels of the product-key memory, with the Python signatures of the reference's kernel layer.
+
+Each function below stands in for the function of the same name in re133/sparse-memory-lm smlm/kernels.py
+(file:line given per function) and calls libsmlm_b200.so through its C ABI (include/smlm_b200.h). All tensors
+must be CUDA tensors; nothing here has a CPU path. Kernels run on the current CUDA stream without host
+synchronisation, so every function can be captured in a CUDA graph.
+"""
+import math
+
+import torch
+
+from . import _lib as L
+
+
+def _contig(t):
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ------------------------------------------------------------------------------------------ selection
+def pk_select(s1, s2, knn):
+    """s1, s2 (N, H, n_keys) bf16 or fp32 sub-key scores -> scores (N, H, knn) (same dtype), indices (N, H, knn)
+    int64 into the n_keys^2 table, softmax weights (N, H, knn) fp32 (reference: kernels.py:214-226).
+
+    Both half top-k, the knn x knn pair sums rounded to the score dtype, the final top-k and the softmax.
+    Order: score descending, ties to the lower index (i1 * n_keys + i2 for the final list)."""
+    if s1.shape != s2.shape or s1.dim() != 3 or s1.dtype != s2.dtype:
+        raise ValueError("pk_select: s1 and s2 must be (N, H, n_keys) tensors of one dtype")
+    dev = L.require_cuda(s1, s2)
+    N, H, NK = s1.shape
+    s1, s2 = _contig(s1), _contig(s2)
+    scores = torch.empty(N, H, knn, dtype=s1.dtype, device=dev)
+    idx = torch.empty(N, H, knn, dtype=torch.int64, device=dev)
+    w = torch.empty(N, H, knn, dtype=torch.float32, device=dev)
+    with L.timed("pk_select", 1):
+        rc = L.lib().smlm_pk_select(L.ptr(s1), L.ptr(s2), L.dtype_code(s1.dtype), N, H, NK, knn, L.ptr(scores),
+                                        L.ptr(idx), L.ptr(w), L.stream(dev))
+    L.check(rc, "pk_select")
+    L.after(dev, "pk_select")
+    return scores, idx, w
+
+
+def select_backward(idx, w, g_w, g_scores, n_keys, dtype):
+    """Dense gradients (ds1, ds2) (N, H, n_keys) of the selection (reference: kernels.py:253-266)."""
+    dev = L.require_cuda(idx, w, g_w, g_scores)
+    N, H, knn = idx.shape
+    ds1 = torch.empty(N, H, n_keys, dtype=dtype, device=dev)
+    ds2 = torch.empty(N, H, n_keys, dtype=dtype, device=dev)
+    g_w = None if g_w is None else _contig(g_w.float())
+    g_scores = None if g_scores is None else _contig(g_scores.to(dtype))
+    with L.timed("select_backward", 1):
+        rc = L.lib().smlm_select_backward(L.ptr(_contig(idx)), L.ptr(_contig(w)), L.ptr(g_w), L.ptr(g_scores),
+                                          L.dtype_code(dtype), N, H, n_keys, knn, L.ptr(ds1), L.ptr(ds2),
+                                          L.stream(dev))
+    L.check(rc, "select_backward")
+    return ds1, ds2
+
+
+class PKSelect(torch.autograd.Function):
+    """Differentiable pk_select (reference: kernels.py:240-266). Backward: softmax backward, the score gradient
+    rounded to the score dtype, summed per sub-key in fp32 (selection order) and rounded once; dense
+    (N, H, n_keys) gradients for the scoring contraction's backward."""
+
+    @staticmethod
+    def forward(ctx, s1, s2, knn):
+        scores, idx, w = pk_select(s1, s2, knn)
+        ctx.save_for_backward(idx, w)
+        ctx.nk, ctx.dtype = s1.shape[-1], s1.dtype
+        ctx.mark_non_differentiable(idx)
+        return scores, idx, w
+
+    @staticmethod
+    def backward(ctx, g_scores, g_idx, g_w):
+        idx, w = ctx.saved_tensors
+        ds1, ds2 = select_backward(idx, w, g_w, g_scores, ctx.nk, ctx.dtype)
+        return ds1, ds2, None
+
+
+def subkey_scores_f32(q, keys):
+    """Exact fp32 sub-key scores (reference: pkm.py:117-123 in fp32): q (N, H, k_dim), keys (H, 2, n_keys, k_dim/2)
+    -> s1, s2 (N, H, n_keys), each score a sequential fmaf chain over the half dimension."""
+    if q.dtype != torch.float32 or keys.dtype != torch.float32:
+        raise ValueError("subkey_scores_f32 needs fp32 queries and keys")
+    dev = L.require_cuda(q, keys)
+    N, H, KD = q.shape
+    Hk, two, NK, half = keys.shape
+    if Hk != H or two != 2 or KD != 2 * half:
+        raise ValueError(f"subkey_scores_f32: query {tuple(q.shape)} does not match keys {tuple(keys.shape)}")
+    q, keys = _contig(q), _contig(keys)
+    s1 = torch.empty(N, H, NK, dtype=torch.float32, device=dev)
+    s2 = torch.empty(N, H, NK, dtype=torch.float32, device=dev)
+    step = 65535 * 64
+    for a in range(0, max(N, 1), step):
+        b = min(N, a + step)
+        if b <= a:
+            break
+        with L.timed("subkey_scores_f32", 1):
+            rc = L.lib().smlm_subkey_scores_f32(L.ptr(q[a:b]), L.ptr(keys), b - a, H, NK, half, L.ptr(s1[a:b]),
+                                                L.ptr(s2[a:b]), L.stream(dev))
+        L.check(rc, "subkey_scores_f32")
+    return s1, s2
+
+
+class SubkeyScoresF32(torch.autograd.Function):
+    """Exact fp32 scoring with autograd: forward the fmaf-chain kernel, backward the two contractions
+    (dq = ds K, dK = ds^T q) of the reference's einsum backward."""
+
+    @staticmethod
+    def forward(ctx, q, keys):
+        ctx.save_for_backward(q, keys)
+        return subkey_scores_f32(q, keys)
+
+    @staticmethod
+    def backward(ctx, ds1, ds2):
+        q, keys = ctx.saved_tensors
+        half = keys.shape[-1]
+        dq = dk = None
+        if ctx.needs_input_grad[0]:
+            dq = torch.cat([torch.einsum("nhk,hkd->nhd", ds1, keys[:, 0]),
+                            torch.einsum("nhk,hkd->nhd", ds2, keys[:, 1])], dim=-1)
+        if ctx.needs_input_grad[1]:
+            dk = torch.stack([torch.einsum("nhk,nhd->hkd", ds1, q[..., :half]),
+                              torch.einsum("nhk,nhd->hkd", ds2, q[..., half:])], dim=1)
+        return dq, dk
+
+
+# ------------------------------------------------------------------------------------------ value bag
+def bag_forward(indices, weights, table, out_dtype=torch.float32):
+    """out[n] = sum_k weights[n, k] * table[indices[n, k]] (fp32 accumulation); table fp32 / bf16
+    (reference: kernels.py:229-237)."""
+    dev = L.require_cuda(indices, weights, table)
+    N, K = indices.shape
+    D = table.shape[1]
+    out = torch.empty(N, D, dtype=out_dtype, device=dev)
+    idx = _contig(indices.long())
+    w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
+    table = _contig(table)
+    with L.timed("bag_forward", 1):
+        rc = L.lib().smlm_bag_forward(L.ptr(idx), L.ptr(w), L.dtype_code(w.dtype), L.ptr(table),
+                                      L.dtype_code(table.dtype), N, K, table.shape[0], D, L.ptr(out),
+                                      L.dtype_code(out_dtype), L.status_ptr(dev), L.stream(dev))
+    L.check(rc, "bag_forward")
+    L.after(dev, "bag_forward")
+    return out
+
+
+def bag_backward_rows(grad_out, indices, weights, table, acc, touched):
+    """grad_out (N, D), indices / weights (N, K) -> per-sample-weight gradient (N, K) fp32;
+    acc[indices[n, k]] += weights[n, k] * grad_out[n] and touched[indices] = True, in place
+    (reference: kernels.py:73-88). Deterministic: sorted rows, no float atomics.
+    acc / touched may be None (frozen table: only the weight gradient)."""
+    dev = L.require_cuda(grad_out, indices, weights, table, acc, touched)
+    N, K = indices.shape
+    D = table.shape[1]
+    if acc is not None and (acc.dtype != torch.float32 or not acc.is_contiguous() or acc.shape != table.shape):
+        raise ValueError("bag_backward_rows: acc must be a contiguous fp32 tensor shaped like the table")
+    if touched is not None and (touched.dtype not in (torch.bool, torch.uint8) or not touched.is_contiguous()):
+        raise ValueError("bag_backward_rows: touched must be a contiguous bool mask")
+    g = _contig(grad_out.float())
+    idx = _contig(indices.long())
+    w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
+    table = _contig(table)
+    gw = torch.empty(N, K, dtype=torch.float32, device=dev)
+    ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, K, table.shape[0], D), dev)
+    with L.timed("bag_backward_rows", L.BACKWARD_LAUNCHES):
+        rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.ptr(idx), L.ptr(w), L.dtype_code(w.dtype), L.ptr(table),
+                                            L.dtype_code(table.dtype), L.ptr(acc), L.ptr(touched), L.ptr(gw), N, K,
+                                            table.shape[0], D, L.ptr(ws), ws.numel(), L.status_ptr(dev),
+                                            L.stream(dev))
+    L.check(rc, "bag_backward_rows")
+    L.after(dev, "bag_backward_rows")
+    return gw
+
+
+def quantize_q4(table, chunk=None):
+    """table (rows, D) fp32 -> packed (rows, D/2) uint8, scales (rows,) fp16 (reference: kernels.py:280-294):
+    per row d = half(w[argmax |w|] / -8) (1 if that is 0), codes clamp(round(w / d), -8, 7) + 8; byte i holds
+    column i (low nibble) and column i + D/2 (high nibble)."""
+    dev = L.require_cuda(table)
+    rows, D = table.shape
+    if D % 2:
+        raise ValueError("quantize_q4 needs an even row width")
+    t = _contig(table.float())
+    packed = torch.empty(rows, D // 2, dtype=torch.uint8, device=dev)
+    scales = torch.empty(rows, dtype=torch.float16, device=dev)
+    L.check(L.lib().smlm_quantize_q4(L.ptr(t), rows, D, L.ptr(packed), L.ptr(scales), L.stream(dev)),
+            "quantize_q4")
+    return packed, scales
+
+
+def dequantize_q4(packed, scales):
+    """Inverse of quantize_q4 (reference: kernels.py:297-300); a format helper for checks, not on the hot path."""
+    lo = (packed & 15).float() - 8
+    hi = (packed >> 4).float() - 8
+    return torch.cat([lo, hi], dim=1) * scales.float()[:, None]
+
+
+def bag_infer(indices, weights, table, scales=None, pre=None, out_bf16=False):
+    """Inference value bag (reference: kernels.py:364-378). table fp32 / bf16 (scales None) or q4-packed uint8
+    (rows, D/2) with fp16 scales. pre: optional (N, D) swilu pre-activation -> out = bag * bf16(silu(pre)).
+    Returns (N, D) fp32, or bf16 with out_bf16."""
+    dev = L.require_cuda(indices, weights, table, scales, pre)
+    N, K = indices.shape
+    q4 = scales is not None
+    D = table.shape[1] * (2 if q4 else 1)
+    out = torch.empty(N, D, dtype=torch.bfloat16 if out_bf16 else torch.float32, device=dev)
+    idx = _contig(indices.long())
+    w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
+    table = _contig(table)
+    if q4:
+        if table.dtype != torch.uint8 or scales.dtype != torch.float16:
+            raise ValueError("bag_infer: q4 tables are uint8 with fp16 scales")
+        tcode = L.Q4
+    else:
+        tcode = L.dtype_code(table.dtype)
+    if pre is not None:
+        pre = _contig(pre if pre.dtype in (torch.float32, torch.bfloat16) else pre.float())
+    with L.timed("bag_infer", 1):
+        rc = L.lib().smlm_bag_infer(L.ptr(idx), L.ptr(w), L.dtype_code(w.dtype), L.ptr(table), tcode,
+                                   L.ptr(_contig(scales) if q4 else None), L.ptr(pre),
+                                   L.dtype_code(pre.dtype) if pre is not None else L.F32, N, K, table.shape[0], D,
+                                   L.ptr(out), L.BF16 if out_bf16 else L.F32, L.status_ptr(dev), L.stream(dev))
+    L.check(rc, "bag_infer")
+    L.after(dev, "bag_infer")
+    return out
+
+
+# ------------------------------------------------------------------------------------------ optimizers
+def _scale_args(grad_scale, device):
+    """(device pointer or None, host float, keep-alive tensor) for a float or 0-d tensor clip factor."""
+    if torch.is_tensor(grad_scale):
+        t = grad_scale.detach().to(device=device, dtype=torch.float32).reshape(1)
+        t = _contig(t)
+        return L.ptr(t), 1.0, t
+    return None, float(grad_scale), None
+
+
+def lazy_adam_step(param, exp_avg, exp_avg_sq, acc, touched, grad_scale, step, lr, beta1, beta2, eps,
+                   value_copy=None):
+    """In-place lazy Adam step over the touched rows (reference: kernels.py:417-433): torch's Adam formula, global
+    step for the bias correction, no weight decay; the touched accumulator rows are zeroed and the mask cleared.
+    grad_scale: 0-d tensor (clip factor) or float; step: the step number after this update (1 for the first).
+    value_copy: optional (rows, D) bf16 / fp32 tensor that receives the updated rows too."""
+    dev = L.require_cuda(param, exp_avg, exp_avg_sq, acc, touched, value_copy)
+    for t in (param, exp_avg, exp_avg_sq, acc):
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.shape != param.shape:
+            raise ValueError("lazy_adam_step: param, moments and acc must be contiguous fp32 of one shape")
+    rows, D = param.shape
+    sp, sf, keep = _scale_args(grad_scale, dev)
+    bc1 = 1 - beta1 ** step
+    bc2 = 1 - beta2 ** step
+    ws = L.workspace(L.lib().smlm_touched_workspace(rows), dev)
+    with L.timed("lazy_adam_step", L.COMPACT_LAUNCHES + 1):
+        rc = L.lib().smlm_lazy_adam_step(L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(acc),
+                                         L.ptr(touched), sp, sf, rows, D, 1 - beta1, beta2, 1 - beta2,
+                                         math.sqrt(bc2), eps, -(lr / bc1), L.ptr(value_copy),
+                                         L.dtype_code(value_copy.dtype) if value_copy is not None else L.F32,
+                                         L.ptr(ws), ws.numel(), L.stream(dev))
+    L.check(rc, "lazy_adam_step")
+    del keep
+
+
+def rowwise_step(param, acc, touched, v, n, grad_scale, lr, beta2, eps, kind):
+    """Row-wise rowrms / rowadagrad step over the touched rows, in place; accumulator rows zeroed, mask cleared
+    (reference: row_optim.py:168-201, formulas of host_rows.c:84-117)."""
+    dev = L.require_cuda(param, acc, touched, v, n)
+    rows, D = param.shape
+    code = {"rowrms": L.ROWRMS, "rowadagrad": L.ROWADAGRAD}[kind]
+    sp, sf, keep = _scale_args(grad_scale, dev)
+    ws = L.workspace(L.lib().smlm_touched_workspace(rows), dev)
+    with L.timed("rowwise_step", L.COMPACT_LAUNCHES + 1):
+        rc = L.lib().smlm_rowwise_step(L.ptr(param), L.ptr(acc), L.ptr(touched), L.ptr(v), L.ptr(n), sp, sf, rows,
+                                       D, code, beta2, eps, lr, L.ptr(ws), ws.numel(), L.stream(dev))
+    L.check(rc, "rowwise_step")
+    del keep
+
+
+def touched_norm(acc, touched):
+    """L2 norm (0-d fp32 tensor on the device) of the accumulator rows marked in `touched`; equals acc.norm()
+    for a RowStore, whose untouched rows are zero (reference: sparse_values.py:143)."""
+    dev = L.require_cuda(acc, touched)
+    rows = acc.shape[0]
+    D = acc.shape[1] if acc.dim() > 1 else 1
+    out = torch.empty((), dtype=torch.float32, device=dev)
+    ws = L.workspace(L.lib().smlm_touched_workspace(rows), dev)
+    with L.timed("touched_norm", L.COMPACT_LAUNCHES + 2):
+        rc = L.lib().smlm_touched_norm(L.ptr(_contig(acc)), L.ptr(touched), rows, D, L.ptr(out), L.ptr(ws),
+                                       ws.numel(), L.stream(dev))
+    L.check(rc, "touched_norm")
+    return out

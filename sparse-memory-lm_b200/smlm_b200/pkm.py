@@ -1,0 +1,209 @@
+"""Product-key memory layer on the sm_100a kernels (reference: re133/sparse-memory-lm smlm/pkm.py).
+
+Same constructor, parameters, initialisation, state_dict keys and forward contract as the reference's
+ProductKeyMemory; the lookup runs on libsmlm_b200.so:
+  * scoring + selection: under bf16 autocast the bf16 sub-key scores (pkm.py:197, the reference's einsum) go
+    through the selection kernel (both half top-k, pair sums, final top-k, softmax); without autocast the
+    scores are computed exactly in fp32 by the fmaf-chain kernel and selected the same way;
+  * value bag: row_sparse_embedding_bag (row-sparse accumulation + lazy optimizer), or the inference bag with
+    the swilu product fused when there is no grad under bf16 autocast (pkm.py:213-224);
+  * decoding (one token, no grad, decode_graph): a captured CUDA graph of the same kernels (pkm.py:159-184).
+Ties in the selection go to the lower index. The query projection, BatchNorm and swilu projections stay
+PyTorch modules (dense host code).
+"""
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import kernels as K
+from .sparse_values import row_sparse_embedding_bag
+
+IMPLS = ("cuda", "triton", "torch")
+
+
+class ProductKeyMemory(nn.Module):
+    def __init__(self, d_in, d_out, n_keys=512, heads=4, knn=32, k_dim=256, v_dim=-1,
+                 query_norm="batchnorm", swilu=True, value_impl="embedding_bag",
+                 keys_weight_decay=True, score_scale="none", score_scale_init=1.0, shared_values=None,
+                 value_grad="dense", impl="cuda"):
+        super().__init__()
+        assert k_dim % 2 == 0 and knn <= n_keys
+        self.d_in, self.d_out = d_in, d_out
+        self.n_keys, self.heads, self.knn, self.k_dim = n_keys, heads, knn, k_dim
+        self.size = n_keys ** 2
+        self.v_dim = v_dim if v_dim > 0 else d_out
+        self.swilu = swilu
+        self.value_impl = value_impl
+        assert value_grad in ("dense", "row_sparse")
+        self.value_grad = value_grad
+        if impl not in IMPLS:
+            raise ValueError(f"unknown impl {impl!r}")
+        if not (1 <= knn <= 32 and n_keys <= 65536):
+            # the selection kernel keeps one selected entry per lane of a warp and packs (i1, i2) into 32 bits
+            raise ValueError(f"the CUDA selection needs 1 <= knn <= 32 and n_keys <= 65536, got n_keys={n_keys}, "
+                             f"knn={knn}")
+        self.impl = "cuda"
+        self.score_scale_init = score_scale_init
+
+        self.keys = nn.Parameter(torch.empty(heads, 2, n_keys, k_dim // 2))
+        if not keys_weight_decay:
+            self.keys.no_weight_decay = True
+        if score_scale == "learned":
+            assert score_scale_init > 0
+            self.log_score_scale = nn.Parameter(torch.empty(heads))
+        elif score_scale == "none":
+            self.log_score_scale = None
+        else:
+            raise ValueError(score_scale)
+        self.query_proj = nn.Linear(d_in, heads * k_dim, bias=True)
+        if query_norm == "batchnorm":
+            self.query_norm = nn.BatchNorm1d(heads * k_dim)
+        elif query_norm == "none":
+            self.query_norm = None
+        else:
+            raise ValueError(query_norm)
+        if shared_values is not None:
+            assert shared_values.weight.shape == (self.size, self.v_dim)
+            self.values = shared_values
+        else:
+            self.values = nn.Embedding(self.size, self.v_dim)
+        if swilu:
+            self.swilu_proj = nn.Linear(d_in, self.v_dim)
+            self.value_proj = nn.Linear(self.v_dim, d_out)
+        else:
+            assert self.v_dim == d_out
+        self.record = False
+        self.last_indices = None
+        self.last_scores = None
+        self.last_weights = None
+        self.reset_parameters()
+
+    @torch.no_grad()
+    def reset_parameters(self):
+        """Initialisation of the reference (pkm.py:94-109)."""
+        bound = 1 / math.sqrt(self.k_dim)
+        nn.init.uniform_(self.keys, -bound, bound)
+        nn.init.normal_(self.values.weight, mean=0.0, std=self.v_dim ** -0.5)
+        nn.init.xavier_uniform_(self.query_proj.weight)
+        nn.init.zeros_(self.query_proj.bias)
+        if self.swilu:
+            nn.init.normal_(self.swilu_proj.weight, mean=0.0, std=self.d_out ** -0.5)
+            nn.init.normal_(self.value_proj.weight, mean=0.0, std=self.d_out ** -0.5)
+            nn.init.zeros_(self.swilu_proj.bias)
+            nn.init.zeros_(self.value_proj.bias)
+        if self.log_score_scale is not None:
+            nn.init.constant_(self.log_score_scale, math.log(self.score_scale_init))
+        self.values.weight.pk_value_param = True
+
+    def score_scale(self):
+        if self.log_score_scale is None:
+            return torch.ones(self.heads, device=self.keys.device)
+        return self.log_score_scale.exp()
+
+    def subkey_scores(self, query):
+        """query (N, heads, k_dim) -> sub-key scores s1, s2 (N, heads, n_keys) (reference: pkm.py:117-123).
+        fp32 queries: the exact fmaf-chain kernel; bf16 queries: the bf16 contraction (fp32 accumulation)."""
+        if query.dtype == torch.float32:
+            return K.SubkeyScoresF32.apply(query, self.keys)
+        half = self.k_dim // 2
+        k1, k2 = self.keys[:, 0].to(query.dtype), self.keys[:, 1].to(query.dtype)
+        s1 = torch.einsum("nhd,hkd->nhk", query[..., :half], k1)
+        s2 = torch.einsum("nhd,hkd->nhk", query[..., half:], k2)
+        return s1, s2
+
+    def get_indices(self, query):
+        """query (N, heads, k_dim) -> scores, indices (N, heads, knn): the product-key top-k
+        (reference: pkm.py:125-136), ties to the lower index."""
+        s1, s2 = self.subkey_scores(query)
+        scores, indices, _ = K.PKSelect.apply(s1, s2, self.knn)
+        return scores, indices
+
+    def read_values(self, indices, weights):
+        """indices, weights (N, heads*knn) -> (N, v_dim) (reference: pkm.py:138-148)."""
+        w = self.values.weight
+        if self.value_grad == "row_sparse":
+            return row_sparse_embedding_bag(indices, weights, w, self.impl)
+        if self.value_impl == "embedding_bag":
+            return F.embedding_bag(indices, w, per_sample_weights=weights.to(w.dtype), mode="sum")
+        return torch.einsum("nj,njd->nd", weights.to(w.dtype), F.embedding(indices, w))
+
+    def forward(self, x):
+        shape = x.shape
+        x = x.reshape(-1, self.d_in)
+        if not x.is_cuda:
+            raise ValueError("ProductKeyMemory of smlm_b200 runs on CUDA only (no CPU fallback)")
+        if (getattr(self, "decode_graph", False) and x.shape[0] == 1 and not self.record
+                and not torch.is_grad_enabled()):
+            return self._graph_forward(x).view(*shape[:-1], self.d_out)
+        return self._forward(x).view(*shape[:-1], self.d_out)
+
+    def _graph_forward(self, x):
+        """One-token decoding without grad: replays a CUDA graph of _forward captured for this shape (same
+        kernels as the eager path, so bit-identical; it removes the per-launch host overhead)."""
+        ac = torch.is_autocast_enabled("cuda")
+        key = (tuple(x.shape), x.dtype, ac, torch.get_autocast_dtype("cuda") if ac else None,
+               id(getattr(self.values, "infer_table", None)))
+        g = getattr(self, "_graph", None)
+        if g is None or g[0] != key:
+            static_x = x.clone()
+            ctx = (torch.autocast("cuda", dtype=key[3], cache_enabled=False) if ac
+                   else torch.autocast("cuda", enabled=False))
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s), ctx:
+                for _ in range(2):
+                    self._forward(static_x)
+            torch.cuda.current_stream().wait_stream(s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph), ctx:
+                static_out = self._forward(static_x)
+            g = self._graph = (key, graph, static_x, static_out)
+        _, graph, static_x, static_out = g
+        static_x.copy_(x)
+        graph.replay()
+        return static_out.clone()
+
+    def _select(self, q, autocast_bf16):
+        """q (N, heads, k_dim) -> scores, indices, weights (N, heads, knn)."""
+        s1, s2 = self.subkey_scores(q.to(torch.bfloat16) if autocast_bf16 else q.float())
+        scores, indices, weights = K.PKSelect.apply(s1, s2, self.knn)
+        if self.log_score_scale is not None:
+            logits = scores.float() * self.log_score_scale.float().exp().view(1, self.heads, 1)
+            weights = F.softmax(logits, dim=-1)
+        return scores, indices, weights
+
+    def _forward(self, x):
+        N = x.shape[0]
+        q = self.query_proj(x)
+        if self.query_norm is not None:
+            q = self.query_norm(q.to(self.query_norm.weight.dtype))     # BN in fp32 under autocast
+        q = q.view(N, self.heads, self.k_dim)
+        autocast_bf16 = (torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16)
+        with torch.autocast("cuda", enabled=False):
+            scores, indices, weights = self._select(q, autocast_bf16)
+        if self.record:
+            self.last_indices = indices.detach()
+            self.last_scores = scores.detach()
+            self.last_weights = weights.detach()
+        if not torch.is_grad_enabled() and self.swilu and autocast_bf16:
+            # inference: value bag on the inference table (fp32 / bf16 / q4) with the swilu product and the
+            # bf16 cast fused (reference: pkm.py:213-224)
+            pre = self.swilu_proj(x)
+            t = getattr(self.values, "infer_table", None) or (self.values.weight, None)
+            out = K.bag_infer(indices.view(N, -1), weights.view(N, -1), t[0], t[1], pre=pre, out_bf16=True)
+            return self.value_proj(out)
+        out = self.read_values(indices.view(N, -1), weights.view(N, -1))
+        if self.swilu:
+            out = self.value_proj(out * F.silu(self.swilu_proj(x)).to(out.dtype))
+        return out
+
+    def macs_per_token(self):
+        """Multiply-accumulates per token (reference: pkm.py:230-237)."""
+        m = self.d_in * self.heads * self.k_dim
+        m += self.heads * 2 * self.n_keys * (self.k_dim // 2)
+        m += self.heads * self.knn * self.v_dim
+        if self.swilu:
+            m += self.d_in * self.v_dim + self.v_dim * self.d_out + self.v_dim
+        return m

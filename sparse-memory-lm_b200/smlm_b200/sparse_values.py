@@ -1,0 +1,244 @@
+"""Row-sparse gradients and the lazy Adam of the product-key value table, on the sm_100a kernels.
+
+Same API and semantics as re133/sparse-memory-lm smlm/sparse_values.py:
+  * RowStore (sparse_values.py:26-41): one persistent fp32 accumulator shaped like the table, a bool `touched`
+    mask and a deferred clip factor `grad_scale` (float or 0-d device tensor).
+  * row_sparse_embedding_bag (110-123): forward = value bag; backward adds w * grad_out into the read rows of
+    the accumulator and returns the per-sample-weight gradient; the table never gets a .grad.
+  * clip_row_sparse (137-151): global norm over the accumulated rows, clip factor stored in the RowStore.
+  * LazyRowAdam (154-362): Adam (no weight decay) on the rows read since the last step only; unread rows keep
+    values and state bit for bit; global step count for the bias correction; state format
+    smlm.lazy_row_adam.v1.
+The only implementation is "cuda" (libsmlm_b200.so); the reference's "torch" / "triton" values are accepted
+as aliases so that configurations carry over, and CPU tables raise.
+"""
+import torch
+
+from . import kernels as K
+
+IMPLS = ("cuda", "triton", "torch")        # every value selects the CUDA kernels
+
+
+def _check_impl(impl):
+    if impl not in IMPLS:
+        raise ValueError(f"unknown impl {impl!r}")
+
+
+class RowStore:
+    def __init__(self, table):
+        if table.dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError(f"row-sparse tables must be fp32 or bf16, got {table.dtype}")
+        self.acc = torch.zeros(table.shape, dtype=torch.float32, device=table.device)
+        self.touched = torch.zeros(table.shape[0], dtype=torch.bool, device=table.device)
+        self.grad_scale = 1.0           # set by clipping, applied in the optimizer step
+
+    def reset(self, rows=None):
+        if rows is None:
+            self.acc.zero_()
+            self.touched.zero_()
+        else:
+            self.acc.index_fill_(0, rows, 0.0)
+            self.touched.index_fill_(0, rows, False)
+        self.grad_scale = 1.0
+
+    def norm(self):
+        """acc.norm() over the touched rows (untouched rows of a RowStore are zero)."""
+        return K.touched_norm(self.acc, self.touched)
+
+
+def row_store(table):
+    """The RowStore attached to a (possibly shared) table parameter; created on first use."""
+    if getattr(table, "host_values", False):
+        raise NotImplementedError("host-RAM value tables (smlm/host_values.py) are not part of this build")
+    st = getattr(table, "row_store", None)
+    if st is None or st.acc.device != table.device or st.acc.shape != table.shape:
+        st = RowStore(table)
+        table.row_store = st
+    return st
+
+
+class _RowSparseBag(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, weights, indices, table, store, impl="cuda"):
+        n, j = indices.shape
+        w = weights.reshape(n, j).to(table.dtype)
+        out = K.bag_forward(indices, w, table, out_dtype=table.dtype)
+        ctx.save_for_backward(w, indices)
+        ctx.table, ctx.store, ctx.wshape, ctx.wdtype = table, store, weights.shape, weights.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        table, store = ctx.table, ctx.store
+        w, indices = ctx.saved_tensors
+        acc = store.acc if store is not None else None
+        touched = store.touched if store is not None else None
+        gw = K.bag_backward_rows(grad_out, indices, w, table, acc, touched)
+        # drop the RowStore reference so that `del table.row_store` after training frees the accumulator
+        ctx.table = ctx.store = None
+        return gw.view(ctx.wshape).to(ctx.wdtype), None, None, None, None
+
+
+def row_sparse_embedding_bag(indices, weights, table, impl="cuda"):
+    """sum_j weights[:, j] * table[indices[:, j]] with row-sparse gradient accumulation into table.row_store
+    (reference: sparse_values.py:110-123)."""
+    _check_impl(impl)
+    if not torch.is_grad_enabled():
+        return K.bag_forward(indices, weights.to(table.dtype), table, out_dtype=table.dtype)
+    if not table.requires_grad:
+        # frozen table: gradient for the weights only, no row accumulator
+        return _RowSparseBag.apply(weights, indices, table, None, impl)
+    # the table goes in as an input so that the output needs a gradient even when only the table is trained;
+    # its backward returns None for it, the gradient goes into table.row_store instead
+    return _RowSparseBag.apply(weights, indices, table, row_store(table), impl)
+
+
+def row_sparse_tables(model):
+    """Distinct value-table parameters that use row-sparse gradients (reference: sparse_values.py:126-134)."""
+    seen, out = set(), []
+    for m in model.modules():
+        if (getattr(m, "value_grad", "dense") == "row_sparse" and m.values.weight.requires_grad
+                and id(m.values.weight) not in seen):
+            seen.add(id(m.values.weight))
+            out.append(m.values.weight)
+    return out
+
+
+def clip_row_sparse(tables, max_norm):
+    """Global norm over the accumulated row gradients of all row-sparse tables; the clip factor (0-d device
+    tensor, no host sync) is stored and applied in the optimizer step. Returns the pre-clip norm
+    (reference: sparse_values.py:137-151)."""
+    if not tables:
+        return None
+    norms = [row_store(t).norm() for t in tables]
+    total = torch.linalg.vector_norm(torch.stack(norms))
+    coef = torch.clamp(max_norm / (total + 1e-6), max=1.0)
+    for t in tables:
+        row_store(t).grad_scale = coef
+    return total
+
+
+class LazyRowAdam(torch.optim.Optimizer):
+    """Adam (no weight decay) on the rows read since the last step; rows that were not read keep their values and
+    their Adam state bit-for-bit (global step count for bias correction, as torch SparseAdam / TF LazyAdam).
+    One fused kernel per table reads only the touched rows (reference: sparse_values.py:154-362).
+
+    value_copy_dtype=torch.bfloat16 keeps a bf16 copy of each table (`table.value_copy`) that the step refreshes
+    for the updated rows: the forward can read the copy (half the gather bytes) while the fp32 table stays the
+    master."""
+
+    def __init__(self, params, lr, betas=(0.9, 0.95), eps=1e-8, name="memory_values", impl="cuda",
+                 state_dtype="fp32", value_copy_dtype=None):
+        params = list(params)
+        _check_impl(impl)
+        if state_dtype != "fp32":
+            if state_dtype in ("bf16", "int8"):
+                raise NotImplementedError("compact LazyRowAdam states (bf16 / int8) are not built yet")
+            raise ValueError(f"unknown state_dtype: {state_dtype}")
+        if any(not p.is_cuda or p.dtype != torch.float32 or p.ndim != 2 or not p.is_contiguous() for p in params):
+            raise ValueError("LazyRowAdam needs contiguous fp32 CUDA tables")
+        super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=0.0))
+        for g in self.param_groups:
+            g["name"] = name
+            g["base_lr"] = lr
+        self.impl = "cuda"
+        self.state_dtype = state_dtype
+        self.value_copy_dtype = value_copy_dtype
+        if value_copy_dtype is not None:
+            for p in params:
+                p.value_copy = p.detach().to(value_copy_dtype)
+
+    def _state(self, p):
+        state = self.state[p]
+        if not state:
+            state["step"] = torch.zeros((), dtype=torch.float32)
+            state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+        return state
+
+    @torch.no_grad()
+    def step(self):
+        for group in self.param_groups:
+            b1, b2 = group["betas"]
+            for p in group["params"]:
+                st = row_store(p)
+                state = self._state(p)
+                state["step"] += 1
+                K.lazy_adam_step(p, state["exp_avg"], state["exp_avg_sq"], st.acc, st.touched, st.grad_scale,
+                                 int(state["step"]), group["lr"], b1, b2, group["eps"],
+                                 value_copy=getattr(p, "value_copy", None))
+                st.grad_scale = 1.0         # the kernel has zeroed the read accumulator rows and the mask
+
+    def zero_grad(self, set_to_none=True):
+        # the accumulator is cleared in step(); rows accumulated by a backward without a following step stay in
+        # table.row_store (row_store(table).reset() drops them)
+        pass
+
+    def _params(self):
+        return [p for g in self.param_groups for p in g["params"]]
+
+    def _group_positions(self, params):
+        pos = {id(p): i for i, p in enumerate(params)}
+        return [[pos[id(p)] for p in g["params"]] for g in self.param_groups]
+
+    def state_dict(self):
+        """Moments and step count per table, in parameter order (format smlm.lazy_row_adam.v1)."""
+        params = self._params()
+        return {"format": "smlm.lazy_row_adam.v1", "state_dtype": self.state_dtype,
+                "shapes": [list(p.shape) for p in params],
+                "param_groups": [{**{k: v for k, v in g.items() if k != "params"}, "params": idx}
+                                 for g, idx in zip(self.param_groups, self._group_positions(params))],
+                "state": [dict(self.state[p]) for p in params]}
+
+    def load_state_dict(self, state_dict):
+        if state_dict.get("format") != "smlm.lazy_row_adam.v1":
+            raise ValueError("not a LazyRowAdam state dict (smlm.lazy_row_adam.v1)")
+        params = self._params()
+        if state_dict["state_dtype"] != self.state_dtype:
+            raise ValueError(f"LazyRowAdam state is {state_dict['state_dtype']}, this optimizer keeps "
+                             f"{self.state_dtype}")
+        if state_dict["shapes"] != [list(p.shape) for p in params]:
+            raise ValueError("LazyRowAdam state was saved for other tables (shapes differ)")
+        groups = state_dict["param_groups"]
+        if [g["params"] for g in groups] != self._group_positions(params):
+            raise ValueError("LazyRowAdam state has other parameter groups")
+        for g, saved in zip(self.param_groups, groups):
+            g.update({k: (tuple(v) if k == "betas" else v) for k, v in saved.items() if k != "params"})
+        for p, saved in zip(params, state_dict["state"]):
+            if not saved:
+                continue
+            self.state[p] = {k: (v.detach().clone().cpu() if k == "step" else v.to(device=p.device, copy=True))
+                             for k, v in saved.items()}
+
+
+class OptimizerSet:
+    """Several optimizers driven as one (reference: sparse_values.py:365-395)."""
+
+    def __init__(self, *opts):
+        self.opts = [o for o in opts if o is not None]
+
+    @property
+    def param_groups(self):
+        return [g for o in self.opts for g in o.param_groups]
+
+    def step(self):
+        for o in self.opts:
+            o.step()
+
+    def zero_grad(self, set_to_none=True):
+        for o in self.opts:
+            o.zero_grad(set_to_none=set_to_none)
+
+    def state_dict(self):
+        return {"format": "smlm.optimizer_set.v1",
+                "optimizers": [{"type": type(o).__name__, "state_dict": o.state_dict()} for o in self.opts]}
+
+    def load_state_dict(self, state_dict):
+        if state_dict.get("format") != "smlm.optimizer_set.v1":
+            raise ValueError("not an OptimizerSet state dict (smlm.optimizer_set.v1)")
+        saved = state_dict["optimizers"]
+        if [s["type"] for s in saved] != [type(o).__name__ for o in self.opts]:
+            raise ValueError("OptimizerSet state holds other optimizers: "
+                             f"{[s['type'] for s in saved]} vs {[type(o).__name__ for o in self.opts]}")
+        for o, s in zip(self.opts, saved):
+            o.load_state_dict(s["state_dict"])

@@ -1,0 +1,86 @@
+"""The C ABI library: loads without a GPU, exports every entry point include/smlm_b200.h declares, rejects bad
+arguments on the host (no launch), and the Python layer refuses CPU tensors (there is no CPU fallback)."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+from smlm_b200 import _lib as L
+from smlm_b200 import kernels as K
+
+HEADER = os.path.join(ROOT, "include", "smlm_b200.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    return re.findall(r"SMLM_API\s+[\w\s\*]*?\b(smlm_\w+)\s*\(", text)
+
+
+def test_library_exports_every_declared_entry_point():
+    names = declared()
+    assert len(names) >= 14
+    so = ctypes.CDLL(L.LIB_PATH)
+    for n in names:
+        assert hasattr(so, n), f"{n} declared in smlm_b200.h but not exported"
+    assert set(names) == set(L.SIGNATURES), "ctypes signatures out of sync with the header"
+    lib = L.load()
+    assert lib.smlm_version() >= 100
+
+
+def test_host_side_argument_checks_return_invalid():
+    lib = L.load()
+    s = ctypes.c_void_p(0x1000)   # never dereferenced: the checks fail before any launch
+    rc = lib.smlm_pk_select(s, s, L.BF16, 4, 2, 64, 33, s, s, s, None)
+    assert rc == L.ERR_INVALID and b"knn" in lib.smlm_last_error()
+    rc = lib.smlm_pk_select(s, s, L.BF16, 4, 2, 1 << 17, 32, s, s, s, None)
+    assert rc == L.ERR_INVALID
+    rc = lib.smlm_bag_forward(s, s, L.F32, s, 7, 4, 8, 16, 32, s, L.F32, None, None)
+    assert rc == L.ERR_INVALID and b"table" in lib.smlm_last_error()
+    rc = lib.smlm_rowwise_step(s, s, s, s, None, None, 1.0, 10, 8, L.ROWRMS, 0.95, 1e-8, 0.01, s, 0, None)
+    assert rc == L.ERR_INVALID and b"count" in lib.smlm_last_error()
+    rc = lib.smlm_quantize_q4(s, 10, 7, s, s, None)
+    assert rc == L.ERR_INVALID
+    with pytest.raises(ValueError, match="knn"):
+        L.check(lib.smlm_pk_select(s, s, L.BF16, 4, 2, 64, 0, s, s, s, None), "pk_select")
+    # empty inputs are fine and launch nothing
+    assert lib.smlm_bag_forward(None, None, L.F32, None, L.F32, 0, 8, 16, 32, None, L.F32, None, None) == L.OK
+
+
+def test_python_api_refuses_cpu_tensors():
+    t = torch.zeros(16, 8)
+    idx = torch.zeros(2, 4, dtype=torch.long)
+    w = torch.zeros(2, 4)
+    with pytest.raises(ValueError, match="CUDA"):
+        K.bag_forward(idx, w, t)
+    with pytest.raises(ValueError, match="CUDA"):
+        K.pk_select(torch.zeros(2, 2, 16, dtype=torch.bfloat16), torch.zeros(2, 2, 16, dtype=torch.bfloat16), 4)
+    from smlm_b200.pkm import ProductKeyMemory
+    mem = ProductKeyMemory(16, 16, n_keys=8, heads=2, knn=4, k_dim=8, query_norm="none", swilu=False)
+    with pytest.raises(ValueError, match="CUDA"):
+        mem(torch.zeros(3, 16))
+    from smlm_b200.sparse_values import LazyRowAdam
+    with pytest.raises(ValueError, match="CUDA"):
+        LazyRowAdam([torch.nn.Parameter(torch.zeros(16, 8))], lr=1e-3)
+
+
+def test_layer_rejects_unsupported_shapes():
+    from smlm_b200.pkm import ProductKeyMemory
+    with pytest.raises(ValueError, match="knn"):
+        ProductKeyMemory(32, 32, n_keys=64, knn=33, k_dim=16)
+    with pytest.raises(ValueError, match="n_keys"):
+        ProductKeyMemory(32, 32, n_keys=1 << 17, knn=4, k_dim=16)
+    # any n_keys / knn within the limits, powers of two or not (the reference's Triton path needed powers of two)
+    ProductKeyMemory(32, 32, n_keys=24, knn=5, k_dim=16)
+
+
+def test_state_dict_formats_match_reference():
+    from smlm_b200.pkm import ProductKeyMemory
+    mem = ProductKeyMemory(24, 24, n_keys=16, heads=2, knn=4, k_dim=16)
+    keys = set(mem.state_dict())
+    assert {"keys", "query_proj.weight", "query_proj.bias", "values.weight", "swilu_proj.weight",
+            "value_proj.weight", "query_norm.running_mean"} <= keys
+    from smlm_b200.row_optim import state_bytes
+    assert state_bytes("rowrms", 100) == 804 and state_bytes("rowadagrad", 100) == 404

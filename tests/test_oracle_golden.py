@@ -1,0 +1,227 @@
+"""Pins the CPU oracle (oracle/pkm_oracle.c, oracle/torch_path.py) to the reference's own outputs, the golden
+fixtures made by tests/golden/make_golden.py from re133/sparse-memory-lm. CPU only."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from oracle import torch_path as TP
+from util import bf16_from_bits, close, golden, tie_free_rows
+
+
+def canonical_ok(s1, s2, knn, sc, idx, bf16):
+    """Every returned index carries its returned score, the list is sorted by (score desc, index asc), no index
+    twice, and the scores are the knn best pair scores of the half top-k lists."""
+    s1f = torch.as_tensor(s1).float()
+    s2f = torch.as_tensor(s2).float()
+    N, H, NK = s1f.shape
+    idx = torch.as_tensor(idx)
+    own = s1f.gather(-1, idx // NK) + s2f.gather(-1, idx % NK)
+    if bf16:
+        own = own.bfloat16().float()
+    sc = torch.as_tensor(sc).float()
+    assert torch.equal(own, sc)
+    flat_s = sc.view(-1, knn)
+    flat_i = idx.view(-1, knn)
+    ok_order = (flat_s[:, :-1] > flat_s[:, 1:]) | ((flat_s[:, :-1] == flat_s[:, 1:]) & (flat_i[:, :-1] < flat_i[:, 1:]))
+    assert bool(ok_order.all())
+
+
+def test_select_bf16_matches_reference():
+    g = golden("select_bf16.npz")
+    ties_seen = 0
+    for c in range(int(g["n_cases"])):
+        N, H, NK, knn = (int(x) for x in g[f"c{c}_shape"])
+        s1, s2 = g[f"c{c}_s1"], g[f"c{c}_s2"]
+        sc, idx, w = O.select(s1, s2, knn, bf16=True)
+        sc_t = bf16_from_bits(sc).float()
+        # selected scores exactly the reference's (torch.topk path and Triton kernel)
+        assert np.array_equal(sc, g[f"c{c}_torch_scores"])
+        assert np.array_equal(sc, g[f"c{c}_triton_scores"])
+        canonical_ok(bf16_from_bits(s1), bf16_from_bits(s2), knn, sc_t, idx, bf16=True)
+        # index sets equal to the reference wherever no tie makes the set ambiguous
+        free = tie_free_rows(bf16_from_bits(s1), bf16_from_bits(s2), knn, bf16=True)
+        ti = np.sort(g[f"c{c}_triton_idx"].reshape(-1, knn), -1)
+        ri = np.sort(g[f"c{c}_torch_idx"].reshape(-1, knn), -1)
+        oi = np.sort(idx.reshape(-1, knn), -1)
+        assert np.array_equal(oi[free], ti[free]) and np.array_equal(oi[free], ri[free])
+        ties_seen += int((~free).sum())
+        np.testing.assert_allclose(w, g[f"c{c}_triton_w"], rtol=0, atol=1e-6)
+        np.testing.assert_allclose(w, g[f"c{c}_torch_w"], rtol=0, atol=1e-6)
+    assert ties_seen > 0          # the coarse-grid case really exercises ties
+
+
+def test_select_f32_matches_reference_on_reference_scores():
+    g = golden("select_f32.npz")
+    for c in range(int(g["n_cases"])):
+        N, H, NK, knn, kd = (int(x) for x in g[f"c{c}_shape"])
+        s1, s2 = g[f"c{c}_s1"], g[f"c{c}_s2"]
+        sc, idx, w = O.select(s1, s2, knn, bf16=False)
+        free = tie_free_rows(torch.from_numpy(s1), torch.from_numpy(s2), knn, bf16=False)
+        assert free.all()                                   # continuous scores: no ties
+        assert np.array_equal(sc, g[f"c{c}_scores"])         # bit-exact scores
+        # bit-exact index sets; within equal scores torch.topk's order is unspecified, ours is index ascending
+        assert np.array_equal(np.sort(idx, -1), np.sort(g[f"c{c}_idx"], -1))
+        canonical_ok(s1, s2, knn, sc, idx, bf16=False)
+        np.testing.assert_allclose(w, g[f"c{c}_w"], rtol=0, atol=1e-6)
+
+
+def test_fmaf_scores_close_to_reference_einsum():
+    """The oracle's fixed-order fmaf scores agree with the reference's einsum to fp32 rounding."""
+    g = golden("select_f32.npz")
+    for c in range(int(g["n_cases"])):
+        s1, s2 = O.subkey_scores_f32(g[f"c{c}_q"], g[f"c{c}_keys"])
+        np.testing.assert_allclose(s1, g[f"c{c}_s1"], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(s2, g[f"c{c}_s2"], rtol=1e-5, atol=1e-6)
+
+
+def test_select_backward_matches_reference():
+    g = golden("select_backward.npz")
+    N, H, NK, knn = (int(x) for x in g["shape"])
+    ds1, ds2 = O.select_backward(g["idx"], g["w"], g["g"], None, NK, bf16=True)
+    d1, e1 = bf16_from_bits(ds1).float(), bf16_from_bits(g["ds1"]).float()
+    d2, e2 = bf16_from_bits(ds2).float(), bf16_from_bits(g["ds2"]).float()
+    scale = float(e1.abs().max())
+    torch.testing.assert_close(d1, e1, rtol=2 ** -7, atol=2 ** -8 * scale)
+    torch.testing.assert_close(d2, e2, rtol=2 ** -7, atol=2 ** -8 * scale)
+    assert torch.equal(d1 != 0, e1 != 0) and torch.equal(d2 != 0, e2 != 0)
+
+
+def test_bag_forward_backward_match_reference():
+    g = golden("bag.npz")
+    out, bad = O.bag_forward(g["idx"], g["w"], g["table"])
+    assert bad == 0
+    close(out, g["out"])
+    acc = np.ones_like(g["table"])
+    touched = np.zeros(g["table"].shape[0], np.uint8)
+    gw = O.bag_backward(g["g"], g["idx"], g["w"], g["table"], acc, touched)
+    close(gw, g["gw"])
+    close(acc, g["acc"])
+    assert np.array_equal(touched.astype(bool), g["touched"])
+    # bf16 table: weights rounded to bf16 as the reference's forward does (sparse_values.py:71)
+    wb = O.bf16_bits_to_f32(O.f32_to_bf16_bits(g["w"]))
+    out_b, _ = O.bag_forward(g["idx"], wb, g["table_bf16"], bf16=True)
+    close(out_b, g["out_bf16_table"])
+
+
+def test_bag_backward_chunked_schedule_only_changes_rounding():
+    g = golden("bag.npz")
+    accs = []
+    for chunk in (0, 64, 7):
+        acc = np.zeros_like(g["table"])
+        touched = np.zeros(g["table"].shape[0], np.uint8)
+        O.bag_backward(g["g"], g["idx"], g["w"], g["table"], acc, touched, chunk=chunk)
+        accs.append(acc)
+    close(accs[1], accs[0])
+    close(accs[2], accs[0])
+
+
+def test_lazy_adam_matches_reference_three_steps():
+    g = golden("lazy_adam.npz")
+    p = g["base"].copy()
+    m, v = np.zeros_like(p), np.zeros_like(p)
+    pr, mr, vr = p.copy(), m.copy(), v.copy()
+    for step in range(3):
+        acc, touched = g[f"acc{step}"].copy(), g[f"touched{step}"].astype(np.uint8)
+        prev = p.copy()
+        O.lazy_adam(p, m, v, acc, touched.copy(), float(g[f"scale{step}"]), step + 1, float(g["lr"]),
+                    float(g["beta1"]), float(g["beta2"]), float(g["eps"]))
+        close(p, g[f"p{step}"], msg="values")
+        close(m, g[f"m{step}"], msg="exp_avg")
+        close(v, g[f"v{step}"], msg="exp_avg_sq")
+        unread = ~g[f"touched{step}"]
+        assert np.array_equal(p[unread], prev[unread])       # unread rows bit-identical
+        if O.ref_lib() is not None:
+            acc_r = g[f"acc{step}"].copy()
+            O.ref_lazy_adam(pr, mr, vr, acc_r, touched.copy(), float(g[f"scale{step}"]), step + 1, float(g["lr"]),
+                            float(g["beta1"]), float(g["beta2"]), float(g["eps"]))
+            assert np.array_equal(p, pr) and np.array_equal(m, mr) and np.array_equal(v, vr)
+
+
+@pytest.mark.parametrize("kind", ["rowrms", "rowadagrad"])
+def test_rowwise_matches_reference(kind):
+    g = golden("rowwise.npz")
+    p = g["initial"].copy()
+    v = np.zeros(p.shape[0], np.float32)
+    n = np.zeros(p.shape[0], np.int32)
+    for s in range(4):
+        acc = g[f"{kind}_acc{s}"].copy()
+        touched = g[f"{kind}_touched{s}"].astype(np.uint8)
+        O.rowwise(p, acc, touched, v, n, 1.0, kind, float(g["beta2"]), float(g["eps"]), float(g["lr"]))
+        assert not touched.any() and not acc.any()
+    for c in ("0", "1"):
+        np.testing.assert_allclose(p, g[f"{kind}_c{c}_p"], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(v, g[f"{kind}_c{c}_v"], rtol=1e-5, atol=1e-9)
+        if kind == "rowrms":
+            assert np.array_equal(n, g[f"{kind}_c{c}_n"])
+    np.testing.assert_array_equal(p, g[f"{kind}_c1_p"])       # the reference's C loop: bit for bit
+
+
+def test_q4_and_inference_bag_match_reference():
+    g = golden("infer.npz")
+    packed, scales = O.quantize_q4(g["table"])
+    assert np.array_equal(packed, g["packed"]) and np.array_equal(scales, g["scales"])
+    pre = g["pre"]
+    for kind, tab, tt in (("fp32", g["table"], "f32"), ("bf16", O.f32_to_bf16_bits(g["table"]), "bf16"),
+                          ("q4", g["packed"], "q4")):
+        sc = g["scales"] if kind == "q4" else None
+        close(O.bag_infer(g["idx"], g["w"], tab, tt, scales=sc), g[f"{kind}_plain"], msg=kind)
+        ref = g[f"{kind}_swilu"]
+        close(O.bag_infer(g["idx"], g["w"], tab, tt, scales=sc, pre=pre), ref, msg=kind)
+        ob = O.bag_infer(g["idx"], g["w"], tab, tt, scales=sc, pre=pre, out_bf16=True)
+        rb = O.bf16_bits_to_f32(g[f"{kind}_swilu_bf16"])
+        scale = float(np.abs(ref).max())
+        np.testing.assert_allclose(ob, rb, rtol=2 ** -7, atol=2 ** -8 * scale)
+
+
+def _load_layer(g, v):
+    n_keys, heads, knn, k_dim, d, N, bn, swilu = (int(x) for x in g[f"v{v}_cfg"])
+    mem = TP.TorchPKM(d, d, n_keys=n_keys, heads=heads, knn=knn, k_dim=k_dim,
+                      query_norm="batchnorm" if bn else "none", swilu=bool(swilu), canonical=False)
+    pre = f"v{v}_param_"
+    sd = {k[len(pre):]: torch.from_numpy(g[k]) for k in g.files if k.startswith(pre)}
+    mem.load_state_dict(sd, strict=False)
+    return mem
+
+
+@pytest.mark.parametrize("v", [0, 1])
+def test_torch_path_restatement_equals_reference_layer(v):
+    """The torch restatement (the layer-level oracle) reproduces the reference layer: the same index selection
+    exactly, floats to the rounding that torch's CPU GEMMs / index_put_ vary with the thread count."""
+    g = golden("layer.npz")
+    mem = _load_layer(g, v)
+    x = torch.from_numpy(g[f"v{v}_x"])
+    out = mem(x)
+    out.backward(torch.from_numpy(g[f"v{v}_gout"]))
+    st = TP.row_store(mem.values.weight)
+    close(out.detach(), g[f"v{v}_out"], rtol=1e-6, atol=1e-6)
+    assert torch.equal(mem.last_indices, torch.from_numpy(g[f"v{v}_idx"]))
+    # torch's CPU index_put_(accumulate=True) sums in a thread-count dependent order: fp32 rounding only
+    close(st.acc, g[f"v{v}_acc"], rtol=1e-6, atol=1e-6)
+    assert torch.equal(st.touched, torch.from_numpy(g[f"v{v}_touched"]))
+    close(mem.keys.grad, g[f"v{v}_keys_grad"], rtol=1e-6, atol=1e-6)
+    close(mem.query_proj.weight.grad, g[f"v{v}_qw_grad"], rtol=1e-6, atol=1e-6)
+    opt = TP.TorchLazyRowAdam([mem.values.weight], lr=1e-3, betas=(0.9, 0.98), eps=1e-8)
+    opt.step()
+    close(mem.values.weight.detach(), g[f"v{v}_values_after"], rtol=1e-6, atol=1e-6)
+    # canonical tie rule: same selection on these (tie-free) inputs
+    mem2 = _load_layer(g, v)
+    mem2.canonical = True
+    mem2(x)
+    assert torch.equal(mem2.last_indices, mem.last_indices)
+
+
+def test_oracle_select_equals_bruteforce_product_search():
+    """The product-key search returns exactly the top-k of a brute-force search over all n_keys^2 keys
+    (the reference's tests/test_pkm.py:16-37), here on the oracle with fp32 scores."""
+    gen = torch.Generator().manual_seed(1)
+    for n_keys, knn in ((16, 8), (16, 16), (32, 5), (8, 1)):
+        H, half = 3, 8
+        keys = torch.randn(H, 2, n_keys, half, generator=gen)
+        q = torch.randn(50, H, 2 * half, generator=gen)
+        s1, s2 = O.subkey_scores_f32(q.numpy(), keys.numpy())
+        sc, idx, _ = O.select(s1, s2, knn, bf16=False)
+        full = torch.from_numpy(s1)[..., :, None] + torch.from_numpy(s2)[..., None, :]
+        bf, bi = full.reshape(50, H, -1).topk(knn, dim=-1)
+        assert np.array_equal(sc, bf.numpy())
+        assert np.array_equal(np.sort(idx, -1), np.sort(bi.numpy(), -1))

@@ -19,7 +19,7 @@ struct TouchedBufs {
     double* partials;
 };
 
-constexpr int PARTIALS = 4096;  // per-warp partial sums of the norm kernel (fixed: deterministic order)
+constexpr int PARTIALS = 8192;  // per-warp partial sums of the norm kernel (fixed: deterministic order)
 
 static size_t select_tmp_bytes(int64_t rows) {
     size_t bytes = 0;
@@ -209,6 +209,7 @@ __global__ void __launch_bounds__(256) rowwise_kernel(RowArgs a) {
 // --------------------------------------------------------------------------------------------------- norm
 // Pass 1: warp w sums the squares of rows list[w], list[w + W], ... (double); W = PARTIALS fixed, so the
 // summation order does not depend on the device. Pass 2: one warp adds the PARTIALS in a fixed tree.
+template <int VEC>
 __global__ void __launch_bounds__(256) touched_sq_kernel(const float* acc, const int32_t* list, const int32_t* count,
                                                          int d, double* partials) {
     const int lane = lane_id();
@@ -218,9 +219,20 @@ __global__ void __launch_bounds__(256) touched_sq_kernel(const float* acc, const
     double s = 0.0;
     for (int i = w; i < n; i += PARTIALS) {
         const int64_t base = (int64_t)list[i] * d;
-        for (int c = lane; c < d; c += 32) {
-            const double x = acc[base + c];
-            s = fma(x, x, s);
+        if constexpr (VEC == 4) {
+#pragma unroll 3
+            for (int c = lane * 4; c < d; c += 128) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(acc + base + c));
+                s = fma((double)x.x, (double)x.x, s);
+                s = fma((double)x.y, (double)x.y, s);
+                s = fma((double)x.z, (double)x.z, s);
+                s = fma((double)x.w, (double)x.w, s);
+            }
+        } else {
+            for (int c = lane; c < d; c += 32) {
+                const double x = acc[base + c];
+                s = fma(x, x, s);
+            }
         }
     }
     s = warp_sum_d(s);
@@ -309,7 +321,10 @@ extern "C" int smlm_touched_norm(const float* acc, const uint8_t* touched, int64
     TouchedBufs b;
     int rc = compact_touched(touched, rows, workspace, workspace_bytes, &b, st);
     if (rc != SMLM_OK) return rc;
-    touched_sq_kernel<<<PARTIALS / 8, 256, 0, st>>>(acc, b.list, b.count, (int)d, b.partials);
+    if (d % 4 == 0 && reinterpret_cast<uintptr_t>(acc) % 16 == 0)
+        touched_sq_kernel<4><<<PARTIALS / 8, 256, 0, st>>>(acc, b.list, b.count, (int)d, b.partials);
+    else
+        touched_sq_kernel<1><<<PARTIALS / 8, 256, 0, st>>>(acc, b.list, b.count, (int)d, b.partials);
     SMLM_LAUNCHED("touched_sq_kernel");
     norm_finish_kernel<<<1, 32, 0, st>>>(b.partials, norm_out);
     SMLM_LAUNCHED("norm_finish_kernel");

@@ -34,7 +34,7 @@ def make(rows, D, N, K_, seed, skew=True, dtype=torch.float32):
     (1000, 23, 8, 40, torch.float32), (1000, 23, 8, 40, torch.bfloat16), (300, 1, 4, 5, torch.float32),
     (2048, 96, 32, 96, torch.float32), (4096, 64, 32, 48, torch.float32), (777, 1000, 6, 33, torch.float32)])
 def test_bag_forward_bit_exact_vs_oracle(rows, D, N, K_, dtype):
-    table, idx, w, _ = make(rows, D, N, K_, rows + D)
+    table, idx, w, _ = make(rows, D, N, K_, rows + D, dtype=dtype)
     wt = w.to(dtype)
     out = K.bag_forward(idx.to(DEV), wt.to(DEV), table.to(DEV)).cpu()
     if dtype == torch.bfloat16:

@@ -77,6 +77,9 @@ def test_layer_fp32_step_matches_reference_path():
     close(mem.keys.grad.cpu(), ref.keys.grad, msg="keys grad")
     close(mem.query_proj.weight.grad.cpu(), ref.query_proj.weight.grad, msg="query grad")
     close(mem.query_proj.bias.grad.cpu(), ref.query_proj.bias.grad, msg="query bias grad")
+    # Adam on the gradient each path really holds would amplify summation-order noise of near-zero gradients
+    # (the first step moves by ~lr * sign(g)); the step itself is compared on one accumulator
+    st_r.acc.copy_(st.acc.cpu())
     opt, opt_r = LazyRowAdam([mem.values.weight], lr=1e-3, betas=(0.9, 0.98)), \
         TP.TorchLazyRowAdam([ref.values.weight], lr=1e-3, betas=(0.9, 0.98))
     opt.step()

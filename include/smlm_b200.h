@@ -48,6 +48,7 @@ extern "C" {
 
 /* device status word bits */
 #define SMLM_FLAG_INDEX_RANGE 1
+#define SMLM_FLAG_TIMEOUT 4 /* a bounded wait inside a kernel gave up; that call's outputs are invalid */
 
 /* row-wise optimizer kinds (smlm/row_optim.py:21 KINDS) */
 #define SMLM_ROWRMS 0
@@ -160,6 +161,21 @@ SMLM_API int smlm_select_backward(const int64_t *indices, const float *weights, 
  * q: (n, h, 2 half), keys: (h, 2, nk, half). Replaces pkm.py:117-123 subkey_scores in fp32. */
 SMLM_API int smlm_subkey_scores_f32(const float *q, const float *keys, int64_t n, int64_t h, int64_t nk, int64_t half,
                            float *s1, float *s2, void *stream);
+
+SMLM_API size_t smlm_score_select_workspace(int64_t n, int64_t h);
+
+/* Fused scoring + selection under bf16 (the autocast path): q (n, h, 2 half) bf16, keys (h, 2, nk, half) bf16.
+ * Per (token, head, half) the sub-key scores are a tensor-core GEMM (tcgen05, bf16 operands, fp32 accumulate,
+ * TMA-fed, accumulators in TMEM), rounded to bf16 as the reference's bf16 einsum output; their top-knn
+ * (score desc, index asc) is kept in the GEMM epilogue, so the (n, h, nk) score tensors are never written.
+ * Then the pairs / final top-knn / softmax of smlm_pk_select. Outputs as smlm_pk_select with bf16 scores.
+ * s1_out / s2_out (optional, bf16 (n, h, nk)): the rounded sub-key scores, for checking only.
+ * half in {64, 128}; nk % 8 == 0; 1 <= knn <= 32. A kernel-internal wait that gives up raises
+ * SMLM_FLAG_TIMEOUT in *status (outputs then invalid); nothing traps.
+ * Replaces pkm.py:117-123 subkey_scores (bf16 autocast) + kernels.py:214 pk_select. */
+SMLM_API int smlm_score_select(const void *q, const void *keys, int64_t n, int64_t h, int64_t nk, int64_t half,
+                               int64_t knn, void *scores, int64_t *indices, float *weights, void *s1_out,
+                               void *s2_out, void *workspace, size_t workspace_bytes, int *status, void *stream);
 
 #ifdef __cplusplus
 }

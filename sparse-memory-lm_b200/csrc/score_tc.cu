@@ -1,0 +1,540 @@
+// Fused sub-key scoring + per-half top-k on the 5th-generation tensor cores (sm_100a).
+//
+// For one head h and one half of the query (k = 128 dimensions), scores S = Q_h,half (tokens x 128) x K_h,half^T
+// (128 x n_keys) are a bf16 GEMM with fp32 accumulation. S never reaches global memory: each accumulator tile
+// lives in tensor memory (TMEM) and the epilogue keeps, per token, the top-32 of the bf16-rounded scores (order:
+// score descending, sub-key index ascending), which is exactly what the reference's `einsum` (bf16 output) +
+// per-half top-k computes. A second small kernel (select.cu, pk_pairs_kernel) forms the knn x knn pairs and the
+// softmax from the two per-half lists.
+//
+// CTA = 6 warps, persistent over units (128-token tile, head); a unit runs half 0 then half 1:
+//   warp 0      TMA producer: Q tile (128 tokens x 128, two 64-wide 128B-swizzled boxes, double-buffered) and
+//               key tiles (128 keys x 128) through a 3-stage ring, completion by mbarrier transaction counts.
+//   warp 1      allocates 256 TMEM columns (two 128-column fp32 accumulators); lane 0 issues tcgen05.mma
+//               (M=128, N=128, K=16, kind::f16, bf16 in / fp32 accumulate), 8 per key tile, and commits to
+//               the stage's "empty" barrier and the accumulator's "full" barrier.
+//   warps 2-5   epilogue: tcgen05.ld of the 128 x 128 accumulator (warp w reads TMEM lanes 32 (w % 4) ..),
+//               one token per thread. Scores are rounded to bf16 in pairs and compared against the thread's
+//               current 32nd-best score (bf16x2 compare); the rare survivors go to a per-thread candidate list
+//               in shared memory that the warp merges into the sorted top-32 when any lane's list fills.
+// Every mbarrier wait is bounded (about one second); on timeout the kernel raises SMLM_FLAG_TIMEOUT in the
+// status word, every role unwinds, the MMA issuer waits (bounded) for its last commit, and TMEM is freed.
+// No TMA multicast is used (the kernel only reads this GPU's memory).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace smlm {
+
+int launch_pk_pairs(const uint32_t* lists, int64_t rows_nh, int nk, int knn, void* scores, int64_t* idx, float* w,
+                    cudaStream_t st);
+
+namespace tc {
+
+constexpr int BM = 128;          // tokens per tile (UMMA M)
+constexpr int BN = 128;          // sub-keys per tile (UMMA N)
+constexpr int STAGES = 3;        // key-tile ring
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = 64 + EPI_WARPS * 32;
+constexpr int CAND = 64;         // candidate slots per token
+constexpr int ATOM = 64;         // bf16 elements per 128-byte swizzle atom (K direction)
+constexpr int ATOM_BYTES_A = BM * 128;
+constexpr int ATOM_BYTES_B = BN * 128;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr unsigned long long WAIT_NS = 1000000000ull;  // bound of every mbarrier wait
+
+// ------------------------------------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false (and the abort flag set) if the phase did not complete within WAIT_NS or another role
+// has aborted already.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = now_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (now_ns() - t0 > WAIT_NS) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+// Bounded wait that ignores the abort flag (used to drain in-flight MMAs before TMEM is freed).
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = now_ns();
+    while (!mbar_try_wait(bar, parity) && now_ns() - t0 < WAIT_NS) {
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] x B[smem]^T, bf16 operands, fp32 accumulator.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes: thread t gets lane (base + t).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major, 128B-swizzled operand tile (rows of 128 bytes, 8-row groups
+// 1024 bytes apart): start address >> 4, leading offset 1 (unused for this layout), stride offset 1024 >> 4,
+// descriptor version 1, swizzle mode 2 (128B).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3ffffu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, N >> 3, M >> 4.
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+// ------------------------------------------------------------------------------------------ top-k pieces
+template <int N>
+__device__ __forceinline__ void sort_desc(uint32_t (&a)[N]) {
+#pragma unroll
+    for (int k = 2; k <= N; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1)
+#pragma unroll
+            for (int i = 0; i < N; i++) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const uint32_t x = a[i], y = a[l];
+                    const uint32_t hi = max(x, y), lo = min(x, y);
+                    if ((i & k) == 0) { a[i] = hi; a[l] = lo; }
+                    else { a[i] = lo; a[l] = hi; }
+                }
+            }
+}
+// a is bitonic; sorts it descending
+__device__ __forceinline__ void merge_desc32(uint32_t (&a)[32]) {
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1)
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const int l = i ^ j;
+            if (l > i) {
+                const uint32_t x = a[i], y = a[l];
+                a[i] = max(x, y);
+                a[l] = min(x, y);
+            }
+        }
+}
+
+// key of a bf16 score: order code << 16 | (0xffff - sub-key index); larger is better, distinct per index
+__device__ __forceinline__ uint32_t score_key(uint32_t bits16, int col) {
+    return (order_code16(bits16) << 16) | (uint32_t)(0xffff - col);
+}
+
+struct Epi {
+    uint32_t* cand;  // [CAND][128] (slot-major: thread e's slot i at i * 128 + e)
+    uint32_t* top;   // [32][128]
+    int e;           // epilogue thread index 0..127
+    int cnt;
+    __nv_bfloat162 thr2;
+
+    __device__ __forceinline__ void reset() {
+#pragma unroll
+        for (int i = 0; i < 32; i++) top[i * 128 + e] = 0;
+        cnt = 0;
+        thr2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)0xff80));  // -inf
+    }
+    // Merges the candidates into the sorted top-32 and raises the threshold (all 32 lanes together).
+    __device__ __forceinline__ void flush() {
+        uint32_t c[CAND];
+#pragma unroll
+        for (int i = 0; i < CAND; i++) c[i] = i < cnt ? cand[i * 128 + e] : 0u;
+        sort_desc<CAND>(c);
+        uint32_t t[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) t[i] = max(top[i * 128 + e], c[31 - i]);
+        merge_desc32(t);
+#pragma unroll
+        for (int i = 0; i < 32; i++) top[i * 128 + e] = t[i];
+        cnt = 0;
+        if (t[31] != 0) {
+            const unsigned short b = (unsigned short)decode_code16(t[31] >> 16);
+            thr2 = __bfloat162bfloat162(__ushort_as_bfloat16(b));
+        }
+    }
+    // 32 consecutive scores (fp32 bits) of columns col0 .. col0+31; columns >= nk are ignored.
+    __device__ __forceinline__ void take(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
+        __nv_bfloat162 p[16];
+        unsigned m[16];
+        unsigned any = 0;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            float lo = __uint_as_float(v[2 * i]), hi = __uint_as_float(v[2 * i + 1]);
+            if (col0 + 2 * i >= nk) lo = -INFINITY;
+            if (col0 + 2 * i + 1 >= nk) hi = -INFINITY;
+            p[i] = __floats2bfloat162_rn(lo, hi);
+            m[i] = __hgt2_mask(p[i], thr2);
+            any |= m[i];
+        }
+        if (dbg) {
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                if (col0 + i < nk) dbg[col0 + i] = (i & 1) ? __bfloat16_as_ushort(p[i >> 1].y)
+                                                            : __bfloat16_as_ushort(p[i >> 1].x);
+        }
+        if (any) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                if (m[i] & 0xffffu) cand[(cnt++) * 128 + e] = score_key(__bfloat16_as_ushort(p[i].x), col0 + 2 * i);
+                if (m[i] & 0xffff0000u) cand[(cnt++) * 128 + e] = score_key(__bfloat16_as_ushort(p[i].y), col0 + 2 * i + 1);
+            }
+        }
+        if (__any_sync(FULL, cnt > CAND - 32)) flush();
+    }
+};
+
+struct Params {
+    int n, heads, nk, atoms;  // atoms = half / 64
+    uint32_t* lists;          // [n][heads][2][32]
+    uint16_t* dbg1;           // optional bf16 scores [n][heads][nk], half 0
+    uint16_t* dbg2;           // half 1
+    int* status;
+};
+
+__global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_constant__ CUtensorMap tq,
+                                                                const __grid_constant__ CUtensorMap tk, Params P) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int a_bytes = P.atoms * ATOM_BYTES_A;
+    const int b_bytes = P.atoms * ATOM_BYTES_B;
+    uint8_t* sA = smem;                              // 2 x a_bytes
+    uint8_t* sB = sA + 2 * a_bytes;                  // STAGES x b_bytes
+    uint32_t* cand = reinterpret_cast<uint32_t*>(sB + STAGES * b_bytes);
+    uint32_t* top = cand + CAND * 128;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(top + 32 * 128);
+    uint64_t* full_b = bars;
+    uint64_t* empty_b = bars + STAGES;
+    uint64_t* a_full = bars + 2 * STAGES;
+    uint64_t* a_empty = a_full + 2;
+    uint64_t* t_full = a_empty + 2;
+    uint64_t* t_empty = t_full + 2;
+    uint64_t* done = t_empty + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = (P.n + BM - 1) / BM;
+    const int units = tiles_m * P.heads;
+    const int ntiles = (P.nk + BN - 1) / BN;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; i++) {
+            mbar_init(smem_addr(&full_b[i]), 1);
+            mbar_init(smem_addr(&empty_b[i]), 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(smem_addr(&a_full[i]), 1);
+            mbar_init(smem_addr(&a_empty[i]), 1);
+            mbar_init(smem_addr(&t_full[i]), 1);
+            mbar_init(smem_addr(&t_empty[i]), EPI_WARPS);
+        }
+        mbar_init(smem_addr(done), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_holder), TMEM_COLS);
+        tmem_relinquish();
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int a_iter = 0;
+            for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+                const int tm = u / P.heads, h = u % P.heads;
+                for (int half = 0; half < 2; half++) {
+                    const int ab = a_iter & 1;
+                    if (!mbar_wait(smem_addr(&a_empty[ab]), ((a_iter >> 1) & 1) ^ 1, abort_flag)) break;
+                    mbar_expect_tx(smem_addr(&a_full[ab]), a_bytes);
+                    for (int i = 0; i < P.atoms; i++)
+                        tma_load_3d(smem_addr(sA + ab * a_bytes + i * ATOM_BYTES_A), &tq, smem_addr(&a_full[ab]),
+                                    i * ATOM, h * 2 + half, tm * BM);
+                    a_iter++;
+                    for (int t = 0; t < ntiles; t++) {
+                        if (!mbar_wait(smem_addr(&empty_b[s]), ph ^ 1, abort_flag)) break;
+                        mbar_expect_tx(smem_addr(&full_b[s]), b_bytes);
+                        for (int i = 0; i < P.atoms; i++)
+                            tma_load_2d(smem_addr(sB + s * b_bytes + i * ATOM_BYTES_B), &tk, smem_addr(&full_b[s]),
+                                        i * ATOM, (h * 2 + half) * P.nk + t * BN);
+                        if (++s == STAGES) { s = 0; ph ^= 1; }
+                    }
+                    if (*abort_flag) break;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            int a_iter = 0, t_iter = 0;
+            for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+                for (int half = 0; half < 2; half++) {
+                    const int ab = a_iter & 1;
+                    if (!mbar_wait(smem_addr(&a_full[ab]), (a_iter >> 1) & 1, abort_flag)) break;
+                    fence_after();
+                    const uint32_t a_base = smem_addr(sA + ab * a_bytes);
+                    for (int t = 0; t < ntiles; t++) {
+                        if (!mbar_wait(smem_addr(&full_b[s]), ph, abort_flag)) break;
+                        const int tb = t_iter & 1;
+                        if (!mbar_wait(smem_addr(&t_empty[tb]), ((t_iter >> 1) & 1) ^ 1, abort_flag)) break;
+                        fence_after();
+                        const uint32_t d = tmem + tb * BN;
+                        const uint32_t b_base = smem_addr(sB + s * b_bytes);
+                        for (int i = 0; i < P.atoms; i++) {
+#pragma unroll
+                            for (int j = 0; j < ATOM / 16; j++) {
+                                const uint64_t ad = sw128_desc(a_base + i * ATOM_BYTES_A + j * 32);
+                                const uint64_t bd = sw128_desc(b_base + i * ATOM_BYTES_B + j * 32);
+                                umma_bf16(d, ad, bd, IDESC, (i | j) != 0);
+                            }
+                        }
+                        umma_commit(smem_addr(&empty_b[s]));
+                        umma_commit(smem_addr(&t_full[tb]));
+                        t_iter++;
+                        if (++s == STAGES) { s = 0; ph ^= 1; }
+                    }
+                    umma_commit(smem_addr(&a_empty[ab]));
+                    a_iter++;
+                    if (*abort_flag) break;
+                }
+            }
+            // all issued MMAs complete before TMEM can be freed
+            umma_commit(smem_addr(done));
+            mbar_wait_drain(smem_addr(done), 0);
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+        const int row = quarter * 32 + lane;    // token row within the tile
+        Epi ep{cand, top, row, 0, {}};
+        int t_iter = 0;
+        for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+            const int tm = u / P.heads, h = u % P.heads;
+            const int64_t n = (int64_t)tm * BM + row;
+            for (int half = 0; half < 2; half++) {
+                ep.reset();
+                uint16_t* dbg = half ? P.dbg2 : P.dbg1;
+                if (dbg && n < P.n) dbg += (n * P.heads + h) * (int64_t)P.nk;
+                else dbg = nullptr;
+                bool ok = true;
+                for (int t = 0; t < ntiles; t++) {
+                    const int tb = t_iter & 1;
+                    // warp-uniform outcome: the TMEM loads below are .sync.aligned
+                    if (!__all_sync(FULL, mbar_wait(smem_addr(&t_full[tb]), (t_iter >> 1) & 1, abort_flag))) {
+                        ok = false;
+                        break;
+                    }
+                    fence_after();
+                    const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + tb * BN;
+                    uint32_t v0[32], v1[32], v2[32], v3[32];
+                    tmem_ld32(base + 0, v0);
+                    tmem_ld32(base + 32, v1);
+                    tmem_ld32(base + 64, v2);
+                    tmem_ld32(base + 96, v3);
+                    tmem_wait_ld();
+                    fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_addr(&t_empty[tb]));
+                    t_iter++;
+                    const int c0 = t * BN;
+                    ep.take(v0, c0, P.nk, dbg);
+                    ep.take(v1, c0 + 32, P.nk, dbg);
+                    ep.take(v2, c0 + 64, P.nk, dbg);
+                    ep.take(v3, c0 + 96, P.nk, dbg);
+                }
+                if (!ok) break;
+                if (__any_sync(FULL, ep.cnt > 0)) ep.flush();
+                if (n < P.n) {
+                    uint32_t* dst = P.lists + ((n * P.heads + h) * 2 + half) * 32;
+#pragma unroll
+                    for (int i = 0; i < 32; i++) dst[i] = top[i * 128 + row];
+                }
+            }
+        }
+    }
+
+    __syncthreads();
+    if (threadIdx.x == 0 && *abort_flag) flag(P.status, SMLM_FLAG_TIMEOUT);
+    if (warp == 1) {
+        fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+size_t smem_bytes(int atoms) {
+    return 1024 + 2 * (size_t)atoms * ATOM_BYTES_A + STAGES * (size_t)atoms * ATOM_BYTES_B + CAND * 128 * 4 +
+           32 * 128 * 4 + 16 * 8 + 16;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+}  // namespace tc
+}  // namespace smlm
+
+using namespace smlm;
+
+extern "C" size_t smlm_score_select_workspace(int64_t n, int64_t h) {
+    return (size_t)std::max<int64_t>(n, 0) * std::max<int64_t>(h, 0) * 2 * 32 * sizeof(uint32_t) + 256;
+}
+
+extern "C" int smlm_score_select(const void* q, const void* keys, int64_t n, int64_t h, int64_t nk, int64_t half,
+                                 int64_t knn, void* scores, int64_t* indices, float* weights, void* s1_out,
+                                 void* s2_out, void* workspace, size_t workspace_bytes, int* status, void* stream) {
+    SMLM_CHECK_ARG(n >= 0 && h > 0, "score_select: bad n / heads");
+    SMLM_CHECK_ARG(half == 64 || half == 128, "score_select: the half dimension must be 64 or 128, got %lld",
+                   (long long)half);
+    SMLM_CHECK_ARG(knn >= 1 && knn <= 32, "score_select: knn must be in [1, 32]");
+    SMLM_CHECK_ARG(nk >= knn && nk <= 65536 && nk % 8 == 0, "score_select: need knn <= n_keys <= 65536, n_keys % 8 == 0");
+    SMLM_CHECK_ARG(n < (1ll << 31) / std::max<int64_t>(h, 1) / 64 && h * 2 * nk < (1ll << 31),
+                   "score_select: sizes beyond 32-bit TMA coordinates");
+    if (n == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(q && keys && scores && indices && weights, "score_select: null pointer");
+    SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(keys) % 16 == 0,
+                   "score_select: q and keys must be 16-byte aligned");
+    const size_t need = smlm_score_select_workspace(n, h);
+    if (workspace == nullptr || workspace_bytes < need) {
+        set_error("score_select: workspace too small (%zu < %zu)", workspace_bytes, need);
+        return SMLM_ERR_WORKSPACE;
+    }
+    auto encode = tc::encode_fn();
+    if (!encode) {
+        set_error("score_select: cuTensorMapEncodeTiled is not available from the driver");
+        return SMLM_ERR_CUDA;
+    }
+    CUtensorMap tq, tk;
+    {
+        cuuint64_t dims[3] = {(cuuint64_t)half, (cuuint64_t)(2 * h), (cuuint64_t)n};
+        cuuint64_t strides[2] = {(cuuint64_t)half * 2, (cuuint64_t)(2 * h * half * 2)};
+        cuuint32_t box[3] = {tc::ATOM, 1, tc::BM};
+        cuuint32_t es[3] = {1, 1, 1};
+        CUresult r = encode(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, es,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            set_error("score_select: query tensor map encode failed (%d)", (int)r);
+            return SMLM_ERR_CUDA;
+        }
+    }
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)half, (cuuint64_t)(h * 2 * nk)};
+        cuuint64_t strides[1] = {(cuuint64_t)half * 2};
+        cuuint32_t box[2] = {tc::ATOM, tc::BN};
+        cuuint32_t es[2] = {1, 1};
+        CUresult r = encode(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(keys), dims, strides, box, es,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            set_error("score_select: key tensor map encode failed (%d)", (int)r);
+            return SMLM_ERR_CUDA;
+        }
+    }
+    cudaStream_t st = as_stream(stream);
+    uint32_t* lists = static_cast<uint32_t*>(workspace);
+    const int atoms = (int)(half / tc::ATOM);
+    const size_t smem = tc::smem_bytes(atoms);
+    SMLM_CUDA(cudaFuncSetAttribute(tc::score_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int64_t units = ((n + tc::BM - 1) / tc::BM) * h;
+    const int grid = (int)std::min<int64_t>(units, sm_count());
+    tc::Params P{(int)n, (int)h, (int)nk, atoms, lists, static_cast<uint16_t*>(s1_out), static_cast<uint16_t*>(s2_out),
+                 status};
+    tc::score_topk_kernel<<<grid, tc::THREADS, smem, st>>>(tq, tk, P);
+    SMLM_LAUNCHED("score_topk_kernel");
+    return launch_pk_pairs(lists, n * h, (int)nk, (int)knn, scores, indices, weights, st);
+}

@@ -134,6 +134,90 @@ __device__ __forceinline__ uint32_t pair_code(float v1, float v2) {
     return code_of<F32>(bits_of_float<F32>(v1 + v2));
 }
 
+// Pairs, final top-knn and softmax of one (token, head) row, given each half's top-knn keys (lane a holds
+// entry a of the sorted lists, keys in the u64 format above). Writes row `row` of the outputs.
+template <bool F32>
+__device__ void cartesian_select(uint64_t key1, uint64_t key2, int nk, int knn, uint64_t* buf, uint32_t* sfix,
+                                 int64_t row, void* scores_out, int64_t* idx_out, float* w_out) {
+    const int lane = lane_id();
+    const float v1 = score_of_code<F32>(key_code(key1));
+    const float v2 = score_of_code<F32>(key_code(key2));
+    const uint32_t i1 = key_index(key1), i2 = key_index(key2);
+
+    // dominance-pruned pairs: lane a owns b < m_a = knn / (a + 1)
+    const int m_a = lane < knn ? knn / (lane + 1) : 0;
+    int incl = m_a;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int x = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += x;
+    }
+    const int total = __shfl_sync(FULL, incl, 31);
+    const int off_a = incl - m_a;
+    for (int b = 0; b < knn; b++) {
+        const float v2b = __shfl_sync(FULL, v2, b);
+        const uint32_t i2b = __shfl_sync(FULL, i2, b);
+        if (b < m_a) buf[off_a + b] = make_key(pair_code<F32>(v1, v2b), i1 * (uint32_t)nk + i2b);
+    }
+    __syncwarp();
+    sort_prefix(buf, total);
+    const uint64_t best = lane < knn ? buf[lane] : 0;
+    const uint32_t t_code = key_code(__shfl_sync(FULL, best, knn - 1));
+
+    // a pair outside the pruned set can only tie with T at the first excluded column of each list row
+    bool tie_out = false;
+    {
+        const int bu = m_a < knn ? m_a : 0;
+        const float v2u = __shfl_sync(FULL, v2, bu);
+        tie_out = lane < knn && m_a < knn && pair_code<F32>(v1, v2u) == t_code;
+    }
+    uint64_t out_key = best;
+    if (__ballot_sync(FULL, tie_out)) {
+        const int c = __popc(__ballot_sync(FULL, lane < knn && key_code(best) > t_code));
+        unsigned mask = 0;
+        for (int b = 0; b < knn; b++) {
+            const float v2b = __shfl_sync(FULL, v2, b);
+            if (lane < knn && pair_code<F32>(v1, v2b) == t_code) mask |= 1u << b;
+        }
+        sfix[lane] = i2;
+        __syncwarp();
+        for (int r = c; r < knn; r++) {
+            uint32_t mine = 0xffffffffu;
+            for (unsigned mm = mask; mm; mm &= mm - 1) {
+                const int b = __ffs(mm) - 1;
+                const uint32_t full = i1 * (uint32_t)nk + sfix[b];
+                mine = full < mine ? full : mine;
+            }
+            uint32_t win = mine;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) win = min(win, __shfl_xor_sync(FULL, win, o));
+            if (mine == win && mask) {
+                const uint32_t j2 = win - i1 * (uint32_t)nk;
+                for (unsigned mm = mask; mm; mm &= mm - 1) {
+                    const int b = __ffs(mm) - 1;
+                    if (sfix[b] == j2) { mask &= ~(1u << b); break; }
+                }
+            }
+            if (lane == r) out_key = make_key(t_code, win);
+        }
+        __syncwarp();
+    }
+
+    // softmax over the knn selected scores, fp32
+    const float sc = score_of_code<F32>(key_code(out_key));
+    const float mx = warp_max(lane < knn ? sc : -INFINITY);
+    const float e = lane < knn ? expf(sc - mx) : 0.f;
+    const float tot = warp_sum(e);
+    if (lane < knn) {
+        const int64_t o = row * knn + lane;
+        if constexpr (F32) static_cast<float*>(scores_out)[o] = sc;
+        else static_cast<uint16_t*>(scores_out)[o] = (uint16_t)decode_code16(key_code(out_key));
+        idx_out[o] = key_index(out_key);
+        w_out[o] = e / tot;
+    }
+    __syncwarp();
+}
+
 template <bool F32>
 __global__ void __launch_bounds__(SEL_WARPS * 32) pk_select_kernel(const void* s1, const void* s2, int64_t rows_nh,
                                                                     int nk, int knn, void* scores_out,
@@ -152,83 +236,36 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) pk_select_kernel(const void* s
         half_topk<F32>(s2, off, nk, knn, buf);
         const uint64_t key2 = lane < knn ? buf[lane] : 0;
         __syncwarp();
-        const float v1 = score_of_code<F32>(key_code(key1));
-        const float v2 = score_of_code<F32>(key_code(key2));
-        const uint32_t i1 = key_index(key1), i2 = key_index(key2);
-
-        // dominance-pruned pairs: lane a owns b < m_a = knn / (a + 1)
-        const int m_a = lane < knn ? knn / (lane + 1) : 0;
-        int incl = m_a;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int x = __shfl_up_sync(FULL, incl, o);
-            if (lane >= o) incl += x;
-        }
-        const int total = __shfl_sync(FULL, incl, 31);
-        const int off_a = incl - m_a;
-        for (int b = 0; b < knn; b++) {
-            const float v2b = __shfl_sync(FULL, v2, b);
-            const uint32_t i2b = __shfl_sync(FULL, i2, b);
-            if (b < m_a) buf[off_a + b] = make_key(pair_code<F32>(v1, v2b), i1 * (uint32_t)nk + i2b);
-        }
-        __syncwarp();
-        sort_prefix(buf, total);
-        const uint64_t best = lane < knn ? buf[lane] : 0;
-        const uint32_t t_code = key_code(__shfl_sync(FULL, best, knn - 1));
-
-        // a pair outside the pruned set can only tie with T at the first excluded column of each list row
-        bool tie_out = false;
-        {
-            const int bu = m_a < knn ? m_a : 0;
-            const float v2u = __shfl_sync(FULL, v2, bu);
-            tie_out = lane < knn && m_a < knn && pair_code<F32>(v1, v2u) == t_code;
-        }
-        uint64_t out_key = best;
-        if (__ballot_sync(FULL, tie_out)) {
-            const int c = __popc(__ballot_sync(FULL, lane < knn && key_code(best) > t_code));
-            unsigned mask = 0;
-            for (int b = 0; b < knn; b++) {
-                const float v2b = __shfl_sync(FULL, v2, b);
-                if (lane < knn && pair_code<F32>(v1, v2b) == t_code) mask |= 1u << b;
-            }
-            sfix[wib][lane] = i2;
-            __syncwarp();
-            for (int r = c; r < knn; r++) {
-                uint32_t mine = 0xffffffffu;
-                for (unsigned mm = mask; mm; mm &= mm - 1) {
-                    const int b = __ffs(mm) - 1;
-                    const uint32_t full = i1 * (uint32_t)nk + sfix[wib][b];
-                    mine = full < mine ? full : mine;
-                }
-                uint32_t win = mine;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) win = min(win, __shfl_xor_sync(FULL, win, o));
-                if (mine == win && mask) {
-                    const uint32_t j2 = win - i1 * (uint32_t)nk;
-                    for (unsigned mm = mask; mm; mm &= mm - 1) {
-                        const int b = __ffs(mm) - 1;
-                        if (sfix[wib][b] == j2) { mask &= ~(1u << b); break; }
-                    }
-                }
-                if (lane == r) out_key = make_key(t_code, win);
-            }
-            __syncwarp();
-        }
-
-        // softmax over the knn selected scores, fp32
-        const float sc = score_of_code<F32>(key_code(out_key));
-        const float mx = warp_max(lane < knn ? sc : -INFINITY);
-        const float e = lane < knn ? expf(sc - mx) : 0.f;
-        const float tot = warp_sum(e);
-        if (lane < knn) {
-            const int64_t o = row * knn + lane;
-            if constexpr (F32) static_cast<float*>(scores_out)[o] = sc;
-            else static_cast<uint16_t*>(scores_out)[o] = (uint16_t)decode_code16(key_code(out_key));
-            idx_out[o] = key_index(out_key);
-            w_out[o] = e / tot;
-        }
-        __syncwarp();
+        cartesian_select<F32>(key1, key2, nk, knn, buf, sfix[wib], row, scores_out, idx_out, w_out);
     }
+}
+
+// Pairs + softmax from per-half top lists of bf16 scores, as written by the fused scoring kernel: lists[row][half]
+// hold 32 keys (order code of the bf16 score << 16 | (0xffff - sub-key index)), sorted descending.
+__global__ void __launch_bounds__(SEL_WARPS * 32) pk_pairs_kernel(const uint32_t* lists, int64_t rows_nh, int nk,
+                                                                   int knn, void* scores_out, int64_t* idx_out,
+                                                                   float* w_out) {
+    __shared__ uint64_t sbuf[SEL_WARPS][SEL_CAP];
+    __shared__ uint32_t sfix[SEL_WARPS][32];
+    const int lane = lane_id();
+    const int wib = threadIdx.x >> 5;
+    const int64_t warps = (int64_t)gridDim.x * SEL_WARPS;
+    for (int64_t row = (int64_t)blockIdx.x * SEL_WARPS + wib; row < rows_nh; row += warps) {
+        const uint32_t a = lists[(row * 2 + 0) * 32 + lane];
+        const uint32_t b = lists[(row * 2 + 1) * 32 + lane];
+        const uint64_t key1 = lane < knn ? make_key(a >> 16, 0xffffu - (a & 0xffffu)) : 0;
+        const uint64_t key2 = lane < knn ? make_key(b >> 16, 0xffffu - (b & 0xffffu)) : 0;
+        cartesian_select<false>(key1, key2, nk, knn, sbuf[wib], sfix[wib], row, scores_out, idx_out, w_out);
+    }
+}
+
+int launch_pk_pairs(const uint32_t* lists, int64_t rows_nh, int nk, int knn, void* scores, int64_t* idx, float* w,
+                    cudaStream_t st) {
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((rows_nh + SEL_WARPS - 1) / SEL_WARPS,
+                                                                   (int64_t)sm_count() * 8));
+    pk_pairs_kernel<<<blocks, SEL_WARPS * 32, 0, st>>>(lists, rows_nh, nk, knn, scores, idx, w);
+    SMLM_LAUNCHED("pk_pairs_kernel");
+    return SMLM_OK;
 }
 
 // ------------------------------------------------------------------------------------ selection backward

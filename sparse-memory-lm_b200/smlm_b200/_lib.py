@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libs
 OK, ERR_INVALID, ERR_CUDA, ERR_WORKSPACE = 0, 1, 2, 3
 F32, BF16, F16, Q4 = 0, 1, 2, 3
 FLAG_INDEX_RANGE = 1
+FLAG_TIMEOUT = 4
 ROWRMS, ROWADAGRAD = 0, 1
 SCORE_F32_EXACT, SCORE_BF16 = 0, 1
 
@@ -46,6 +47,8 @@ SIGNATURES = {
     "smlm_pk_select": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
     "smlm_select_backward": (_i32, [_p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "smlm_subkey_scores_f32": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "smlm_score_select_workspace": (_sz, [_i64, _i64]),
+    "smlm_score_select": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _sz, _p, _p]),
 }
 
 _LIB = None
@@ -178,5 +181,7 @@ def after(device, what):
         return
     torch.cuda.synchronize(device)
     flags = read_status(device)
+    if flags & FLAG_TIMEOUT:
+        raise RuntimeError(f"{what}: a kernel-internal wait timed out (device status {flags:#x}); outputs invalid")
     if flags & FLAG_INDEX_RANGE:
         raise IndexError(f"{what}: row index out of range (device status {flags:#x})")

@@ -123,6 +123,70 @@ class SubkeyScoresF32(torch.autograd.Function):
         return dq, dk
 
 
+def fused_scoring_ok(half, n_keys, knn):
+    """Shapes the tensor-core scoring kernel takes (the half dimension is one or two 64-wide swizzle atoms)."""
+    return half in (64, 128) and n_keys % 8 == 0 and 1 <= knn <= 32 and knn <= n_keys <= 65536
+
+
+def score_select(q, keys, knn, dump=False):
+    """Fused bf16 scoring + selection on the tensor cores (reference: pkm.py:117-136 under bf16 autocast and
+    kernels.py:214 pk_select): q (N, H, k_dim) bf16, keys (H, 2, n_keys, k_dim/2) bf16 -> scores (N, H, knn) bf16,
+    indices int64, weights fp32. The sub-key scores are never materialised; dump=True also returns them
+    (s1, s2 bf16 (N, H, n_keys)) for checking."""
+    if q.dtype != torch.bfloat16 or keys.dtype != torch.bfloat16:
+        raise ValueError("score_select needs bf16 queries and keys")
+    dev = L.require_cuda(q, keys)
+    N, H, KD = q.shape
+    Hk, two, NK, half = keys.shape
+    if Hk != H or two != 2 or KD != 2 * half or not fused_scoring_ok(half, NK, knn):
+        raise ValueError(f"score_select: unsupported shapes q {tuple(q.shape)}, keys {tuple(keys.shape)}, knn {knn}")
+    q, keys = _contig(q), _contig(keys)
+    scores = torch.empty(N, H, knn, dtype=torch.bfloat16, device=dev)
+    idx = torch.empty(N, H, knn, dtype=torch.int64, device=dev)
+    w = torch.empty(N, H, knn, dtype=torch.float32, device=dev)
+    s1 = s2 = None
+    if dump:
+        s1 = torch.empty(N, H, NK, dtype=torch.bfloat16, device=dev)
+        s2 = torch.empty(N, H, NK, dtype=torch.bfloat16, device=dev)
+    ws = L.workspace(L.lib().smlm_score_select_workspace(N, H), dev)
+    with L.timed("score_select", 2):
+        rc = L.lib().smlm_score_select(L.ptr(q), L.ptr(keys), N, H, NK, half, knn, L.ptr(scores), L.ptr(idx),
+                                       L.ptr(w), L.ptr(s1), L.ptr(s2), L.ptr(ws), ws.numel(), L.status_ptr(dev),
+                                       L.stream(dev))
+    L.check(rc, "score_select")
+    L.after(dev, "score_select")
+    if dump:
+        return scores, idx, w, s1, s2
+    return scores, idx, w
+
+
+class ScoreSelect(torch.autograd.Function):
+    """Differentiable fused scoring + selection (bf16). Backward: the selection backward of PKSelect into dense
+    bf16 (N, H, n_keys) score gradients, then the scoring contraction's backward in bf16 (fp32 accumulate),
+    as the reference's autocast einsum backward does."""
+
+    @staticmethod
+    def forward(ctx, q, keys, knn):
+        scores, idx, w = score_select(q, keys, knn)
+        ctx.save_for_backward(q, keys, idx, w)
+        ctx.mark_non_differentiable(idx)
+        return scores, idx, w
+
+    @staticmethod
+    def backward(ctx, g_scores, g_idx, g_w):
+        q, keys, idx, w = ctx.saved_tensors
+        half, nk = keys.shape[-1], keys.shape[-2]
+        ds1, ds2 = select_backward(idx, w, g_w, g_scores, nk, torch.bfloat16)
+        dq = dk = None
+        if ctx.needs_input_grad[0]:
+            dq = torch.cat([torch.einsum("nhk,hkd->nhd", ds1, keys[:, 0]),
+                            torch.einsum("nhk,hkd->nhd", ds2, keys[:, 1])], dim=-1)
+        if ctx.needs_input_grad[1]:
+            dk = torch.stack([torch.einsum("nhk,nhd->hkd", ds1, q[..., :half]),
+                              torch.einsum("nhk,nhd->hkd", ds2, q[..., half:])], dim=1)
+        return dq, dk, None
+
+
 # ------------------------------------------------------------------------------------------ value bag
 def bag_forward(indices, weights, table, out_dtype=torch.float32):
     """out[n] = sum_k weights[n, k] * table[indices[n, k]] (fp32 accumulation); table fp32 / bf16

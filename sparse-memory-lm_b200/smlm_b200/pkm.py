@@ -2,9 +2,10 @@
 
 Same constructor, parameters, initialisation, state_dict keys and forward contract as the reference's
 ProductKeyMemory; the lookup runs on libsmlm_b200.so:
-  * scoring + selection: under bf16 autocast the bf16 sub-key scores (pkm.py:197, the reference's einsum) go
-    through the selection kernel (both half top-k, pair sums, final top-k, softmax); without autocast the
-    scores are computed exactly in fp32 by the fmaf-chain kernel and selected the same way;
+  * scoring + selection: under bf16 autocast one fused tensor-core kernel computes the bf16 sub-key scores
+    (pkm.py:197, the reference's einsum) and keeps each half's top-k in its epilogue, then the pairs / final
+    top-k / softmax kernel; without autocast the scores are computed exactly in fp32 by the fmaf-chain kernel
+    and selected by the selection kernel (both half top-k, pair sums, final top-k, softmax);
   * value bag: row_sparse_embedding_bag (row-sparse accumulation + lazy optimizer), or the inference bag with
     the swilu product fused when there is no grad under bf16 autocast (pkm.py:213-224);
   * decoding (one token, no grad, decode_graph): a captured CUDA graph of the same kernels (pkm.py:159-184).
@@ -166,9 +167,15 @@ class ProductKeyMemory(nn.Module):
         return static_out.clone()
 
     def _select(self, q, autocast_bf16):
-        """q (N, heads, k_dim) -> scores, indices, weights (N, heads, knn)."""
-        s1, s2 = self.subkey_scores(q.to(torch.bfloat16) if autocast_bf16 else q.float())
-        scores, indices, weights = K.PKSelect.apply(s1, s2, self.knn)
+        """q (N, heads, k_dim) -> scores, indices, weights (N, heads, knn). Under bf16 autocast the fused
+        tensor-core scoring + selection (no (N, heads, n_keys) score tensors); in fp32 the exact fmaf-chain scores
+        and the selection kernel."""
+        if autocast_bf16 and K.fused_scoring_ok(self.k_dim // 2, self.n_keys, self.knn):
+            scores, indices, weights = K.ScoreSelect.apply(q.to(torch.bfloat16), self.keys.to(torch.bfloat16),
+                                                           self.knn)
+        else:
+            s1, s2 = self.subkey_scores(q.to(torch.bfloat16) if autocast_bf16 else q.float())
+            scores, indices, weights = K.PKSelect.apply(s1, s2, self.knn)
         if self.log_score_scale is not None:
             logits = scores.float() * self.log_score_scale.float().exp().view(1, self.heads, 1)
             weights = F.softmax(logits, dim=-1)

@@ -117,8 +117,10 @@ def test_layer_golden(v):
 
 
 def test_layer_bf16_autocast_selection_equals_reference_selection():
-    """Under bf16 autocast the sub-key scores are the reference's bf16 einsum; the selection on them equals the
-    oracle's canonical selection bit for bit."""
+    """Under bf16 autocast the layer scores with the fused tensor-core kernel; its selection equals the oracle's
+    canonical selection on the kernel's bf16 sub-key scores bit for bit, and those scores are the reference's
+    bf16 einsum scores to within one bf16 step."""
+    from smlm_b200 import kernels as K
     ref, mem, x, gout = config1_pair(N=512)
     mem.record = True
     xx = x.to(DEV)
@@ -127,11 +129,15 @@ def test_layer_bf16_autocast_selection_equals_reference_selection():
     out.float().backward(gout.to(DEV))
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         q = mem.query_proj(xx).view(-1, 4, 256)
-        s1, s2 = mem.subkey_scores(q.to(torch.bfloat16))
+    with torch.no_grad():
+        _, idx, w, s1, s2 = K.score_select(q.to(torch.bfloat16), mem.keys.to(torch.bfloat16), 32, dump=True)
+        e1, e2 = mem.subkey_scores(q.to(torch.bfloat16))
+    assert torch.equal(mem.last_indices, idx)
     osc, oidx, ow = O.select(s1.cpu().contiguous().view(torch.int16).numpy().view(np.uint16),
                              s2.cpu().contiguous().view(torch.int16).numpy().view(np.uint16), 32, bf16=True)
     assert np.array_equal(mem.last_indices.cpu().numpy(), oidx)
     np.testing.assert_allclose(mem.last_weights.cpu().numpy(), ow, rtol=0, atol=1e-6)
+    assert float((s1 == e1).float().mean()) > 0.99 and float((s2 == e2).float().mean()) > 0.99
     assert mem.keys.grad is not None and mem.keys.grad.abs().sum() > 0
 
 

@@ -1,0 +1,93 @@
+"""The fused tensor-core scoring + selection kernel (score_tc.cu): its bf16 sub-key scores equal the bf16 einsum
+of the reference's autocast path to within one bf16 rounding step (fp32 summation order differs), and its
+selection equals the oracle's canonical selection on its own scores bit for bit."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from smlm_b200 import kernels as K
+from util import bits_of_bf16
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def inputs(N, H, NK, half, seed):
+    gen = torch.Generator().manual_seed(seed)
+    q = (torch.randn(N, H, 2 * half, generator=gen)).bfloat16()
+    keys = (torch.randn(H, 2, NK, half, generator=gen) * half ** -0.5).bfloat16()
+    return q.to(DEV), keys.to(DEV)
+
+
+def einsum_scores(q, keys):
+    half = keys.shape[-1]
+    s1 = torch.einsum("nhd,hkd->nhk", q[..., :half], keys[:, 0])
+    s2 = torch.einsum("nhd,hkd->nhk", q[..., half:], keys[:, 1])
+    return s1, s2
+
+
+@pytest.mark.parametrize("N,H,NK,half,knn", [
+    (128, 1, 128, 128, 32), (1000, 4, 1024, 128, 32), (300, 2, 256, 64, 8), (77, 3, 200, 128, 5),
+    (4096, 4, 4096, 128, 32), (1, 4, 512, 128, 32), (257, 1, 40, 64, 4)])
+def test_fused_selection_bit_exact_on_its_scores(N, H, NK, half, knn):
+    q, keys = inputs(N, H, NK, half, N + NK)
+    sc, idx, w, s1, s2 = K.score_select(q, keys, knn, dump=True)
+    osc, oidx, ow = O.select(bits_of_bf16(s1), bits_of_bf16(s2), knn, bf16=True)
+    assert np.array_equal(bits_of_bf16(sc), osc)
+    assert np.array_equal(idx.cpu().numpy(), oidx)
+    np.testing.assert_allclose(w.cpu().numpy(), ow, rtol=0, atol=1e-6)
+    # the kernel's scores are the bf16 GEMM scores: within one bf16 step of cuBLAS's, almost always equal
+    e1, e2 = einsum_scores(q, keys)
+    for a, b in ((s1, e1), (s2, e2)):
+        a, b = a.float(), b.float()
+        ulp = torch.where(b == 0, torch.full_like(b, 2.0 ** -133), b.abs() * 2.0 ** -7)
+        assert bool(((a - b).abs() <= ulp).all())
+        assert float((a == b).float().mean()) > 0.99
+
+
+def test_fused_matches_unfused_selection():
+    """Same selection as einsum + pk_select wherever the two bf16 score tensors agree on the row."""
+    q, keys = inputs(2048, 4, 1024, 128, 5)
+    sc, idx, w, s1, s2 = K.score_select(q, keys, 32, dump=True)
+    e1, e2 = einsum_scores(q, keys)
+    psc, pidx, pw = K.pk_select(e1, e2, 32)
+    same = ((s1 == e1).all(-1) & (s2 == e2).all(-1)).cpu()
+    assert float(same.float().mean()) > 0.5
+    assert torch.equal(idx.cpu()[same], pidx.cpu()[same])
+    assert torch.equal(sc.cpu()[same], psc.cpu()[same])
+
+
+def test_fused_determinism_and_ties():
+    """Coarse keys / queries produce exact score ties at every stage; two runs are bit-identical and equal the
+    oracle on the kernel's scores."""
+    gen = torch.Generator().manual_seed(9)
+    N, H, NK, half = 512, 2, 512, 128
+    q = torch.randint(-2, 3, (N, H, 2 * half), generator=gen).bfloat16().to(DEV)
+    keys = (torch.randint(-1, 2, (H, 2, NK, half), generator=gen).float() / 8).bfloat16().to(DEV)
+    a = K.score_select(q, keys, 32, dump=True)
+    b = K.score_select(q, keys, 32)
+    assert torch.equal(a[1], b[1]) and torch.equal(a[0], b[0]) and torch.equal(a[2], b[2])
+    osc, oidx, _ = O.select(bits_of_bf16(a[3]), bits_of_bf16(a[4]), 32, bf16=True)
+    assert np.array_equal(a[1].cpu().numpy(), oidx)
+
+
+def test_score_select_backward_matches_unfused():
+    """ScoreSelect's backward (dense bf16 score gradients, bf16 contractions) equals the einsum + PKSelect path's
+    gradients on the same selection."""
+    q, keys = inputs(512, 4, 256, 128, 3)
+    gen = torch.Generator().manual_seed(4)
+    gw = torch.randn(512, 4, 32, generator=gen).to(DEV)
+    qa, ka = q.clone().requires_grad_(), keys.clone().requires_grad_()
+    sc, idx, w = K.ScoreSelect.apply(qa, ka, 32)
+    (w * gw).sum().backward()
+    qb, kb = q.clone().requires_grad_(), keys.clone().requires_grad_()
+    s1, s2 = einsum_scores(qb, kb)
+    sc2, idx2, w2 = K.PKSelect.apply(s1, s2, 32)
+    same_rows = (idx == idx2).all(-1).all(-1)
+    assert float(same_rows.float().mean()) > 0.9
+    (w2 * gw).sum().backward()
+    if bool(same_rows.all()):
+        torch.testing.assert_close(qa.grad.float(), qb.grad.float(), rtol=2 ** -7, atol=1e-3)
+        torch.testing.assert_close(ka.grad.float(), kb.grad.float(), rtol=2 ** -7, atol=1e-3)
+    assert qa.grad.abs().sum() > 0 and ka.grad.abs().sum() > 0

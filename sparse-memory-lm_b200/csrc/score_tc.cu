@@ -8,15 +8,18 @@
 // softmax from the two per-half lists.
 //
 // CTA = 6 warps, persistent over units (128-token tile, head); a unit runs half 0 then half 1:
-//   warp 0      TMA producer: Q tile (128 tokens x 128, two 64-wide 128B-swizzled boxes, double-buffered) and
-//               key tiles (128 keys x 128) through a 3-stage ring, completion by mbarrier transaction counts.
+//   warp 0      TMA producer: Q tile (128 tokens x 128, two 64-wide 128B-swizzled boxes) and key tiles
+//               (128 keys x 128) through a 3-stage ring, completion by mbarrier transaction counts.
 //   warp 1      allocates 256 TMEM columns (two 128-column fp32 accumulators); lane 0 issues tcgen05.mma
 //               (M=128, N=128, K=16, kind::f16, bf16 in / fp32 accumulate), 8 per key tile, and commits to
 //               the stage's "empty" barrier and the accumulator's "full" barrier.
-//   warps 2-5   epilogue: tcgen05.ld of the 128 x 128 accumulator (warp w reads TMEM lanes 32 (w % 4) ..),
-//               one token per thread. Scores are rounded to bf16 in pairs and compared against the thread's
-//               current 32nd-best score (bf16x2 compare); the rare survivors go to a per-thread candidate list
-//               in shared memory that the warp merges into the sorted top-32 when any lane's list fills.
+//   warps 2-9   epilogue: tcgen05.ld of the 128 x 128 accumulator; warp w reads TMEM lanes 32 (w % 4) ..
+//               (the lane quarter it may access), one token per thread, and columns [0, 64) (warps 2-5) or
+//               [64, 128) (warps 6-9) of every tile. Scores are rounded to bf16 in pairs and compared against
+//               the thread's current 32nd-best (bf16x2 compare); survivors queue in a per-thread list in shared
+//               memory, and once any lane holds FLUSH_AT of them the warp inserts them in lockstep into the
+//               register-resident sorted top-32 (a min/max bubble). Each token ends with one sorted top-32 per
+//               column set; the pair kernel merges the two.
 // Every mbarrier wait is bounded (about one second); on timeout the kernel raises SMLM_FLAG_TIMEOUT in the
 // status word, every role unwinds, the MMA issuer waits (bounded) for its last commit, and TMEM is freed.
 // No TMA multicast is used (the kernel only reads this GPU's memory).
@@ -35,9 +38,11 @@ namespace tc {
 constexpr int BM = 128;          // tokens per tile (UMMA M)
 constexpr int BN = 128;          // sub-keys per tile (UMMA N)
 constexpr int STAGES = 3;        // key-tile ring
-constexpr int EPI_WARPS = 4;
-constexpr int THREADS = 64 + EPI_WARPS * 32;
-constexpr int CAND = 64;         // candidate slots per token
+constexpr int EPI_WARPS = 8;     // two per TMEM lane quarter: column halves [0, 64) and [64, 128) of a tile
+constexpr int EPI_THREADS = EPI_WARPS * 32;
+constexpr int THREADS = 64 + EPI_THREADS;
+constexpr int FLUSH_AT = 12;     // a warp merges its candidates once any lane holds this many
+constexpr int CAND = FLUSH_AT - 1 + 32;
 constexpr int ATOM = 64;         // bf16 elements per 128-byte swizzle atom (K direction)
 constexpr int ATOM_BYTES_A = BM * 128;
 constexpr int ATOM_BYTES_B = BN * 128;
@@ -180,91 +185,111 @@ __device__ __forceinline__ void sort_desc(uint32_t (&a)[N]) {
                 }
             }
 }
-// a is bitonic; sorts it descending
-__device__ __forceinline__ void merge_desc32(uint32_t (&a)[32]) {
-#pragma unroll
-    for (int j = 16; j > 0; j >>= 1)
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-            const int l = i ^ j;
-            if (l > i) {
-                const uint32_t x = a[i], y = a[l];
-                a[i] = max(x, y);
-                a[l] = min(x, y);
-            }
-        }
-}
 
 // key of a bf16 score: order code << 16 | (0xffff - sub-key index); larger is better, distinct per index
 __device__ __forceinline__ uint32_t score_key(uint32_t bits16, int col) {
     return (order_code16(bits16) << 16) | (uint32_t)(0xffff - col);
 }
 
+// Per-thread (= per token) running top-32 of one column stream, in registers, sorted descending.
 struct Epi {
-    uint32_t* cand;  // [CAND][128] (slot-major: thread e's slot i at i * 128 + e)
-    uint32_t* top;   // [32][128]
-    int e;           // epilogue thread index 0..127
+    uint32_t* cand;   // [CAND][EPI_THREADS] candidate keys (slot-major: conflict-free per-thread lists)
+    uint32_t* stage;  // [16][EPI_THREADS] the chunk's packed bf16 pairs, for the slow path
+    int e;            // epilogue thread index
     int cnt;
+    uint32_t top[32];
     __nv_bfloat162 thr2;
 
-    __device__ __forceinline__ void reset() {
-#pragma unroll
-        for (int i = 0; i < 32; i++) top[i * 128 + e] = 0;
-        cnt = 0;
-        thr2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)0xff80));  // -inf
+    __device__ __forceinline__ void set_thr() {
+        const uint32_t b = top[31] ? decode_code16(top[31] >> 16) : 0xff80u;  // fewer than 32 yet: -inf
+        thr2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)b));
     }
-    // Merges the candidates into the sorted top-32 and raises the threshold (all 32 lanes together).
-    __device__ __forceinline__ void flush() {
-        uint32_t c[CAND];
+    // k enters the sorted list, the smallest entry leaves (k is the carry of a min/max bubble)
+    __device__ __forceinline__ void insert(uint32_t k) {
 #pragma unroll
-        for (int i = 0; i < CAND; i++) c[i] = i < cnt ? cand[i * 128 + e] : 0u;
-        sort_desc<CAND>(c);
-        uint32_t t[32];
-#pragma unroll
-        for (int i = 0; i < 32; i++) t[i] = max(top[i * 128 + e], c[31 - i]);
-        merge_desc32(t);
-#pragma unroll
-        for (int i = 0; i < 32; i++) top[i * 128 + e] = t[i];
-        cnt = 0;
-        if (t[31] != 0) {
-            const unsigned short b = (unsigned short)decode_code16(t[31] >> 16);
-            thr2 = __bfloat162bfloat162(__ushort_as_bfloat16(b));
+        for (int i = 0; i < 32; i++) {
+            const uint32_t hi = max(top[i], k);
+            k = min(top[i], k);
+            top[i] = hi;
         }
     }
-    // 32 consecutive scores (fp32 bits) of columns col0 .. col0+31; columns >= nk are ignored.
-    __device__ __forceinline__ void take(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
-        __nv_bfloat162 p[16];
-        unsigned m[16];
-        unsigned any = 0;
+    __device__ __forceinline__ void pack(const uint32_t (&v)[32], int col0, int nk, __nv_bfloat162 (&p)[16]) {
 #pragma unroll
         for (int i = 0; i < 16; i++) {
             float lo = __uint_as_float(v[2 * i]), hi = __uint_as_float(v[2 * i + 1]);
             if (col0 + 2 * i >= nk) lo = -INFINITY;
             if (col0 + 2 * i + 1 >= nk) hi = -INFINITY;
             p[i] = __floats2bfloat162_rn(lo, hi);
+        }
+    }
+    __device__ __forceinline__ void dump(const __nv_bfloat162 (&p)[16], int col0, int nk, uint16_t* dbg) {
+        if (!dbg) return;
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (col0 + i < nk)
+                dbg[col0 + i] = (i & 1) ? __bfloat16_as_ushort(p[i >> 1].y) : __bfloat16_as_ushort(p[i >> 1].x);
+    }
+    // first chunk of a stream: the list is its 32 keys, sorted (columns >= nk enter as empty keys)
+    __device__ __forceinline__ void first(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
+        __nv_bfloat162 p[16];
+        pack(v, col0, nk, p);
+        dump(p, col0, nk, dbg);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            top[2 * i] = col0 + 2 * i < nk ? score_key(__bfloat16_as_ushort(p[i].x), col0 + 2 * i) : 0u;
+            top[2 * i + 1] = col0 + 2 * i + 1 < nk ? score_key(__bfloat16_as_ushort(p[i].y), col0 + 2 * i + 1) : 0u;
+        }
+        sort_desc<32>(top);
+        cnt = 0;
+        set_thr();
+    }
+    // merges the buffered candidates, all lanes in lockstep (one insertion slot per candidate rank)
+    __device__ __forceinline__ void flush() {
+        const int mx = __reduce_max_sync(FULL, (unsigned)cnt);
+        for (int k = 0; k < mx; k++) {
+            if (k < cnt) {
+                const uint32_t key = cand[k * EPI_THREADS + e];
+                if (key > top[31]) insert(key);
+            }
+        }
+        cnt = 0;
+        set_thr();
+    }
+    // 32 consecutive scores (fp32 bits) of columns col0 .. col0+31: a bf16x2 compare against the current
+    // 32nd-best filters them; survivors are queued, and merged once any lane has FLUSH_AT of them.
+    __device__ __forceinline__ void take(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
+        __nv_bfloat162 p[16];
+        pack(v, col0, nk, p);
+        dump(p, col0, nk, dbg);
+        unsigned m[16];
+        unsigned any = 0;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
             m[i] = __hgt2_mask(p[i], thr2);
             any |= m[i];
         }
-        if (dbg) {
-#pragma unroll
-            for (int i = 0; i < 32; i++)
-                if (col0 + i < nk) dbg[col0 + i] = (i & 1) ? __bfloat16_as_ushort(p[i >> 1].y)
-                                                            : __bfloat16_as_ushort(p[i >> 1].x);
-        }
-        if (any) {
+        if (__any_sync(FULL, any != 0)) {
+            uint32_t bits = 0;
 #pragma unroll
             for (int i = 0; i < 16; i++) {
-                if (m[i] & 0xffffu) cand[(cnt++) * 128 + e] = score_key(__bfloat16_as_ushort(p[i].x), col0 + 2 * i);
-                if (m[i] & 0xffff0000u) cand[(cnt++) * 128 + e] = score_key(__bfloat16_as_ushort(p[i].y), col0 + 2 * i + 1);
+                bits |= ((m[i] & 1u) | ((m[i] >> 30) & 2u)) << (2 * i);
+                stage[i * EPI_THREADS + e] = *reinterpret_cast<const uint32_t*>(&p[i]);
+            }
+            while (bits) {
+                const int i = __ffs(bits) - 1;
+                bits &= bits - 1;
+                const uint32_t w = stage[(i >> 1) * EPI_THREADS + e];
+                cand[cnt * EPI_THREADS + e] = score_key((i & 1) ? (w >> 16) : (w & 0xffffu), col0 + i);
+                cnt++;
             }
         }
-        if (__any_sync(FULL, cnt > CAND - 32)) flush();
+        if (__any_sync(FULL, cnt >= FLUSH_AT)) flush();
     }
 };
 
 struct Params {
     int n, heads, nk, atoms;  // atoms = half / 64
-    uint32_t* lists;          // [n][heads][2][32]
+    uint32_t* lists;          // [n][heads][2 halves][2 column sets][32]
     uint16_t* dbg1;           // optional bf16 scores [n][heads][nk], half 0
     uint16_t* dbg2;           // half 1
     int* status;
@@ -276,16 +301,16 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int a_bytes = P.atoms * ATOM_BYTES_A;
     const int b_bytes = P.atoms * ATOM_BYTES_B;
-    uint8_t* sA = smem;                              // 2 x a_bytes
-    uint8_t* sB = sA + 2 * a_bytes;                  // STAGES x b_bytes
+    uint8_t* sA = smem;                              // a_bytes (one query tile)
+    uint8_t* sB = sA + a_bytes;                      // STAGES x b_bytes
     uint32_t* cand = reinterpret_cast<uint32_t*>(sB + STAGES * b_bytes);
-    uint32_t* top = cand + CAND * 128;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(top + 32 * 128);
+    uint32_t* stage = cand + CAND * EPI_THREADS;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stage + 16 * EPI_THREADS);
     uint64_t* full_b = bars;
     uint64_t* empty_b = bars + STAGES;
     uint64_t* a_full = bars + 2 * STAGES;
-    uint64_t* a_empty = a_full + 2;
-    uint64_t* t_full = a_empty + 2;
+    uint64_t* a_empty = a_full + 1;
+    uint64_t* t_full = a_empty + 1;
     uint64_t* t_empty = t_full + 2;
     uint64_t* done = t_empty + 2;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
@@ -301,9 +326,9 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
             mbar_init(smem_addr(&full_b[i]), 1);
             mbar_init(smem_addr(&empty_b[i]), 1);
         }
+        mbar_init(smem_addr(a_full), 1);
+        mbar_init(smem_addr(a_empty), 1);
         for (int i = 0; i < 2; i++) {
-            mbar_init(smem_addr(&a_full[i]), 1);
-            mbar_init(smem_addr(&a_empty[i]), 1);
             mbar_init(smem_addr(&t_full[i]), 1);
             mbar_init(smem_addr(&t_empty[i]), EPI_WARPS);
         }
@@ -329,12 +354,11 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
             for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
                 const int tm = u / P.heads, h = u % P.heads;
                 for (int half = 0; half < 2; half++) {
-                    const int ab = a_iter & 1;
-                    if (!mbar_wait(smem_addr(&a_empty[ab]), ((a_iter >> 1) & 1) ^ 1, abort_flag)) break;
-                    mbar_expect_tx(smem_addr(&a_full[ab]), a_bytes);
+                    if (!mbar_wait(smem_addr(a_empty), (a_iter & 1) ^ 1, abort_flag)) break;
+                    mbar_expect_tx(smem_addr(a_full), a_bytes);
                     for (int i = 0; i < P.atoms; i++)
-                        tma_load_3d(smem_addr(sA + ab * a_bytes + i * ATOM_BYTES_A), &tq, smem_addr(&a_full[ab]),
-                                    i * ATOM, h * 2 + half, tm * BM);
+                        tma_load_3d(smem_addr(sA + i * ATOM_BYTES_A), &tq, smem_addr(a_full), i * ATOM, h * 2 + half,
+                                    tm * BM);
                     a_iter++;
                     for (int t = 0; t < ntiles; t++) {
                         if (!mbar_wait(smem_addr(&empty_b[s]), ph ^ 1, abort_flag)) break;
@@ -356,10 +380,9 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
             int a_iter = 0, t_iter = 0;
             for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
                 for (int half = 0; half < 2; half++) {
-                    const int ab = a_iter & 1;
-                    if (!mbar_wait(smem_addr(&a_full[ab]), (a_iter >> 1) & 1, abort_flag)) break;
+                    if (!mbar_wait(smem_addr(a_full), a_iter & 1, abort_flag)) break;
                     fence_after();
-                    const uint32_t a_base = smem_addr(sA + ab * a_bytes);
+                    const uint32_t a_base = smem_addr(sA);
                     for (int t = 0; t < ntiles; t++) {
                         if (!mbar_wait(smem_addr(&full_b[s]), ph, abort_flag)) break;
                         const int tb = t_iter & 1;
@@ -380,7 +403,7 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                         t_iter++;
                         if (++s == STAGES) { s = 0; ph ^= 1; }
                     }
-                    umma_commit(smem_addr(&a_empty[ab]));
+                    umma_commit(smem_addr(a_empty));
                     a_iter++;
                     if (*abort_flag) break;
                 }
@@ -392,14 +415,18 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
     } else {
         // ------------------------------------------------------------------ epilogue
         const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+        const int cset = (warp - 2) >> 2;        // column set: [0, 64) or [64, 128) of every tile
         const int row = quarter * 32 + lane;    // token row within the tile
-        Epi ep{cand, top, row, 0, {}};
+        Epi ep;
+        ep.cand = cand;
+        ep.stage = stage;
+        ep.e = (warp - 2) * 32 + lane;
+        ep.cnt = 0;
         int t_iter = 0;
         for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
             const int tm = u / P.heads, h = u % P.heads;
             const int64_t n = (int64_t)tm * BM + row;
             for (int half = 0; half < 2; half++) {
-                ep.reset();
                 uint16_t* dbg = half ? P.dbg2 : P.dbg1;
                 if (dbg && n < P.n) dbg += (n * P.heads + h) * (int64_t)P.nk;
                 else dbg = nullptr;
@@ -412,29 +439,27 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                         break;
                     }
                     fence_after();
-                    const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + tb * BN;
-                    uint32_t v0[32], v1[32], v2[32], v3[32];
+                    const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + tb * BN + cset * 64;
+                    uint32_t v0[32], v1[32];
                     tmem_ld32(base + 0, v0);
                     tmem_ld32(base + 32, v1);
-                    tmem_ld32(base + 64, v2);
-                    tmem_ld32(base + 96, v3);
                     tmem_wait_ld();
                     fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_addr(&t_empty[tb]));
                     t_iter++;
-                    const int c0 = t * BN;
-                    ep.take(v0, c0, P.nk, dbg);
+                    const int c0 = t * BN + cset * 64;
+                    if (t == 0) ep.first(v0, c0, P.nk, dbg);
+                    else ep.take(v0, c0, P.nk, dbg);
                     ep.take(v1, c0 + 32, P.nk, dbg);
-                    ep.take(v2, c0 + 64, P.nk, dbg);
-                    ep.take(v3, c0 + 96, P.nk, dbg);
                 }
                 if (!ok) break;
                 if (__any_sync(FULL, ep.cnt > 0)) ep.flush();
                 if (n < P.n) {
-                    uint32_t* dst = P.lists + ((n * P.heads + h) * 2 + half) * 32;
+                    uint32_t* dst = P.lists + (((n * P.heads + h) * 2 + half) * 2 + cset) * 32;
 #pragma unroll
-                    for (int i = 0; i < 32; i++) dst[i] = top[i * 128 + row];
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<uint4*>(dst + i) = make_uint4(ep.top[i], ep.top[i + 1], ep.top[i + 2], ep.top[i + 3]);
                 }
             }
         }
@@ -449,8 +474,8 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
 }
 
 size_t smem_bytes(int atoms) {
-    return 1024 + 2 * (size_t)atoms * ATOM_BYTES_A + STAGES * (size_t)atoms * ATOM_BYTES_B + CAND * 128 * 4 +
-           32 * 128 * 4 + 16 * 8 + 16;
+    return 1024 + (size_t)atoms * ATOM_BYTES_A + STAGES * (size_t)atoms * ATOM_BYTES_B + CAND * EPI_THREADS * 4 +
+           16 * EPI_THREADS * 4 + 16 * 8 + 16;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -471,7 +496,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 using namespace smlm;
 
 extern "C" size_t smlm_score_select_workspace(int64_t n, int64_t h) {
-    return (size_t)std::max<int64_t>(n, 0) * std::max<int64_t>(h, 0) * 2 * 32 * sizeof(uint32_t) + 256;
+    return (size_t)std::max<int64_t>(n, 0) * std::max<int64_t>(h, 0) * 2 * 2 * 32 * sizeof(uint32_t) + 256;
 }
 
 extern "C" int smlm_score_select(const void* q, const void* keys, int64_t n, int64_t h, int64_t nk, int64_t half,

@@ -240,8 +240,9 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) pk_select_kernel(const void* s
     }
 }
 
-// Pairs + softmax from per-half top lists of bf16 scores, as written by the fused scoring kernel: lists[row][half]
-// hold 32 keys (order code of the bf16 score << 16 | (0xffff - sub-key index)), sorted descending.
+// Pairs + softmax from per-half top lists of bf16 scores, as written by the fused scoring kernel:
+// lists[row][half][set] hold 32 keys (order code of the bf16 score << 16 | (0xffff - sub-key index)), sorted
+// descending, one list per column set; the two sets of a half are merged here.
 __global__ void __launch_bounds__(SEL_WARPS * 32) pk_pairs_kernel(const uint32_t* lists, int64_t rows_nh, int nk,
                                                                    int knn, void* scores_out, int64_t* idx_out,
                                                                    float* w_out) {
@@ -251,10 +252,21 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) pk_pairs_kernel(const uint32_t
     const int wib = threadIdx.x >> 5;
     const int64_t warps = (int64_t)gridDim.x * SEL_WARPS;
     for (int64_t row = (int64_t)blockIdx.x * SEL_WARPS + wib; row < rows_nh; row += warps) {
-        const uint32_t a = lists[(row * 2 + 0) * 32 + lane];
-        const uint32_t b = lists[(row * 2 + 1) * 32 + lane];
-        const uint64_t key1 = lane < knn ? make_key(a >> 16, 0xffffu - (a & 0xffffu)) : 0;
-        const uint64_t key2 = lane < knn ? make_key(b >> 16, 0xffffu - (b & 0xffffu)) : 0;
+        uint32_t hk[2];
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            // two sorted lists (column sets) -> the bitonic max sequence -> one sorted list, across lanes
+            const uint32_t* l = lists + ((row * 2 + half) * 2) * 32;
+            uint32_t k = max(l[lane], l[32 + 31 - lane]);
+#pragma unroll
+            for (int j = 16; j > 0; j >>= 1) {
+                const uint32_t x = __shfl_xor_sync(FULL, k, j);
+                k = (lane & j) ? min(k, x) : max(k, x);
+            }
+            hk[half] = k;
+        }
+        const uint64_t key1 = lane < knn ? make_key(hk[0] >> 16, 0xffffu - (hk[0] & 0xffffu)) : 0;
+        const uint64_t key2 = lane < knn ? make_key(hk[1] >> 16, 0xffffu - (hk[1] & 0xffffu)) : 0;
         cartesian_select<false>(key1, key2, nk, knn, sbuf[wib], sfix[wib], row, scores_out, idx_out, w_out);
     }
 }

@@ -7,7 +7,7 @@
 // per-half top-k computes. A second small kernel (select.cu, pk_pairs_kernel) forms the knn x knn pairs and the
 // softmax from the two per-half lists.
 //
-// CTA = 6 warps, persistent over units (128-token tile, head); a unit runs half 0 then half 1:
+// CTA = 10 warps, persistent over units (128-token tile, head); a unit runs half 0 then half 1:
 //   warp 0      TMA producer: Q tile (128 tokens x 128, two 64-wide 128B-swizzled boxes) and key tiles
 //               (128 keys x 128) through a 3-stage ring, completion by mbarrier transaction counts.
 //   warp 1      allocates 256 TMEM columns (two 128-column fp32 accumulators); lane 0 issues tcgen05.mma
@@ -15,11 +15,11 @@
 //               the stage's "empty" barrier and the accumulator's "full" barrier.
 //   warps 2-9   epilogue: tcgen05.ld of the 128 x 128 accumulator; warp w reads TMEM lanes 32 (w % 4) ..
 //               (the lane quarter it may access), one token per thread, and columns [0, 64) (warps 2-5) or
-//               [64, 128) (warps 6-9) of every tile. Scores are rounded to bf16 in pairs and compared against
-//               the thread's current 32nd-best (bf16x2 compare); survivors queue in a per-thread list in shared
-//               memory, and once any lane holds FLUSH_AT of them the warp inserts them in lockstep into the
-//               register-resident sorted top-32 (a min/max bubble). Each token ends with one sorted top-32 per
-//               column set; the pair kernel merges the two.
+//               [64, 128) (warps 6-9) of every tile. Each score is compared in fp32 against the exact rounding
+//               bound of the thread's current 32nd-best bf16 score; survivors queue in a per-thread list in
+//               shared memory, and once any lane holds FLUSH_AT of them the warp merges them in lockstep, 16
+//               at a time (sort the batch, bitonic merge into the register-resident sorted top-32). Each
+//               token ends with one sorted top-32 per column set; the pair kernel merges the two.
 // Every mbarrier wait is bounded (about one second); on timeout the kernel raises SMLM_FLAG_TIMEOUT in the
 // status word, every role unwinds, the MMA issuer waits (bounded) for its last commit, and TMEM is freed.
 // No TMA multicast is used (the kernel only reads this GPU's memory).
@@ -41,8 +41,9 @@ constexpr int STAGES = 3;        // key-tile ring
 constexpr int EPI_WARPS = 8;     // two per TMEM lane quarter: column halves [0, 64) and [64, 128) of a tile
 constexpr int EPI_THREADS = EPI_WARPS * 32;
 constexpr int THREADS = 64 + EPI_THREADS;
-constexpr int FLUSH_AT = 12;     // a warp merges its candidates once any lane holds this many
-constexpr int CAND = FLUSH_AT - 1 + 32;
+constexpr int BATCH = 16;        // candidates merged into the top-32 per sorted batch
+constexpr int FLUSH_AT = BATCH;  // a warp merges its candidates once any lane holds this many
+constexpr int CAND = 48;         // >= FLUSH_AT - 1 + 32 (one chunk can add 32)
 constexpr int ATOM = 64;         // bf16 elements per 128-byte swizzle atom (K direction)
 constexpr int ATOM_BYTES_A = BM * 128;
 constexpr int ATOM_BYTES_B = BN * 128;
@@ -67,14 +68,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+// The waiting thread may be suspended (up to ~0.1 ms) until the phase completes instead of spinning, so
+// waiting warps leave the issue slots to the working ones.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(100000u)
         : "memory");
     return ok != 0;
 }
@@ -186,100 +189,109 @@ __device__ __forceinline__ void sort_desc(uint32_t (&a)[N]) {
             }
 }
 
+// a is bitonic; sorts it descending (5 stages of 16 independent compare-exchanges)
+__device__ __forceinline__ void merge_desc32(uint32_t (&a)[32]) {
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1)
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const int l = i ^ j;
+            if (l > i) {
+                const uint32_t x = a[i], y = a[l];
+                a[i] = max(x, y);
+                a[l] = min(x, y);
+            }
+        }
+}
+
 // key of a bf16 score: order code << 16 | (0xffff - sub-key index); larger is better, distinct per index
 __device__ __forceinline__ uint32_t score_key(uint32_t bits16, int col) {
     return (order_code16(bits16) << 16) | (uint32_t)(0xffff - col);
 }
 
+// Smallest fp32 b such that bf16_rn(v) > t exactly when v >= b (t: bf16 bits of a finite threshold or -inf).
+// With u the next bf16 above t, the rounding midpoint m = (t + u) / 2 rounds to the even one of t, u: it passes
+// if u is even, otherwise only values above m pass.
+__device__ __forceinline__ float pass_bound(uint32_t t) {
+    uint32_t u;
+    if ((t & 0x8000u) == 0) u = t + 1;           // +0 and positives: one step up
+    else if (t == 0x8000u) u = 0x0001u;          // -0 -> smallest positive
+    else u = t - 1;                              // negatives: one step toward zero
+    const float m = 0.5f * (bf16_bits_to_f32(t) + bf16_bits_to_f32(u));  // exact
+    if ((u & 1u) == 0) return m;
+    const uint32_t mb = __float_as_uint(m);
+    return __uint_as_float(m > 0.f ? mb + 1 : mb - 1);                   // next fp32 above m
+}
+
 // Per-thread (= per token) running top-32 of one column stream, in registers, sorted descending.
 struct Epi {
     uint32_t* cand;   // [CAND][EPI_THREADS] candidate keys (slot-major: conflict-free per-thread lists)
-    uint32_t* stage;  // [16][EPI_THREADS] the chunk's packed bf16 pairs, for the slow path
+    float4* stage;    // [8][EPI_THREADS] the chunk's 32 scores, for reading survivors back by index
     int e;            // epilogue thread index
     int cnt;
     uint32_t top[32];
-    __nv_bfloat162 thr2;
+    float bound;      // fp32 scores >= bound round to a bf16 above the current 32nd-best
 
     __device__ __forceinline__ void set_thr() {
-        const uint32_t b = top[31] ? decode_code16(top[31] >> 16) : 0xff80u;  // fewer than 32 yet: -inf
-        thr2 = __bfloat162bfloat162(__ushort_as_bfloat16((unsigned short)b));
+        bound = pass_bound(top[31] ? decode_code16(top[31] >> 16) : 0xff80u);   // fewer than 32 yet: -inf
     }
-    // k enters the sorted list, the smallest entry leaves (k is the carry of a min/max bubble)
-    __device__ __forceinline__ void insert(uint32_t k) {
+    // candidates [base, base + BATCH) enter the list: sort the batch, take the elementwise max of the list's tail
+    // and the reversed batch (a bitonic sequence holding the best 32 of both), clean it into order
+    __device__ __forceinline__ void merge_batch(int base) {
+        uint32_t c[BATCH];
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-            const uint32_t hi = max(top[i], k);
-            k = min(top[i], k);
-            top[i] = hi;
-        }
-    }
-    __device__ __forceinline__ void pack(const uint32_t (&v)[32], int col0, int nk, __nv_bfloat162 (&p)[16]) {
+        for (int i = 0; i < BATCH; i++) c[i] = base + i < cnt ? cand[(base + i) * EPI_THREADS + e] : 0u;
+        sort_desc<BATCH>(c);
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            float lo = __uint_as_float(v[2 * i]), hi = __uint_as_float(v[2 * i + 1]);
-            if (col0 + 2 * i >= nk) lo = -INFINITY;
-            if (col0 + 2 * i + 1 >= nk) hi = -INFINITY;
-            p[i] = __floats2bfloat162_rn(lo, hi);
-        }
+        for (int i = 0; i < BATCH; i++) top[32 - BATCH + i] = max(top[32 - BATCH + i], c[BATCH - 1 - i]);
+        merge_desc32(top);
     }
-    __device__ __forceinline__ void dump(const __nv_bfloat162 (&p)[16], int col0, int nk, uint16_t* dbg) {
+    __device__ __forceinline__ void dump(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
         if (!dbg) return;
 #pragma unroll
         for (int i = 0; i < 32; i++)
-            if (col0 + i < nk)
-                dbg[col0 + i] = (i & 1) ? __bfloat16_as_ushort(p[i >> 1].y) : __bfloat16_as_ushort(p[i >> 1].x);
+            if (col0 + i < nk) dbg[col0 + i] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i])));
     }
     // first chunk of a stream: the list is its 32 keys, sorted (columns >= nk enter as empty keys)
     __device__ __forceinline__ void first(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
-        __nv_bfloat162 p[16];
-        pack(v, col0, nk, p);
-        dump(p, col0, nk, dbg);
+        dump(v, col0, nk, dbg);
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            top[2 * i] = col0 + 2 * i < nk ? score_key(__bfloat16_as_ushort(p[i].x), col0 + 2 * i) : 0u;
-            top[2 * i + 1] = col0 + 2 * i + 1 < nk ? score_key(__bfloat16_as_ushort(p[i].y), col0 + 2 * i + 1) : 0u;
-        }
+        for (int i = 0; i < 32; i++)
+            top[i] = col0 + i < nk
+                         ? score_key(__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]))), col0 + i)
+                         : 0u;
         sort_desc<32>(top);
         cnt = 0;
         set_thr();
     }
-    // merges the buffered candidates, all lanes in lockstep (one insertion slot per candidate rank)
+    // merges the buffered candidates, all lanes in lockstep, BATCH at a time
     __device__ __forceinline__ void flush() {
         const int mx = __reduce_max_sync(FULL, (unsigned)cnt);
-        for (int k = 0; k < mx; k++) {
-            if (k < cnt) {
-                const uint32_t key = cand[k * EPI_THREADS + e];
-                if (key > top[31]) insert(key);
-            }
-        }
+        for (int base = 0; base < mx; base += BATCH) merge_batch(base);
         cnt = 0;
         set_thr();
     }
-    // 32 consecutive scores (fp32 bits) of columns col0 .. col0+31: a bf16x2 compare against the current
-    // 32nd-best filters them; survivors are queued, and merged once any lane has FLUSH_AT of them.
+    // 32 consecutive scores (fp32 bits) of columns col0 .. col0+31: an fp32 compare against the exact bound
+    // filters them; survivors are queued, and merged once any lane has FLUSH_AT of them.
     __device__ __forceinline__ void take(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
-        __nv_bfloat162 p[16];
-        pack(v, col0, nk, p);
-        dump(p, col0, nk, dbg);
-        unsigned m[16];
-        unsigned any = 0;
+        dump(v, col0, nk, dbg);
+        uint32_t part[4] = {0u, 0u, 0u, 0u};  // four independent chains
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            m[i] = __hgt2_mask(p[i], thr2);
-            any |= m[i];
-        }
-        if (__any_sync(FULL, any != 0)) {
-            uint32_t bits = 0;
+        for (int i = 0; i < 32; i++)
+            if (__uint_as_float(v[i]) >= bound) part[i & 3] |= 1u << i;
+        uint32_t bits = (part[0] | part[1]) | (part[2] | part[3]);
+        if (col0 + 32 > nk) bits &= nk - col0 <= 0 ? 0u : (0xffffffffu >> (32 - (nk - col0)));
+        if (bits) {
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                bits |= ((m[i] & 1u) | ((m[i] >> 30) & 2u)) << (2 * i);
-                stage[i * EPI_THREADS + e] = *reinterpret_cast<const uint32_t*>(&p[i]);
-            }
+            for (int j = 0; j < 8; j++)
+                stage[j * EPI_THREADS + e] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                         __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            const float* sf = reinterpret_cast<const float*>(stage);
             while (bits) {
                 const int i = __ffs(bits) - 1;
                 bits &= bits - 1;
-                const uint32_t w = stage[(i >> 1) * EPI_THREADS + e];
-                cand[cnt * EPI_THREADS + e] = score_key((i & 1) ? (w >> 16) : (w & 0xffffu), col0 + i);
+                const float x = sf[((i >> 2) * EPI_THREADS + e) * 4 + (i & 3)];
+                cand[cnt * EPI_THREADS + e] = score_key(__bfloat16_as_ushort(__float2bfloat16_rn(x)), col0 + i);
                 cnt++;
             }
         }
@@ -304,8 +316,8 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
     uint8_t* sA = smem;                              // a_bytes (one query tile)
     uint8_t* sB = sA + a_bytes;                      // STAGES x b_bytes
     uint32_t* cand = reinterpret_cast<uint32_t*>(sB + STAGES * b_bytes);
-    uint32_t* stage = cand + CAND * EPI_THREADS;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stage + 16 * EPI_THREADS);
+    float4* stage = reinterpret_cast<float4*>(cand + CAND * EPI_THREADS);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stage + 8 * EPI_THREADS);
     uint64_t* full_b = bars;
     uint64_t* empty_b = bars + STAGES;
     uint64_t* a_full = bars + 2 * STAGES;
@@ -475,7 +487,7 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
 
 size_t smem_bytes(int atoms) {
     return 1024 + (size_t)atoms * ATOM_BYTES_A + STAGES * (size_t)atoms * ATOM_BYTES_B + CAND * EPI_THREADS * 4 +
-           16 * EPI_THREADS * 4 + 16 * 8 + 16;
+           8 * EPI_THREADS * 16 + 16 * 8 + 16;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {

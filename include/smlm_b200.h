@@ -177,6 +177,20 @@ SMLM_API int smlm_score_select(const void *q, const void *keys, int64_t n, int64
                                int64_t knn, void *scores, int64_t *indices, float *weights, void *s1_out,
                                void *s2_out, void *workspace, size_t workspace_bytes, int *status, void *stream);
 
+/* Allocation-free variant of smlm_score_select (same inputs, outputs and results; no debug score outputs), for
+ * callers that cannot allocate device memory at call time: a host framework that has reserved the GPU's memory
+ * in its own pool, or a latency-critical serving loop where cudaMalloc / cudaFree would synchronise the device.
+ * No counterpart in the reference. Its scratch is a static device array inside the library, sized for at most
+ * SMLM_NOALLOC_MAX_ROWS (token, head) rows (n * h; 8 MiB, held by every GPU that loads the library until the
+ * process exits); larger calls return SMLM_ERR_INVALID. The first call on a device looks up that array's device
+ * address (cudaGetSymbolAddress) with the device current; make that first call before any stream capture. All
+ * calls share the one array, so calls that overlap on the GPU (other streams, other threads) race: serialise
+ * them. The call allocates nothing: no cudaMalloc / cudaFree, no allocating library routine. */
+#define SMLM_NOALLOC_MAX_ROWS 16384
+SMLM_API int smlm_score_select_noalloc(const void *q, const void *keys, int64_t n, int64_t h, int64_t nk,
+                                       int64_t half, int64_t knn, void *scores, int64_t *indices, float *weights,
+                                       int *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,6 +26,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace smlm {
@@ -571,6 +573,104 @@ extern "C" int smlm_score_select(const void* q, const void* keys, int64_t n, int
     const int grid = (int)std::min<int64_t>(units, sm_count());
     tc::Params P{(int)n, (int)h, (int)nk, atoms, lists, static_cast<uint16_t*>(s1_out), static_cast<uint16_t*>(s2_out),
                  status};
+    tc::score_topk_kernel<<<grid, tc::THREADS, smem, st>>>(tq, tk, P);
+    SMLM_LAUNCHED("score_topk_kernel");
+    return launch_pk_pairs(lists, n * h, (int)nk, (int)knn, scores, indices, weights, st);
+}
+
+// ------------------------------------------------------------------------------- allocation-free variant
+// Some callers cannot allocate device memory at call time: a host framework that has reserved the GPU's memory
+// in its own pool (so a cudaMalloc of the scratch would fail or fragment it), or a latency-critical serving
+// loop where a cudaMalloc / cudaFree would synchronise the device. smlm_score_select_noalloc serves them: its
+// scratch, the per-half top lists of at most SMLM_NOALLOC_MAX_ROWS (token, head) rows (512 bytes each, 8 MiB in
+// all), is this array in the library's static device memory. Every GPU that loads the library holds it until
+// the process exits. All calls share it, so calls that overlap on the GPU (other streams, other threads) race.
+static __device__ __align__(256) uint32_t g_noalloc_lists[(size_t)SMLM_NOALLOC_MAX_ROWS * 2 * 2 * 32];
+
+namespace smlm {
+namespace tc {
+
+// Device address of g_noalloc_lists on the current device, looked up once per device (host code only sees a
+// host-side stand-in under that name, which must never reach a kernel).
+static int noalloc_scratch(uint32_t** out) {
+    static std::mutex mu;
+    static uint32_t* addr[64] = {};
+    int dev = 0;
+    SMLM_CUDA(cudaGetDevice(&dev));
+    SMLM_CHECK_ARG(dev >= 0 && dev < 64, "score_select_noalloc: device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        SMLM_CUDA(cudaGetSymbolAddress(&p, g_noalloc_lists));
+        addr[dev] = static_cast<uint32_t*>(p);
+    }
+    *out = addr[dev];
+    return SMLM_OK;
+}
+
+}  // namespace tc
+}  // namespace smlm
+
+extern "C" int smlm_score_select_noalloc(const void* q, const void* keys, int64_t n, int64_t h, int64_t nk,
+                                         int64_t half, int64_t knn, void* scores, int64_t* indices, float* weights,
+                                         int* status, void* stream) {
+    SMLM_CHECK_ARG(n >= 0 && h > 0, "score_select_noalloc: bad n / heads");
+    SMLM_CHECK_ARG(n * h <= SMLM_NOALLOC_MAX_ROWS,
+                   "score_select_noalloc: n * heads = %lld exceeds the static scratch (SMLM_NOALLOC_MAX_ROWS = %d); "
+                   "split the call or use smlm_score_select with a workspace",
+                   (long long)(n * h), SMLM_NOALLOC_MAX_ROWS);
+    SMLM_CHECK_ARG(half == 64 || half == 128, "score_select_noalloc: the half dimension must be 64 or 128, got %lld",
+                   (long long)half);
+    SMLM_CHECK_ARG(knn >= 1 && knn <= 32, "score_select_noalloc: knn must be in [1, 32]");
+    SMLM_CHECK_ARG(nk >= knn && nk <= 65536 && nk % 8 == 0,
+                   "score_select_noalloc: need knn <= n_keys <= 65536, n_keys % 8 == 0");
+    SMLM_CHECK_ARG(h * 2 * nk < (1ll << 31), "score_select_noalloc: sizes beyond 32-bit TMA coordinates");
+    if (n == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(q && keys && scores && indices && weights, "score_select_noalloc: null pointer");
+    SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(keys) % 16 == 0,
+                   "score_select_noalloc: q and keys must be 16-byte aligned");
+    uint32_t* lists = nullptr;
+    int rc = tc::noalloc_scratch(&lists);
+    if (rc != SMLM_OK) return rc;
+    auto encode = tc::encode_fn();
+    if (!encode) {
+        set_error("score_select_noalloc: cuTensorMapEncodeTiled is not available from the driver");
+        return SMLM_ERR_CUDA;
+    }
+    CUtensorMap tq, tk;
+    {
+        cuuint64_t dims[3] = {(cuuint64_t)half, (cuuint64_t)(2 * h), (cuuint64_t)n};
+        cuuint64_t strides[2] = {(cuuint64_t)half * 2, (cuuint64_t)(2 * h * half * 2)};
+        cuuint32_t box[3] = {tc::ATOM, 1, tc::BM};
+        cuuint32_t es[3] = {1, 1, 1};
+        if (encode(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            set_error("score_select_noalloc: query tensor map encode failed");
+            return SMLM_ERR_CUDA;
+        }
+    }
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)half, (cuuint64_t)(h * 2 * nk)};
+        cuuint64_t strides[1] = {(cuuint64_t)half * 2};
+        cuuint32_t box[2] = {tc::ATOM, tc::BN};
+        cuuint32_t es[2] = {1, 1};
+        if (encode(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(keys), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            set_error("score_select_noalloc: key tensor map encode failed");
+            return SMLM_ERR_CUDA;
+        }
+    }
+    cudaStream_t st = as_stream(stream);
+    const int atoms = (int)(half / tc::ATOM);
+    const size_t smem = tc::smem_bytes(atoms);
+    SMLM_CUDA(cudaFuncSetAttribute(tc::score_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int64_t units = ((n + tc::BM - 1) / tc::BM) * h;
+    const int grid = (int)std::min<int64_t>(units, sm_count());
+    // every (token, head) row of the lists is written by the scoring kernel before the pair kernel reads it,
+    // so the previous call's contents need no clearing
+    tc::Params P{(int)n, (int)h, (int)nk, atoms, lists, nullptr, nullptr, status};
     tc::score_topk_kernel<<<grid, tc::THREADS, smem, st>>>(tq, tk, P);
     SMLM_LAUNCHED("score_topk_kernel");
     return launch_pk_pairs(lists, n * h, (int)nk, (int)knn, scores, indices, weights, st);

@@ -49,6 +49,7 @@ SIGNATURES = {
     "smlm_subkey_scores_f32": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "smlm_score_select_workspace": (_sz, [_i64, _i64]),
     "smlm_score_select": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _sz, _p, _p]),
+    "smlm_score_select_noalloc": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
 }
 
 _LIB = None

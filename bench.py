@@ -36,6 +36,9 @@ sys.path.insert(0, os.path.join(ROOT, "sparse-memory-lm_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "PKM layer tokens/s (fwd+bwd+opt) at 16.8M rows"
+# DRAM bytes (read + write) of one lazy Adam launch per touched row, from the ncu capture in
+# profiles/lazy_adam_kernel_pkm-layer-1m.md (7.612 GB / 621,696 rows); traffic scales with the touched rows.
+ADAM_TRAFFIC_PER_ROW = 12244
 D_MODEL, HEADS, KNN, K_DIM = 384, 4, 32, 256
 
 
@@ -234,7 +237,8 @@ def run_cuda(args, world, rank, local):
     adam_ms = statistics.mean(per_kernel["lazy_adam_step"])
     adam_bytes = rows * 1 + U * (4 + 4 + 1) + U * D_MODEL * 4 * 8    # mask scan, row list, p/m/v/acc r+w
     roof = {"kernel": "lazy_adam_step", "bound": "hbm", "achieved": adam_bytes / (adam_ms / 1e3) / 1e9,
-            "peak": hbm, "peak_source": peak_src, "unit": "GB/s", "traffic": None,
+            "peak": hbm, "peak_source": peak_src, "unit": "GB/s", "traffic": round(ADAM_TRAFFIC_PER_ROW * U),
+            "traffic_source": "ncu dram bytes per touched row on a 1M-row capture, scaled by the measured rows",
             "algorithmic_bytes": adam_bytes, "unique_rows": U}
     roof["frac"] = roof["achieved"] / roof["peak"]
     M = N * HEADS * KNN

@@ -37,8 +37,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "PKM layer tokens/s (fwd+bwd+opt) at 16.8M rows"
 # DRAM bytes (read + write) of one lazy Adam launch per touched row, from the ncu capture in
-# profiles/lazy_adam_kernel_pkm-layer-1m.md (7.612 GB / 621,696 rows); traffic scales with the touched rows.
-ADAM_TRAFFIC_PER_ROW = 12244
+# profiles/lazy_adam_kernel_pkm-layer-1m.md; traffic scales with the touched rows. None until measured for the
+# current kernel (the step no longer rewrites the accumulator rows it consumes).
+ADAM_TRAFFIC_PER_ROW = None
 D_MODEL, HEADS, KNN, K_DIM = 384, 4, 32, 256
 
 
@@ -194,7 +195,7 @@ def run_cuda(args, world, rank, local):
         with torch.autocast("cuda", dtype=torch.bfloat16):
             out = mem(xs[i])
         out.backward(gs[i])
-        uniq.append(int(st.touched.sum()))
+        uniq.append(st.touched_rows())
         opt.step()
         opt.zero_grad(set_to_none=True)
     U = sum(uniq) / len(uniq)
@@ -235,16 +236,19 @@ def run_cuda(args, world, rank, local):
     peak_src = "measured" if hbm else "fallback"
     hbm = hbm or 6650.0
     adam_ms = statistics.mean(per_kernel["lazy_adam_step"])
-    adam_bytes = rows * 1 + U * (4 + 4 + 1) + U * D_MODEL * 4 * 8    # mask scan, row list, p/m/v/acc r+w
+    # mask scan, row list, read p / m / v / acc, write p / m / v (the clean RowStore keeps consumed acc rows)
+    adam_bytes = rows * 1 + U * (4 + 4 + 1) + U * D_MODEL * 4 * 7
     roof = {"kernel": "lazy_adam_step", "bound": "hbm", "achieved": adam_bytes / (adam_ms / 1e3) / 1e9,
-            "peak": hbm, "peak_source": peak_src, "unit": "GB/s", "traffic": round(ADAM_TRAFFIC_PER_ROW * U),
+            "peak": hbm, "peak_source": peak_src, "unit": "GB/s",
+            "traffic": round(ADAM_TRAFFIC_PER_ROW * U) if ADAM_TRAFFIC_PER_ROW else None,
             "traffic_source": "ncu dram bytes per touched row on a 1M-row capture, scaled by the measured rows",
             "algorithmic_bytes": adam_bytes, "unique_rows": U}
     roof["frac"] = roof["achieved"] / roof["peak"]
     M = N * HEADS * KNN
     kernel_bytes = {
         "bag_forward": M * (D_MODEL * 4 + 12) + N * D_MODEL * 4,
-        "bag_backward_rows": U * D_MODEL * 4 * 3 + M * (8 * 4 + 4 + 4) + N * D_MODEL * 4,
+        # table row once per run + accumulator row written (first touch of the step: not read) + sort + gw
+        "bag_backward_rows": U * D_MODEL * 4 * 2 + M * (8 * 4 + 4 + 4) + N * D_MODEL * 4,
         "lazy_adam_step": adam_bytes,
     }
     breakdown = {}

@@ -50,6 +50,13 @@ extern "C" {
 #define SMLM_FLAG_INDEX_RANGE 1
 #define SMLM_FLAG_TIMEOUT 4 /* a bounded wait inside a kernel gave up; that call's outputs are invalid */
 
+/* flags of smlm_bag_backward_rows: rows whose touched byte is 0 are written, not accumulated (the caller
+ * guarantees such rows count as zero, e.g. a RowStore whose untouched rows are never read as data) */
+#define SMLM_BWD_FIRST_TOUCH_WRITES 1
+/* flags of the optimizer steps: leave the consumed accumulator rows unchanged instead of zeroing them (they
+ * count as zero once their touched byte is cleared) */
+#define SMLM_STEP_KEEP_ACC 1
+
 /* row-wise optimizer kinds (smlm/row_optim.py:21 KINDS) */
 #define SMLM_ROWRMS 0
 #define SMLM_ROWADAGRAD 1
@@ -98,11 +105,14 @@ SMLM_API size_t smlm_bag_backward_workspace(int64_t n, int64_t k, int64_t rows, 
  * results are bit-identical from run to run.
  * Replaces kernels.py:73 bag_backward_rows (and sparse_values.py:97-103, the aten per-sample-weight
  * backward + index_put_ accumulation). grad_out: F32 (n, d); weights F32/BF16; table F32/BF16; acc F32.
- * acc == NULL (and touched == NULL): only gw is computed (frozen table, sparse_values.py:118-120). */
+ * acc == NULL (and touched == NULL): only gw is computed (frozen table, sparse_values.py:118-120).
+ * row_sqnorm (optional, fp32 (rows,)): the squared L2 norm of every accumulator row written by this call.
+ * flags: SMLM_BWD_FIRST_TOUCH_WRITES. */
 SMLM_API int smlm_bag_backward_rows(const float *grad_out, const int64_t *indices, const void *weights,
-                           int weights_dtype, const void *table, int table_dtype, float *acc, uint8_t *touched,
-                           float *gw, int64_t n, int64_t k, int64_t rows, int64_t d, void *workspace,
-                           size_t workspace_bytes, int *status, void *stream);
+                                    int weights_dtype, const void *table, int table_dtype, float *acc,
+                                    uint8_t *touched, float *row_sqnorm, int flags, float *gw, int64_t n, int64_t k,
+                                    int64_t rows, int64_t d, void *workspace, size_t workspace_bytes, int *status,
+                                    void *stream);
 
 /* ------------------------------------------------------------------------------- row-sparse optimizers */
 
@@ -114,28 +124,36 @@ SMLM_API size_t smlm_touched_workspace(int64_t rows);
  * (smlm/host_rows.c:63-80, no contraction into FMA), so results are bit-identical to it.
  * scale = *grad_scale_dev if grad_scale_dev is not NULL, else grad_scale.
  * value_copy (optional, copy_dtype BF16 or F32, (rows, d)): the updated rows are also written there.
+ * flags: SMLM_STEP_KEEP_ACC (acc rows are not zeroed).
  * Replaces kernels.py:417 lazy_adam_step (and LazyRowAdam.step's torch path, sparse_values.py:270-305). */
 SMLM_API int smlm_lazy_adam_step(float *param, float *exp_avg, float *exp_avg_sq, float *acc, uint8_t *touched,
-                        const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
-                        float one_minus_b1, float b2, float one_minus_b2, float bc2_sqrt, float eps,
-                        float neg_step_size, void *value_copy, int copy_dtype, void *workspace,
-                        size_t workspace_bytes, void *stream);
+                                 const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
+                                 float one_minus_b1, float b2, float one_minus_b2, float bc2_sqrt, float eps,
+                                 float neg_step_size, void *value_copy, int copy_dtype, int flags, void *workspace,
+                                 size_t workspace_bytes, void *stream);
 
 /* Row-wise optimizer on the touched rows (smlm/row_optim.py; formulas of host_rows.c:84-117):
  *   q = mean over the row of g^2 (summed in double), g = acc[r] * scale
  *   SMLM_ROWRMS:     v[r] = b2 v[r] + (1 - b2) q;  count[r] += 1;  denom = sqrt(v[r] / (1 - b2^count[r])) + eps
  *   SMLM_ROWADAGRAD: v[r] += q;                                      denom = sqrt(v[r]) + eps
  *   p[r] -= (lr / denom) * g;  acc[r] = 0;  touched[r] = 0.
- * count may be NULL for SMLM_ROWADAGRAD. Replaces RowWiseOptimizer._masked (row_optim.py:179-201). */
+ * count may be NULL for SMLM_ROWADAGRAD. flags: SMLM_STEP_KEEP_ACC.
+ * Replaces RowWiseOptimizer._masked (row_optim.py:179-201). */
 SMLM_API int smlm_rowwise_step(float *param, float *acc, uint8_t *touched, float *v, int32_t *count,
-                      const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d, int kind, float b2,
-                      float eps, float lr, void *workspace, size_t workspace_bytes, void *stream);
+                               const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d, int kind,
+                               float b2, float eps, float lr, int flags, void *workspace, size_t workspace_bytes,
+                               void *stream);
 
-/* L2 norm of the accumulator over the touched rows, written to *norm_out (device fp32). Rows that were not
- * touched hold zeros in a RowStore (the backward only adds to touched rows, the step zeroes them), so this is
- * the reference's acc.norm() (sparse_values.py:143) without reading the untouched rows. Deterministic. */
-SMLM_API int smlm_touched_norm(const float *acc, const uint8_t *touched, int64_t rows, int64_t d, float *norm_out,
-                      void *workspace, size_t workspace_bytes, void *stream);
+/* L2 norm of the accumulator over the touched rows, written to *norm_out (device fp32): the reference's
+ * acc.norm() (sparse_values.py:143) for an accumulator whose untouched rows count as zero. With row_sqnorm
+ * (the per-row squared norms the backward wrote) only 4 bytes per touched row are read, else the rows of acc.
+ * Deterministic (fixed partial-sum order). */
+SMLM_API int smlm_touched_norm(const float *acc, const float *row_sqnorm, const uint8_t *touched, int64_t rows,
+                               int64_t d, float *norm_out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* acc rows whose touched byte is 0 are set to zero: turns "untouched rows count as zero" into actual zeros
+ * before an accumulator is handed to code that reads it as a dense tensor (RowStore.acc). */
+SMLM_API int smlm_zero_untouched(float *acc, const uint8_t *touched, int64_t rows, int64_t d, void *stream);
 
 /* ------------------------------------------------------------------------- product-key scoring / select */
 

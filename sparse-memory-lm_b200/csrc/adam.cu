@@ -76,6 +76,7 @@ struct AdamArgs {
     float one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step;
     void* copy;
     int copy_dtype;
+    int keep_acc;  // leave the consumed accumulator rows as they are (they count as zero once untouched)
 };
 
 // Element update in the reference C loop's order (host_rows.c:69-76), every operation rounded on its own.
@@ -112,7 +113,7 @@ __global__ void __launch_bounds__(256) lazy_adam_kernel(AdamArgs a) {
                 *reinterpret_cast<float4*>(a.p + base + c) = p;
                 *reinterpret_cast<float4*>(a.m + base + c) = m;
                 *reinterpret_cast<float4*>(a.v + base + c) = v;
-                *reinterpret_cast<float4*>(a.acc + base + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (!a.keep_acc) *reinterpret_cast<float4*>(a.acc + base + c) = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (a.copy) {
                     if (a.copy_dtype == SMLM_BF16) {
                         uint2 o;
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(256) lazy_adam_kernel(AdamArgs a) {
                 a.p[base + c] = p;
                 a.m[base + c] = m;
                 a.v[base + c] = v;
-                a.acc[base + c] = 0.f;
+                if (!a.keep_acc) a.acc[base + c] = 0.f;
                 if (a.copy) {
                     if (a.copy_dtype == SMLM_BF16) static_cast<uint16_t*>(a.copy)[base + c] = (uint16_t)f32_to_bf16_bits(p);
                     else static_cast<float*>(a.copy)[base + c] = p;
@@ -154,6 +155,7 @@ struct RowArgs {
     float scale;
     int d, kind;
     float b2, eps, lr;
+    int keep_acc;
 };
 
 // Formulas and rounding of the reference C loop (host_rows.c:84-117): q summed in double, row state in fp32.
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(256) rowwise_kernel(RowArgs a) {
             for (int t = 0; t < VEC; t++) {
                 const float gk = __fmul_rn(a.acc[base + c + t], scale);
                 a.p[base + c + t] = __fsub_rn(a.p[base + c + t], __fmul_rn(step, gk));
-                a.acc[base + c + t] = 0.f;
+                if (!a.keep_acc) a.acc[base + c + t] = 0.f;
             }
         }
         __syncwarp();
@@ -239,6 +241,30 @@ __global__ void __launch_bounds__(256) touched_sq_kernel(const float* acc, const
     if (lane == 0) partials[w] = s;
 }
 
+// Pass 1 from per-row squared norms (4 bytes per touched row instead of the row itself).
+__global__ void __launch_bounds__(256) touched_rowsq_kernel(const float* sqnorm, const int32_t* list,
+                                                            const int32_t* count, double* partials) {
+    const int lane = lane_id();
+    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (w >= PARTIALS) return;
+    const int n = *count;
+    double s = 0.0;
+    for (int i = w * 32 + lane; i < n; i += PARTIALS * 32) s += (double)sqnorm[list[i]];
+    s = warp_sum_d(s);
+    if (lane == 0) partials[w] = s;
+}
+
+// acc rows whose touched byte is 0 <- 0 (turns "untouched rows count as zero" into actual zeros).
+__global__ void __launch_bounds__(256) zero_untouched_kernel(float* acc, const uint8_t* touched, int64_t rows, int d) {
+    const int lane = lane_id();
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        if (touched[r]) continue;
+        float* row = acc + r * d;
+        for (int c = lane; c < d; c += 32) row[c] = 0.f;
+    }
+}
+
 __global__ void norm_finish_kernel(const double* partials, float* out) {
     const int lane = lane_id();
     double s = 0.0;
@@ -259,13 +285,14 @@ extern "C" size_t smlm_touched_workspace(int64_t rows) {
 extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_sq, float* acc, uint8_t* touched,
                                    const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
                                    float one_minus_b1, float b2, float one_minus_b2, float bc2_sqrt, float eps,
-                                   float neg_step_size, void* value_copy, int copy_dtype, void* workspace,
+                                   float neg_step_size, void* value_copy, int copy_dtype, int flags, void* workspace,
                                    size_t workspace_bytes, void* stream) {
     SMLM_CHECK_ARG(rows >= 0 && d >= 0, "lazy_adam_step: negative size");
     SMLM_CHECK_ARG(rows < (int64_t)0x7fffffff, "lazy_adam_step: rows must be below 2^31");
     SMLM_CHECK_ARG(d < (1 << 30), "lazy_adam_step: d too large");
     SMLM_CHECK_ARG(value_copy == nullptr || copy_dtype == SMLM_F32 || copy_dtype == SMLM_BF16,
                    "lazy_adam_step: value copy must be fp32 or bf16");
+    SMLM_CHECK_ARG((flags & ~SMLM_STEP_KEEP_ACC) == 0, "lazy_adam_step: unknown flags %d", flags);
     if (rows == 0) return SMLM_OK;
     SMLM_CHECK_ARG(param && exp_avg && exp_avg_sq && acc && touched, "lazy_adam_step: null pointer");
     cudaStream_t st = as_stream(stream);
@@ -273,7 +300,8 @@ extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_
     int rc = compact_touched(touched, rows, workspace, workspace_bytes, &b, st);
     if (rc != SMLM_OK) return rc;
     AdamArgs a{param, exp_avg, exp_avg_sq, acc, touched, b.list, b.count, grad_scale_dev, grad_scale, (int)d,
-               one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step_size, value_copy, copy_dtype};
+               one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step_size, value_copy, copy_dtype,
+               (flags & SMLM_STEP_KEEP_ACC) ? 1 : 0};
     const bool vec = d % 4 == 0 && reinterpret_cast<uintptr_t>(param) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(exp_avg) % 16 == 0 && reinterpret_cast<uintptr_t>(exp_avg_sq) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(acc) % 16 == 0 &&
@@ -287,19 +315,21 @@ extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_
 
 extern "C" int smlm_rowwise_step(float* param, float* acc, uint8_t* touched, float* v, int32_t* count,
                                  const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d, int kind,
-                                 float b2, float eps, float lr, void* workspace, size_t workspace_bytes,
+                                 float b2, float eps, float lr, int flags, void* workspace, size_t workspace_bytes,
                                  void* stream) {
     SMLM_CHECK_ARG(rows >= 0 && d > 0, "rowwise_step: rows must be >= 0 and the width > 0");
     SMLM_CHECK_ARG(rows < (int64_t)0x7fffffff && d < (1 << 30), "rowwise_step: size too large");
     SMLM_CHECK_ARG(kind == SMLM_ROWRMS || kind == SMLM_ROWADAGRAD, "rowwise_step: unknown kind %d", kind);
     SMLM_CHECK_ARG(kind != SMLM_ROWRMS || count != nullptr, "rowwise_step: rowrms needs the per-row count");
+    SMLM_CHECK_ARG((flags & ~SMLM_STEP_KEEP_ACC) == 0, "rowwise_step: unknown flags %d", flags);
     if (rows == 0) return SMLM_OK;
     SMLM_CHECK_ARG(param && acc && touched && v, "rowwise_step: null pointer");
     cudaStream_t st = as_stream(stream);
     TouchedBufs b;
     int rc = compact_touched(touched, rows, workspace, workspace_bytes, &b, st);
     if (rc != SMLM_OK) return rc;
-    RowArgs a{param, acc, v, count, touched, b.list, b.count, grad_scale_dev, grad_scale, (int)d, kind, b2, eps, lr};
+    RowArgs a{param,      acc,         v,     count, touched, b.list, b.count, grad_scale_dev, grad_scale, (int)d,
+              kind,       b2,          eps,   lr,    (flags & SMLM_STEP_KEEP_ACC) ? 1 : 0};
     const int blocks = persistent_blocks(8, 8);
     if (d % 4 == 0) rowwise_kernel<4><<<blocks, 256, 0, st>>>(a);
     else rowwise_kernel<1><<<blocks, 256, 0, st>>>(a);
@@ -307,8 +337,8 @@ extern "C" int smlm_rowwise_step(float* param, float* acc, uint8_t* touched, flo
     return SMLM_OK;
 }
 
-extern "C" int smlm_touched_norm(const float* acc, const uint8_t* touched, int64_t rows, int64_t d, float* norm_out,
-                                 void* workspace, size_t workspace_bytes, void* stream) {
+extern "C" int smlm_touched_norm(const float* acc, const float* row_sqnorm, const uint8_t* touched, int64_t rows,
+                                 int64_t d, float* norm_out, void* workspace, size_t workspace_bytes, void* stream) {
     SMLM_CHECK_ARG(rows >= 0 && d >= 0, "touched_norm: negative size");
     SMLM_CHECK_ARG(rows < (int64_t)0x7fffffff && d < (1 << 30), "touched_norm: size too large");
     SMLM_CHECK_ARG(norm_out != nullptr, "touched_norm: null output");
@@ -317,16 +347,28 @@ extern "C" int smlm_touched_norm(const float* acc, const uint8_t* touched, int64
         SMLM_CUDA(cudaMemsetAsync(norm_out, 0, sizeof(float), st));
         return SMLM_OK;
     }
-    SMLM_CHECK_ARG(acc && touched, "touched_norm: null pointer");
+    SMLM_CHECK_ARG((acc || row_sqnorm) && touched, "touched_norm: null pointer");
     TouchedBufs b;
     int rc = compact_touched(touched, rows, workspace, workspace_bytes, &b, st);
     if (rc != SMLM_OK) return rc;
-    if (d % 4 == 0 && reinterpret_cast<uintptr_t>(acc) % 16 == 0)
+    if (row_sqnorm)
+        touched_rowsq_kernel<<<PARTIALS / 8, 256, 0, st>>>(row_sqnorm, b.list, b.count, b.partials);
+    else if (d % 4 == 0 && reinterpret_cast<uintptr_t>(acc) % 16 == 0)
         touched_sq_kernel<4><<<PARTIALS / 8, 256, 0, st>>>(acc, b.list, b.count, (int)d, b.partials);
     else
         touched_sq_kernel<1><<<PARTIALS / 8, 256, 0, st>>>(acc, b.list, b.count, (int)d, b.partials);
     SMLM_LAUNCHED("touched_sq_kernel");
     norm_finish_kernel<<<1, 32, 0, st>>>(b.partials, norm_out);
     SMLM_LAUNCHED("norm_finish_kernel");
+    return SMLM_OK;
+}
+
+extern "C" int smlm_zero_untouched(float* acc, const uint8_t* touched, int64_t rows, int64_t d, void* stream) {
+    SMLM_CHECK_ARG(rows >= 0 && d >= 0 && d < (1 << 30), "zero_untouched: bad sizes");
+    if (rows == 0 || d == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(acc && touched, "zero_untouched: null pointer");
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16));
+    zero_untouched_kernel<<<blocks, 256, 0, as_stream(stream)>>>(acc, touched, rows, (int)d);
+    SMLM_LAUNCHED("zero_untouched_kernel");
     return SMLM_OK;
 }

@@ -364,6 +364,8 @@ struct SegArgs {
     float* carry_head;  // (chunks, d)
     float* carry_tail;  // (chunks, d)
     int* chunk_flags;   // (chunks,)
+    float* sqnorm;      // optional (rows,): squared L2 norm of every accumulator row this call writes
+    int first_writes;   // rows whose touched byte is 0 are written (not accumulated): they count as zero
     int64_t m, rows;
     int k, d, P;
     int64_t chunks;
@@ -401,6 +403,7 @@ __global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
         if (cur == NO_ROW || a.acc == nullptr) return;  // acc == NULL: per-sample-weight gradient only
         float* dst = nullptr;
         bool direct = false;
+        float sq = 0.f;
         if (mid) {
             dst = a.carry_head + c * a.d;
             cflags |= FLAG_MID;
@@ -413,22 +416,35 @@ __global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
             dst = a.acc + (int64_t)cur * a.d;
             direct = true;
         }
+        // a row seen for the first time since the optimizer step is written, not read (first_writes mode)
+        const bool accumulate = direct && !(a.first_writes && a.touched && a.touched[cur] == 0);
 #pragma unroll
         for (int s = 0; s < NS; s++) {
             const int col = (lane + 32 * s) * VEC;
             if (col < a.d) {
                 if constexpr (VEC == 4) {
                     float4* q = reinterpret_cast<float4*>(dst + col);
-                    float4 x = direct ? *q : make_float4(0.f, 0.f, 0.f, 0.f);
+                    float4 x = accumulate ? *q : make_float4(0.f, 0.f, 0.f, 0.f);
                     x.x = x.x + sum[s][0]; x.y = x.y + sum[s][1]; x.z = x.z + sum[s][2]; x.w = x.w + sum[s][3];
                     *q = x;
+                    sq = fmaf(x.x, x.x, sq); sq = fmaf(x.y, x.y, sq); sq = fmaf(x.z, x.z, sq); sq = fmaf(x.w, x.w, sq);
                 } else {
 #pragma unroll
-                    for (int i = 0; i < VEC; i++) dst[col + i] = (direct ? dst[col + i] : 0.f) + sum[s][i];
+                    for (int i = 0; i < VEC; i++) {
+                        const float x = (accumulate ? dst[col + i] : 0.f) + sum[s][i];
+                        dst[col + i] = x;
+                        sq = fmaf(x, x, sq);
+                    }
                 }
             }
         }
-        if (direct && lane == 0 && a.touched) a.touched[cur] = 1;
+        if (direct) {
+            if (a.sqnorm) {
+                sq = warp_sum(sq);
+                if (lane == 0) a.sqnorm[cur] = sq;
+            }
+            if (lane == 0 && a.touched) a.touched[cur] = 1;
+        }
     };
 
     for (int64_t b = start; b < end; b += 32) {
@@ -490,6 +506,8 @@ __global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a) {
     if (!(a.chunk_flags[c] & FLAG_TAIL)) return;
     const int64_t end = min((c + 1) * a.P, a.m);
     const uint32_t row = a.keys[end - 1];
+    const bool accumulate = !(a.first_writes && a.touched && a.touched[row] == 0);
+    float sq = 0.f;
     for (int col0 = lane * VEC; col0 < a.d; col0 += 32 * VEC) {
         float tot[VEC];
 #pragma unroll
@@ -506,7 +524,15 @@ __global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a) {
         }
         float* dst = a.acc + (int64_t)row * a.d + col0;
 #pragma unroll
-        for (int i = 0; i < VEC; i++) dst[i] = dst[i] + tot[i];
+        for (int i = 0; i < VEC; i++) {
+            const float x = (accumulate ? dst[i] : 0.f) + tot[i];
+            dst[i] = x;
+            sq = fmaf(x, x, sq);
+        }
+    }
+    if (a.sqnorm) {
+        sq = warp_sum(sq);
+        if (lane == 0) a.sqnorm[row] = sq;
     }
     if (lane == 0 && a.touched) a.touched[row] = 1;
 }
@@ -649,14 +675,18 @@ extern "C" size_t smlm_bag_backward_workspace(int64_t n, int64_t k, int64_t rows
 
 extern "C" int smlm_bag_backward_rows(const float* grad_out, const int64_t* indices, const void* weights,
                                       int weights_dtype, const void* table, int table_dtype, float* acc,
-                                      uint8_t* touched, float* gw, int64_t n, int64_t k, int64_t rows, int64_t d,
-                                      void* workspace, size_t workspace_bytes, int* status, void* stream) {
+                                      uint8_t* touched, float* row_sqnorm, int flags, float* gw, int64_t n,
+                                      int64_t k, int64_t rows, int64_t d, void* workspace, size_t workspace_bytes,
+                                      int* status, void* stream) {
     SMLM_CHECK_ARG(n >= 0 && k >= 0 && rows >= 0 && d >= 0, "bag_backward_rows: negative size");
     SMLM_CHECK_ARG(table_dtype == SMLM_F32 || table_dtype == SMLM_BF16, "bag_backward_rows: table must be fp32 or bf16");
     SMLM_CHECK_ARG(weights_dtype == SMLM_F32 || weights_dtype == SMLM_BF16, "bag_backward_rows: weights must be fp32 or bf16");
     SMLM_CHECK_ARG(n * k < (int64_t)0x7fffffff, "bag_backward_rows: n * k must be below 2^31");
     SMLM_CHECK_ARG(rows < (int64_t)0xffffffff, "bag_backward_rows: rows must be below 2^32 - 1");
     SMLM_CHECK_ARG(d < (1 << 30), "bag_backward_rows: d too large");
+    SMLM_CHECK_ARG((flags & ~SMLM_BWD_FIRST_TOUCH_WRITES) == 0, "bag_backward_rows: unknown flags %d", flags);
+    SMLM_CHECK_ARG(!(flags & SMLM_BWD_FIRST_TOUCH_WRITES) || touched != nullptr,
+                   "bag_backward_rows: first-touch writes need the touched mask");
     if (n == 0 || k == 0) return SMLM_OK;
     SMLM_CHECK_ARG(grad_out && indices && weights && table && gw, "bag_backward_rows: null pointer");
     if (d == 0) {
@@ -673,7 +703,7 @@ extern "C" int smlm_bag_backward_rows(const float* grad_out, const int64_t* indi
     uint32_t *keys_in = bb.keys_in, *keys_out = bb.keys_out, *pos_in = bb.pos_in, *pos_out = bb.pos_out;
     void* sort_tmp = bb.sort_tmp;
     float *carry_head = bb.carry_head, *carry_tail = bb.carry_tail;
-    int* flags = bb.flags;
+    int* chunk_flags = bb.flags;
     cudaStream_t st = as_stream(stream);
     const int kb = (int)std::max<int64_t>(1, std::min<int64_t>((p.m + 255) / 256, (int64_t)sm_count() * 8));
     bb_keys_kernel<<<kb, 256, 0, st>>>(indices, p.m, rows, keys_in, pos_in, status);
@@ -683,7 +713,8 @@ extern "C" int smlm_bag_backward_rows(const float* grad_out, const int64_t* indi
                                               std::max(p.end_bit, 1), st));
     if (d == 0) return SMLM_OK;
     SegArgs a{keys_out, pos_out, grad_out, weights, weights_dtype, table, acc, touched, gw, carry_head,
-              carry_tail, flags, p.m, rows, (int)k, (int)d, p.P, p.chunks};
+              carry_tail, chunk_flags, row_sqnorm, (flags & SMLM_BWD_FIRST_TOUCH_WRITES) ? 1 : 0, p.m, rows, (int)k,
+              (int)d, p.P, p.chunks};
     const uintptr_t tp = reinterpret_cast<uintptr_t>(table);
     const uintptr_t gp = reinterpret_cast<uintptr_t>(grad_out);
     const uintptr_t ap = reinterpret_cast<uintptr_t>(acc);

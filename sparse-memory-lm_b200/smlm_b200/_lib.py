@@ -19,6 +19,8 @@ F32, BF16, F16, Q4 = 0, 1, 2, 3
 FLAG_INDEX_RANGE = 1
 FLAG_TIMEOUT = 4
 ROWRMS, ROWADAGRAD = 0, 1
+BWD_FIRST_TOUCH_WRITES = 1
+STEP_KEEP_ACC = 1
 SCORE_F32_EXACT, SCORE_BF16 = 0, 1
 
 # Kernel launches behind one call, for the benchmark's launch count (checked against the ncu launch list):
@@ -37,13 +39,15 @@ SIGNATURES = {
     "smlm_bag_infer": (_i32, [_p, _p, _i32, _p, _i32, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _i32, _p, _p]),
     "smlm_quantize_q4": (_i32, [_p, _i64, _i64, _p, _p, _p]),
     "smlm_bag_backward_workspace": (_sz, [_i64, _i64, _i64, _i64]),
-    "smlm_bag_backward_rows": (_i32, [_p, _p, _p, _i32, _p, _i32, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _sz,
-                                      _p, _p]),
+    "smlm_bag_backward_rows": (_i32, [_p, _p, _p, _i32, _p, _i32, _p, _p, _p, _i32, _p, _i64, _i64, _i64, _i64,
+                                      _p, _sz, _p, _p]),
     "smlm_touched_workspace": (_sz, [_i64]),
     "smlm_lazy_adam_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32,
-                                   _p, _i32, _p, _sz, _p]),
-    "smlm_rowwise_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _i32, _f32, _f32, _f32, _p, _sz, _p]),
-    "smlm_touched_norm": (_i32, [_p, _p, _i64, _i64, _p, _p, _sz, _p]),
+                                   _p, _i32, _i32, _p, _sz, _p]),
+    "smlm_rowwise_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _i32, _f32, _f32, _f32, _i32, _p, _sz,
+                                 _p]),
+    "smlm_touched_norm": (_i32, [_p, _p, _p, _i64, _i64, _p, _p, _sz, _p]),
+    "smlm_zero_untouched": (_i32, [_p, _p, _i64, _i64, _p]),
     "smlm_pk_select": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
     "smlm_select_backward": (_i32, [_p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "smlm_subkey_scores_f32": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),

@@ -207,11 +207,13 @@ def bag_forward(indices, weights, table, out_dtype=torch.float32):
     return out
 
 
-def bag_backward_rows(grad_out, indices, weights, table, acc, touched):
+def bag_backward_rows(grad_out, indices, weights, table, acc, touched, row_sqnorm=None, first_touch_writes=False):
     """grad_out (N, D), indices / weights (N, K) -> per-sample-weight gradient (N, K) fp32;
     acc[indices[n, k]] += weights[n, k] * grad_out[n] and touched[indices] = True, in place
     (reference: kernels.py:73-88). Deterministic: sorted rows, no float atomics.
-    acc / touched may be None (frozen table: only the weight gradient)."""
+    acc / touched may be None (frozen table: only the weight gradient). row_sqnorm: optional fp32 (rows,) that
+    receives the squared norm of every accumulator row written. first_touch_writes: rows not yet touched are
+    written instead of accumulated (for accumulators whose untouched rows count as zero)."""
     dev = L.require_cuda(grad_out, indices, weights, table, acc, touched)
     N, K = indices.shape
     D = table.shape[1]
@@ -227,7 +229,8 @@ def bag_backward_rows(grad_out, indices, weights, table, acc, touched):
     ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, K, table.shape[0], D), dev)
     with L.timed("bag_backward_rows", L.BACKWARD_LAUNCHES):
         rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.ptr(idx), L.ptr(w), L.dtype_code(w.dtype), L.ptr(table),
-                                            L.dtype_code(table.dtype), L.ptr(acc), L.ptr(touched), L.ptr(gw), N, K,
+                                            L.dtype_code(table.dtype), L.ptr(acc), L.ptr(touched), L.ptr(row_sqnorm),
+                                            L.BWD_FIRST_TOUCH_WRITES if first_touch_writes else 0, L.ptr(gw), N, K,
                                             table.shape[0], D, L.ptr(ws), ws.numel(), L.status_ptr(dev),
                                             L.stream(dev))
     L.check(rc, "bag_backward_rows")
@@ -299,11 +302,12 @@ def _scale_args(grad_scale, device):
 
 
 def lazy_adam_step(param, exp_avg, exp_avg_sq, acc, touched, grad_scale, step, lr, beta1, beta2, eps,
-                   value_copy=None):
+                   value_copy=None, keep_acc=False):
     """In-place lazy Adam step over the touched rows (reference: kernels.py:417-433): torch's Adam formula, global
     step for the bias correction, no weight decay; the touched accumulator rows are zeroed and the mask cleared.
     grad_scale: 0-d tensor (clip factor) or float; step: the step number after this update (1 for the first).
-    value_copy: optional (rows, D) bf16 / fp32 tensor that receives the updated rows too."""
+    value_copy: optional (rows, D) bf16 / fp32 tensor that receives the updated rows too. keep_acc: leave the
+    consumed accumulator rows as they are (for accumulators whose untouched rows count as zero)."""
     dev = L.require_cuda(param, exp_avg, exp_avg_sq, acc, touched, value_copy)
     for t in (param, exp_avg, exp_avg_sq, acc):
         if t.dtype != torch.float32 or not t.is_contiguous() or t.shape != param.shape:
@@ -318,12 +322,12 @@ def lazy_adam_step(param, exp_avg, exp_avg_sq, acc, touched, grad_scale, step, l
                                          L.ptr(touched), sp, sf, rows, D, 1 - beta1, beta2, 1 - beta2,
                                          math.sqrt(bc2), eps, -(lr / bc1), L.ptr(value_copy),
                                          L.dtype_code(value_copy.dtype) if value_copy is not None else L.F32,
-                                         L.ptr(ws), ws.numel(), L.stream(dev))
+                                         L.STEP_KEEP_ACC if keep_acc else 0, L.ptr(ws), ws.numel(), L.stream(dev))
     L.check(rc, "lazy_adam_step")
     del keep
 
 
-def rowwise_step(param, acc, touched, v, n, grad_scale, lr, beta2, eps, kind):
+def rowwise_step(param, acc, touched, v, n, grad_scale, lr, beta2, eps, kind, keep_acc=False):
     """Row-wise rowrms / rowadagrad step over the touched rows, in place; accumulator rows zeroed, mask cleared
     (reference: row_optim.py:168-201, formulas of host_rows.c:84-117)."""
     dev = L.require_cuda(param, acc, touched, v, n)
@@ -333,21 +337,34 @@ def rowwise_step(param, acc, touched, v, n, grad_scale, lr, beta2, eps, kind):
     ws = L.workspace(L.lib().smlm_touched_workspace(rows), dev)
     with L.timed("rowwise_step", L.COMPACT_LAUNCHES + 1):
         rc = L.lib().smlm_rowwise_step(L.ptr(param), L.ptr(acc), L.ptr(touched), L.ptr(v), L.ptr(n), sp, sf, rows,
-                                       D, code, beta2, eps, lr, L.ptr(ws), ws.numel(), L.stream(dev))
+                                       D, code, beta2, eps, lr, L.STEP_KEEP_ACC if keep_acc else 0, L.ptr(ws),
+                                       ws.numel(), L.stream(dev))
     L.check(rc, "rowwise_step")
     del keep
 
 
-def touched_norm(acc, touched):
+def touched_norm(acc, touched, row_sqnorm=None):
     """L2 norm (0-d fp32 tensor on the device) of the accumulator rows marked in `touched`; equals acc.norm()
-    for a RowStore, whose untouched rows are zero (reference: sparse_values.py:143)."""
-    dev = L.require_cuda(acc, touched)
+    for an accumulator whose untouched rows count as zero (reference: sparse_values.py:143). With row_sqnorm (as
+    written by bag_backward_rows) only 4 bytes per touched row are read."""
+    dev = L.require_cuda(acc, touched, row_sqnorm)
     rows = acc.shape[0]
     D = acc.shape[1] if acc.dim() > 1 else 1
     out = torch.empty((), dtype=torch.float32, device=dev)
     ws = L.workspace(L.lib().smlm_touched_workspace(rows), dev)
     with L.timed("touched_norm", L.COMPACT_LAUNCHES + 2):
-        rc = L.lib().smlm_touched_norm(L.ptr(_contig(acc)), L.ptr(touched), rows, D, L.ptr(out), L.ptr(ws),
-                                       ws.numel(), L.stream(dev))
+        rc = L.lib().smlm_touched_norm(L.ptr(_contig(acc)), L.ptr(row_sqnorm), L.ptr(touched), rows, D, L.ptr(out),
+                                       L.ptr(ws), ws.numel(), L.stream(dev))
     L.check(rc, "touched_norm")
     return out
+
+
+def zero_untouched(acc, touched):
+    """acc rows whose touched flag is clear <- 0, in place (makes an accumulator whose untouched rows count as
+    zero an ordinary dense tensor again)."""
+    dev = L.require_cuda(acc, touched)
+    rows = acc.shape[0]
+    D = acc.shape[1] if acc.dim() > 1 else 1
+    with L.timed("zero_untouched", 1):
+        rc = L.lib().smlm_zero_untouched(L.ptr(acc), L.ptr(touched), rows, D, L.stream(dev))
+    L.check(rc, "zero_untouched")

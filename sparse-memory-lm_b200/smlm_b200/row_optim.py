@@ -51,8 +51,8 @@ class RowWiseOptimizer(torch.optim.Optimizer):
                 st = row_store(p)
                 state = self._state(p)
                 state["step"] += 1
-                K.rowwise_step(p, st.acc, st.touched, state["v"], state.get("n"), st.grad_scale, group["lr"],
-                               group["beta2"], group["eps"], self.kind)
+                K.rowwise_step(p, st._acc, st._touched, state["v"], state.get("n"), st.grad_scale, group["lr"],
+                               group["beta2"], group["eps"], self.kind, keep_acc=st.clean)
                 st.grad_scale = 1.0
 
     def zero_grad(self, set_to_none=True):

@@ -39,9 +39,13 @@ def test_host_side_argument_checks_return_invalid():
     assert rc == L.ERR_INVALID
     rc = lib.smlm_bag_forward(s, s, L.F32, s, 7, 4, 8, 16, 32, s, L.F32, None, None)
     assert rc == L.ERR_INVALID and b"table" in lib.smlm_last_error()
-    rc = lib.smlm_rowwise_step(s, s, s, s, None, None, 1.0, 10, 8, L.ROWRMS, 0.95, 1e-8, 0.01, s, 0, None)
+    rc = lib.smlm_rowwise_step(s, s, s, s, None, None, 1.0, 10, 8, L.ROWRMS, 0.95, 1e-8, 0.01, 0, s, 0, None)
     assert rc == L.ERR_INVALID and b"count" in lib.smlm_last_error()
     rc = lib.smlm_quantize_q4(s, 10, 7, s, s, None)
+    assert rc == L.ERR_INVALID
+    rc = lib.smlm_lazy_adam_step(s, s, s, s, s, None, 1.0, 10, 8, 0.1, 0.9, 0.1, 1.0, 1e-8, -1e-3, None, 0, 8, s, 0,
+                                 None)
+    assert rc == L.ERR_INVALID and b"flags" in lib.smlm_last_error()
     assert rc == L.ERR_INVALID
     with pytest.raises(ValueError, match="knn"):
         L.check(lib.smlm_pk_select(s, s, L.BF16, 4, 2, 64, 0, s, s, s, None), "pk_select")

@@ -1,0 +1,103 @@
+"""The RowStore's clean mode (untouched rows count as zero, first touches are written, the step leaves consumed
+rows alone, clip norms from per-row squared norms) gives exactly what the exact, reference-semantics mode gives."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from smlm_b200 import kernels as K
+from smlm_b200.pkm import ProductKeyMemory
+from smlm_b200.sparse_values import LazyRowAdam, clip_row_sparse, row_store
+from util import close, skewed_indices
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def test_first_touch_writes_and_row_norms():
+    """Untouched rows hold garbage: with first-touch writes the result on the touched rows equals accumulating
+    into zeros, the per-row squared norms are the rows' norms, and a second call accumulates."""
+    gen = torch.Generator().manual_seed(1)
+    rows, D, N = 4096, 384, 512
+    table = torch.randn(rows, D, generator=gen) * D ** -0.5
+    idx = skewed_indices(rows, N, 128, gen)
+    w = torch.softmax(torch.randn(N, 128, generator=gen), -1)
+    g = torch.randn(N, D, generator=gen)
+    garbage = torch.randn(rows, D, generator=gen).to(DEV)
+    touched = torch.zeros(rows, dtype=torch.bool, device=DEV)
+    sq = torch.zeros(rows, device=DEV)
+    acc = garbage.clone()
+    args = (g.to(DEV), idx.to(DEV), w.to(DEV), table.to(DEV))
+    K.bag_backward_rows(*args, acc, touched, row_sqnorm=sq, first_touch_writes=True)
+    ref = torch.zeros(rows, D, device=DEV)
+    ref_t = torch.zeros(rows, dtype=torch.bool, device=DEV)
+    K.bag_backward_rows(*args, ref, ref_t)
+    assert torch.equal(touched, ref_t)
+    assert torch.equal(acc[touched], ref[touched])
+    assert torch.equal(acc[~touched], garbage[~touched])           # untouched rows not written
+    torch.testing.assert_close(sq[touched], ref[touched].square().sum(-1), rtol=1e-5, atol=1e-6)
+    # second micro-batch: touched rows accumulate, newly touched ones are written
+    idx2 = skewed_indices(rows, N, 128, gen)
+    args2 = (g.to(DEV), idx2.to(DEV), w.to(DEV), table.to(DEV))
+    K.bag_backward_rows(*args2, acc, touched, row_sqnorm=sq, first_touch_writes=True)
+    K.bag_backward_rows(*args2, ref, ref_t)
+    assert torch.equal(acc[touched], ref[touched])
+    torch.testing.assert_close(sq[touched], ref[touched].square().sum(-1), rtol=1e-5, atol=1e-6)
+    n1 = K.touched_norm(acc, touched, row_sqnorm=sq)
+    n2 = float(ref.double().norm())
+    assert abs(float(n1) - n2) <= 1e-6 * n2
+
+
+def test_keep_acc_step_equals_zeroing_step():
+    gen = torch.Generator().manual_seed(2)
+    rows, D = 2000, 64
+    p = torch.randn(rows, D, generator=gen)
+    acc = torch.randn(rows, D, generator=gen)
+    touched = torch.rand(rows, generator=gen) < 0.4
+    outs = []
+    for keep in (False, True):
+        pp, m, v, a, t = p.clone().to(DEV), torch.zeros(rows, D, device=DEV), torch.zeros(rows, D, device=DEV), \
+            acc.clone().to(DEV), touched.clone().to(DEV)
+        K.lazy_adam_step(pp, m, v, a, t, 1.0, 1, 1e-3, 0.9, 0.98, 1e-8, keep_acc=keep)
+        outs.append((pp, m, v, a, t))
+    for x, y in zip(outs[0][:3], outs[1][:3]):
+        assert torch.equal(x, y)
+    assert torch.equal(outs[1][3], acc.to(DEV))                 # kept
+    assert torch.count_nonzero(outs[0][3][touched.to(DEV)]) == 0
+    assert not outs[0][4].any() and not outs[1][4].any()
+
+
+def test_clean_store_equals_exact_store_over_steps():
+    """Two identical layers, two micro-batches per step, three steps: one store is never read from outside (clean
+    mode), the other is read after every backward (exact mode). Tables, moments and clip norms agree."""
+    mems = []
+    for _ in range(2):
+        torch.manual_seed(0)
+        mems.append(ProductKeyMemory(64, 64, n_keys=64, heads=4, knn=16, k_dim=32, query_norm="none",
+                                     swilu=False, value_grad="row_sparse").to(DEV))
+    mems[1].load_state_dict(mems[0].state_dict())
+    opts = [LazyRowAdam([m.values.weight], lr=1e-2, betas=(0.9, 0.98)) for m in mems]
+    gen = torch.Generator().manual_seed(3)
+    for step in range(3):
+        norms = []
+        for mb in range(2):
+            x = torch.randn(300, 64, generator=gen).to(DEV)
+            g = torch.randn(300, 64, generator=gen).to(DEV)
+            for i, m in enumerate(mems):
+                m(x).backward(g)
+                if i == 1:
+                    row_store(m.values.weight).acc       # read from outside: exact mode
+        assert row_store(mems[0].values.weight).clean and not row_store(mems[1].values.weight).clean
+        for m in mems:
+            norms.append(float(clip_row_sparse([m.values.weight], 0.05)))
+        assert abs(norms[0] - norms[1]) <= 1e-5 * norms[1]
+        for m in mems:
+            row_store(m.values.weight).grad_scale = 0.5        # identical clip factor in both
+        for o in opts:
+            o.step()
+        assert torch.equal(mems[0].values.weight, mems[1].values.weight)
+        for k in ("exp_avg", "exp_avg_sq"):
+            assert torch.equal(opts[0].state[mems[0].values.weight][k], opts[1].state[mems[1].values.weight][k])
+    # exposing the clean store yields the exact accumulator (all zero after the last step)
+    st = row_store(mems[0].values.weight)
+    assert torch.count_nonzero(st.acc) == 0 and not st.touched.any()

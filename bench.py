@@ -17,7 +17,10 @@ step) against the measured HBM copy bandwidth. `cpu_baseline` times the referenc
 restatement under oracle/, the only oracle use in this file) on a bounded sample.
 
 --impl reference times the reference's PyTorch path on the host cores instead (rank 0 only under torchrun).
-With --gpus N > 1 each rank runs its own full layer (replicas, weak scaling) until the row-sharded layer lands.
+With --gpus N > 1 (torchrun, one process per GPU, NCCL) the 16.8M-row table and its optimizer state are
+row-sharded over the N GPUs and each GPU runs 32,768 tokens per step (weak scaling): the lookups, partial bags,
+output gradients and weight gradients cross NVLink through NCCL collectives, the replicated parameters'
+gradients are all-reduced.
 """
 import argparse
 import json
@@ -37,9 +40,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "PKM layer tokens/s (fwd+bwd+opt) at 16.8M rows"
 # DRAM bytes (read + write) of one lazy Adam launch per touched row, from the ncu capture in
-# profiles/lazy_adam_kernel_pkm-layer-1m.md; traffic scales with the touched rows. None until measured for the
-# current kernel (the step no longer rewrites the accumulator rows it consumes).
-ADAM_TRAFFIC_PER_ROW = None
+# profiles/lazy_adam_kernel_pkm-layer-1m.md (6.651 GB for 621,697 touched rows); traffic scales with the
+# touched rows.
+ADAM_TRAFFIC_PER_ROW = 10698
 D_MODEL, HEADS, KNN, K_DIM = 384, 4, 32, 256
 
 
@@ -130,17 +133,21 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------------ layer
-def build_layer(n_keys, device):
+def build_layer(n_keys, device, world=1):
     from smlm_b200.pkm import ProductKeyMemory
     from smlm_b200.sparse_values import LazyRowAdam, OptimizerSet
     torch.manual_seed(0)
+    group = torch.distributed.group.WORLD if world > 1 else None
     with torch.device(device):
         mem = ProductKeyMemory(D_MODEL, D_MODEL, n_keys=n_keys, heads=HEADS, knn=KNN, k_dim=K_DIM,
-                               query_norm="none", swilu=False, value_grad="row_sparse")
+                               query_norm="none", swilu=False, value_grad="row_sparse", shard_group=group)
         # config-1 initialisation: query N(0, 0.02), bias 0, sub-keys N(0, 1/128), values N(0, 384^-0.5)
         with torch.no_grad():
             mem.query_proj.weight.normal_(0, 0.02)
             mem.keys.normal_(0, (K_DIM // 2) ** -0.5)
+    if world > 1:
+        from smlm_b200.sharded import broadcast_replicated
+        broadcast_replicated(mem, group)
     table = mem.values.weight
     dense = [p for p in mem.parameters() if p is not table]
     opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True),
@@ -153,6 +160,9 @@ def train_step(mem, opt, x, g):
     with torch.autocast("cuda", dtype=torch.bfloat16):
         out = mem(x)
     out.backward(g)
+    if mem.shard is not None:
+        from smlm_b200.sharded import allreduce_replicated_grads
+        allreduce_replicated_grads(mem, mem.shard_group)
     vnorm = clip_row_sparse([mem.values.weight], 1.0)
     torch.nn.utils.clip_grad_norm_([p for p in mem.parameters() if p.grad is not None], 1.0, foreach=True)
     opt.step()
@@ -177,8 +187,8 @@ def run_cuda(args, world, rank, local):
     from smlm_b200 import _lib as L
     dev = torch.device("cuda", local)
     N, n_keys = args.tokens, args.rows_per_half
-    rows = n_keys ** 2
-    mem, opt = build_layer(n_keys, dev)
+    mem, opt = build_layer(n_keys, dev, world)
+    rows = mem.values.weight.shape[0]           # this GPU's rows (all of them on one GPU)
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     n_batches = 4
     xs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(n_batches)]
@@ -195,6 +205,9 @@ def run_cuda(args, world, rank, local):
         with torch.autocast("cuda", dtype=torch.bfloat16):
             out = mem(xs[i])
         out.backward(gs[i])
+        if mem.shard is not None:
+            from smlm_b200.sharded import allreduce_replicated_grads
+            allreduce_replicated_grads(mem, mem.shard_group)
         uniq.append(st.touched_rows())
         opt.step()
         opt.zero_grad(set_to_none=True)
@@ -250,6 +263,9 @@ def run_cuda(args, world, rank, local):
         # table row once per run + accumulator row written (first touch of the step: not read) + sort + gw
         "bag_backward_rows": U * D_MODEL * 4 * 2 + M * (8 * 4 + 4 + 4) + N * D_MODEL * 4,
         "lazy_adam_step": adam_bytes,
+        # row-sharded owner side: every rank's lookups scanned (8 B), this shard's ~M rows gathered, partials out
+        "shard_bag_forward": world * M * 8 + M * D_MODEL * 4 + world * N * D_MODEL * 4,
+        "shard_bag_backward_rows": U * D_MODEL * 4 * 2 + world * M * (8 * 4 + 8) + world * N * D_MODEL * 4,
     }
     breakdown = {}
     for name, t in sorted(per_kernel.items()):
@@ -262,15 +278,15 @@ def run_cuda(args, world, rank, local):
     line = {"metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "pkm-layer-b16m" if n_keys == 4096 else f"pkm-layer-{rows}rows",
-                       "rows": rows, "rows_per_half": n_keys, "v_dim": D_MODEL, "heads": HEADS, "knn": KNN,
+            "config": {"workload": "pkm-layer-b16m" if n_keys == 4096 else f"pkm-layer-{n_keys ** 2}rows",
+                       "rows": n_keys ** 2, "rows_per_gpu": rows, "rows_per_half": n_keys, "v_dim": D_MODEL, "heads": HEADS, "knn": KNN,
                        "k_dim": K_DIM, "tokens_per_gpu": N, "global_tokens": N * world,
                        "scoring": "bf16 autocast (bf16 operands, fp32 accumulate)", "values": "fp32 table",
                        "optimizer": "LazyRowAdam fp32 moments + fused AdamW (dense)",
-                       "parallelism": "replicas" if world > 1 else "single",
+                       "parallelism": f"dp{world} tokens + {world}-way row-sharded table" if world > 1 else "single",
                        "l2": "working set > L2: each step gathers ~6.4 GB of table rows and updates ~U rows of "
                              "table + moments (77 GB resident), inputs cycle over 4 batches",
-                       "unique_rows_per_step": round(U)},
+                       "unique_rows_per_step_per_gpu": round(U)},
             "e2e": {"value": round(e2e_tok_s, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 2 * N * D_MODEL * 4, "d2h_bytes_per_step": 4},
             "gpu_launches": launches, "roofline": roof, "kernels": breakdown, "clocks": clocks.summary()}

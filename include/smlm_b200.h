@@ -45,6 +45,11 @@ extern "C" {
 #define SMLM_BF16 1
 #define SMLM_F16 2
 #define SMLM_Q4 3 /* packed 4-bit rows (d/2 bytes) + one fp16 scale per row, see smlm_quantize_q4 */
+/* index types (row-sharded entry points) */
+#define SMLM_I32 4
+#define SMLM_I64 5
+/* compact optimizer state: int8 first-moment codes, uint8 second-moment codes, one fp32 scale per row each */
+#define SMLM_I8 6
 
 /* device status word bits */
 #define SMLM_FLAG_INDEX_RANGE 1
@@ -104,15 +109,16 @@ SMLM_API size_t smlm_bag_backward_workspace(int64_t n, int64_t k, int64_t rows, 
  * runs that cross a work chunk are completed by a second pass in chunk order. No float atomics:
  * results are bit-identical from run to run.
  * Replaces kernels.py:73 bag_backward_rows (and sparse_values.py:97-103, the aten per-sample-weight
- * backward + index_put_ accumulation). grad_out: F32 (n, d); weights F32/BF16; table F32/BF16; acc F32.
- * acc == NULL (and touched == NULL): only gw is computed (frozen table, sparse_values.py:118-120).
- * row_sqnorm (optional, fp32 (rows,)): the squared L2 norm of every accumulator row written by this call.
- * flags: SMLM_BWD_FIRST_TOUCH_WRITES. */
-SMLM_API int smlm_bag_backward_rows(const float *grad_out, const int64_t *indices, const void *weights,
-                                    int weights_dtype, const void *table, int table_dtype, float *acc,
-                                    uint8_t *touched, float *row_sqnorm, int flags, float *gw, int64_t n, int64_t k,
-                                    int64_t rows, int64_t d, void *workspace, size_t workspace_bytes, int *status,
-                                    void *stream);
+ * backward + index_put_ accumulation). grad_out: F32/BF16 (n, d) (grad_dtype); weights F32/BF16; table
+ * F32/BF16; acc F32. acc == NULL (and touched == NULL): only gw is computed (frozen table,
+ * sparse_values.py:118-120). gw == NULL: only acc / touched are updated (table may then be NULL).
+ * touched may be NULL (no mark kept). row_sqnorm (optional, fp32 (rows,)): the squared L2 norm of every
+ * accumulator row written by this call. flags: SMLM_BWD_FIRST_TOUCH_WRITES. */
+SMLM_API int smlm_bag_backward_rows(const void *grad_out, int grad_dtype, const int64_t *indices,
+                                    const void *weights, int weights_dtype, const void *table, int table_dtype,
+                                    float *acc, uint8_t *touched, float *row_sqnorm, int flags, float *gw,
+                                    int64_t n, int64_t k, int64_t rows, int64_t d, void *workspace,
+                                    size_t workspace_bytes, int *status, void *stream);
 
 /* ------------------------------------------------------------------------------- row-sparse optimizers */
 
@@ -131,6 +137,24 @@ SMLM_API int smlm_lazy_adam_step(float *param, float *exp_avg, float *exp_avg_sq
                                  float one_minus_b1, float b2, float one_minus_b2, float bc2_sqrt, float eps,
                                  float neg_step_size, void *value_copy, int copy_dtype, int flags, void *workspace,
                                  size_t workspace_bytes, void *stream);
+
+/* Lazy Adam with compact moments (state_dtype SMLM_BF16: bf16 exp_avg / exp_avg_sq; SMLM_I8: int8 exp_avg codes
+ * c with m = sign(c) (c / 127)^2 exp_avg_scale[row], uint8 exp_avg_sq codes u with v = ((u / 255)
+ * exp_avg_sq_scale[row])^4, the scales fp32 (rows,)). Per touched row, in fp32 with every operation rounded:
+ *   g = acc * grad_scale; m = beta1 m + (1 - beta1) g; v = beta2 v + ((1 - beta2) g) g;
+ *   p = p - (step_size m) / (sqrt(v) / bc2_sqrt + eps)      (step_size = lr / (1 - beta1^step),
+ *                                                               bc2_sqrt = sqrt(1 - beta2^step))
+ * then the moments are stored rounded to nearest even (int8: scales = the row maxima of |m| and v^(1/4), codes
+ * round(127 sign(m) sqrt(|m| / m_scale)) and round(255 v^(1/4) / v_scale), a positive v never gets code 0).
+ * Touched flags cleared, acc rows zeroed unless SMLM_STEP_KEEP_ACC; value_copy as smlm_lazy_adam_step; unread
+ * rows and their state unchanged. Workspace: smlm_touched_workspace(rows).
+ * Replaces kernels.py:498-515 lazy_adam_step_lowmem (kernel kernels.py:445-495). */
+SMLM_API int smlm_lazy_adam_lowmem_step(float *param, void *exp_avg, void *exp_avg_sq, float *exp_avg_scale,
+                                        float *exp_avg_sq_scale, int state_dtype, float *acc, uint8_t *touched,
+                                        const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
+                                        float beta1, float beta2, float one_minus_b1, float one_minus_b2, float eps,
+                                        float step_size, float bc2_sqrt, void *value_copy, int copy_dtype, int flags,
+                                        void *workspace, size_t workspace_bytes, void *stream);
 
 /* Row-wise optimizer on the touched rows (smlm/row_optim.py; formulas of host_rows.c:84-117):
  *   q = mean over the row of g^2 (summed in double), g = acc[r] * scale
@@ -174,6 +198,20 @@ SMLM_API int smlm_select_backward(const int64_t *indices, const float *weights, 
                          const void *grad_scores, int score_dtype, int64_t n, int64_t h, int64_t nk, int64_t knn,
                          void *ds1, void *ds2, void *stream);
 
+/* Backward of the selection, sparse form, for the scoring contraction's backward without dense (n, h, nk)
+ * gradients. Per (token n, head hh, half c) it emits knn lookups (entry e = ((n h + hh) 2 + c) knn + j, the
+ * pair j of the selection) into the keys viewed as (h 2 nk, half): on the first occurrence of a sub-key in the
+ * selection, entry_rows[e] = (hh 2 + c) nk + sub-key and entry_weights[e] (score type) = ds1 / ds2 of
+ * smlm_select_backward at that sub-key; on its later occurrences entry_rows[e] = -1 and entry_weights[e] = 0.
+ * Then, with row_base 0 and shard_rows h 2 nk (the -1 rows are skipped):
+ *   dq (viewed (n h 2, half)) = the value bag of the entries over the keys              (smlm_shard_bag_forward)
+ *   dkeys = its row-sparse backward with the query halves as grad_out, gw NULL   (smlm_shard_bag_backward_rows)
+ * which are the two contractions of the reference's scoring backward restricted to the nonzero gradients.
+ * Replaces kernels.py:253-266 PKSelect.backward together with the autograd backward of pkm.py:117-123. */
+SMLM_API int smlm_select_grad_entries(const int64_t *indices, const float *weights, const float *grad_w,
+                                      const void *grad_scores, int score_dtype, int64_t n, int64_t h, int64_t nk,
+                                      int64_t knn, int64_t *entry_rows, void *entry_weights, void *stream);
+
 /* Exact fp32 sub-key scores: s1[n, h, j] = sum_t q[n, h, t] k[h, 0, j, t] and s2 with the second halves,
  * each a sequential fmaf chain over t = 0 .. half-1 (the order a C loop reproduces bit for bit).
  * q: (n, h, 2 half), keys: (h, 2, nk, half). Replaces pkm.py:117-123 subkey_scores in fp32. */
@@ -208,6 +246,34 @@ SMLM_API int smlm_score_select(const void *q, const void *keys, int64_t n, int64
 SMLM_API int smlm_score_select_noalloc(const void *q, const void *keys, int64_t n, int64_t h, int64_t nk,
                                        int64_t half, int64_t knn, void *scores, int64_t *indices, float *weights,
                                        int *status, void *stream);
+
+/* ------------------------------------------------------------------------------ row-sharded value table
+ * Multi-GPU form of the value bag (no counterpart in the reference, which runs on one device): the table, its
+ * accumulator and its optimizer state are split into contiguous row ranges, one per GPU; rank r holds rows
+ * [row_base, row_base + shard_rows). Every rank receives all ranks' lookups (global row indices) and serves
+ * the ones that fall into its range; lookups of other ranges are skipped without an error. The exchange around
+ * these calls (the lookups' all-gather, the partial bags' and weight gradients' all-to-all) runs on NCCL. */
+
+/* out[n] = sum over the lookups j of token n whose row is in this shard, in j order, of
+ * weights[n, j] * table_shard[indices[n, j] - row_base] (fp32 accumulation): this shard's partial bag.
+ * indices: int32 or int64 global rows (index_dtype SMLM_I32 / SMLM_I64). Tokens with no lookup here get 0. */
+SMLM_API int smlm_shard_bag_forward(const void *indices, int index_dtype, int64_t row_base, const void *weights,
+                                    int weights_dtype, const void *table_shard, int table_dtype, int64_t n, int64_t k,
+                                    int64_t shard_rows, int64_t d, void *out, int out_dtype, void *stream);
+
+/* smlm_bag_backward_rows restricted to this shard's lookups: acc / touched / row_sqnorm are the shard's (local
+ * rows), gw[n, j] is the per-sample-weight gradient of lookups in this shard and 0 for the others. Workspace
+ * size: smlm_bag_backward_workspace(n, k, shard_rows, d). */
+SMLM_API int smlm_shard_bag_backward_rows(const void *grad_out, int grad_dtype, const void *indices, int index_dtype,
+                                          int64_t row_base, const void *weights, int weights_dtype,
+                                          const void *table_shard, int table_dtype, float *acc, uint8_t *touched,
+                                          float *row_sqnorm, int flags, float *gw, int64_t n, int64_t k,
+                                          int64_t shard_rows, int64_t d, void *workspace, size_t workspace_bytes,
+                                          int *status, void *stream);
+
+/* dst[i] = (...((src[0][i] + src[1][i]) + src[2][i]) ... + src[slots-1][i]) in fp32, src (slots, count)
+ * contiguous: the owners' partial results summed in rank order (deterministic). */
+SMLM_API int smlm_slot_sum(const float *src, int64_t slots, int64_t count, float *dst, void *stream);
 
 #ifdef __cplusplus
 }

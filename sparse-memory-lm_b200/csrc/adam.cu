@@ -144,6 +144,147 @@ __global__ void __launch_bounds__(256) lazy_adam_kernel(AdamArgs a) {
     }
 }
 
+// ----------------------------------------------------------------------------------- lazy Adam, compact state
+// bf16 moments, or int8 codes with one fp32 scale per row: m = sign * (code / 127)^2 * m_scale (signed square
+// root), v = ((code / 255) * v_scale)^4 (unsigned fourth root). The update runs in fp32 on the decoded moments;
+// only the stored state is rounded. Operation order and rounding of the reference's compact kernel
+// (kernels.py:445-495): every operation rounded on its own, stores rounded to nearest even, a positive second
+// moment never gets a zero code.
+struct LowArgs {
+    float *p, *acc;
+    void *m, *v;
+    float *m_scale, *v_scale;
+    uint8_t* touched;
+    const int32_t* list;
+    const int32_t* count;
+    const float* scale_dev;
+    float scale;
+    int d;
+    float b1, b2, one_minus_b1, one_minus_b2, eps, step_size, bc2_sqrt;
+    void* copy;
+    int copy_dtype;
+    int keep_acc;
+};
+
+__device__ __forceinline__ float sign_one(float x) { return x < 0.f ? -1.f : 1.f; }
+
+template <bool INT8>
+__device__ __forceinline__ void low_load(const LowArgs& a, int64_t i, float ms, float vs, float& m, float& v) {
+    if constexpr (INT8) {
+        const float mc = __fdiv_rn((float)static_cast<const int8_t*>(a.m)[i], 127.f);
+        m = __fmul_rn(__fmul_rn(__fmul_rn(sign_one(mc), mc), mc), ms);
+        const float vc = __fmul_rn(__fdiv_rn((float)static_cast<const uint8_t*>(a.v)[i], 255.f), vs);
+        v = __fmul_rn(vc, vc);
+        v = __fmul_rn(v, v);
+    } else {
+        m = bf16_bits_to_f32(static_cast<const uint16_t*>(a.m)[i]);
+        v = bf16_bits_to_f32(static_cast<const uint16_t*>(a.v)[i]);
+    }
+}
+
+__device__ __forceinline__ void low_update(const LowArgs& a, float g, float& p, float& m, float& v) {
+    m = __fadd_rn(__fmul_rn(a.b1, m), __fmul_rn(a.one_minus_b1, g));
+    v = __fadd_rn(__fmul_rn(a.b2, v), __fmul_rn(__fmul_rn(a.one_minus_b2, g), g));
+    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), a.bc2_sqrt), a.eps);
+    p = __fsub_rn(p, __fdiv_rn(__fmul_rn(a.step_size, m), denom));
+}
+
+__device__ __forceinline__ float fourth_root(float v) { return __fsqrt_rn(__fsqrt_rn(v)); }
+
+template <bool INT8>
+__device__ __forceinline__ void low_store(const LowArgs& a, int64_t i, float ms, float vs, float p, float m,
+                                          float v) {
+    a.p[i] = p;
+    if constexpr (INT8) {
+        float mq = __fsqrt_rn(__fdiv_rn(fabsf(m), ms > 0.f ? ms : 1.f));
+        mq = rintf(fminf(fmaxf(__fmul_rn(__fmul_rn(sign_one(m), mq), 127.f), -127.f), 127.f));
+        float vq = __fmul_rn(__fdiv_rn(fourth_root(v), vs > 0.f ? vs : 1.f), 255.f);
+        vq = rintf(fminf(fmaxf(vq, 0.f), 255.f));
+        vq = v > 0.f ? fmaxf(vq, 1.f) : 0.f;
+        static_cast<int8_t*>(a.m)[i] = (int8_t)mq;
+        static_cast<uint8_t*>(a.v)[i] = (uint8_t)vq;
+    } else {
+        static_cast<uint16_t*>(a.m)[i] = (uint16_t)f32_to_bf16_bits(m);
+        static_cast<uint16_t*>(a.v)[i] = (uint16_t)f32_to_bf16_bits(v);
+    }
+    if (!a.keep_acc) a.acc[i] = 0.f;
+    if (a.copy) {
+        if (a.copy_dtype == SMLM_BF16) static_cast<uint16_t*>(a.copy)[i] = (uint16_t)f32_to_bf16_bits(p);
+        else static_cast<float*>(a.copy)[i] = p;
+    }
+}
+
+// One warp per touched row. NS > 0: the row (d <= 32 NS) stays in registers between the update and the int8
+// encode, which needs the row maxima of the new moments. NS == 0 (any width): bf16 streams the row once; int8
+// runs the update twice, first for the maxima, then to encode (same inputs, same results).
+template <bool INT8, int NS>
+__global__ void __launch_bounds__(256) lazy_adam_lowmem_kernel(LowArgs a) {
+    const int lane = lane_id();
+    const int n = *a.count;
+    const float scale = a.scale_dev ? *a.scale_dev : a.scale;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
+        const int64_t r = a.list[i];
+        const int64_t base = r * a.d;
+        const float ms_old = INT8 ? a.m_scale[r] : 0.f, vs_old = INT8 ? a.v_scale[r] : 0.f;
+        float ms = 0.f, vs = 0.f;
+        if constexpr (NS > 0) {
+            float p[NS], m[NS], v[NS];
+#pragma unroll
+            for (int s = 0; s < NS; s++) {
+                const int c = lane + 32 * s;
+                p[s] = m[s] = v[s] = 0.f;
+                if (c < a.d) {
+                    const float g = __fmul_rn(a.acc[base + c], scale);
+                    low_load<INT8>(a, base + c, ms_old, vs_old, m[s], v[s]);
+                    p[s] = a.p[base + c];
+                    low_update(a, g, p[s], m[s], v[s]);
+                    if (INT8) {
+                        ms = fmaxf(ms, fabsf(m[s]));
+                        vs = fmaxf(vs, fourth_root(v[s]));
+                    }
+                }
+            }
+            if (INT8) {
+                ms = warp_max(ms);
+                vs = warp_max(vs);
+            }
+#pragma unroll
+            for (int s = 0; s < NS; s++) {
+                const int c = lane + 32 * s;
+                if (c < a.d) low_store<INT8>(a, base + c, ms, vs, p[s], m[s], v[s]);
+            }
+        } else {
+            if (INT8) {
+                for (int c = lane; c < a.d; c += 32) {
+                    float p = a.p[base + c], m, v;
+                    low_load<INT8>(a, base + c, ms_old, vs_old, m, v);
+                    low_update(a, __fmul_rn(a.acc[base + c], scale), p, m, v);
+                    ms = fmaxf(ms, fabsf(m));
+                    vs = fmaxf(vs, fourth_root(v));
+                }
+                ms = warp_max(ms);
+                vs = warp_max(vs);
+            }
+            __syncwarp();
+            for (int c = lane; c < a.d; c += 32) {
+                float p = a.p[base + c], m, v;
+                low_load<INT8>(a, base + c, ms_old, vs_old, m, v);
+                low_update(a, __fmul_rn(a.acc[base + c], scale), p, m, v);
+                low_store<INT8>(a, base + c, ms, vs, p, m, v);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            if (INT8) {
+                a.m_scale[r] = ms;
+                a.v_scale[r] = vs;
+            }
+            a.touched[r] = 0;
+        }
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ row-wise
 struct RowArgs {
     float *p, *acc, *v;
@@ -310,6 +451,45 @@ extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_
     if (vec) lazy_adam_kernel<4><<<blocks, 256, 0, st>>>(a);
     else lazy_adam_kernel<1><<<blocks, 256, 0, st>>>(a);
     SMLM_LAUNCHED("lazy_adam_kernel");
+    return SMLM_OK;
+}
+
+extern "C" int smlm_lazy_adam_lowmem_step(float* param, void* exp_avg, void* exp_avg_sq, float* exp_avg_scale,
+                                          float* exp_avg_sq_scale, int state_dtype, float* acc, uint8_t* touched,
+                                          const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
+                                          float beta1, float beta2, float one_minus_b1, float one_minus_b2, float eps,
+                                          float step_size, float bc2_sqrt, void* value_copy, int copy_dtype,
+                                          int flags, void* workspace, size_t workspace_bytes, void* stream) {
+    SMLM_CHECK_ARG(rows >= 0 && d > 0, "lazy_adam_lowmem_step: rows must be >= 0 and the width > 0");
+    SMLM_CHECK_ARG(rows < (int64_t)0x7fffffff && d < (1 << 30), "lazy_adam_lowmem_step: size too large");
+    SMLM_CHECK_ARG(state_dtype == SMLM_BF16 || state_dtype == SMLM_I8,
+                   "lazy_adam_lowmem_step: state must be bf16 or int8 (SMLM_BF16 / SMLM_I8)");
+    SMLM_CHECK_ARG(value_copy == nullptr || copy_dtype == SMLM_F32 || copy_dtype == SMLM_BF16,
+                   "lazy_adam_lowmem_step: value copy must be fp32 or bf16");
+    SMLM_CHECK_ARG((flags & ~SMLM_STEP_KEEP_ACC) == 0, "lazy_adam_lowmem_step: unknown flags %d", flags);
+    if (rows == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(param && exp_avg && exp_avg_sq && acc && touched, "lazy_adam_lowmem_step: null pointer");
+    SMLM_CHECK_ARG(state_dtype != SMLM_I8 || (exp_avg_scale && exp_avg_sq_scale),
+                   "lazy_adam_lowmem_step: int8 state needs both row scales");
+    cudaStream_t st = as_stream(stream);
+    TouchedBufs b;
+    int rc = compact_touched(touched, rows, workspace, workspace_bytes, &b, st);
+    if (rc != SMLM_OK) return rc;
+    LowArgs a{param, acc, exp_avg, exp_avg_sq, exp_avg_scale, exp_avg_sq_scale, touched, b.list, b.count,
+              grad_scale_dev, grad_scale, (int)d, beta1, beta2, one_minus_b1, one_minus_b2, eps, step_size,
+              bc2_sqrt, value_copy, copy_dtype, (flags & SMLM_STEP_KEEP_ACC) ? 1 : 0};
+    const int blocks = persistent_blocks(8, 8);
+    const bool i8 = state_dtype == SMLM_I8;
+    auto go = [&](auto NSc) {
+        constexpr int NS = decltype(NSc)::value;
+        if (i8) lazy_adam_lowmem_kernel<true, NS><<<blocks, 256, 0, st>>>(a);
+        else lazy_adam_lowmem_kernel<false, NS><<<blocks, 256, 0, st>>>(a);
+    };
+    if (d <= 32 * 4) go(std::integral_constant<int, 4>{});
+    else if (d <= 32 * 12) go(std::integral_constant<int, 12>{});
+    else if (d <= 32 * 16) go(std::integral_constant<int, 16>{});
+    else go(std::integral_constant<int, 0>{});
+    SMLM_LAUNCHED("lazy_adam_lowmem_kernel");
     return SMLM_OK;
 }
 

@@ -69,8 +69,18 @@ __device__ __forceinline__ void store_out(void* out, int dtype, int64_t off, con
 __device__ __forceinline__ float silu_bf16(float p) { return round_bf16(p / (1.0f + expf(-p))); }
 
 // ---------------------------------------------------------------------------------------------- bag gather
+// Lookup indices: int64 or int32 global rows; the table holds rows [row_base, row_base + rows). Rows outside
+// that range are skipped: flagged as an index error, or silently when skip_foreign (a row shard, whose other
+// rows live on other GPUs).
+__device__ __forceinline__ int64_t load_index(const void* idx, int idx32, int64_t i) {
+    return idx32 ? (int64_t)__ldg(static_cast<const int32_t*>(idx) + i) : __ldg(static_cast<const int64_t*>(idx) + i);
+}
+
 struct BagArgs {
-    const int64_t* idx;
+    const void* idx;
+    int idx32;
+    int64_t row_base;
+    int skip_foreign;
     const void* w;
     int w_dtype;
     const void* table;
@@ -85,8 +95,9 @@ struct BagArgs {
 };
 
 // One warp per (token, column block); j-loop over the token's k lookups in chunks of 32 (lane j holds the
-// j-th index / weight of the chunk and broadcasts it), four rows in flight per step. The accumulation is a
-// sequential fmaf chain over j for every column.
+// j-th index / weight of the chunk). The chunk's valid lookups (a warp ballot, in j order) are taken four at a
+// time, four rows in flight per step. The accumulation is a sequential fmaf chain over the valid j for every
+// column.
 template <typename TT, int VEC, int NS>
 __global__ void __launch_bounds__(256) bag_gather_kernel(BagArgs a) {
     const int lane = lane_id();
@@ -104,36 +115,39 @@ __global__ void __launch_bounds__(256) bag_gather_kernel(BagArgs a) {
             for (int i = 0; i < VEC; i++) acc[s][i] = 0.f;
         for (int j0 = 0; j0 < a.k; j0 += 32) {
             const int cnt = min(32, a.k - j0);
-            int64_t my_r = 0;
+            int64_t my_r = -1;
             float my_w = 0.f;
             if (lane < cnt) {
-                my_r = __ldg(a.idx + n * a.k + j0 + lane);
+                my_r = load_index(a.idx, a.idx32, n * a.k + j0 + lane) - a.row_base;
                 my_w = load_weight(a.w, a.w_dtype, n * a.k + j0 + lane);
                 if (my_r < 0 || my_r >= a.rows) {
-                    flag(a.status, SMLM_FLAG_INDEX_RANGE);
+                    if (!a.skip_foreign) flag(a.status, SMLM_FLAG_INDEX_RANGE);
                     my_r = -1;
                 }
             }
-            for (int jj = 0; jj < cnt; jj += 4) {
+            unsigned todo = __ballot_sync(FULL, my_r >= 0);
+            while (todo) {  // warp-uniform
                 int64_t r[4];
                 float wv[4];
+                bool ok[4];
                 float v[4][NS][VEC];
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    r[u] = __shfl_sync(FULL, my_r, (jj + u) & 31);
-                    wv[u] = __shfl_sync(FULL, my_w, (jj + u) & 31);
-                    const bool ok = (jj + u < cnt) && r[u] >= 0;
+                    ok[u] = todo != 0;
+                    const int src = ok[u] ? __ffs(todo) - 1 : 0;
+                    todo &= todo - 1;
+                    r[u] = __shfl_sync(FULL, my_r, src);
+                    wv[u] = __shfl_sync(FULL, my_w, src);
 #pragma unroll
                     for (int s = 0; s < NS; s++) {
                         const int col = c0 + (lane + 32 * s) * VEC;
-                        if (ok && col < a.d) {
+                        if (ok[u] && col < a.d) {
                             Elt<TT>::template load<VEC>(table + r[u] * a.d + col, v[u][s]);
                         } else {
 #pragma unroll
                             for (int i = 0; i < VEC; i++) v[u][s][i] = 0.f;
                         }
                     }
-                    if (!ok) wv[u] = 0.f;
                 }
 #pragma unroll
                 for (int u = 0; u < 4; u++)
@@ -141,7 +155,7 @@ __global__ void __launch_bounds__(256) bag_gather_kernel(BagArgs a) {
                     for (int s = 0; s < NS; s++)
 #pragma unroll
                         for (int i = 0; i < VEC; i++)
-                            if (jj + u < cnt) acc[s][i] = fmaf(wv[u], v[u][s][i], acc[s][i]);
+                            if (ok[u]) acc[s][i] = fmaf(wv[u], v[u][s][i], acc[s][i]);
             }
         }
 #pragma unroll
@@ -337,13 +351,14 @@ static int bit_width_u32(uint64_t x) {
     return b;
 }
 
-__global__ void bb_keys_kernel(const int64_t* idx, int64_t m, int64_t rows, uint32_t* keys, uint32_t* pos,
-                               int* status) {
+// skip_foreign: rows outside [row_base, row_base + rows) belong to other shards (past-the-end key, not flagged).
+__global__ void bb_keys_kernel(const void* idx, int idx32, int64_t row_base, int skip_foreign, int64_t m,
+                               int64_t rows, uint32_t* keys, uint32_t* pos, int* status) {
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < m; p += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = idx[p];
+        const int64_t r = load_index(idx, idx32, p) - row_base;
         uint32_t key = (uint32_t)r;
         if (r < 0 || r >= rows) {
-            flag(status, SMLM_FLAG_INDEX_RANGE);
+            if (!skip_foreign) flag(status, SMLM_FLAG_INDEX_RANGE);
             key = (uint32_t)rows;  // sorts after every valid row; skipped by the segment pass
         }
         keys[p] = key;
@@ -354,7 +369,8 @@ __global__ void bb_keys_kernel(const int64_t* idx, int64_t m, int64_t rows, uint
 struct SegArgs {
     const uint32_t* keys;  // sorted rows
     const uint32_t* pos;   // positions (n * k + j), ascending within a row
-    const float* g;        // grad_out (n, d)
+    const void* g;         // grad_out (n, d), fp32 or bf16
+    int g_dtype;
     const void* w;
     int w_dtype;
     const void* table;
@@ -374,16 +390,24 @@ struct SegArgs {
 // One warp per chunk of P sorted positions. Each run of equal rows is summed in position order; runs that
 // lie inside the chunk go straight into acc (they belong to this chunk alone: no atomics), the run that
 // enters from the previous chunk goes to carry_head, the run that leaves to carry_tail (see fixup).
-template <typename TT, int VEC, int NS>
+// Memory-level parallelism: a batch of 32 positions is loaded one per lane together with its weight and (first-
+// touch mode) its row's touched byte; the next position's grad_out row and, when it starts a run, its table row
+// are loaded while the current position is summed.
+template <typename TT, typename GT, bool GW, int VEC, int NS>
 __global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
     const int lane = lane_id();
     const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (c >= a.chunks) return;
     const TT* table = static_cast<const TT*>(a.table);
+    const GT* g = static_cast<const GT*>(a.g);
     const int64_t start = c * a.P;
     const int64_t end = min(start + (int64_t)a.P, a.m);
     const uint32_t valid_lim = (uint32_t)a.rows;
     const uint32_t first_row = a.keys[start];
+    if (first_row >= valid_lim && !GW) {  // only past-the-end keys from here on: nothing to add
+        if (lane == 0) a.chunk_flags[c] = 0;
+        return;
+    }
     const uint32_t last_row = a.keys[end - 1];
     const uint32_t prev_row = start > 0 ? a.keys[start - 1] : NO_ROW;
     const uint32_t next_row = end < a.m ? a.keys[end] : NO_ROW;
@@ -393,6 +417,7 @@ __global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
     int cflags = 0;
 
     uint32_t cur = NO_ROW;
+    bool cur_fresh = false;  // first-touch mode: the current row had not been touched before this call
     float sum[NS][VEC], trow[NS][VEC];
 #pragma unroll
     for (int s = 0; s < NS; s++)
@@ -417,7 +442,7 @@ __global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
             direct = true;
         }
         // a row seen for the first time since the optimizer step is written, not read (first_writes mode)
-        const bool accumulate = direct && !(a.first_writes && a.touched && a.touched[cur] == 0);
+        const bool accumulate = direct && !cur_fresh;
 #pragma unroll
         for (int s = 0; s < NS; s++) {
             const int col = (lane + 32 * s) * VEC;
@@ -446,50 +471,90 @@ __global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
             if (lane == 0 && a.touched) a.touched[cur] = 1;
         }
     };
+    auto load_g = [&](uint32_t p, float (&v)[NS][VEC]) {
+        const int64_t tok = p / a.k;
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = (lane + 32 * s) * VEC;
+            if (col < a.d) Elt<GT>::template load<VEC>(g + tok * a.d + col, v[s]);
+        }
+    };
+    auto load_t = [&](uint32_t row, float (&v)[NS][VEC]) {
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = (lane + 32 * s) * VEC;
+            if (col < a.d) Elt<TT>::template load<VEC>(table + (int64_t)row * a.d + col, v[s]);
+        }
+    };
 
     for (int64_t b = start; b < end; b += 32) {
         const int cnt = (int)min((int64_t)32, end - b);
         uint32_t my_key = NO_ROW, my_pos = 0;
+        float my_w = 0.f;
+        bool my_fresh = false;
         if (lane < cnt) {
             my_key = a.keys[b + lane];
             my_pos = a.pos[b + lane];
+            if (my_key < valid_lim) {
+                my_w = load_weight(a.w, a.w_dtype, my_pos);
+                my_fresh = a.first_writes && a.touched && a.touched[my_key] == 0;
+            }
+        }
+        float gn[NS][VEC], tn[NS][VEC];
+        uint32_t row_n = __shfl_sync(FULL, my_key, 0);
+        if (row_n < valid_lim) {
+            load_g(__shfl_sync(FULL, my_pos, 0), gn);
+            if (GW && row_n != cur) load_t(row_n, tn);
         }
         for (int t = 0; t < cnt; t++) {
-            const uint32_t row = __shfl_sync(FULL, my_key, t);
+            const uint32_t row = row_n;
             const uint32_t p = __shfl_sync(FULL, my_pos, t);
-            if (row >= valid_lim) {  // out-of-range lookup (flagged when the keys were built)
-                if (lane == 0) a.gw[p] = 0.f;
-                continue;
-            }
-            if (row != cur) {
+            const float wv = __shfl_sync(FULL, my_w, t);
+            const bool fresh = __shfl_sync(FULL, (int)my_fresh, t) != 0;
+            const bool live = row < valid_lim;  // else an out-of-range or skipped lookup (flagged at key build)
+            if (live && row != cur) {
                 flush();
                 cur = row;
+                cur_fresh = fresh;
 #pragma unroll
-                for (int s = 0; s < NS; s++) {
-                    const int col = (lane + 32 * s) * VEC;
+                for (int s = 0; s < NS; s++)
 #pragma unroll
-                    for (int i = 0; i < VEC; i++) sum[s][i] = 0.f;
-                    if (col < a.d) Elt<TT>::template load<VEC>(table + (int64_t)row * a.d + col, trow[s]);
-                }
+                    for (int i = 0; i < VEC; i++) {
+                        sum[s][i] = 0.f;
+                        if (GW) trow[s][i] = tn[s][i];
+                    }
             }
-            const int64_t tok = p / a.k;
-            const float wv = load_weight(a.w, a.w_dtype, p);
+            float gv[NS][VEC];
+#pragma unroll
+            for (int s = 0; s < NS; s++)
+#pragma unroll
+                for (int i = 0; i < VEC; i++) gv[s][i] = gn[s][i];
+            // issue the next position's loads before this position's arithmetic
+            row_n = t + 1 < cnt ? __shfl_sync(FULL, my_key, t + 1) : NO_ROW;
+            if (row_n < valid_lim) {
+                load_g(__shfl_sync(FULL, my_pos, t + 1), gn);
+                if (GW && row_n != row) load_t(row_n, tn);
+            }
+            if (!live) {
+                if (GW && lane == 0) a.gw[p] = 0.f;
+                continue;
+            }
             float dot = 0.f;
 #pragma unroll
             for (int s = 0; s < NS; s++) {
                 const int col = (lane + 32 * s) * VEC;
                 if (col < a.d) {
-                    float gv[VEC];
-                    Elt<float>::template load<VEC>(a.g + tok * a.d + col, gv);
 #pragma unroll
                     for (int i = 0; i < VEC; i++) {
-                        sum[s][i] = fmaf(wv, gv[i], sum[s][i]);
-                        dot = fmaf(gv[i], trow[s][i], dot);
+                        sum[s][i] = fmaf(wv, gv[s][i], sum[s][i]);
+                        if (GW) dot = fmaf(gv[s][i], trow[s][i], dot);
                     }
                 }
             }
-            dot = warp_sum(dot);
-            if (lane == 0) a.gw[p] = dot;
+            if (GW) {
+                dot = warp_sum(dot);
+                if (lane == 0) a.gw[p] = dot;
+            }
         }
     }
     flush();
@@ -537,19 +602,27 @@ __global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a) {
     if (lane == 0 && a.touched) a.touched[row] = 1;
 }
 
-template <typename TT, int VEC>
+template <typename TT, typename GT, bool GW, int VEC>
 static int launch_segment(SegArgs a, cudaStream_t st) {
     const int slots = (a.d + VEC - 1) / VEC;
     const int ns = (slots + 31) / 32;
     const int blocks = (int)((a.chunks + 7) / 8);
-    if (ns <= 1) bb_segment_kernel<TT, VEC, 1><<<blocks, 256, 0, st>>>(a);
-    else if (ns == 2) bb_segment_kernel<TT, VEC, 2><<<blocks, 256, 0, st>>>(a);
-    else if (ns == 3) bb_segment_kernel<TT, VEC, 3><<<blocks, 256, 0, st>>>(a);
-    else bb_segment_kernel<TT, VEC, 4><<<blocks, 256, 0, st>>>(a);
+    if (ns <= 1) bb_segment_kernel<TT, GT, GW, VEC, 1><<<blocks, 256, 0, st>>>(a);
+    else if (ns == 2) bb_segment_kernel<TT, GT, GW, VEC, 2><<<blocks, 256, 0, st>>>(a);
+    else if (ns == 3) bb_segment_kernel<TT, GT, GW, VEC, 3><<<blocks, 256, 0, st>>>(a);
+    else bb_segment_kernel<TT, GT, GW, VEC, 4><<<blocks, 256, 0, st>>>(a);
     SMLM_LAUNCHED("bb_segment_kernel");
     bb_fixup_kernel<VEC><<<blocks, 256, 0, st>>>(a);
     SMLM_LAUNCHED("bb_fixup_kernel");
     return SMLM_OK;
+}
+
+template <typename TT, int VEC>
+static int launch_segment_g(SegArgs a, cudaStream_t st) {
+    if (a.g_dtype == SMLM_F32)
+        return a.gw ? launch_segment<TT, float, true, VEC>(a, st) : launch_segment<TT, float, false, VEC>(a, st);
+    return a.gw ? launch_segment<TT, __nv_bfloat16, true, VEC>(a, st)
+                : launch_segment<TT, __nv_bfloat16, false, VEC>(a, st);
 }
 
 struct BackwardPlan {
@@ -615,8 +688,27 @@ extern "C" int smlm_bag_forward(const int64_t* indices, const void* weights, int
     SMLM_CHECK_ARG(d < (1 << 30) && k < (1 << 30), "bag_forward: d or k too large");
     if (n == 0 || d == 0) return SMLM_OK;
     SMLM_CHECK_ARG(indices && table && out && (k == 0 || weights), "bag_forward: null pointer");
-    BagArgs a{indices, weights, weights_dtype, table, nullptr, SMLM_F32, out, out_dtype, n, rows, (int)k, (int)d,
-              0, status};
+    BagArgs a{indices, 0, 0, 0, weights, weights_dtype, table, nullptr, SMLM_F32, out, out_dtype, n, rows, (int)k,
+              (int)d, 0, status};
+    return launch_bag(a, table_dtype, as_stream(stream));
+}
+
+extern "C" int smlm_shard_bag_forward(const void* indices, int index_dtype, int64_t row_base, const void* weights,
+                                      int weights_dtype, const void* table_shard, int table_dtype, int64_t n,
+                                      int64_t k, int64_t shard_rows, int64_t d, void* out, int out_dtype,
+                                      void* stream) {
+    SMLM_CHECK_ARG(n >= 0 && k >= 0 && shard_rows >= 0 && d >= 0 && row_base >= 0, "shard_bag_forward: negative size");
+    SMLM_CHECK_ARG(index_dtype == SMLM_I32 || index_dtype == SMLM_I64, "shard_bag_forward: int32 or int64 indices");
+    SMLM_CHECK_ARG(table_dtype == SMLM_F32 || table_dtype == SMLM_BF16, "shard_bag_forward: table must be fp32 or bf16");
+    SMLM_CHECK_ARG(weights_dtype == SMLM_F32 || weights_dtype == SMLM_BF16,
+                   "shard_bag_forward: weights must be fp32 or bf16");
+    SMLM_CHECK_ARG(out_dtype == SMLM_F32 || out_dtype == SMLM_BF16, "shard_bag_forward: out must be fp32 or bf16");
+    SMLM_CHECK_ARG(d < (1 << 30) && k < (1 << 30), "shard_bag_forward: d or k too large");
+    if (n == 0 || d == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(indices && out && (k == 0 || weights) && (table_shard || shard_rows == 0),
+                   "shard_bag_forward: null pointer");
+    BagArgs a{indices, index_dtype == SMLM_I32, row_base, 1, weights, weights_dtype, table_shard, nullptr, SMLM_F32,
+              out, out_dtype, n, shard_rows, (int)k, (int)d, 0, nullptr};
     return launch_bag(a, table_dtype, as_stream(stream));
 }
 
@@ -649,8 +741,8 @@ extern "C" int smlm_bag_infer(const int64_t* indices, const void* weights, int w
         SMLM_LAUNCHED("bag_q4_kernel");
         return SMLM_OK;
     }
-    BagArgs a{indices, weights, weights_dtype, table, pre, pre_dtype, out, out_dtype, n, rows, (int)k, (int)d, 0,
-              status};
+    BagArgs a{indices, 0, 0, 0, weights, weights_dtype, table, pre, pre_dtype, out, out_dtype, n, rows, (int)k,
+              (int)d, 0, status};
     return launch_bag(a, table_dtype, st);
 }
 
@@ -673,30 +765,34 @@ extern "C" size_t smlm_bag_backward_workspace(int64_t n, int64_t k, int64_t rows
     return layout_backward(p, d, nullptr, &b);
 }
 
-extern "C" int smlm_bag_backward_rows(const float* grad_out, const int64_t* indices, const void* weights,
-                                      int weights_dtype, const void* table, int table_dtype, float* acc,
-                                      uint8_t* touched, float* row_sqnorm, int flags, float* gw, int64_t n,
-                                      int64_t k, int64_t rows, int64_t d, void* workspace, size_t workspace_bytes,
-                                      int* status, void* stream) {
-    SMLM_CHECK_ARG(n >= 0 && k >= 0 && rows >= 0 && d >= 0, "bag_backward_rows: negative size");
-    SMLM_CHECK_ARG(table_dtype == SMLM_F32 || table_dtype == SMLM_BF16, "bag_backward_rows: table must be fp32 or bf16");
-    SMLM_CHECK_ARG(weights_dtype == SMLM_F32 || weights_dtype == SMLM_BF16, "bag_backward_rows: weights must be fp32 or bf16");
-    SMLM_CHECK_ARG(n * k < (int64_t)0x7fffffff, "bag_backward_rows: n * k must be below 2^31");
-    SMLM_CHECK_ARG(rows < (int64_t)0xffffffff, "bag_backward_rows: rows must be below 2^32 - 1");
-    SMLM_CHECK_ARG(d < (1 << 30), "bag_backward_rows: d too large");
-    SMLM_CHECK_ARG((flags & ~SMLM_BWD_FIRST_TOUCH_WRITES) == 0, "bag_backward_rows: unknown flags %d", flags);
+namespace smlm {
+// Both backward entry points: indices int64 / int32, table rows [row_base, row_base + rows) (skip_foreign: other
+// rows are another shard's, skipped silently; else flagged).
+static int backward_impl(const char* fn, const void* grad_out, int grad_dtype, const void* indices, int idx32,
+                         int64_t row_base, int skip_foreign, const void* weights, int weights_dtype,
+                         const void* table, int table_dtype, float* acc, uint8_t* touched, float* row_sqnorm,
+                         int flags, float* gw, int64_t n, int64_t k, int64_t rows, int64_t d, void* workspace,
+                         size_t workspace_bytes, int* status, void* stream) {
+    SMLM_CHECK_ARG(n >= 0 && k >= 0 && rows >= 0 && d >= 0, "%s: negative size", fn);
+    SMLM_CHECK_ARG(table_dtype == SMLM_F32 || table_dtype == SMLM_BF16, "%s: table must be fp32 or bf16", fn);
+    SMLM_CHECK_ARG(weights_dtype == SMLM_F32 || weights_dtype == SMLM_BF16, "%s: weights must be fp32 or bf16", fn);
+    SMLM_CHECK_ARG(grad_dtype == SMLM_F32 || grad_dtype == SMLM_BF16, "%s: grad_out must be fp32 or bf16", fn);
+    SMLM_CHECK_ARG(n * k < (int64_t)0x7fffffff, "%s: n * k must be below 2^31", fn);
+    SMLM_CHECK_ARG(rows < (int64_t)0xffffffff, "%s: rows must be below 2^32 - 1", fn);
+    SMLM_CHECK_ARG(d < (1 << 30), "%s: d too large", fn);
+    SMLM_CHECK_ARG((flags & ~SMLM_BWD_FIRST_TOUCH_WRITES) == 0, "%s: unknown flags %d", fn, flags);
     SMLM_CHECK_ARG(!(flags & SMLM_BWD_FIRST_TOUCH_WRITES) || touched != nullptr,
-                   "bag_backward_rows: first-touch writes need the touched mask");
+                   "%s: first-touch writes need the touched mask", fn);
     if (n == 0 || k == 0) return SMLM_OK;
-    SMLM_CHECK_ARG(grad_out && indices && weights && table && gw, "bag_backward_rows: null pointer");
-    if (d == 0) {
+    SMLM_CHECK_ARG(grad_out && indices && weights && (table || !gw) && (gw || acc), "%s: null pointer", fn);
+    if (d == 0 && gw) {
         SMLM_CUDA(cudaMemsetAsync(gw, 0, sizeof(float) * n * k, as_stream(stream)));
     }
     BackwardPlan p = plan_backward(n, k, rows);
     BackwardBufs bb;
     const size_t need = layout_backward(p, d, nullptr, &bb);
     if (workspace == nullptr || workspace_bytes < need) {
-        set_error("bag_backward_rows: workspace too small (%zu < %zu)", workspace_bytes, need);
+        set_error("%s: workspace too small (%zu < %zu)", fn, workspace_bytes, need);
         return SMLM_ERR_WORKSPACE;
     }
     layout_backward(p, d, workspace, &bb);
@@ -706,20 +802,44 @@ extern "C" int smlm_bag_backward_rows(const float* grad_out, const int64_t* indi
     int* chunk_flags = bb.flags;
     cudaStream_t st = as_stream(stream);
     const int kb = (int)std::max<int64_t>(1, std::min<int64_t>((p.m + 255) / 256, (int64_t)sm_count() * 8));
-    bb_keys_kernel<<<kb, 256, 0, st>>>(indices, p.m, rows, keys_in, pos_in, status);
+    bb_keys_kernel<<<kb, 256, 0, st>>>(indices, idx32, row_base, skip_foreign, p.m, rows, keys_in, pos_in, status);
     SMLM_LAUNCHED("bb_keys_kernel");
     size_t sort_bytes = p.sort_bytes;
     SMLM_CUDA(cub::DeviceRadixSort::SortPairs(sort_tmp, sort_bytes, keys_in, keys_out, pos_in, pos_out, (int)p.m, 0,
                                               std::max(p.end_bit, 1), st));
     if (d == 0) return SMLM_OK;
-    SegArgs a{keys_out, pos_out, grad_out, weights, weights_dtype, table, acc, touched, gw, carry_head,
+    SegArgs a{keys_out, pos_out, grad_out, grad_dtype, weights, weights_dtype, table, acc, touched, gw, carry_head,
               carry_tail, chunk_flags, row_sqnorm, (flags & SMLM_BWD_FIRST_TOUCH_WRITES) ? 1 : 0, p.m, rows, (int)k,
               (int)d, p.P, p.chunks};
     const uintptr_t tp = reinterpret_cast<uintptr_t>(table);
     const uintptr_t gp = reinterpret_cast<uintptr_t>(grad_out);
     const uintptr_t ap = reinterpret_cast<uintptr_t>(acc);
-    const bool vec = d % 4 == 0 && gp % 16 == 0 && ap % 16 == 0 &&
+    const bool vec = d % 4 == 0 && gp % (grad_dtype == SMLM_F32 ? 16 : 8) == 0 && ap % 16 == 0 &&
                      tp % (table_dtype == SMLM_F32 ? 16 : 8) == 0;
-    if (table_dtype == SMLM_F32) return vec ? launch_segment<float, 4>(a, st) : launch_segment<float, 1>(a, st);
-    return vec ? launch_segment<__nv_bfloat16, 4>(a, st) : launch_segment<__nv_bfloat16, 1>(a, st);
+    if (table_dtype == SMLM_F32) return vec ? launch_segment_g<float, 4>(a, st) : launch_segment_g<float, 1>(a, st);
+    return vec ? launch_segment_g<__nv_bfloat16, 4>(a, st) : launch_segment_g<__nv_bfloat16, 1>(a, st);
+}
+}  // namespace smlm
+
+extern "C" int smlm_bag_backward_rows(const void* grad_out, int grad_dtype, const int64_t* indices,
+                                      const void* weights, int weights_dtype, const void* table, int table_dtype,
+                                      float* acc, uint8_t* touched, float* row_sqnorm, int flags, float* gw,
+                                      int64_t n, int64_t k, int64_t rows, int64_t d, void* workspace,
+                                      size_t workspace_bytes, int* status, void* stream) {
+    return backward_impl("bag_backward_rows", grad_out, grad_dtype, indices, 0, 0, 0, weights, weights_dtype, table,
+                         table_dtype, acc, touched, row_sqnorm, flags, gw, n, k, rows, d, workspace, workspace_bytes,
+                         status, stream);
+}
+
+extern "C" int smlm_shard_bag_backward_rows(const void* grad_out, int grad_dtype, const void* indices,
+                                            int index_dtype, int64_t row_base, const void* weights,
+                                            int weights_dtype, const void* table_shard, int table_dtype, float* acc,
+                                            uint8_t* touched, float* row_sqnorm, int flags, float* gw, int64_t n,
+                                            int64_t k, int64_t shard_rows, int64_t d, void* workspace,
+                                            size_t workspace_bytes, int* status, void* stream) {
+    SMLM_CHECK_ARG(index_dtype == SMLM_I32 || index_dtype == SMLM_I64, "shard_bag_backward_rows: int32 or int64 indices");
+    SMLM_CHECK_ARG(row_base >= 0, "shard_bag_backward_rows: negative row base");
+    return backward_impl("shard_bag_backward_rows", grad_out, grad_dtype, indices, index_dtype == SMLM_I32, row_base,
+                         1, weights, weights_dtype, table_shard, table_dtype, acc, touched, row_sqnorm, flags, gw, n,
+                         k, shard_rows, d, workspace, workspace_bytes, status, stream);
 }

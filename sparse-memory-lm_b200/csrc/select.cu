@@ -281,6 +281,62 @@ int launch_pk_pairs(const uint32_t* lists, int64_t rows_nh, int nk, int knn, voi
 }
 
 // ------------------------------------------------------------------------------------ selection backward
+// Per selected pair (one lane each, lane < knn) of one (token, head): dl = w (g_w - sum(w g_w)) + g_scores,
+// ds = dl rounded to the score type, then per sub-key of each half the sum of ds over the pairs that use it, in
+// selection order (fp32), kept by the lane of the sub-key's first occurrence. Invalid indices contribute nothing.
+struct PairGrad {
+    uint32_t a1, a2;  // the pair's sub-keys
+    float s1, s2;     // per-sub-key sums (meaningful on the first occurrence)
+    bool first1, first2;
+};
+
+template <bool F32>
+__device__ __forceinline__ PairGrad pair_grad(const int64_t* idx, const float* w, const float* gw, const void* gs,
+                                              int64_t row, int nk, int knn, int lane) {
+    const int64_t o = row * knn + lane;
+    const bool on = lane < knn;
+    const float wj = on ? w[o] : 0.f;
+    float dl = 0.f;
+    if (gw) {
+        const float g = on ? gw[o] : 0.f;
+        const float dot = warp_sum(wj * g);
+        dl = wj * (g - dot);
+    }
+    if (gs && on) {
+        const float g2 = F32 ? static_cast<const float*>(gs)[o] : bf16_bits_to_f32(static_cast<const uint16_t*>(gs)[o]);
+        dl = dl + g2;
+    }
+    int64_t full = on ? idx[o] : 0;
+    if (full < 0 || full >= (int64_t)nk * nk) full = 0, dl = 0.f;
+    const float ds = F32 ? dl : round_bf16(dl);
+    PairGrad r;
+    r.a1 = (uint32_t)(full / nk);
+    r.a2 = (uint32_t)(full % nk);
+    r.s1 = r.s2 = 0.f;
+    r.first1 = r.first2 = on;
+    for (int j = 0; j < knn; j++) {
+        const uint32_t b1 = __shfl_sync(FULL, r.a1, j);
+        const uint32_t b2 = __shfl_sync(FULL, r.a2, j);
+        const float dj = __shfl_sync(FULL, ds, j);
+        if (b1 == r.a1) {
+            r.s1 = r.s1 + dj;
+            if (j < lane) r.first1 = false;
+        }
+        if (b2 == r.a2) {
+            r.s2 = r.s2 + dj;
+            if (j < lane) r.first2 = false;
+        }
+    }
+    return r;
+}
+
+template <bool F32>
+__device__ __forceinline__ void store_grad(void* dst, int64_t i, float v) {
+    if constexpr (F32) static_cast<float*>(dst)[i] = v;
+    else static_cast<uint16_t*>(dst)[i] = (uint16_t)f32_to_bf16_bits(v);
+}
+
+// Dense form: ds1 / ds2 (n, h, nk) rows zeroed, then each sub-key's sum written by its first occurrence.
 template <bool F32>
 __global__ void __launch_bounds__(256) select_backward_kernel(const int64_t* idx, const float* w, const float* gw,
                                                               const void* gs, int64_t rows_nh, int nk, int knn,
@@ -288,61 +344,39 @@ __global__ void __launch_bounds__(256) select_backward_kernel(const int64_t* idx
     const int lane = lane_id();
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows_nh; row += warps) {
-        const int64_t o = row * knn + lane;
-        const bool on = lane < knn;
-        const float wj = on ? w[o] : 0.f;
-        float dl = 0.f;
-        if (gw) {
-            const float g = on ? gw[o] : 0.f;
-            const float dot = warp_sum(wj * g);
-            dl = wj * (g - dot);
-        }
-        if (gs && on) {
-            const float g2 = F32 ? static_cast<const float*>(gs)[o]
-                                 : bf16_bits_to_f32(static_cast<const uint16_t*>(gs)[o]);
-            dl = dl + g2;
-        }
-        int64_t full = on ? idx[o] : 0;
-        if (full < 0 || full >= (int64_t)nk * nk) full = 0, dl = 0.f;  // invalid index: contributes nothing
-        const float ds = F32 ? dl : round_bf16(dl);
-        const uint32_t a1 = (uint32_t)(full / nk), a2 = (uint32_t)(full % nk);
-        // zero both rows, then write the per-sub-key sums (first occurrence of a sub-key writes its sum)
+        const PairGrad g = pair_grad<F32>(idx, w, gw, gs, row, nk, knn, lane);
         const int64_t base = row * nk;
-        if constexpr (F32) {
-            for (int k = lane; k < nk; k += 32) {
-                static_cast<float*>(ds1)[base + k] = 0.f;
-                static_cast<float*>(ds2)[base + k] = 0.f;
-            }
-        } else {
-            for (int k = lane; k < nk; k += 32) {
-                static_cast<uint16_t*>(ds1)[base + k] = 0;
-                static_cast<uint16_t*>(ds2)[base + k] = 0;
-            }
+        for (int k = lane; k < nk; k += 32) {
+            store_grad<F32>(ds1, base + k, 0.f);
+            store_grad<F32>(ds2, base + k, 0.f);
         }
         __syncwarp();
-        float s1 = 0.f, s2 = 0.f;
-        bool first1 = on, first2 = on;
-        for (int j = 0; j < knn; j++) {
-            const uint32_t b1 = __shfl_sync(FULL, a1, j);
-            const uint32_t b2 = __shfl_sync(FULL, a2, j);
-            const float dj = __shfl_sync(FULL, ds, j);
-            if (b1 == a1) {
-                s1 = s1 + dj;
-                if (j < lane) first1 = false;
-            }
-            if (b2 == a2) {
-                s2 = s2 + dj;
-                if (j < lane) first2 = false;
-            }
-        }
-        if constexpr (F32) {
-            if (first1) static_cast<float*>(ds1)[base + a1] = s1;
-            if (first2) static_cast<float*>(ds2)[base + a2] = s2;
-        } else {
-            if (first1) static_cast<uint16_t*>(ds1)[base + a1] = (uint16_t)f32_to_bf16_bits(s1);
-            if (first2) static_cast<uint16_t*>(ds2)[base + a2] = (uint16_t)f32_to_bf16_bits(s2);
-        }
+        if (g.first1) store_grad<F32>(ds1, base + g.a1, g.s1);
+        if (g.first2) store_grad<F32>(ds2, base + g.a2, g.s2);
         __syncwarp();
+    }
+}
+
+// Sparse form: per (token, head, half) the knn selected sub-keys become the lookups of a value bag over the
+// sub-key table viewed as (h * 2 * nk, half) rows: on a sub-key's first occurrence, row (head * 2 + half) * nk +
+// sub-key with the sub-key's sum as weight; on later occurrences row -1, weight 0 (skipped by the bag). dq is
+// that bag over the keys; dkeys is the bag's row-sparse backward with the query halves as the output gradient.
+template <bool F32>
+__global__ void __launch_bounds__(256) select_grad_entries_kernel(const int64_t* idx, const float* w, const float* gw,
+                                                                  const void* gs, int64_t rows_nh, int heads, int nk,
+                                                                  int knn, int64_t* entry_rows, void* entry_w) {
+    const int lane = lane_id();
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows_nh; row += warps) {
+        const PairGrad g = pair_grad<F32>(idx, w, gw, gs, row, nk, knn, lane);
+        if (lane < knn) {
+            const int hh = (int)(row % heads);
+            const int64_t e1 = (row * 2 + 0) * knn + lane, e2 = (row * 2 + 1) * knn + lane;
+            entry_rows[e1] = g.first1 ? (int64_t)(hh * 2 + 0) * nk + g.a1 : -1;
+            entry_rows[e2] = g.first2 ? (int64_t)(hh * 2 + 1) * nk + g.a2 : -1;
+            store_grad<F32>(entry_w, e1, g.first1 ? g.s1 : 0.f);
+            store_grad<F32>(entry_w, e2, g.first2 ? g.s2 : 0.f);
+        }
     }
 }
 
@@ -464,5 +498,26 @@ extern "C" int smlm_subkey_scores_f32(const float* q, const float* keys, int64_t
     SMLM_CHECK_ARG(grid.y <= 65535, "subkey_scores_f32: too many tokens for one call (%lld)", (long long)n);
     subkey_scores_kernel<<<grid, 256, 0, as_stream(stream)>>>(q, keys, n, (int)h, (int)nk, (int)half, s1, s2);
     SMLM_LAUNCHED("subkey_scores_kernel");
+    return SMLM_OK;
+}
+
+extern "C" int smlm_select_grad_entries(const int64_t* indices, const float* weights, const float* grad_w,
+                                        const void* grad_scores, int score_dtype, int64_t n, int64_t h, int64_t nk,
+                                        int64_t knn, int64_t* entry_rows, void* entry_weights, void* stream) {
+    SMLM_CHECK_ARG(score_dtype == SMLM_F32 || score_dtype == SMLM_BF16, "select_grad_entries: fp32 or bf16 only");
+    SMLM_CHECK_ARG(n >= 0 && h > 0 && knn >= 1 && knn <= 32 && nk >= knn && nk <= 65536,
+                   "select_grad_entries: bad sizes");
+    if (n == 0) return SMLM_OK;
+    SMLM_CHECK_ARG(indices && weights && entry_rows && entry_weights, "select_grad_entries: null pointer");
+    const int64_t rows = n * h;
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, (int64_t)sm_count() * 16));
+    cudaStream_t st = as_stream(stream);
+    if (score_dtype == SMLM_F32)
+        select_grad_entries_kernel<true><<<blocks, 256, 0, st>>>(indices, weights, grad_w, grad_scores, rows, (int)h,
+                                                                 (int)nk, (int)knn, entry_rows, entry_weights);
+    else
+        select_grad_entries_kernel<false><<<blocks, 256, 0, st>>>(indices, weights, grad_w, grad_scores, rows, (int)h,
+                                                                  (int)nk, (int)knn, entry_rows, entry_weights);
+    SMLM_LAUNCHED("select_grad_entries_kernel");
     return SMLM_OK;
 }

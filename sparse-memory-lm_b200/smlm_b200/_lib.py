@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libs
 
 OK, ERR_INVALID, ERR_CUDA, ERR_WORKSPACE = 0, 1, 2, 3
 F32, BF16, F16, Q4 = 0, 1, 2, 3
+I32, I64 = 4, 5
 FLAG_INDEX_RANGE = 1
 FLAG_TIMEOUT = 4
 ROWRMS, ROWADAGRAD = 0, 1
@@ -26,8 +27,13 @@ SCORE_F32_EXACT, SCORE_BF16 = 0, 1
 # Kernel launches behind one call, for the benchmark's launch count (checked against the ncu launch list):
 # the backward = key build + radix sort (histogram, exclusive sum, one onesweep pass per 8 key bits at the
 # benchmark's 25-bit rows) + segment pass + fix-up; touched-row compaction = cub select (tile-state init + scan).
-BACKWARD_LAUNCHES = 1 + 6 + 2
 COMPACT_LAUNCHES = 2
+
+
+def backward_launches(rows):
+    """Launches of one smlm_bag_backward_rows call over a table of `rows` rows (sort keys carry rows + 1 values)."""
+    bits = max(1, int(rows).bit_length())
+    return 1 + 2 + (bits + 7) // 8 + 2
 
 _p, _i64, _i32, _f32, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
 
@@ -39,8 +45,8 @@ SIGNATURES = {
     "smlm_bag_infer": (_i32, [_p, _p, _i32, _p, _i32, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _i32, _p, _p]),
     "smlm_quantize_q4": (_i32, [_p, _i64, _i64, _p, _p, _p]),
     "smlm_bag_backward_workspace": (_sz, [_i64, _i64, _i64, _i64]),
-    "smlm_bag_backward_rows": (_i32, [_p, _p, _p, _i32, _p, _i32, _p, _p, _p, _i32, _p, _i64, _i64, _i64, _i64,
-                                      _p, _sz, _p, _p]),
+    "smlm_bag_backward_rows": (_i32, [_p, _i32, _p, _p, _i32, _p, _i32, _p, _p, _p, _i32, _p, _i64, _i64, _i64,
+                                      _i64, _p, _sz, _p, _p]),
     "smlm_touched_workspace": (_sz, [_i64]),
     "smlm_lazy_adam_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32,
                                    _p, _i32, _i32, _p, _sz, _p]),
@@ -50,9 +56,14 @@ SIGNATURES = {
     "smlm_zero_untouched": (_i32, [_p, _p, _i64, _i64, _p]),
     "smlm_pk_select": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
     "smlm_select_backward": (_i32, [_p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "smlm_select_grad_entries": (_i32, [_p, _p, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "smlm_subkey_scores_f32": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "smlm_score_select_workspace": (_sz, [_i64, _i64]),
     "smlm_score_select": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _sz, _p, _p]),
+    "smlm_shard_bag_forward": (_i32, [_p, _i32, _i64, _p, _i32, _p, _i32, _i64, _i64, _i64, _i64, _p, _i32, _p]),
+    "smlm_shard_bag_backward_rows": (_i32, [_p, _i32, _p, _i32, _i64, _p, _i32, _p, _i32, _p, _p, _p, _i32, _p,
+                                            _i64, _i64, _i64, _i64, _p, _sz, _p, _p]),
+    "smlm_slot_sum": (_i32, [_p, _i64, _i64, _p, _p]),
     "smlm_score_select_noalloc": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
 }
 

@@ -55,6 +55,44 @@ def select_backward(idx, w, g_w, g_scores, n_keys, dtype):
     return ds1, ds2
 
 
+def select_grad_entries(idx, w, g_w, g_scores, n_keys, dtype):
+    """Sparse selection gradient (N * H * 2, knn) lookups into the keys viewed as (H * 2 * n_keys, half): rows
+    (int64) and weights (score dtype), ds1 / ds2 of select_backward at each sub-key's first occurrence; later
+    occurrences are row -1, weight 0."""
+    dev = L.require_cuda(idx, w, g_w, g_scores)
+    N, H, knn = idx.shape
+    rows = torch.empty(N * H * 2, knn, dtype=torch.int64, device=dev)
+    ew = torch.empty(N * H * 2, knn, dtype=dtype, device=dev)
+    g_w = None if g_w is None else _contig(g_w.float())
+    g_scores = None if g_scores is None else _contig(g_scores.to(dtype))
+    with L.timed("select_grad_entries", 1):
+        rc = L.lib().smlm_select_grad_entries(L.ptr(_contig(idx)), L.ptr(_contig(w)), L.ptr(g_w), L.ptr(g_scores),
+                                              L.dtype_code(dtype), N, H, n_keys, knn, L.ptr(rows), L.ptr(ew),
+                                              L.stream(dev))
+    L.check(rc, "select_grad_entries")
+    return rows, ew
+
+
+def scoring_backward_sparse(q, keys, idx, w, g_w, g_scores, need_dq=True, need_dkeys=True):
+    """Gradients of q (N, H, 2 half) and keys (H, 2, n_keys, half) through the selection and the sub-key scoring
+    contraction, from the nonzero score gradients only: dq is a value bag over the keys, dkeys the row-sparse
+    bag backward with the query halves; both accumulate in fp32 and round once to the keys' dtype, as the
+    reference's autocast einsum backward does with its dense, mostly-zero (N, H, n_keys) gradients."""
+    H, _, NK, half = keys.shape
+    N = q.shape[0]
+    rows, ew = select_grad_entries(idx, w, g_w, g_scores, NK, keys.dtype)
+    table = _contig(keys).view(H * 2 * NK, half)
+    dq = dk = None
+    if need_dq:
+        dq = shard_bag_forward(rows, ew, table, 0, out_dtype=q.dtype, name="select_dq").view(N, H, 2 * half)
+    if need_dkeys:
+        acc = torch.zeros(H * 2 * NK, half, dtype=torch.float32, device=keys.device)
+        shard_bag_backward_rows(_contig(q).view(N * H * 2, half), rows, ew, table, 0, acc, None, want_gw=False,
+                                name="select_dkeys")
+        dk = acc.to(keys.dtype).view(H, 2, NK, half)
+    return dq, dk
+
+
 class PKSelect(torch.autograd.Function):
     """Differentiable pk_select (reference: kernels.py:240-266). Backward: softmax backward, the score gradient
     rounded to the score dtype, summed per sub-key in fp32 (selection order) and rounded once; dense
@@ -161,9 +199,9 @@ def score_select(q, keys, knn, dump=False):
 
 
 class ScoreSelect(torch.autograd.Function):
-    """Differentiable fused scoring + selection (bf16). Backward: the selection backward of PKSelect into dense
-    bf16 (N, H, n_keys) score gradients, then the scoring contraction's backward in bf16 (fp32 accumulate),
-    as the reference's autocast einsum backward does."""
+    """Differentiable fused scoring + selection (bf16). Backward: the selection backward of PKSelect restricted to
+    its nonzero sub-key gradients (scoring_backward_sparse), with the rounding of the reference's autocast
+    einsum backward (bf16 operands, fp32 accumulation, bf16 results)."""
 
     @staticmethod
     def forward(ctx, q, keys, knn):
@@ -175,20 +213,13 @@ class ScoreSelect(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_scores, g_idx, g_w):
         q, keys, idx, w = ctx.saved_tensors
-        half, nk = keys.shape[-1], keys.shape[-2]
-        ds1, ds2 = select_backward(idx, w, g_w, g_scores, nk, torch.bfloat16)
-        dq = dk = None
-        if ctx.needs_input_grad[0]:
-            dq = torch.cat([torch.einsum("nhk,hkd->nhd", ds1, keys[:, 0]),
-                            torch.einsum("nhk,hkd->nhd", ds2, keys[:, 1])], dim=-1)
-        if ctx.needs_input_grad[1]:
-            dk = torch.stack([torch.einsum("nhk,nhd->hkd", ds1, q[..., :half]),
-                              torch.einsum("nhk,nhd->hkd", ds2, q[..., half:])], dim=1)
+        dq, dk = scoring_backward_sparse(q, keys, idx, w, g_w, g_scores, ctx.needs_input_grad[0],
+                                         ctx.needs_input_grad[1])
         return dq, dk, None
 
 
 # ------------------------------------------------------------------------------------------ value bag
-def bag_forward(indices, weights, table, out_dtype=torch.float32):
+def bag_forward(indices, weights, table, out_dtype=torch.float32, name="bag_forward"):
     """out[n] = sum_k weights[n, k] * table[indices[n, k]] (fp32 accumulation); table fp32 / bf16
     (reference: kernels.py:229-237)."""
     dev = L.require_cuda(indices, weights, table)
@@ -198,7 +229,7 @@ def bag_forward(indices, weights, table, out_dtype=torch.float32):
     idx = _contig(indices.long())
     w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
     table = _contig(table)
-    with L.timed("bag_forward", 1):
+    with L.timed(name, 1):
         rc = L.lib().smlm_bag_forward(L.ptr(idx), L.ptr(w), L.dtype_code(w.dtype), L.ptr(table),
                                       L.dtype_code(table.dtype), N, K, table.shape[0], D, L.ptr(out),
                                       L.dtype_code(out_dtype), L.status_ptr(dev), L.stream(dev))
@@ -207,35 +238,109 @@ def bag_forward(indices, weights, table, out_dtype=torch.float32):
     return out
 
 
-def bag_backward_rows(grad_out, indices, weights, table, acc, touched, row_sqnorm=None, first_touch_writes=False):
-    """grad_out (N, D), indices / weights (N, K) -> per-sample-weight gradient (N, K) fp32;
+def bag_backward_rows(grad_out, indices, weights, table, acc, touched, row_sqnorm=None, first_touch_writes=False,
+                      want_gw=True):
+    """grad_out (N, D) fp32 / bf16, indices / weights (N, K) -> per-sample-weight gradient (N, K) fp32;
     acc[indices[n, k]] += weights[n, k] * grad_out[n] and touched[indices] = True, in place
     (reference: kernels.py:73-88). Deterministic: sorted rows, no float atomics.
-    acc / touched may be None (frozen table: only the weight gradient). row_sqnorm: optional fp32 (rows,) that
-    receives the squared norm of every accumulator row written. first_touch_writes: rows not yet touched are
-    written instead of accumulated (for accumulators whose untouched rows count as zero)."""
+    acc / touched may be None (frozen table: only the weight gradient); want_gw=False skips the weight gradient
+    (returns None; table may then be None). row_sqnorm: optional fp32 (rows,) that receives the squared norm of
+    every accumulator row written. first_touch_writes: rows not yet touched are written instead of accumulated
+    (for accumulators whose untouched rows count as zero)."""
     dev = L.require_cuda(grad_out, indices, weights, table, acc, touched)
     N, K = indices.shape
-    D = table.shape[1]
-    if acc is not None and (acc.dtype != torch.float32 or not acc.is_contiguous() or acc.shape != table.shape):
+    D = grad_out.shape[1]
+    rows = acc.shape[0] if acc is not None else table.shape[0]
+    if acc is not None and (acc.dtype != torch.float32 or not acc.is_contiguous() or acc.shape[1] != D or
+                            (table is not None and acc.shape != table.shape)):
         raise ValueError("bag_backward_rows: acc must be a contiguous fp32 tensor shaped like the table")
     if touched is not None and (touched.dtype not in (torch.bool, torch.uint8) or not touched.is_contiguous()):
         raise ValueError("bag_backward_rows: touched must be a contiguous bool mask")
-    g = _contig(grad_out.float())
+    if table is None and want_gw:
+        raise ValueError("bag_backward_rows: the weight gradient needs the table")
+    g = _contig(grad_out if grad_out.dtype in (torch.float32, torch.bfloat16) else grad_out.float())
     idx = _contig(indices.long())
     w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
-    table = _contig(table)
-    gw = torch.empty(N, K, dtype=torch.float32, device=dev)
-    ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, K, table.shape[0], D), dev)
-    with L.timed("bag_backward_rows", L.BACKWARD_LAUNCHES):
-        rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.ptr(idx), L.ptr(w), L.dtype_code(w.dtype), L.ptr(table),
-                                            L.dtype_code(table.dtype), L.ptr(acc), L.ptr(touched), L.ptr(row_sqnorm),
-                                            L.BWD_FIRST_TOUCH_WRITES if first_touch_writes else 0, L.ptr(gw), N, K,
-                                            table.shape[0], D, L.ptr(ws), ws.numel(), L.status_ptr(dev),
-                                            L.stream(dev))
+    table = _contig(table) if table is not None else None
+    gw = torch.empty(N, K, dtype=torch.float32, device=dev) if want_gw else None
+    flags = L.BWD_FIRST_TOUCH_WRITES if first_touch_writes else 0
+    ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, K, rows, D), dev)
+    t_code = L.dtype_code(table.dtype) if table is not None else L.F32
+    with L.timed("bag_backward_rows", L.backward_launches(rows)):
+        rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), L.ptr(w),
+                                            L.dtype_code(w.dtype), L.ptr(table), t_code, L.ptr(acc), L.ptr(touched),
+                                            L.ptr(row_sqnorm), flags, L.ptr(gw), N, K, rows, D, L.ptr(ws),
+                                            ws.numel(), L.status_ptr(dev), L.stream(dev))
     L.check(rc, "bag_backward_rows")
     L.after(dev, "bag_backward_rows")
     return gw
+
+
+# --------------------------------------------------------------------------------- row-sharded value table
+def _index_code(idx):
+    if idx.dtype == torch.int32:
+        return L.I32
+    if idx.dtype == torch.int64:
+        return L.I64
+    raise ValueError(f"row indices must be int32 or int64, got {idx.dtype}")
+
+
+def shard_bag_forward(indices, weights, table_shard, row_base, out_dtype=torch.float32, name="shard_bag_forward"):
+    """Partial value bag (N, D) (fp32 accumulation, out_dtype fp32 / bf16) of the lookups whose global row lies in
+    [row_base, row_base + rows of table_shard); other lookups are skipped (they belong to other ranks' shards)."""
+    dev = L.require_cuda(indices, weights, table_shard)
+    N, Kk = indices.shape
+    rows, D = table_shard.shape
+    out = torch.empty(N, D, dtype=out_dtype, device=dev)
+    idx = _contig(indices)
+    w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
+    t = _contig(table_shard)
+    with L.timed(name, 1):
+        rc = L.lib().smlm_shard_bag_forward(L.ptr(idx), _index_code(idx), int(row_base), L.ptr(w),
+                                            L.dtype_code(w.dtype), L.ptr(t) if rows else None,
+                                            L.dtype_code(t.dtype), N, Kk, rows, D, L.ptr(out),
+                                            L.dtype_code(out_dtype), L.stream(dev))
+    L.check(rc, "shard_bag_forward")
+    return out
+
+
+def shard_bag_backward_rows(grad_out, indices, weights, table_shard, row_base, acc, touched, row_sqnorm=None,
+                            first_touch_writes=False, want_gw=True, name="shard_bag_backward_rows"):
+    """bag_backward_rows restricted to the lookups in this shard's rows: acc / touched / row_sqnorm hold the
+    shard's local rows; returns the weight gradient (N, K) fp32, 0 for other shards' lookups (None when
+    want_gw=False)."""
+    dev = L.require_cuda(grad_out, indices, weights, table_shard, acc, touched)
+    N, Kk = indices.shape
+    rows, D = table_shard.shape
+    if acc is not None and (acc.dtype != torch.float32 or not acc.is_contiguous() or acc.shape != table_shard.shape):
+        raise ValueError("shard_bag_backward_rows: acc must be a contiguous fp32 tensor shaped like the shard")
+    g = _contig(grad_out if grad_out.dtype in (torch.float32, torch.bfloat16) else grad_out.float())
+    idx = _contig(indices)
+    w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
+    t = _contig(table_shard)
+    gw = torch.empty(N, Kk, dtype=torch.float32, device=dev) if want_gw else None
+    ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, Kk, rows, D), dev)
+    flags = L.BWD_FIRST_TOUCH_WRITES if first_touch_writes else 0
+    with L.timed(name, L.backward_launches(rows)):
+        rc = L.lib().smlm_shard_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), _index_code(idx),
+                                                  int(row_base), L.ptr(w), L.dtype_code(w.dtype),
+                                                  L.ptr(t) if rows else None, L.dtype_code(t.dtype), L.ptr(acc),
+                                                  L.ptr(touched), L.ptr(row_sqnorm), flags, L.ptr(gw), N, Kk, rows, D,
+                                                  L.ptr(ws), ws.numel(), L.status_ptr(dev), L.stream(dev))
+    L.check(rc, "shard_bag_backward_rows")
+    L.after(dev, "shard_bag_backward_rows")
+    return gw
+
+
+def slot_sum(x):
+    """x (S, M) fp32 -> (M,) the sum over slots in slot order."""
+    dev = L.require_cuda(x)
+    x = _contig(x.float())
+    out = torch.empty(x.shape[1:], dtype=torch.float32, device=dev)
+    with L.timed("slot_sum", 1):
+        rc = L.lib().smlm_slot_sum(L.ptr(x), x.shape[0], out.numel(), L.ptr(out), L.stream(dev))
+    L.check(rc, "slot_sum")
+    return out
 
 
 def quantize_q4(table, chunk=None):

@@ -15,10 +15,12 @@ PyTorch modules (dense host code).
 import math
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 from torch import nn
 
 from . import kernels as K
+from .sharded import RowShard, sharded_embedding_bag
 from .sparse_values import row_sparse_embedding_bag
 
 IMPLS = ("cuda", "triton", "torch")
@@ -28,7 +30,10 @@ class ProductKeyMemory(nn.Module):
     def __init__(self, d_in, d_out, n_keys=512, heads=4, knn=32, k_dim=256, v_dim=-1,
                  query_norm="batchnorm", swilu=True, value_impl="embedding_bag",
                  keys_weight_decay=True, score_scale="none", score_scale_init=1.0, shared_values=None,
-                 value_grad="dense", impl="cuda"):
+                 value_grad="dense", impl="cuda", shard_group=None):
+        """shard_group (no counterpart in the reference): a torch.distributed process group over which the value
+        table is row-sharded (one process per GPU; values.weight then holds this rank's rows only, and the
+        lookups are exchanged with the other ranks). Needs value_grad="row_sparse"."""
         super().__init__()
         assert k_dim % 2 == 0 and knn <= n_keys
         self.d_in, self.d_out = d_in, d_out
@@ -65,11 +70,20 @@ class ProductKeyMemory(nn.Module):
             self.query_norm = None
         else:
             raise ValueError(query_norm)
+        self.shard = self.shard_group = None
+        if shard_group is not None and dist.get_world_size(shard_group) > 1:
+            if value_grad != "row_sparse" or shared_values is not None:
+                raise ValueError("a row-sharded value table needs value_grad='row_sparse' and its own values")
+            self.shard = RowShard(self.size, dist.get_world_size(shard_group), dist.get_rank(shard_group))
+            self.shard_group = shard_group
         if shared_values is not None:
             assert shared_values.weight.shape == (self.size, self.v_dim)
             self.values = shared_values
         else:
-            self.values = nn.Embedding(self.size, self.v_dim)
+            self.values = nn.Embedding(self.shard.count if self.shard else self.size, self.v_dim)
+        if self.shard is not None:
+            self.values.weight.row_shard = self.shard
+            self.values.weight.shard_group = shard_group
         if swilu:
             self.swilu_proj = nn.Linear(d_in, self.v_dim)
             self.value_proj = nn.Linear(self.v_dim, d_out)
@@ -124,6 +138,8 @@ class ProductKeyMemory(nn.Module):
     def read_values(self, indices, weights):
         """indices, weights (N, heads*knn) -> (N, v_dim) (reference: pkm.py:138-148)."""
         w = self.values.weight
+        if self.shard is not None:
+            return sharded_embedding_bag(indices, weights, w, self.shard, self.shard_group)
         if self.value_grad == "row_sparse":
             return row_sparse_embedding_bag(indices, weights, w, self.impl)
         if self.value_impl == "embedding_bag":
@@ -136,7 +152,7 @@ class ProductKeyMemory(nn.Module):
         if not x.is_cuda:
             raise ValueError("ProductKeyMemory of smlm_b200 runs on CUDA only (no CPU fallback)")
         if (getattr(self, "decode_graph", False) and x.shape[0] == 1 and not self.record
-                and not torch.is_grad_enabled()):
+                and not torch.is_grad_enabled() and self.shard is None):
             return self._graph_forward(x).view(*shape[:-1], self.d_out)
         return self._forward(x).view(*shape[:-1], self.d_out)
 
@@ -194,7 +210,7 @@ class ProductKeyMemory(nn.Module):
             self.last_indices = indices.detach()
             self.last_scores = scores.detach()
             self.last_weights = weights.detach()
-        if not torch.is_grad_enabled() and self.swilu and autocast_bf16:
+        if not torch.is_grad_enabled() and self.swilu and autocast_bf16 and self.shard is None:
             # inference: value bag on the inference table (fp32 / bf16 / q4) with the swilu product and the
             # bf16 cast fused (reference: pkm.py:213-224)
             pre = self.swilu_proj(x)

@@ -1,0 +1,181 @@
+"""Row-sharded value table over the GPUs of one process group (one process per GPU, NCCL).
+
+The reference runs the product-key memory on one device. Here the value table, its row-sparse gradient store and
+its lazy-Adam state are split into contiguous row ranges, one per rank (owner = row // ceil(rows / world)); the
+keys, the query projection and everything else stay replicated and data-parallel. Tokens stay on their rank:
+
+  forward   every rank scores and selects its own tokens; the lookups (int32 global row, weight) are all-gathered;
+            each owner computes, for every rank's tokens, the partial bag over the lookups in its rows
+            (smlm_shard_bag_forward); an all-to-all returns each rank the partial bags of its tokens, which are
+            summed in owner order (smlm_slot_sum).
+  backward  the output gradients are all-gathered; each owner runs the deterministic row-sparse backward over
+            the lookups in its rows (its accumulator, touched mask and squared row norms; the weight gradient
+            of its lookups, 0 for the others); an all-to-all returns the weight gradients, summed in owner order
+            (each lookup has exactly one nonzero term, so the sum is exact).
+  clip      the squared norm of every rank's accumulator rows is all-gathered and summed in rank order.
+  step      each rank's LazyRowAdam updates its own rows only.
+
+A P-rank step over batches x_0 .. x_{P-1} is the one-rank step over their concatenation (row gradients summed over
+all tokens; the replicated parameters' gradients summed with allreduce_replicated_grads); only the fp32 summation
+order of the bag (owner partials) and of the row sums differ. Every rank must pass the same number of tokens.
+Data-path exchange volume per rank and step (N tokens, K lookups, D columns, P ranks): lookups 8 N K P,
+partial bags and output gradients 2 x 4 N D P, weight gradients 4 N K P bytes received.
+"""
+import torch
+import torch.distributed as dist
+
+from . import kernels as K
+
+
+class RowShard:
+    """Rank `rank`'s contiguous row range of a `rows`-row table split over `world` ranks: rows
+    [base, base + count), ceil(rows / world) per rank (the last ranks may hold fewer, or none)."""
+
+    def __init__(self, rows, world, rank):
+        if world < 1 or not 0 <= rank < world or rows < 0:
+            raise ValueError(f"bad shard: rows={rows}, world={world}, rank={rank}")
+        if rows >= 2 ** 31:
+            raise ValueError("row-sharded tables exchange int32 row indices: rows must be below 2^31")
+        self.rows, self.world, self.rank = rows, world, rank
+        self.per = -(-rows // world) if rows else 0
+        self.base = min(rows, rank * self.per)
+        self.count = max(0, min(rows, self.base + self.per) - self.base)
+
+    def owner(self, row):
+        return row // self.per
+
+    def take(self, full):
+        """This rank's rows of a full-table tensor."""
+        return full[self.base:self.base + self.count]
+
+    def __repr__(self):
+        return f"RowShard(rows={self.rows}, world={self.world}, rank={self.rank}, base={self.base}, count={self.count})"
+
+
+class CudaShardOps:
+    """The owner-side kernels (libsmlm_b200.so)."""
+
+    def bag_forward(self, idx, w, table, base):
+        return K.shard_bag_forward(idx, w, table, base)
+
+    def bag_backward(self, g, idx, w, table, base, store):
+        if store is None:
+            return K.shard_bag_backward_rows(g, idx, w, table, base, None, None)
+        return K.shard_bag_backward_rows(g, idx, w, table, base, store._acc, store._touched,
+                                         row_sqnorm=store._sqnorm if store.clean else None,
+                                         first_touch_writes=store.clean)
+
+    def slot_sum(self, x):
+        return K.slot_sum(x)
+
+
+CUDA_OPS = CudaShardOps()
+
+
+def _all_gather(x, group, world):
+    out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+def _all_to_all(x, group):
+    out = torch.empty_like(x)
+    dist.all_to_all_single(out, x.contiguous(), group=group)
+    return out
+
+
+class _ShardedBag(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, weights, indices, table, store, shard, group, ops):
+        P = shard.world
+        N, Kk = indices.shape
+        w = weights.reshape(N, Kk).to(table.dtype)
+        all_idx = _all_gather(indices.to(torch.int32), group, P)
+        all_w = _all_gather(w, group, P)
+        part = ops.bag_forward(all_idx, all_w, table, shard.base)            # (P N, D): this owner's partials
+        D = part.shape[1]
+        out = ops.slot_sum(_all_to_all(part, group).view(P, N * D)).view(N, D)
+        ctx.save_for_backward(all_idx, all_w)
+        ctx.table, ctx.store, ctx.shard, ctx.group, ctx.ops = table, store, shard, group, ops
+        ctx.wshape, ctx.wdtype = weights.shape, weights.dtype
+        return out.to(table.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        all_idx, all_w = ctx.saved_tensors
+        shard, group, ops = ctx.shard, ctx.group, ctx.ops
+        P = shard.world
+        N, Kk = all_idx.shape[0] // P, all_idx.shape[1]
+        g = grad_out.contiguous()
+        if g.dtype not in (torch.float32, torch.bfloat16):
+            g = g.float()
+        all_g = _all_gather(g, group, P)
+        gw_part = ops.bag_backward(all_g, all_idx, all_w, ctx.table, shard.base, ctx.store)   # (P N, K)
+        gw = ops.slot_sum(_all_to_all(gw_part, group).view(P, N * Kk)).view(N, Kk)
+        ctx.table = ctx.store = ctx.ops = None
+        return gw.view(ctx.wshape).to(ctx.wdtype), None, None, None, None, None, None
+
+
+def sharded_embedding_bag(indices, weights, table, shard, group, ops=None, store=None):
+    """sum_j weights[:, j] * V[indices[:, j]] for a table V whose rows [shard.base, shard.base + shard.count) are
+    `table` on this rank; row gradients go into the shard's RowStore (`store`, default table.row_store).
+    Collective: every rank of `group` calls it with the same token count."""
+    from .sparse_values import row_store
+    ops = ops or CUDA_OPS
+    if indices.ndim != 2 or weights.shape[:1] != indices.shape[:1]:
+        raise ValueError("sharded_embedding_bag: indices (N, K) and weights (N, K) expected")
+    if table.shape[0] != shard.count:
+        raise ValueError(f"table has {table.shape[0]} rows but the shard holds {shard.count}")
+    if store is None and torch.is_grad_enabled() and table.requires_grad:
+        store = row_store(table)
+    if not torch.is_grad_enabled():
+        with torch.no_grad():
+            return _ShardedBag.forward(_NoCtx(), weights, indices, table, None, shard, group, ops)
+    return _ShardedBag.apply(weights, indices, table, store, shard, group, ops)
+
+
+class _NoCtx:
+    """Stand-in autograd context for the no-grad forward."""
+
+    def save_for_backward(self, *t):
+        pass
+
+
+def replicated_params(module):
+    """Parameters that every rank holds in full (everything but row-sharded value tables)."""
+    return [p for p in module.parameters() if getattr(p, "row_shard", None) is None]
+
+
+def allreduce_replicated_grads(module, group=None):
+    """Sum the replicated parameters' gradients over the ranks (one flat NCCL all-reduce)."""
+    grads = [p.grad for p in replicated_params(module) if p.grad is not None]
+    if not grads:
+        return
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    dist.all_reduce(flat, group=group)
+    off = 0
+    for g in grads:
+        g.copy_(flat[off:off + g.numel()].view_as(g))
+        off += g.numel()
+
+
+def sharded_sq_norm(local_sq, group, world):
+    """Sum over ranks, in rank order, of a 0-d fp32 device tensor (deterministic on every rank)."""
+    parts = _all_gather(local_sq.reshape(1).float(), group, world)
+    total = parts[0]
+    for i in range(1, world):
+        total = total + parts[i]
+    return total.reshape(())
+
+
+def broadcast_replicated(module, group=None, src=0):
+    """Give every rank rank `src`'s copy of the replicated parameters and buffers (one flat broadcast)."""
+    ts = [p.data for p in replicated_params(module)] + [b for b in module.buffers() if b.is_floating_point()]
+    if not ts:
+        return
+    flat = torch.cat([t.reshape(-1).float() for t in ts])
+    dist.broadcast(flat, src=dist.get_global_rank(group, src) if group is not None else src, group=group)
+    off = 0
+    for t in ts:
+        t.copy_(flat[off:off + t.numel()].view_as(t))
+        off += t.numel()

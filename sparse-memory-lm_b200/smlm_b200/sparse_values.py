@@ -152,7 +152,19 @@ def clip_row_sparse(tables, max_norm):
     if not tables:
         return None
     norms = [row_store(t).norm() for t in tables]
-    total = torch.linalg.vector_norm(torch.stack(norms))
+    sharded = [i for i, t in enumerate(tables) if getattr(t, "row_shard", None) is not None]
+    if sharded:
+        # row-sharded tables: each rank holds part of the rows; their squared norms are summed over the ranks
+        from .sharded import sharded_sq_norm
+        t0 = tables[sharded[0]]
+        sq = torch.stack([norms[i].float() for i in sharded]).square().sum()
+        total_sq = sharded_sq_norm(sq, t0.shard_group, t0.row_shard.world)
+        rest = [norms[i].float() for i in range(len(tables)) if i not in sharded]
+        if rest:
+            total_sq = total_sq + torch.stack(rest).square().sum()
+        total = total_sq.sqrt()
+    else:
+        total = torch.linalg.vector_norm(torch.stack(norms))
     coef = torch.clamp(max_norm / (total + 1e-6), max=1.0)
     for t in tables:
         row_store(t).grad_scale = coef

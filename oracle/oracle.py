@@ -39,6 +39,7 @@ def lib():
         L.orc_quantize_q4.argtypes = [_p, _i64, _i64, _p, _p]
         L.orc_bag_infer.argtypes = [_p, _p, _p, _i32, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _i32]
         L.orc_lazy_adam.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32, _f32]
+        L.orc_lazy_adam_lowmem.argtypes = [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i32] + [_f32] * 8
         L.orc_rowwise.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _f32, _i32, _f32, _f32, _f32]
         L.orc_touched_norm.argtypes = [_p, _p, _i64, _i64]
         L.orc_touched_norm.restype = ctypes.c_double
@@ -185,6 +186,16 @@ def lazy_adam(p, m, v, acc, touched, grad_scale, step, lr, beta1, beta2, eps):
     rows, d = p.shape
     lib().orc_lazy_adam(_ptr(p), _ptr(m), _ptr(v), _ptr(acc), _ptr(touched), rows, d, grad_scale,
                         s["one_minus_b1"], s["b2"], s["one_minus_b2"], s["bc2_sqrt"], eps, s["neg_step_size"])
+
+
+def lazy_adam_lowmem(p, m, v, m_scale, v_scale, acc, touched, grad_scale, step, lr, beta1, beta2, eps, int8):
+    """In place. bf16: m, v uint16 bit arrays; int8: m int8, v uint8 codes with fp32 row scales."""
+    import math
+    rows, d = p.shape
+    lib().orc_lazy_adam_lowmem(_ptr(p), _ptr(m), _ptr(v), _ptr(m_scale) if int8 else None,
+                               _ptr(v_scale) if int8 else None, _ptr(acc), _ptr(touched), rows, d, int(int8),
+                               grad_scale, beta1, beta2, 1 - beta1, 1 - beta2, eps, lr / (1 - beta1 ** step),
+                               math.sqrt(1 - beta2 ** step))
 
 
 def ref_lazy_adam(p, m, v, acc, touched, grad_scale, step, lr, beta1, beta2, eps, threads=1):

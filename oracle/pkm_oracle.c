@@ -13,7 +13,8 @@
  *   - bag:      smlm/sparse_values.py:66-85 / kernels.py:179-194 (sum_j w_j * table[idx_j]), fmaf over j;
  *   - backward: smlm/sparse_values.py:88-107 / kernels.py:34-88: gw = <grad_out, row>, acc[row] += sum of
  *               w * grad_out over the row's lookups in position order, touched[row] = 1;
- *   - lazy Adam: smlm/sparse_values.py:270-305 with the operation order of smlm/host_rows.c:63-80;
+ *   - lazy Adam: smlm/sparse_values.py:270-305 with the operation order of smlm/host_rows.c:63-80; compact
+ *               (bf16 / int8) moments: sparse_values.py:193-255 and kernels.py:445-495;
  *   - row-wise: smlm/row_optim.py:1-15, 168-201 with the formulas of smlm/host_rows.c:84-117;
  *   - select backward: smlm/kernels.py:253-266; inference bag + q4: kernels.py:280-378.
  */
@@ -297,6 +298,68 @@ void orc_lazy_adam(float *p, float *m, float *v, float *acc, uint8_t *touched, i
         }
         touched[r] = 0;
     }
+}
+
+/* Lazy Adam with compact moments (smlm/sparse_values.py:193-255 torch path, kernels.py:445-495 kernel):
+ * int8 = 0: bf16 m, v (uint16 bits); int8 = 1: int8 m codes, uint8 v codes, fp32 row scales. The update runs
+ * in fp32 on the decoded moments, one rounding per operation; stores round to nearest even (rintf under the
+ * default rounding mode); a positive v never gets code 0. */
+static float sign_one(float x) { return x < 0.0f ? -1.0f : 1.0f; }
+
+void orc_lazy_adam_lowmem(float *p, void *m_state, void *v_state, float *m_scale, float *v_scale, float *acc,
+                          uint8_t *touched, int64_t rows, int64_t d, int int8, float grad_scale, float b1, float b2,
+                          float one_minus_b1, float one_minus_b2, float eps, float step_size, float bc2_sqrt) {
+    float *mn = malloc(sizeof(float) * (size_t)(d ? d : 1)), *vn = malloc(sizeof(float) * (size_t)(d ? d : 1));
+    for (int64_t r = 0; r < rows; r++) {
+        if (!touched[r]) continue;
+        float ms = 0.0f, vs = 0.0f;
+        for (int64_t c = 0; c < d; c++) {
+            const int64_t o = r * d + c;
+            const float g = acc[o] * grad_scale;
+            float m, v;
+            if (int8) {
+                const float mc = (float)((int8_t *)m_state)[o] / 127.0f;
+                m = sign_one(mc) * mc * mc * m_scale[r];
+                v = (float)((uint8_t *)v_state)[o] / 255.0f * v_scale[r];
+                v = v * v;
+                v = v * v;
+            } else {
+                m = bf16_f32(((uint16_t *)m_state)[o]);
+                v = bf16_f32(((uint16_t *)v_state)[o]);
+            }
+            m = b1 * m + one_minus_b1 * g;
+            v = b2 * v + one_minus_b2 * g * g;
+            const float denom = sqrtf(v) / bc2_sqrt + eps;
+            p[o] = p[o] - step_size * m / denom;
+            mn[c] = m;
+            vn[c] = v;
+            if (fabsf(m) > ms) ms = fabsf(m);
+            if (sqrtf(sqrtf(v)) > vs) vs = sqrtf(sqrtf(v));
+            acc[o] = 0.0f;
+        }
+        for (int64_t c = 0; c < d; c++) {
+            const int64_t o = r * d + c;
+            if (int8) {
+                float mq = sqrtf(fabsf(mn[c]) / (ms > 0.0f ? ms : 1.0f));
+                mq = rintf(fminf(fmaxf(sign_one(mn[c]) * mq * 127.0f, -127.0f), 127.0f));
+                float vq = sqrtf(sqrtf(vn[c])) / (vs > 0.0f ? vs : 1.0f) * 255.0f;
+                vq = rintf(fminf(fmaxf(vq, 0.0f), 255.0f));
+                vq = vn[c] > 0.0f ? fmaxf(vq, 1.0f) : 0.0f;
+                ((int8_t *)m_state)[o] = (int8_t)mq;
+                ((uint8_t *)v_state)[o] = (uint8_t)vq;
+            } else {
+                ((uint16_t *)m_state)[o] = f32_bf16(mn[c]);
+                ((uint16_t *)v_state)[o] = f32_bf16(vn[c]);
+            }
+        }
+        if (int8) {
+            m_scale[r] = ms;
+            v_scale[r] = vs;
+        }
+        touched[r] = 0;
+    }
+    free(mn);
+    free(vn);
 }
 
 /* kind 0 rowrms, 1 rowadagrad (row_optim.py module docstring; host_rows.c:84-117) */

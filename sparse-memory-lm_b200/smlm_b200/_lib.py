@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libs
 
 OK, ERR_INVALID, ERR_CUDA, ERR_WORKSPACE = 0, 1, 2, 3
 F32, BF16, F16, Q4 = 0, 1, 2, 3
-I32, I64 = 4, 5
+I32, I64, I8 = 4, 5, 6
 FLAG_INDEX_RANGE = 1
 FLAG_TIMEOUT = 4
 ROWRMS, ROWADAGRAD = 0, 1
@@ -50,6 +50,8 @@ SIGNATURES = {
     "smlm_touched_workspace": (_sz, [_i64]),
     "smlm_lazy_adam_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32,
                                    _p, _i32, _i32, _p, _sz, _p]),
+    "smlm_lazy_adam_lowmem_step": (_i32, [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32,
+                                          _f32, _f32, _f32, _f32, _p, _i32, _i32, _p, _sz, _p]),
     "smlm_rowwise_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _i32, _f32, _f32, _f32, _i32, _p, _sz,
                                  _p]),
     "smlm_touched_norm": (_i32, [_p, _p, _p, _i64, _i64, _p, _p, _sz, _p]),

@@ -432,6 +432,42 @@ def lazy_adam_step(param, exp_avg, exp_avg_sq, acc, touched, grad_scale, step, l
     del keep
 
 
+def lazy_adam_lowmem_step(param, exp_avg, exp_avg_sq, exp_avg_scale, exp_avg_sq_scale, acc, touched, grad_scale,
+                          step, lr, beta1, beta2, eps, value_copy=None, keep_acc=False):
+    """In-place lazy Adam over the touched rows with compact moments (reference: kernels.py:498-515): bf16
+    exp_avg / exp_avg_sq, or int8 / uint8 codes with fp32 row scales (exp_avg_scale, exp_avg_sq_scale given).
+    Same arguments and effects as lazy_adam_step otherwise."""
+    dev = L.require_cuda(param, exp_avg, exp_avg_sq, exp_avg_scale, exp_avg_sq_scale, acc, touched, value_copy)
+    rows, D = param.shape
+    for t in (param, acc):
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.shape != param.shape:
+            raise ValueError("lazy_adam_lowmem_step: param and acc must be contiguous fp32 of one shape")
+    if exp_avg.dtype == torch.int8 and exp_avg_sq.dtype == torch.uint8:
+        code = L.I8
+        for t in (exp_avg_scale, exp_avg_sq_scale):
+            if t is None or t.dtype != torch.float32 or t.shape != (rows,) or not t.is_contiguous():
+                raise ValueError("lazy_adam_lowmem_step: int8 moments need fp32 (rows,) scales")
+    elif exp_avg.dtype == torch.bfloat16 and exp_avg_sq.dtype == torch.bfloat16:
+        code = L.BF16
+    else:
+        raise ValueError("lazy_adam_lowmem_step: moments must be bf16 / bf16 or int8 / uint8")
+    for t in (exp_avg, exp_avg_sq):
+        if not t.is_contiguous() or t.shape != param.shape:
+            raise ValueError("lazy_adam_lowmem_step: moments must be contiguous and shaped like the table")
+    sp, sf, keep = _scale_args(grad_scale, dev)
+    bc1 = 1 - beta1 ** step
+    bc2 = 1 - beta2 ** step
+    ws = L.workspace(L.lib().smlm_touched_workspace(rows), dev)
+    with L.timed("lazy_adam_lowmem_step", L.COMPACT_LAUNCHES + 1):
+        rc = L.lib().smlm_lazy_adam_lowmem_step(
+            L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(exp_avg_scale), L.ptr(exp_avg_sq_scale), code,
+            L.ptr(acc), L.ptr(touched), sp, sf, rows, D, beta1, beta2, 1 - beta1, 1 - beta2, eps, lr / bc1,
+            math.sqrt(bc2), L.ptr(value_copy), L.dtype_code(value_copy.dtype) if value_copy is not None else L.F32,
+            L.STEP_KEEP_ACC if keep_acc else 0, L.ptr(ws), ws.numel(), L.stream(dev))
+    L.check(rc, "lazy_adam_lowmem_step")
+    del keep
+
+
 def rowwise_step(param, acc, touched, v, n, grad_scale, lr, beta2, eps, kind, keep_acc=False):
     """Row-wise rowrms / rowadagrad step over the touched rows, in place; accumulator rows zeroed, mask cleared
     (reference: row_optim.py:168-201, formulas of host_rows.c:84-117)."""

@@ -176,6 +176,10 @@ class LazyRowAdam(torch.optim.Optimizer):
     their Adam state bit-for-bit (global step count for bias correction, as torch SparseAdam / TF LazyAdam).
     One fused kernel per table reads only the touched rows (reference: sparse_values.py:154-362).
 
+    state_dtype="bf16" / "int8" keeps compact moments (reference: sparse_values.py:163-168, kernels.py:445-515):
+    bf16 exp_avg / exp_avg_sq, or int8 signed-square-root exp_avg and uint8 fourth-root exp_avg_sq codes with one
+    fp32 scale per row each (exp_avg_scale, exp_avg_sq_scale); the update runs in fp32 on the decoded moments.
+
     value_copy_dtype=torch.bfloat16 keeps a bf16 copy of each table (`table.value_copy`) that the step refreshes
     for the updated rows: the forward can read the copy (half the gather bytes) while the fp32 table stays the
     master."""
@@ -184,12 +188,14 @@ class LazyRowAdam(torch.optim.Optimizer):
                  state_dtype="fp32", value_copy_dtype=None):
         params = list(params)
         _check_impl(impl)
-        if state_dtype != "fp32":
-            if state_dtype in ("bf16", "int8"):
-                raise NotImplementedError("compact LazyRowAdam states (bf16 / int8) are not built yet")
+        if state_dtype not in ("fp32", "bf16", "int8"):
             raise ValueError(f"unknown state_dtype: {state_dtype}")
-        if any(not p.is_cuda or p.dtype != torch.float32 or p.ndim != 2 or not p.is_contiguous() for p in params):
-            raise ValueError("LazyRowAdam needs contiguous fp32 CUDA tables")
+        if any(p.dtype != torch.float32 or p.ndim != 2 or not p.is_contiguous() or p.shape[1] == 0 for p in params):
+            raise ValueError("LazyRowAdam needs contiguous fp32 tables with nonzero width (2-D, float32)")
+        if not 0 <= lr or not 0 <= eps or not all(0 <= b < 1 for b in betas):
+            raise ValueError("invalid LazyRowAdam learning rate, epsilon or betas")
+        if any(not p.is_cuda for p in params):
+            raise ValueError("LazyRowAdam of this build runs on CUDA tables only (no CPU fallback)")
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=0.0))
         for g in self.param_groups:
             g["name"] = name
@@ -205,8 +211,14 @@ class LazyRowAdam(torch.optim.Optimizer):
         state = self.state[p]
         if not state:
             state["step"] = torch.zeros((), dtype=torch.float32)
-            state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
-            state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            int8 = self.state_dtype == "int8"
+            mdt = {"fp32": torch.float32, "bf16": torch.bfloat16, "int8": torch.int8}[self.state_dtype]
+            vdt = torch.uint8 if int8 else mdt
+            state["exp_avg"] = torch.zeros_like(p, dtype=mdt, memory_format=torch.contiguous_format)
+            state["exp_avg_sq"] = torch.zeros_like(p, dtype=vdt, memory_format=torch.contiguous_format)
+            if int8:
+                state["exp_avg_scale"] = torch.zeros(p.shape[0], dtype=torch.float32, device=p.device)
+                state["exp_avg_sq_scale"] = torch.zeros(p.shape[0], dtype=torch.float32, device=p.device)
         return state
 
     @torch.no_grad()
@@ -217,9 +229,15 @@ class LazyRowAdam(torch.optim.Optimizer):
                 st = row_store(p)
                 state = self._state(p)
                 state["step"] += 1
-                K.lazy_adam_step(p, state["exp_avg"], state["exp_avg_sq"], st._acc, st._touched, st.grad_scale,
-                                 int(state["step"]), group["lr"], b1, b2, group["eps"],
-                                 value_copy=getattr(p, "value_copy", None), keep_acc=st.clean)
+                if self.state_dtype == "fp32":
+                    K.lazy_adam_step(p, state["exp_avg"], state["exp_avg_sq"], st._acc, st._touched,
+                                     st.grad_scale, int(state["step"]), group["lr"], b1, b2, group["eps"],
+                                     value_copy=getattr(p, "value_copy", None), keep_acc=st.clean)
+                else:
+                    K.lazy_adam_lowmem_step(p, state["exp_avg"], state["exp_avg_sq"], state.get("exp_avg_scale"),
+                                            state.get("exp_avg_sq_scale"), st._acc, st._touched, st.grad_scale,
+                                            int(state["step"]), group["lr"], b1, b2, group["eps"],
+                                            value_copy=getattr(p, "value_copy", None), keep_acc=st.clean)
                 st.grad_scale = 1.0         # the kernel has zeroed the read accumulator rows and the mask
 
     def zero_grad(self, set_to_none=True):

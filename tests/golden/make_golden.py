@@ -25,8 +25,8 @@ from smlm.sparse_values import LazyRowAdam, RowStore, _RowSparseBag, row_store  
 
 
 def bits(t):
-    """bf16 tensor -> uint16 bit patterns."""
-    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    """bf16 tensor -> uint16 bit patterns (a copy: later in-place updates of t do not show through)."""
+    return t.detach().contiguous().view(torch.int16).numpy().view(np.uint16).copy()
 
 
 def save(name, **arrays):
@@ -154,6 +154,48 @@ def gen_lazy_adam():
          eps=np.float64(1e-8), **arrays)
 
 
+def gen_lazy_adam_lowmem():
+    """LazyRowAdam with bf16 / int8 moments: the reference's torch path (after steps 0, 3, 7, 11) and its Triton
+    kernel (interpreter; final state) on the scenario of its test_triton_matches_torch_in_each_state_mode (17 rows,
+    per-row gradient scales 1e-7 .. 1e3, 7 rows per step, clip factor 0.25 every third step), 12 steps, widths 23
+    and 384."""
+    arrays = {}
+    for mode in ("bf16", "int8"):
+        for dim in (23, 384):
+            for impl in ("torch", "triton"):
+                gen = torch.Generator().manual_seed(13)
+                initial = torch.randn(17, dim, generator=gen) * 0.05
+                p = torch.nn.Parameter(initial.clone())
+                opt = LazyRowAdam([p], lr=0.002, state_dtype=mode, impl=impl)
+                row_scales = torch.logspace(-7, 3, 17)[:, None]
+                key = f"{mode}_{dim}_{impl}"
+                arrays[f"{mode}_{dim}_initial"] = initial
+                for step in range(12):
+                    rows = torch.randperm(17, generator=gen)[:7]
+                    grads = torch.randn(7, dim, generator=gen) * row_scales[rows]
+                    scale = 0.25 if step % 3 == 0 else 1.0
+                    st = row_store(p)
+                    st.acc[rows] = grads
+                    st.touched[rows] = True
+                    st.grad_scale = scale
+                    opt.step()
+                    s = opt.state[p]
+                    arrays[f"{mode}_{dim}_rows{step}"] = rows
+                    arrays[f"{mode}_{dim}_grads{step}"] = grads
+                    arrays[f"{mode}_{dim}_scale{step}"] = np.float32(scale)
+                    if step not in ((11,) if impl == "triton" else (0, 3, 7, 11)):
+                        continue                    # checkpoints of the trajectory (the kernel: final state)
+                    arrays[f"{key}_p{step}"] = p.detach().clone()
+                    m, v = s["exp_avg"], s["exp_avg_sq"]
+                    arrays[f"{key}_m{step}"] = bits(m) if mode == "bf16" else m.clone()
+                    arrays[f"{key}_v{step}"] = bits(v) if mode == "bf16" else v.clone()
+                    if mode == "int8":
+                        arrays[f"{key}_ms{step}"] = s["exp_avg_scale"].clone()
+                        arrays[f"{key}_vs{step}"] = s["exp_avg_sq_scale"].clone()
+    save("lazy_adam_lowmem.npz", lr=np.float64(0.002), beta1=np.float64(0.9), beta2=np.float64(0.95),
+         eps=np.float64(1e-8), **arrays)
+
+
 def gen_rowwise():
     """RowWiseOptimizer on a host table, torch formulas (SMLM_HOST_C=0) and the C loop (=1); the visits of the
     reference's test_host_path_matches_formula_and_keeps_unread_rows."""
@@ -255,6 +297,7 @@ if __name__ == "__main__":
     gen_select_backward()
     gen_bag()
     gen_lazy_adam()
+    gen_lazy_adam_lowmem()
     gen_rowwise()
     gen_infer()
     gen_layer()

@@ -88,3 +88,23 @@ def test_state_dict_formats_match_reference():
             "value_proj.weight", "query_norm.running_mean"} <= keys
     from smlm_b200.row_optim import state_bytes
     assert state_bytes("rowrms", 100) == 804 and state_bytes("rowadagrad", 100) == 404
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16", "int8"])
+def test_lazy_adam_argument_validation(mode):
+    """The reference's constructor checks (tests/test_lowmem_values.py), before any device work."""
+    from smlm_b200.sparse_values import LazyRowAdam
+    P = torch.nn.Parameter
+    for dtype in (torch.float16, torch.bfloat16, torch.float64):
+        with pytest.raises(ValueError, match="fp32|float32"):
+            LazyRowAdam([P(torch.zeros(4, 7, dtype=dtype))], lr=0.01, state_dtype=mode)
+    for shape in ((5,), (2, 3, 4), (2, 0)):
+        with pytest.raises(ValueError, match="contiguous fp32 tables"):
+            LazyRowAdam([P(torch.zeros(shape))], lr=0.01, state_dtype=mode)
+    with pytest.raises(ValueError, match="contiguous fp32 tables"):
+        LazyRowAdam([P(torch.zeros(7, 11).t())], lr=0.01, state_dtype=mode)
+    for options in ({"lr": float("nan")}, {"eps": float("nan")}, {"lr": -0.1}, {"eps": -0.1}, {"betas": (0.9, 1.0)}):
+        with pytest.raises(ValueError):
+            LazyRowAdam([P(torch.zeros(4, 7))], state_dtype=mode, **dict({"lr": 0.01}, **options))
+    with pytest.raises(ValueError, match="state_dtype"):
+        LazyRowAdam([P(torch.zeros(4, 7))], lr=0.01, state_dtype="fp16")

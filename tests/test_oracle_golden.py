@@ -138,6 +138,65 @@ def test_lazy_adam_matches_reference_three_steps():
             assert np.array_equal(p, pr) and np.array_equal(m, mr) and np.array_equal(v, vr)
 
 
+def lowmem_replay(g, mode, dim, on_step=None):
+    """Replays the fixture's 12 steps through the oracle; returns the final state."""
+    key = f"{mode}_{dim}"
+    p = g[f"{key}_initial"].astype(np.float32).copy()
+    R = p.shape[0]
+    i8 = mode == "int8"
+    m = np.zeros((R, dim), np.int8 if i8 else np.uint16)
+    v = np.zeros((R, dim), np.uint8 if i8 else np.uint16)
+    ms, vs = np.zeros(R, np.float32), np.zeros(R, np.float32)
+    for step in range(12):
+        acc = np.zeros((R, dim), np.float32)
+        touched = np.zeros(R, np.uint8)
+        rows = g[f"{key}_rows{step}"]
+        acc[rows] = g[f"{key}_grads{step}"]
+        touched[rows] = 1
+        prev = (p.copy(), m.copy(), v.copy(), ms.copy(), vs.copy())
+        O.lazy_adam_lowmem(p, m, v, ms, vs, acc, touched, float(g[f"{key}_scale{step}"]), step + 1, float(g["lr"]),
+                           float(g["beta1"]), float(g["beta2"]), float(g["eps"]), i8)
+        unread = np.ones(R, bool)
+        unread[rows] = False
+        for a, b in zip((p, m, v, ms, vs), prev):                 # unread rows and their state bit-identical
+            assert np.array_equal(a[unread], b[unread])
+        assert not touched.any() and not acc.any()
+        if on_step:
+            on_step(step, p, m, v, ms, vs)
+    return p, m, v, ms, vs
+
+
+@pytest.mark.parametrize("mode", ["bf16", "int8"])
+@pytest.mark.parametrize("dim", [23, 384])
+def test_lazy_adam_lowmem_matches_reference(mode, dim):
+    """Compact-moment lazy Adam: bit-exact against the reference's Triton kernel (kernels.py:445-495, run in the
+    interpreter) after 12 steps; within fp32 ulps of its PyTorch path (sparse_values.py:206-255, whose divisions
+    by Python scalars round differently) at steps 0, 3, 7, 11."""
+    g = golden("lazy_adam_lowmem.npz")
+    key = f"{mode}_{dim}"
+    dec = lambda m, v, ms, vs: ((np.sign(m) * (m / 127.0) ** 2 * ms[:, None], (v / 255.0 * vs[:, None]) ** 4)
+                                if mode == "int8" else (bf16_from_bits(m).float().numpy(),
+                                                        bf16_from_bits(v).float().numpy()))
+
+    def check_torch(step, p, m, v, ms, vs):
+        t = f"{key}_torch"
+        if f"{t}_p{step}" not in g:
+            return
+        close(p, g[f"{t}_p{step}"], msg="values vs torch path")
+        ref = dec(g[f"{t}_m{step}"], g[f"{t}_v{step}"], g.get(f"{t}_ms{step}"), g.get(f"{t}_vs{step}"))
+        for a, b in zip(dec(m, v, ms, vs), ref):
+            scale = np.maximum(np.abs(b).max(axis=1, keepdims=True), 1e-30)
+            # a stored code may sit on the other side of a rounding boundary: one code step of the row's scale
+            assert np.all(np.abs(a - b) <= scale * (2.0 ** -7 if mode == "bf16" else 2.0 / 127)), "moments"
+
+    p, m, v, ms, vs = lowmem_replay(g, mode, dim, check_torch)
+    t = f"{key}_triton"
+    assert np.array_equal(p, g[f"{t}_p11"])
+    assert np.array_equal(m, g[f"{t}_m11"]) and np.array_equal(v, g[f"{t}_v11"])
+    if mode == "int8":
+        assert np.array_equal(ms, g[f"{t}_ms11"]) and np.array_equal(vs, g[f"{t}_vs11"])
+
+
 @pytest.mark.parametrize("kind", ["rowrms", "rowadagrad"])
 def test_rowwise_matches_reference(kind):
     g = golden("rowwise.npz")

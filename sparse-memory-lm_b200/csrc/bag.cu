@@ -394,7 +394,7 @@ struct SegArgs {
 // touch mode) its row's touched byte; the next position's grad_out row and, when it starts a run, its table row
 // are loaded while the current position is summed.
 template <typename TT, typename GT, bool GW, int VEC, int NS>
-__global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
+__global__ void __launch_bounds__(128) bb_segment_kernel(SegArgs a) {
     const int lane = lane_id();
     const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (c >= a.chunks) return;
@@ -561,6 +561,214 @@ __global__ void __launch_bounds__(256) bb_segment_kernel(SegArgs a) {
     if (lane == 0) a.chunk_flags[c] = cflags;
 }
 
+// Per-sample-weight gradient, gather-shaped: gw[n, j] = <grad_out[n], table[row(n, j)]>. One warp per token
+// holds the token's grad_out row in registers and walks its lookups in chunks of 32, four table rows in flight
+// and their four dot products reduced together; lane j keeps the dot of lookup j, stored coalesced per chunk.
+// Lookups outside the table (or outside the shard) get 0.
+struct GwArgs {
+    const void* g;
+    const void* idx;
+    int idx32;
+    int64_t row_base;
+    const void* table;
+    float* gw;
+    int64_t n, rows;
+    int k, d;
+};
+
+template <typename TT, typename GT, int NS>
+__global__ void __launch_bounds__(128) bb_gw_kernel(GwArgs a) {
+    const int lane = lane_id();
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const TT* table = static_cast<const TT*>(a.table);
+    const GT* g = static_cast<const GT*>(a.g);
+    for (int64_t n = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < a.n; n += warps) {
+        float gv[NS][4];
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = (lane + 32 * s) * 4;
+            if (col < a.d) Elt<GT>::template load<4>(g + n * a.d + col, gv[s]);
+            else gv[s][0] = gv[s][1] = gv[s][2] = gv[s][3] = 0.f;
+        }
+        for (int j0 = 0; j0 < a.k; j0 += 32) {
+            const int cnt = min(32, a.k - j0);
+            int64_t my_r = -1;
+            if (lane < cnt) {
+                const int64_t r = load_index(a.idx, a.idx32, n * a.k + j0 + lane) - a.row_base;
+                my_r = (r >= 0 && r < a.rows) ? r : -1;
+            }
+            float mine = 0.f;  // lane j: the dot of lookup j0 + j
+#pragma unroll 1
+            for (int jj = 0; jj < cnt; jj += 4) {
+                float v[4][NS][4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int64_t r = __shfl_sync(FULL, my_r, (jj + u) & 31);  // -1 past cnt (lanes >= cnt)
+#pragma unroll
+                    for (int s = 0; s < NS; s++) {
+                        const int col = (lane + 32 * s) * 4;
+                        if (r >= 0 && col < a.d) Elt<TT>::template load<4>(table + r * a.d + col, v[u][s]);
+                        else v[u][s][0] = v[u][s][1] = v[u][s][2] = v[u][s][3] = 0.f;
+                    }
+                }
+                float dot[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    dot[u] = 0.f;
+#pragma unroll
+                    for (int s = 0; s < NS; s++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) dot[u] = fmaf(gv[s][i], v[u][s][i], dot[u]);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                    for (int u = 0; u < 4; u++) dot[u] += __shfl_xor_sync(FULL, dot[u], o);
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+                    if (lane == jj + u) mine = dot[u];
+            }
+            if (lane < cnt) a.gw[n * a.k + j0 + lane] = mine;
+        }
+    }
+}
+
+template <typename TT, typename GT>
+static void launch_gw(GwArgs a, cudaStream_t st) {
+    const int ns = (a.d + 127) / 128;
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((a.n + 3) / 4, (int64_t)sm_count() * 32));
+    if (ns <= 1) bb_gw_kernel<TT, GT, 1><<<blocks, 128, 0, st>>>(a);
+    else if (ns == 2) bb_gw_kernel<TT, GT, 2><<<blocks, 128, 0, st>>>(a);
+    else if (ns == 3) bb_gw_kernel<TT, GT, 3><<<blocks, 128, 0, st>>>(a);
+    else bb_gw_kernel<TT, GT, 4><<<blocks, 128, 0, st>>>(a);
+}
+
+// The segment pass without the weight gradient (bb_gw_kernel computes it), with the per-position work cut down:
+// per batch of 32 sorted positions each lane fetches one position's row, token (one division per lane),
+// weight and first-touch flag; the warp then walks the batch's in-range prefix (out-of-range keys sort last)
+// with the next position's grad_out row in flight in a second register buffer, adds w * grad_out row to the
+// run's sum, and writes each finished run's row once (with its squared norm and touched flag). Same summation
+// order and results as bb_segment_kernel.
+template <typename GT, int NS>
+__global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a) {
+    const int lane = lane_id();
+    const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (c >= a.chunks) return;
+    const GT* g = static_cast<const GT*>(a.g);
+    const int64_t start = c * a.P;
+    const int64_t end = min(start + (int64_t)a.P, a.m);
+    const uint32_t valid_lim = (uint32_t)a.rows;
+    const uint32_t first_row = a.keys[start];
+    if (first_row >= valid_lim) {
+        if (lane == 0) a.chunk_flags[c] = 0;
+        return;
+    }
+    const uint32_t last_row = a.keys[end - 1];
+    const uint32_t prev_row = start > 0 ? a.keys[start - 1] : NO_ROW;
+    const uint32_t next_row = end < a.m ? a.keys[end] : NO_ROW;
+    const bool head_cross = prev_row == first_row;
+    const bool tail_cross = last_row < valid_lim && next_row == last_row;
+    const bool mid = head_cross && tail_cross && first_row == last_row;
+    int cflags = 0;
+    constexpr uint32_t FRESH = 0x80000000u;
+
+    uint32_t cur = NO_ROW;
+    bool cur_fresh = false;
+    float sum[NS][4];
+#pragma unroll
+    for (int s = 0; s < NS; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
+
+    auto flush = [&]() {
+        if (cur == NO_ROW) return;
+        float* dst;
+        bool direct = false;
+        if (mid) {
+            dst = a.carry_head + c * a.d;
+            cflags |= FLAG_MID;
+        } else if (head_cross && cur == first_row) {
+            dst = a.carry_head + c * a.d;
+        } else if (tail_cross && cur == last_row) {
+            dst = a.carry_tail + c * a.d;
+            cflags |= FLAG_TAIL;
+        } else {
+            dst = a.acc + (int64_t)cur * a.d;
+            direct = true;
+        }
+        const bool accumulate = direct && !cur_fresh;
+        float sq = 0.f;
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = (lane + 32 * s) * 4;
+            if (col < a.d) {
+                float4* q = reinterpret_cast<float4*>(dst + col);
+                float4 x = accumulate ? *q : make_float4(0.f, 0.f, 0.f, 0.f);
+                x.x = x.x + sum[s][0]; x.y = x.y + sum[s][1]; x.z = x.z + sum[s][2]; x.w = x.w + sum[s][3];
+                *q = x;
+                sq = fmaf(x.x, x.x, sq); sq = fmaf(x.y, x.y, sq); sq = fmaf(x.z, x.z, sq); sq = fmaf(x.w, x.w, sq);
+            }
+        }
+        if (direct) {
+            if (a.sqnorm) {
+                sq = warp_sum(sq);
+                if (lane == 0) a.sqnorm[cur] = sq;
+            }
+            if (lane == 0 && a.touched) a.touched[cur] = 1;
+        }
+    };
+    auto load_g = [&](uint32_t tokf, float (&v)[NS][4]) {
+        const GT* src = g + (size_t)(tokf & ~FRESH) * a.d;
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = (lane + 32 * s) * 4;
+            if (col < a.d) Elt<GT>::template load<4>(src + col, v[s]);
+        }
+    };
+    auto step = [&](uint32_t row, uint32_t tokf, float wv, const float (&gv)[NS][4]) {
+        if (row != cur) {
+            flush();
+            cur = row;
+            cur_fresh = (tokf & FRESH) != 0;
+#pragma unroll
+            for (int s = 0; s < NS; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
+        }
+#pragma unroll
+        for (int s = 0; s < NS; s++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) sum[s][i] = fmaf(wv, gv[s][i], sum[s][i]);
+    };
+
+    for (int64_t b = start; b < end; b += 32) {
+        const int cnt = (int)min((int64_t)32, end - b);
+        uint32_t my_key = NO_ROW, my_tokf = 0;
+        float my_w = 0.f;
+        if (lane < cnt) {
+            my_key = a.keys[b + lane];
+            if (my_key < valid_lim) {
+                const uint32_t p = a.pos[b + lane];
+                const bool fresh = a.first_writes && a.touched && a.touched[my_key] == 0;
+                my_tokf = p / (uint32_t)a.k | (fresh ? FRESH : 0u);
+                my_w = load_weight(a.w, a.w_dtype, p);
+            }
+        }
+        const int nv = __popc(__ballot_sync(FULL, my_key < valid_lim));  // in-range keys: a prefix
+        if (nv == 0) break;
+        float ga[NS][4], gb[NS][4];
+        load_g(__shfl_sync(FULL, my_tokf, 0), ga);
+        int t = 0;
+        for (; t + 1 < nv; t += 2) {
+            load_g(__shfl_sync(FULL, my_tokf, t + 1), gb);
+            step(__shfl_sync(FULL, my_key, t), __shfl_sync(FULL, my_tokf, t), __shfl_sync(FULL, my_w, t), ga);
+            if (t + 2 < nv) load_g(__shfl_sync(FULL, my_tokf, t + 2), ga);
+            step(__shfl_sync(FULL, my_key, t + 1), __shfl_sync(FULL, my_tokf, t + 1), __shfl_sync(FULL, my_w, t + 1),
+                 gb);
+        }
+        if (t < nv)
+            step(__shfl_sync(FULL, my_key, t), __shfl_sync(FULL, my_tokf, t), __shfl_sync(FULL, my_w, t), ga);
+    }
+    flush();
+    if (lane == 0) a.chunk_flags[c] = cflags;
+}
+
 // Completes the runs that cross chunk borders, in chunk order: tail of the run's first chunk, the full
 // chunks it covers, then the head of the chunk where it ends.
 template <int VEC>
@@ -606,13 +814,19 @@ template <typename TT, typename GT, bool GW, int VEC>
 static int launch_segment(SegArgs a, cudaStream_t st) {
     const int slots = (a.d + VEC - 1) / VEC;
     const int ns = (slots + 31) / 32;
-    const int blocks = (int)((a.chunks + 7) / 8);
-    if (ns <= 1) bb_segment_kernel<TT, GT, GW, VEC, 1><<<blocks, 256, 0, st>>>(a);
-    else if (ns == 2) bb_segment_kernel<TT, GT, GW, VEC, 2><<<blocks, 256, 0, st>>>(a);
-    else if (ns == 3) bb_segment_kernel<TT, GT, GW, VEC, 3><<<blocks, 256, 0, st>>>(a);
-    else bb_segment_kernel<TT, GT, GW, VEC, 4><<<blocks, 256, 0, st>>>(a);
+    const int blocks = (int)((a.chunks + 3) / 4);
+    if (!GW && VEC == 4 && ns <= 4 && a.acc != nullptr) {
+        if (ns <= 1) bb_rowsum_kernel<GT, 1><<<blocks, 128, 0, st>>>(a);
+        else if (ns == 2) bb_rowsum_kernel<GT, 2><<<blocks, 128, 0, st>>>(a);
+        else if (ns == 3) bb_rowsum_kernel<GT, 3><<<blocks, 128, 0, st>>>(a);
+        else bb_rowsum_kernel<GT, 4><<<blocks, 128, 0, st>>>(a);
+        SMLM_LAUNCHED("bb_rowsum_kernel");
+    } else if (ns <= 1) bb_segment_kernel<TT, GT, GW, VEC, 1><<<blocks, 128, 0, st>>>(a);
+    else if (ns == 2) bb_segment_kernel<TT, GT, GW, VEC, 2><<<blocks, 128, 0, st>>>(a);
+    else if (ns == 3) bb_segment_kernel<TT, GT, GW, VEC, 3><<<blocks, 128, 0, st>>>(a);
+    else bb_segment_kernel<TT, GT, GW, VEC, 4><<<blocks, 128, 0, st>>>(a);
     SMLM_LAUNCHED("bb_segment_kernel");
-    bb_fixup_kernel<VEC><<<blocks, 256, 0, st>>>(a);
+    bb_fixup_kernel<VEC><<<(int)((a.chunks + 7) / 8), 256, 0, st>>>(a);
     SMLM_LAUNCHED("bb_fixup_kernel");
     return SMLM_OK;
 }
@@ -816,6 +1030,20 @@ static int backward_impl(const char* fn, const void* grad_out, int grad_dtype, c
     const uintptr_t ap = reinterpret_cast<uintptr_t>(acc);
     const bool vec = d % 4 == 0 && gp % (grad_dtype == SMLM_F32 ? 16 : 8) == 0 && ap % 16 == 0 &&
                      tp % (table_dtype == SMLM_F32 ? 16 : 8) == 0;
+    if (gw && vec && d <= 512) {
+        // the weight gradient by its own gather-shaped kernel; the segment pass then sums rows only
+        GwArgs ga{grad_out, indices, idx32, row_base, table, gw, n, rows, (int)k, (int)d};
+        if (table_dtype == SMLM_F32) {
+            if (grad_dtype == SMLM_F32) launch_gw<float, float>(ga, st);
+            else launch_gw<float, __nv_bfloat16>(ga, st);
+        } else {
+            if (grad_dtype == SMLM_F32) launch_gw<__nv_bfloat16, float>(ga, st);
+            else launch_gw<__nv_bfloat16, __nv_bfloat16>(ga, st);
+        }
+        SMLM_LAUNCHED("bb_gw_kernel");
+        a.gw = nullptr;
+        if (acc == nullptr) return SMLM_OK;
+    }
     if (table_dtype == SMLM_F32) return vec ? launch_segment_g<float, 4>(a, st) : launch_segment_g<float, 1>(a, st);
     return vec ? launch_segment_g<__nv_bfloat16, 4>(a, st) : launch_segment_g<__nv_bfloat16, 1>(a, st);
 }

@@ -275,6 +275,45 @@ SMLM_API int smlm_shard_bag_backward_rows(const void *grad_out, int grad_dtype, 
  * contiguous: the owners' partial results summed in rank order (deterministic). */
 SMLM_API int smlm_slot_sum(const float *src, int64_t slots, int64_t count, float *dst, void *stream);
 
+/* ----------------------------------------------- row-sharded exchange through peer memory (NVLink, CUDA IPC)
+ * The same exchange as the NCCL collectives above, fused into the owner's kernels: every rank owns one exchange
+ * block in its HBM (flags, its lookups, a receive area for the owners' partial bags and one for the weight
+ * gradients), mapped into the other ranks' processes with CUDA IPC (no multicast objects anywhere). The owner's
+ * forward kernel reads each rank's lookups over NVLink and stores that rank's partial bag straight into its
+ * receive area; the weight-gradient kernel stores each in-shard lookup's gradient straight into the requesting
+ * rank's area. Ranks announce progress by writing an epoch (one per forward, > 0, the same on every rank) into
+ * each other's flags after a system-scope fence; every wait is bounded (10 s of %globaltimer) and a timeout
+ * raises SMLM_FLAG_TIMEOUT in *status (required) and ends every later wait at once. One forward may be
+ * outstanding per exchange (its backward runs before the next forward). All ranks call the same entries with the
+ * same n, k, n_cap, d. The block is allocated once by smlm_xchg_alloc (the library's only device allocation,
+ * made at setup, not per step). */
+SMLM_API size_t smlm_xchg_bytes(int world, int64_t n_cap, int64_t k, int64_t d);
+/* cudaMalloc of the block (zeroed) and its IPC handle (cudaIpcMemHandle_t, 64 bytes) for the other ranks */
+SMLM_API int smlm_xchg_alloc(size_t bytes, void **block, void *ipc_handle);
+/* maps another rank's block (cudaIpcOpenMemHandle, peer access enabled); unmap with smlm_xchg_close */
+SMLM_API int smlm_xchg_open(const void *ipc_handle, void **block);
+SMLM_API int smlm_xchg_close(void *block);
+SMLM_API int smlm_xchg_free(void *block);
+
+/* Forward of the sharded bag: publishes this rank's lookups (idx int32 global rows and fp32 weights, (n, k)),
+ * computes this shard's partial bags of every rank's tokens into their receive areas, waits for every owner and
+ * writes out (n, d) fp32 = the partials summed in owner order. all_idx / all_w ((world n, k)) receive every
+ * rank's lookups (for the backward). peers_dev: device array of world block pointers (this rank's own included).
+ * d % 4 == 0, d <= 512, table and out 16-byte aligned. */
+SMLM_API int smlm_xchg_forward(void *const *peers_dev, void *my_block, int rank, int world, const int32_t *idx,
+                               const float *weights, int64_t n, int64_t k, int64_t n_cap, const void *table_shard,
+                               int table_dtype, int64_t row_base, int64_t shard_rows, int64_t d, int32_t *all_idx,
+                               float *all_w, float *out, int64_t epoch, int *status, void *stream);
+/* Backward, owner side: weight gradients of this shard's lookups of every rank (grad_all: the all-gathered
+ * output gradients (world n, d), fp32 / bf16) into the requesting ranks' areas. */
+SMLM_API int smlm_xchg_backward_gw(void *const *peers_dev, int rank, int world, const void *grad_all, int grad_dtype,
+                                   const int32_t *all_idx, int64_t n, int64_t k, int64_t n_cap,
+                                   const void *table_shard, int table_dtype, int64_t row_base, int64_t shard_rows,
+                                   int64_t d, int64_t epoch, int *status, void *stream);
+/* Backward, requester side: waits for every owner's weight gradients and copies them to gw (n, k) fp32. */
+SMLM_API int smlm_xchg_collect_gw(void *const *peers_dev, int rank, int world, int64_t n, int64_t k, int64_t n_cap,
+                                  int64_t d, float *gw, int64_t epoch, int *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

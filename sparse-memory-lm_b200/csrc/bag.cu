@@ -11,39 +11,6 @@
 namespace smlm {
 
 // ------------------------------------------------------------------------------------------- vector loads
-template <typename T>
-struct Elt;
-template <>
-struct Elt<float> {
-    template <int VEC>
-    __device__ __forceinline__ static void load(const float* p, float (&v)[VEC]) {
-        if constexpr (VEC == 4) {
-            float4 x = __ldg(reinterpret_cast<const float4*>(p));
-            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-        } else {
-#pragma unroll
-            for (int i = 0; i < VEC; i++) v[i] = __ldg(p + i);
-        }
-    }
-};
-template <>
-struct Elt<__nv_bfloat16> {
-    template <int VEC>
-    __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&v)[VEC]) {
-        if constexpr (VEC == 4) {
-            uint2 x = __ldg(reinterpret_cast<const uint2*>(p));
-            v[0] = bf16_bits_to_f32(x.x & 0xffffu);
-            v[1] = bf16_bits_to_f32(x.x >> 16);
-            v[2] = bf16_bits_to_f32(x.y & 0xffffu);
-            v[3] = bf16_bits_to_f32(x.y >> 16);
-        } else {
-            const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
-#pragma unroll
-            for (int i = 0; i < VEC; i++) v[i] = bf16_bits_to_f32(__ldg(q + i));
-        }
-    }
-};
-
 __device__ __forceinline__ float load_weight(const void* w, int dtype, int64_t i) {
     if (dtype == SMLM_F32) return __ldg(static_cast<const float*>(w) + i);
     return bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(w) + i));

@@ -127,4 +127,39 @@ __device__ __forceinline__ void flag(int* status, int bit) {
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
+// Vector loads of VEC elements (fp32 or bf16) widened to fp32 (16-byte / 8-byte loads for VEC == 4).
+template <typename T>
+struct Elt;
+template <>
+struct Elt<float> {
+    template <int VEC>
+    __device__ __forceinline__ static void load(const float* p, float (&v)[VEC]) {
+        if constexpr (VEC == 4) {
+            float4 x = __ldg(reinterpret_cast<const float4*>(p));
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; i++) v[i] = __ldg(p + i);
+        }
+    }
+};
+template <>
+struct Elt<__nv_bfloat16> {
+    template <int VEC>
+    __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&v)[VEC]) {
+        if constexpr (VEC == 4) {
+            uint2 x = __ldg(reinterpret_cast<const uint2*>(p));
+            v[0] = bf16_bits_to_f32(x.x & 0xffffu);
+            v[1] = bf16_bits_to_f32(x.x >> 16);
+            v[2] = bf16_bits_to_f32(x.y & 0xffffu);
+            v[3] = bf16_bits_to_f32(x.y >> 16);
+        } else {
+            const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+#pragma unroll
+            for (int i = 0; i < VEC; i++) v[i] = bf16_bits_to_f32(__ldg(q + i));
+        }
+    }
+};
+
+
 }  // namespace smlm

@@ -66,6 +66,16 @@ SIGNATURES = {
     "smlm_shard_bag_backward_rows": (_i32, [_p, _i32, _p, _i32, _i64, _p, _i32, _p, _i32, _p, _p, _p, _i32, _p,
                                             _i64, _i64, _i64, _i64, _p, _sz, _p, _p]),
     "smlm_slot_sum": (_i32, [_p, _i64, _i64, _p, _p]),
+    "smlm_xchg_bytes": (_sz, [_i32, _i64, _i64, _i64]),
+    "smlm_xchg_alloc": (_i32, [_sz, _p, _p]),
+    "smlm_xchg_open": (_i32, [_p, _p]),
+    "smlm_xchg_close": (_i32, [_p]),
+    "smlm_xchg_free": (_i32, [_p]),
+    "smlm_xchg_forward": (_i32, [_p, _p, _i32, _i32, _p, _p, _i64, _i64, _i64, _p, _i32, _i64, _i64, _i64, _p, _p,
+                                 _p, _i64, _p, _p]),
+    "smlm_xchg_backward_gw": (_i32, [_p, _i32, _i32, _p, _i32, _p, _i64, _i64, _i64, _p, _i32, _i64, _i64, _i64,
+                                     _i64, _p, _p]),
+    "smlm_xchg_collect_gw": (_i32, [_p, _i32, _i32, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "smlm_score_select_noalloc": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
 }
 

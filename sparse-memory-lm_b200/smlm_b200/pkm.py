@@ -30,10 +30,11 @@ class ProductKeyMemory(nn.Module):
     def __init__(self, d_in, d_out, n_keys=512, heads=4, knn=32, k_dim=256, v_dim=-1,
                  query_norm="batchnorm", swilu=True, value_impl="embedding_bag",
                  keys_weight_decay=True, score_scale="none", score_scale_init=1.0, shared_values=None,
-                 value_grad="dense", impl="cuda", shard_group=None):
+                 value_grad="dense", impl="cuda", shard_group=None, shard_exchange="p2p"):
         """shard_group (no counterpart in the reference): a torch.distributed process group over which the value
         table is row-sharded (one process per GPU; values.weight then holds this rank's rows only, and the
-        lookups are exchanged with the other ranks). Needs value_grad="row_sparse"."""
+        lookups are exchanged with the other ranks). Needs value_grad="row_sparse". shard_exchange: "p2p" (the
+        exchange fused into the kernels through peer memory over NVLink) or "nccl" (NCCL collectives)."""
         super().__init__()
         assert k_dim % 2 == 0 and knn <= n_keys
         self.d_in, self.d_out = d_in, d_out
@@ -74,8 +75,11 @@ class ProductKeyMemory(nn.Module):
         if shard_group is not None and dist.get_world_size(shard_group) > 1:
             if value_grad != "row_sparse" or shared_values is not None:
                 raise ValueError("a row-sharded value table needs value_grad='row_sparse' and its own values")
+            if shard_exchange not in ("p2p", "nccl"):
+                raise ValueError(f"unknown shard_exchange {shard_exchange!r}")
             self.shard = RowShard(self.size, dist.get_world_size(shard_group), dist.get_rank(shard_group))
             self.shard_group = shard_group
+            self.shard_exchange = shard_exchange
         if shared_values is not None:
             assert shared_values.weight.shape == (self.size, self.v_dim)
             self.values = shared_values
@@ -139,7 +143,8 @@ class ProductKeyMemory(nn.Module):
         """indices, weights (N, heads*knn) -> (N, v_dim) (reference: pkm.py:138-148)."""
         w = self.values.weight
         if self.shard is not None:
-            return sharded_embedding_bag(indices, weights, w, self.shard, self.shard_group)
+            return sharded_embedding_bag(indices, weights, w, self.shard, self.shard_group,
+                                         exchange=self.shard_exchange)
         if self.value_grad == "row_sparse":
             return row_sparse_embedding_bag(indices, weights, w, self.impl)
         if self.value_impl == "embedding_bag":

@@ -21,9 +21,12 @@ order of the bag (owner partials) and of the row sums differ. Every rank must pa
 Data-path exchange volume per rank and step (N tokens, K lookups, D columns, P ranks): lookups 8 N K P,
 partial bags and output gradients 2 x 4 N D P, weight gradients 4 N K P bytes received.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from . import kernels as K
 
 
@@ -116,11 +119,148 @@ class _ShardedBag(torch.autograd.Function):
         return gw.view(ctx.wshape).to(ctx.wdtype), None, None, None, None, None, None
 
 
-def sharded_embedding_bag(indices, weights, table, shard, group, ops=None, store=None):
+class PeerExchange:
+    """The exchange blocks of every rank mapped into this process (CUDA IPC over NVLink) for the fused exchange:
+    the owner's kernels read the other ranks' lookups and write their partial bags and weight gradients through
+    peer pointers, with epoch flags and bounded waits (smlm_xchg_* in the C ABI). Collective to build and to
+    close; sized for up to n_cap tokens per rank."""
+
+    def __init__(self, shard, group, n_cap, k, d, device):
+        lib = L.lib()
+        self.shard, self.group, self.n_cap, self.k, self.d = shard, group, int(n_cap), int(k), int(d)
+        self.device = device
+        nbytes = lib.smlm_xchg_bytes(shard.world, self.n_cap, self.k, self.d)
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(device):
+            L.check(lib.smlm_xchg_alloc(nbytes, ctypes.byref(base), handle), "xchg_alloc")
+        self.block = base.value
+        handles = [None] * shard.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened = []
+        ptrs = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == shard.rank:
+                    ptrs.append(self.block)
+                    continue
+                peer = ctypes.c_void_p()
+                L.check(lib.smlm_xchg_open(ctypes.create_string_buffer(h, 64), ctypes.byref(peer)), "xchg_open")
+                self.opened.append(peer.value)
+                ptrs.append(peer.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.epoch = 0
+
+    def next_epoch(self):
+        self.epoch += 1
+        return self.epoch
+
+    def close(self):
+        """Unmaps the peers' blocks and frees this rank's (collective: no rank may touch a block after)."""
+        if self.block is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        lib = L.lib()
+        with torch.cuda.device(self.device):
+            for p in self.opened:
+                lib.smlm_xchg_close(ctypes.c_void_p(p))
+            dist.barrier(group=self.group)
+            lib.smlm_xchg_free(ctypes.c_void_p(self.block))
+        self.block, self.opened = None, []
+
+
+def peer_exchange(table, shard, group, n, k):
+    """The table's PeerExchange, built on first use or rebuilt (collectively) when n outgrows its capacity."""
+    x = getattr(table, "peer_exchange", None)
+    if x is None or x.n_cap < n or x.k != k or x.d != table.shape[1]:
+        if x is not None:
+            x.close()
+        x = PeerExchange(shard, group, n, k, table.shape[1], table.device)
+        table.peer_exchange = x
+    return x
+
+
+class _PeerBag(torch.autograd.Function):
+    """The sharded bag with the exchange fused into the owner's kernels (peer memory) instead of NCCL
+    collectives for the lookups, partial bags and weight gradients; the output gradients are all-gathered."""
+
+    @staticmethod
+    def forward(ctx, weights, indices, table, store, shard, group):
+        P = shard.world
+        N, Kk = indices.shape
+        x = peer_exchange(table, shard, group, N, Kk)
+        dev = table.device
+        idx = indices.to(torch.int32).contiguous()
+        w = weights.reshape(N, Kk).float().contiguous()
+        all_idx = torch.empty(P * N, Kk, dtype=torch.int32, device=dev)
+        all_w = torch.empty(P * N, Kk, dtype=torch.float32, device=dev)
+        out = torch.empty(N, table.shape[1], dtype=torch.float32, device=dev)
+        epoch = x.next_epoch()
+        t = table.detach()
+        with L.timed("xchg_forward", 3):
+            rc = L.lib().smlm_xchg_forward(
+                L.ptr(x.peers), ctypes.c_void_p(x.block), shard.rank, P, L.ptr(idx), L.ptr(w), N, Kk, x.n_cap,
+                L.ptr(t) if shard.count else None, L.dtype_code(t.dtype), shard.base, shard.count, t.shape[1],
+                L.ptr(all_idx), L.ptr(all_w), L.ptr(out), epoch, L.status_ptr(dev), L.stream(dev))
+        L.check(rc, "xchg_forward")
+        L.after(dev, "xchg_forward")
+        ctx.save_for_backward(all_idx, all_w)
+        ctx.table, ctx.store, ctx.shard, ctx.group, ctx.x, ctx.epoch = table, store, shard, group, x, epoch
+        ctx.wshape, ctx.wdtype = weights.shape, weights.dtype
+        return out.to(table.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        all_idx, all_w = ctx.saved_tensors
+        shard, x, store = ctx.shard, ctx.x, ctx.store
+        P = shard.world
+        N, Kk = all_idx.shape[0] // P, all_idx.shape[1]
+        dev = all_idx.device
+        g = grad_out.contiguous()
+        if g.dtype not in (torch.float32, torch.bfloat16):
+            g = g.float()
+        all_g = _all_gather(g, ctx.group, P)
+        t = ctx.table.detach()
+        status = L.status_ptr(dev)
+        with L.timed("xchg_backward_gw", 1):
+            rc = L.lib().smlm_xchg_backward_gw(
+                L.ptr(x.peers), shard.rank, P, L.ptr(all_g), L.dtype_code(all_g.dtype), L.ptr(all_idx), N, Kk,
+                x.n_cap, L.ptr(t) if shard.count else None, L.dtype_code(t.dtype), shard.base, shard.count,
+                t.shape[1], ctx.epoch, status, L.stream(dev))
+        L.check(rc, "xchg_backward_gw")
+        if store is not None and shard.count:
+            K.shard_bag_backward_rows(all_g, all_idx, all_w, t, shard.base, store._acc, store._touched,
+                                      row_sqnorm=store._sqnorm if store.clean else None,
+                                      first_touch_writes=store.clean, want_gw=False)
+        gw = torch.empty(N, Kk, dtype=torch.float32, device=dev)
+        with L.timed("xchg_collect_gw", 1):
+            rc = L.lib().smlm_xchg_collect_gw(L.ptr(x.peers), shard.rank, P, N, Kk, x.n_cap, t.shape[1],
+                                              L.ptr(gw), ctx.epoch, status, L.stream(dev))
+        L.check(rc, "xchg_collect_gw")
+        L.after(dev, "xchg_collect_gw")
+        ctx.table = ctx.store = ctx.x = None
+        return gw.view(ctx.wshape).to(ctx.wdtype), None, None, None, None, None
+
+
+def sharded_embedding_bag(indices, weights, table, shard, group, ops=None, store=None, exchange="nccl"):
     """sum_j weights[:, j] * V[indices[:, j]] for a table V whose rows [shard.base, shard.base + shard.count) are
     `table` on this rank; row gradients go into the shard's RowStore (`store`, default table.row_store).
-    Collective: every rank of `group` calls it with the same token count."""
+    Collective: every rank of `group` calls it with the same token count. exchange="nccl": NCCL collectives
+    around the owner kernels (any owner ops); "p2p": the exchange fused into the owner's kernels through peer
+    memory (CUDA kernels only; the backward of a forward runs before the next forward)."""
     from .sparse_values import row_store
+    if exchange not in ("nccl", "p2p"):
+        raise ValueError(f"unknown exchange {exchange!r}")
+    if exchange == "p2p" and ops is None:
+        if indices.ndim != 2 or table.shape[0] != shard.count:
+            raise ValueError("sharded_embedding_bag: indices (N, K) and this rank's table shard expected")
+        if store is None and torch.is_grad_enabled() and table.requires_grad:
+            store = row_store(table)
+        if not torch.is_grad_enabled():
+            with torch.no_grad():
+                return _PeerBag.forward(_NoCtx(), weights, indices, table, None, shard, group)
+        return _PeerBag.apply(weights, indices, table, store, shard, group)
     ops = ops or CUDA_OPS
     if indices.ndim != 2 or weights.shape[:1] != indices.shape[:1]:
         raise ValueError("sharded_embedding_bag: indices (N, K) and weights (N, K) expected")

@@ -1,7 +1,7 @@
-"""Row-sharded product-key memory on 2 GPUs (NCCL, one process per GPU; skipped with fewer GPUs): two ranks with
-the table split by rows equal one GPU running the same layer on the concatenated batches — outputs, the rows'
-accumulated gradients, the replicated parameters' summed gradients, the clip norm, and the table after two
-LazyRowAdam steps."""
+"""Row-sharded product-key memory on 2 GPUs (one process per GPU; skipped with fewer GPUs), with the exchange by
+NCCL collectives and fused through peer memory: two ranks with the table split by rows equal one GPU running the
+same layer on the concatenated batches — outputs, the rows' accumulated gradients, the replicated parameters'
+summed gradients, the clip norm, and the table after two LazyRowAdam steps."""
 import os
 import socket
 
@@ -20,11 +20,11 @@ def free_port():
         return s.getsockname()[1]
 
 
-def make_layer(group=None):
+def make_layer(group=None, exchange="nccl"):
     from smlm_b200.pkm import ProductKeyMemory
     torch.manual_seed(0)
     return ProductKeyMemory(64, 64, n_keys=64, heads=4, knn=16, k_dim=64, query_norm="none", swilu=False,
-                            value_grad="row_sparse", shard_group=group)
+                            value_grad="row_sparse", shard_group=group, shard_exchange=exchange)
 
 
 def data(steps, N):
@@ -42,7 +42,7 @@ def run_step(mem, opt, x, g, autocast):
     return out.detach(), norm
 
 
-def worker(rank, port, autocast, q):
+def worker(rank, port, autocast, exchange, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -53,7 +53,7 @@ def worker(rank, port, autocast, q):
         from smlm_b200.sharded import allreduce_replicated_grads
         from smlm_b200.sparse_values import LazyRowAdam, row_store
         ref = make_layer().to(dev)                                   # one GPU, full table
-        mem = make_layer(dist.group.WORLD).to(dev)
+        mem = make_layer(dist.group.WORLD, exchange).to(dev)
         sd = {k: v for k, v in ref.state_dict().items() if k != "values.weight"}
         mem.load_state_dict(sd, strict=False)
         with torch.no_grad():
@@ -80,6 +80,10 @@ def worker(rank, port, autocast, q):
             torch.testing.assert_close(mem.values.weight, mem.shard.take(ref.values.weight), rtol=1e-5, atol=1e-6)
             for m in (ref, mem):
                 m.zero_grad(set_to_none=True)
+        x = getattr(mem.values.weight, "peer_exchange", None)
+        if x is not None:
+            assert exchange == "p2p" and x.epoch == 2
+            x.close()
         q.put((rank, "ok"))
     except Exception as e:
         q.put((rank, f"{type(e).__name__}: {e}"))
@@ -91,9 +95,11 @@ def worker(rank, port, autocast, q):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD,
                     reason="needs 2 GPUs")
 @pytest.mark.parametrize("autocast", [False, True])
-def test_sharded_layer_equals_one_gpu(autocast):
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+def test_sharded_layer_equals_one_gpu(autocast, exchange):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    mp.start_processes(worker, args=(free_port(), autocast, q), nprocs=WORLD, join=True, start_method="spawn")
+    mp.start_processes(worker, args=(free_port(), autocast, exchange, q), nprocs=WORLD, join=True,
+                       start_method="spawn")
     res = dict(q.get() for _ in range(WORLD))
     assert res == {r: "ok" for r in range(WORLD)}, res

@@ -57,7 +57,33 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows-per-half", type=int, default=1024)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
+    ap.add_argument("--case", choices=["layer", "scoring"], default="layer",
+                    help="scoring: only the fused sub-key scoring + selection of the workload's layer (a small "
+                         "standalone case for profiler captures; prints its time per call)")
     return ap.parse_args()
+
+
+def run_scoring_case(args):
+    """The fused tensor-core scoring + selection alone at the workload's shape (bf16 queries and keys), for
+    profiler captures of score_topk_kernel / pk_pairs_kernel on a few hundred MB."""
+    from smlm_b200 import kernels as K
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    n_keys, N = args.rows_per_half, args.tokens
+    q = torch.randn(N, HEADS, K_DIM, device=dev, generator=gen).bfloat16()
+    keys = (torch.randn(HEADS, 2, n_keys, K_DIM // 2, device=dev, generator=gen) * (K_DIM // 2) ** -0.5).bfloat16()
+    for _ in range(args.warmup):
+        K.score_select(q, keys, KNN)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        K.score_select(q, keys, KNN)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    print(json.dumps({"case": "scoring", "tokens": N, "rows_per_half": n_keys, "ms_per_call": round(ms, 4),
+                      "flops_per_call": 2 * N * HEADS * 2 * n_keys * (K_DIM // 2)}), flush=True)
 
 
 def dist_setup(args):
@@ -341,6 +367,9 @@ def cpu_reference(n_keys, N, steps, warmup):
 
 def main():
     args = parse()
+    if args.case == "scoring":
+        run_scoring_case(args)
+        return
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         if rank == 0:

@@ -129,6 +129,41 @@ __device__ void half_topk(const void* s, int64_t off, int nk, int knn, uint64_t*
     sort_prefix(buf, cnt);
 }
 
+// Bitonic sort of one key per lane, descending across the warp.
+__device__ __forceinline__ uint64_t warp_sort32_desc(uint64_t v, int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const uint64_t o = __shfl_xor_sync(FULL, v, stride);
+            const bool desc = (lane & size) == 0 || size == 32;
+            const bool lower = (lane & stride) == 0;
+            v = (lower == desc) ? (v > o ? v : o) : (v < o ? v : o);
+        }
+    }
+    return v;
+}
+
+// Top 32 (descending, one per lane) of two descending lane sequences: max(a[i], b[31 - i]) is bitonic and holds
+// the 32 largest; a half-cleaner network sorts it.
+__device__ __forceinline__ uint64_t warp_merge_top32(uint64_t a, uint64_t b, int lane) {
+    const uint64_t br = __shfl_sync(FULL, b, 31 - lane);
+    uint64_t v = a > br ? a : br;
+#pragma unroll
+    for (int stride = 16; stride > 0; stride >>= 1) {
+        const uint64_t o = __shfl_xor_sync(FULL, v, stride);
+        v = (lane & stride) == 0 ? (v > o ? v : o) : (v < o ? v : o);
+    }
+    return v;
+}
+
+// The 32 largest of 128 keys (4 per lane), sorted descending, one per lane.
+__device__ __forceinline__ uint64_t warp_top32_of_128(uint64_t (&k)[4], int lane) {
+#pragma unroll
+    for (int r = 0; r < 4; r++) k[r] = warp_sort32_desc(k[r], lane);
+    return warp_merge_top32(warp_merge_top32(k[0], k[1], lane), warp_merge_top32(k[2], k[3], lane), lane);
+}
+
 template <bool F32>
 __device__ __forceinline__ uint32_t pair_code(float v1, float v2) {
     return code_of<F32>(bits_of_float<F32>(v1 + v2));
@@ -144,7 +179,8 @@ __device__ void cartesian_select(uint64_t key1, uint64_t key2, int nk, int knn, 
     const float v2 = score_of_code<F32>(key_code(key2));
     const uint32_t i1 = key_index(key1), i2 = key_index(key2);
 
-    // dominance-pruned pairs: lane a owns b < m_a = knn / (a + 1)
+    // dominance-pruned pairs: lane a owns b < m_a = knn / (a + 1); at most 119 (knn = 32) pairs, held in
+    // registers as candidate c = 32 r + lane, r < 4, and reduced to the sorted top 32 without shared memory
     const int m_a = lane < knn ? knn / (lane + 1) : 0;
     int incl = m_a;
 #pragma unroll
@@ -154,14 +190,27 @@ __device__ void cartesian_select(uint64_t key1, uint64_t key2, int nk, int knn, 
     }
     const int total = __shfl_sync(FULL, incl, 31);
     const int off_a = incl - m_a;
-    for (int b = 0; b < knn; b++) {
-        const float v2b = __shfl_sync(FULL, v2, b);
-        const uint32_t i2b = __shfl_sync(FULL, i2, b);
-        if (b < m_a) buf[off_a + b] = make_key(pair_code<F32>(v1, v2b), i1 * (uint32_t)nk + i2b);
+    uint64_t cand[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const int c = 32 * r + lane;
+        // the row a of candidate c: the last a with off_a <= c (offsets ascend with a)
+        int a = 0;
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const int probe = a + step;
+            const int off_p = __shfl_sync(FULL, off_a, probe & 31);
+            if (probe < 32 && off_p <= c) a = probe;
+        }
+        const int b = c - __shfl_sync(FULL, off_a, a);
+        const float v1a = __shfl_sync(FULL, v1, a);
+        const uint32_t i1a = __shfl_sync(FULL, i1, a);
+        const float v2b = __shfl_sync(FULL, v2, b & 31);
+        const uint32_t i2b = __shfl_sync(FULL, i2, b & 31);
+        cand[r] = c < total ? make_key(pair_code<F32>(v1a, v2b), i1a * (uint32_t)nk + i2b) : 0;
     }
-    __syncwarp();
-    sort_prefix(buf, total);
-    const uint64_t best = lane < knn ? buf[lane] : 0;
+    const uint64_t best_all = warp_top32_of_128(cand, lane);
+    const uint64_t best = lane < knn ? best_all : 0;
     const uint32_t t_code = key_code(__shfl_sync(FULL, best, knn - 1));
 
     // a pair outside the pruned set can only tie with T at the first excluded column of each list row

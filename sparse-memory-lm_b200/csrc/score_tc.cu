@@ -15,11 +15,15 @@
 //               the stage's "empty" barrier and the accumulator's "full" barrier.
 //   warps 2-9   epilogue: tcgen05.ld of the 128 x 128 accumulator; warp w reads TMEM lanes 32 (w % 4) ..
 //               (the lane quarter it may access), one token per thread, and columns [0, 64) (warps 2-5) or
-//               [64, 128) (warps 6-9) of every tile. Each score is compared in fp32 against the exact rounding
-//               bound of the thread's current 32nd-best bf16 score; survivors queue in a per-thread list in
-//               shared memory, and once any lane holds FLUSH_AT of them the warp merges them in lockstep, 16
-//               at a time (sort the batch, bitonic merge into the register-resident sorted top-32). Each
-//               token ends with one sorted top-32 per column set; the pair kernel merges the two.
+//               [64, 128) (warps 6-9) of every tile.
+// Each half's key tiles go through the tensor cores twice (the GEMM is cheap next to the selection). Pre-pass:
+// every thread keeps the 32 largest maxima of its 32-column groups; their 32nd is a bf16 score that 32
+// distinct columns reach, so the token's top 32 lies at or above it (the two column-set threads of a token
+// take the larger of their two bounds). Selection pass: each score is compared in fp32 against the exact
+// rounding bound of max(that floor, the thread's current 32nd-best); the few survivors queue in a per-thread
+// list in shared memory, and once any lane holds FLUSH_AT of them the warp merges them in lockstep, 16 at a
+// time (sort the batch, bitonic merge into the register-resident sorted top-32). Each token ends with one
+// sorted top-32 per column set; the pair kernel merges the two.
 // Every mbarrier wait is bounded (about one second); on timeout the kernel raises SMLM_FLAG_TIMEOUT in the
 // status word, every role unwinds, the MMA issuer waits (bounded) for its last commit, and TMEM is freed.
 // No TMA multicast is used (the kernel only reads this GPU's memory).
@@ -225,6 +229,33 @@ __device__ __forceinline__ float pass_bound(uint32_t t) {
     return __uint_as_float(m > 0.f ? mb + 1 : mb - 1);                   // next fp32 above m
 }
 
+// Smallest fp32 b such that bf16_rn(v) >= t exactly when v >= b: the pass bound of the next bf16 below t
+// (+0 and -0 are one value; t = -inf lets everything pass).
+__device__ __forceinline__ float pass_bound_ge(uint32_t t) {
+    if (t == 0xff80u) return -INFINITY;
+    uint32_t p;
+    if (t == 0x0000u || t == 0x8000u) p = 0x8001u;   // just below zero: the negative subnormal closest to it
+    else if (t & 0x8000u) p = t + 1;                   // negatives: one step away from zero
+    else p = t - 1;                                    // positives: one step toward zero
+    return pass_bound(p);
+}
+
+// The two column-set threads of a token (epilogue threads e and e ^ 128) swap their pre-pass bounds through
+// shared memory: each publishes (sequence << 32) | bound and polls for the partner's entry of the same sequence,
+// for a bounded time; if it does not come (an aborting partner), its own bound, equally valid, is used.
+__device__ __forceinline__ uint32_t exchange_bound(uint64_t* pre, int e, uint32_t seq, uint32_t own,
+                                                   volatile int* abort_flag) {
+    volatile uint64_t* slots = pre;
+    slots[e] = ((uint64_t)seq << 32) | own;
+    __threadfence_block();
+    const uint64_t t0 = now_ns();
+    while (true) {
+        const uint64_t p = slots[e ^ 128];
+        if ((uint32_t)(p >> 32) == seq) return (uint32_t)p;
+        if (*abort_flag || now_ns() - t0 > WAIT_NS) return own;
+    }
+}
+
 // Per-thread (= per token) running top-32 of one column stream, in registers, sorted descending.
 struct Epi {
     uint32_t* cand;   // [CAND][EPI_THREADS] candidate keys (slot-major: conflict-free per-thread lists)
@@ -232,10 +263,28 @@ struct Epi {
     int e;            // epilogue thread index
     int cnt;
     uint32_t top[32];
-    float bound;      // fp32 scores >= bound round to a bf16 above the current 32nd-best
+    float bound;      // fp32 scores >= bound round to a bf16 above the current 32nd-best (and >= floor)
+    float floor;      // scores below the token's pre-pass bound never enter the union's top 32
 
     __device__ __forceinline__ void set_thr() {
-        bound = pass_bound(top[31] ? decode_code16(top[31] >> 16) : 0xff80u);   // fewer than 32 yet: -inf
+        bound = fmaxf(pass_bound(top[31] ? decode_code16(top[31] >> 16) : 0xff80u), floor);  // < 32 yet: -inf
+    }
+    // Pre-pass: the maximum of 32 consecutive scores (columns >= nk excluded) is queued as a key; the merged list
+    // then holds the 32 largest such group maxima, and its 32nd entry is a score reached by 32 distinct columns.
+    __device__ __forceinline__ void group_max(const uint32_t (&v)[32], int col0, int nk) {
+        float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (col0 + i < nk) m[i & 3] = fmaxf(m[i & 3], __uint_as_float(v[i]));
+        const float mx = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+        cand[cnt * EPI_THREADS + e] =
+            mx == -INFINITY ? 0u : order_code16(__bfloat16_as_ushort(__float2bfloat16_rn(mx))) << 16;
+        cnt++;
+    }
+    __device__ __forceinline__ void clear() {
+#pragma unroll
+        for (int i = 0; i < 32; i++) top[i] = 0u;
+        cnt = 0;
     }
     // candidates [base, base + BATCH) enter the list: sort the batch, take the elementwise max of the list's tail
     // and the reversed batch (a bitonic sequence holding the best 32 of both), clean it into order
@@ -254,23 +303,18 @@ struct Epi {
         for (int i = 0; i < 32; i++)
             if (col0 + i < nk) dbg[col0 + i] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i])));
     }
-    // first chunk of a stream: the list is its 32 keys, sorted (columns >= nk enter as empty keys)
-    __device__ __forceinline__ void first(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
-        dump(v, col0, nk, dbg);
-#pragma unroll
-        for (int i = 0; i < 32; i++)
-            top[i] = col0 + i < nk
-                         ? score_key(__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]))), col0 + i)
-                         : 0u;
-        sort_desc<32>(top);
-        cnt = 0;
-        set_thr();
-    }
     // merges the buffered candidates, all lanes in lockstep, BATCH at a time
     __device__ __forceinline__ void flush() {
         const int mx = __reduce_max_sync(FULL, (unsigned)cnt);
         for (int base = 0; base < mx; base += BATCH) merge_batch(base);
         cnt = 0;
+        set_thr();
+    }
+    // Pass 2 of a stream starts with an empty list and the floor from the pre-pass bound t (bf16 order code of
+    // a score that 32 distinct columns of the token reach; 0: none): scores equal to it still pass.
+    __device__ __forceinline__ void start_pass2(uint32_t t) {
+        clear();
+        floor = t ? pass_bound_ge(decode_code16(t)) : -INFINITY;
         set_thr();
     }
     // 32 consecutive scores (fp32 bits) of columns col0 .. col0+31: an fp32 compare against the exact bound
@@ -319,7 +363,8 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
     uint8_t* sB = sA + a_bytes;                      // STAGES x b_bytes
     uint32_t* cand = reinterpret_cast<uint32_t*>(sB + STAGES * b_bytes);
     float4* stage = reinterpret_cast<float4*>(cand + CAND * EPI_THREADS);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stage + 8 * EPI_THREADS);
+    uint64_t* pre = reinterpret_cast<uint64_t*>(stage + 8 * EPI_THREADS);  // [EPI_THREADS] pre-pass bounds
+    uint64_t* bars = pre + EPI_THREADS;
     uint64_t* full_b = bars;
     uint64_t* empty_b = bars + STAGES;
     uint64_t* a_full = bars + 2 * STAGES;
@@ -354,6 +399,7 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
         tmem_alloc(smem_addr(tmem_holder), TMEM_COLS);
         tmem_relinquish();
     }
+    for (int i = threadIdx.x; i < EPI_THREADS; i += THREADS) pre[i] = 0;  // sequence 0: nothing published
     fence_before();
     __syncthreads();
     fence_after();
@@ -374,12 +420,13 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                         tma_load_3d(smem_addr(sA + i * ATOM_BYTES_A), &tq, smem_addr(a_full), i * ATOM, h * 2 + half,
                                     tm * BM);
                     a_iter++;
-                    for (int t = 0; t < ntiles; t++) {
+                    for (int t = 0; t < 2 * ntiles; t++) {  // pre-pass, then the selection pass
+                        const int kt = t < ntiles ? t : t - ntiles;
                         if (!mbar_wait(smem_addr(&empty_b[s]), ph ^ 1, abort_flag)) break;
                         mbar_expect_tx(smem_addr(&full_b[s]), b_bytes);
                         for (int i = 0; i < P.atoms; i++)
                             tma_load_2d(smem_addr(sB + s * b_bytes + i * ATOM_BYTES_B), &tk, smem_addr(&full_b[s]),
-                                        i * ATOM, (h * 2 + half) * P.nk + t * BN);
+                                        i * ATOM, (h * 2 + half) * P.nk + kt * BN);
                         if (++s == STAGES) { s = 0; ph ^= 1; }
                     }
                     if (*abort_flag) break;
@@ -397,7 +444,7 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                     if (!mbar_wait(smem_addr(a_full), a_iter & 1, abort_flag)) break;
                     fence_after();
                     const uint32_t a_base = smem_addr(sA);
-                    for (int t = 0; t < ntiles; t++) {
+                    for (int t = 0; t < 2 * ntiles; t++) {  // the same key tiles twice (pre-pass, selection)
                         if (!mbar_wait(smem_addr(&full_b[s]), ph, abort_flag)) break;
                         const int tb = t_iter & 1;
                         if (!mbar_wait(smem_addr(&t_empty[tb]), ((t_iter >> 1) & 1) ^ 1, abort_flag)) break;
@@ -437,6 +484,7 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
         ep.e = (warp - 2) * 32 + lane;
         ep.cnt = 0;
         int t_iter = 0;
+        uint32_t pre_seq = 0;
         for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
             const int tm = u / P.heads, h = u % P.heads;
             const int64_t n = (int64_t)tm * BM + row;
@@ -445,7 +493,9 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                 if (dbg && n < P.n) dbg += (n * P.heads + h) * (int64_t)P.nk;
                 else dbg = nullptr;
                 bool ok = true;
-                for (int t = 0; t < ntiles; t++) {
+                ep.clear();
+                ep.floor = -INFINITY;
+                for (int t = 0; t < 2 * ntiles; t++) {
                     const int tb = t_iter & 1;
                     // warp-uniform outcome: the TMEM loads below are .sync.aligned
                     if (!__all_sync(FULL, mbar_wait(smem_addr(&t_full[tb]), (t_iter >> 1) & 1, abort_flag))) {
@@ -462,10 +512,24 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_addr(&t_empty[tb]));
                     t_iter++;
-                    const int c0 = t * BN + cset * 64;
-                    if (t == 0) ep.first(v0, c0, P.nk, dbg);
-                    else ep.take(v0, c0, P.nk, dbg);
-                    ep.take(v1, c0 + 32, P.nk, dbg);
+                    if (t < ntiles) {
+                        // pre-pass: group maxima of 32 columns, merged 16 at a time (every lane holds the same count)
+                        const int c0 = t * BN + cset * 64;
+                        ep.group_max(v0, c0, P.nk);
+                        ep.group_max(v1, c0 + 32, P.nk);
+                        if (ep.cnt == BATCH) ep.flush();
+                        if (t == ntiles - 1) {
+                            if (ep.cnt) ep.flush();
+                            // the better of the two column-set threads' bounds (both are valid for the union)
+                            const uint32_t own = ep.top[31] >> 16;
+                            const uint32_t other = exchange_bound(pre, ep.e, ++pre_seq, own, abort_flag);
+                            ep.start_pass2(max(own, other));
+                        }
+                    } else {
+                        const int c0 = (t - ntiles) * BN + cset * 64;
+                        ep.take(v0, c0, P.nk, dbg);
+                        ep.take(v1, c0 + 32, P.nk, dbg);
+                    }
                 }
                 if (!ok) break;
                 if (__any_sync(FULL, ep.cnt > 0)) ep.flush();
@@ -489,7 +553,7 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
 
 size_t smem_bytes(int atoms) {
     return 1024 + (size_t)atoms * ATOM_BYTES_A + STAGES * (size_t)atoms * ATOM_BYTES_B + CAND * EPI_THREADS * 4 +
-           8 * EPI_THREADS * 16 + 16 * 8 + 16;
+           8 * EPI_THREADS * 16 + EPI_THREADS * 8 + 16 * 8 + 16;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {

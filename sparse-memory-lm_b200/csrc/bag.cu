@@ -736,6 +736,124 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a) {
     if (lane == 0) a.chunk_flags[c] = cflags;
 }
 
+// bb_rowsum_kernel with four chunks per warp, one per quarter-warp (8 lanes x 4 NSQ columns hold a row): the
+// quarters run the same instruction stream on different chunks, so the per-position control (shuffles, run
+// tests, loop) serves four positions, and a warp keeps four rows in flight. Same summation order and results.
+template <typename GT, int NSQ>
+__global__ void __launch_bounds__(128) bb_rowsum4_kernel(SegArgs a) {
+    const int lane = lane_id();
+    const int ql = lane & 7;
+    const int quarter = lane >> 3;
+    const unsigned qmask = 0xffu << (8 * quarter);
+    const int64_t c = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + quarter;
+    if (c >= a.chunks) return;
+    const GT* g = static_cast<const GT*>(a.g);
+    const int64_t start = c * a.P;
+    const int64_t end = min(start + (int64_t)a.P, a.m);
+    const uint32_t valid_lim = (uint32_t)a.rows;
+    const uint32_t first_row = a.keys[start];
+    if (first_row >= valid_lim) {
+        if (ql == 0) a.chunk_flags[c] = 0;
+        return;
+    }
+    const uint32_t last_row = a.keys[end - 1];
+    const uint32_t prev_row = start > 0 ? a.keys[start - 1] : NO_ROW;
+    const uint32_t next_row = end < a.m ? a.keys[end] : NO_ROW;
+    const bool head_cross = prev_row == first_row;
+    const bool tail_cross = last_row < valid_lim && next_row == last_row;
+    const bool mid = head_cross && tail_cross && first_row == last_row;
+    int cflags = 0;
+    constexpr uint32_t FRESH = 0x80000000u;
+
+    uint32_t cur = NO_ROW;
+    bool cur_fresh = false;
+    float sum[NSQ][4];
+#pragma unroll
+    for (int s = 0; s < NSQ; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
+
+    auto flush = [&]() {
+        if (cur == NO_ROW) return;
+        float* dst;
+        bool direct = false;
+        if (mid) {
+            dst = a.carry_head + c * a.d;
+            cflags |= FLAG_MID;
+        } else if (head_cross && cur == first_row) {
+            dst = a.carry_head + c * a.d;
+        } else if (tail_cross && cur == last_row) {
+            dst = a.carry_tail + c * a.d;
+            cflags |= FLAG_TAIL;
+        } else {
+            dst = a.acc + (int64_t)cur * a.d;
+            direct = true;
+        }
+        const bool accumulate = direct && !cur_fresh;
+        float sq = 0.f;
+#pragma unroll
+        for (int s = 0; s < NSQ; s++) {
+            const int col = (ql + 8 * s) * 4;
+            if (col < a.d) {
+                float4* q = reinterpret_cast<float4*>(dst + col);
+                float4 x = accumulate ? *q : make_float4(0.f, 0.f, 0.f, 0.f);
+                x.x = x.x + sum[s][0]; x.y = x.y + sum[s][1]; x.z = x.z + sum[s][2]; x.w = x.w + sum[s][3];
+                *q = x;
+                sq = fmaf(x.x, x.x, sq); sq = fmaf(x.y, x.y, sq); sq = fmaf(x.z, x.z, sq); sq = fmaf(x.w, x.w, sq);
+            }
+        }
+        if (direct) {
+            if (a.sqnorm) {
+#pragma unroll
+                for (int o = 4; o > 0; o >>= 1) sq += __shfl_xor_sync(qmask, sq, o);
+                if (ql == 0) a.sqnorm[cur] = sq;
+            }
+            if (ql == 0 && a.touched) a.touched[cur] = 1;
+        }
+    };
+
+    for (int64_t b = start; b < end; b += 8) {
+        const int cnt = (int)min((int64_t)8, end - b);
+        uint32_t my_key = NO_ROW, my_tokf = 0;
+        float my_w = 0.f;
+        if (ql < cnt) {
+            my_key = a.keys[b + ql];
+            if (my_key < valid_lim) {
+                const uint32_t p = a.pos[b + ql];
+                const bool fresh = a.first_writes && a.touched && a.touched[my_key] == 0;
+                my_tokf = p / (uint32_t)a.k | (fresh ? FRESH : 0u);
+                my_w = load_weight(a.w, a.w_dtype, p);
+            }
+        }
+        const int nv = __popc((__ballot_sync(qmask, my_key < valid_lim) >> (8 * quarter)) & 0xffu);
+        if (nv == 0) break;
+        for (int t = 0; t < nv; t++) {
+            const uint32_t row = __shfl_sync(qmask, my_key, t, 8);
+            const uint32_t tokf = __shfl_sync(qmask, my_tokf, t, 8);
+            const float wv = __shfl_sync(qmask, my_w, t, 8);
+            float gv[NSQ][4];
+            const GT* src = g + (size_t)(tokf & ~FRESH) * a.d;
+#pragma unroll
+            for (int s = 0; s < NSQ; s++) {
+                const int col = (ql + 8 * s) * 4;
+                if (col < a.d) Elt<GT>::template load<4>(src + col, gv[s]);
+                else gv[s][0] = gv[s][1] = gv[s][2] = gv[s][3] = 0.f;
+            }
+            if (row != cur) {
+                flush();
+                cur = row;
+                cur_fresh = (tokf & FRESH) != 0;
+#pragma unroll
+                for (int s = 0; s < NSQ; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
+            }
+#pragma unroll
+            for (int s = 0; s < NSQ; s++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) sum[s][i] = fmaf(wv, gv[s][i], sum[s][i]);
+        }
+    }
+    flush();
+    if (ql == 0) a.chunk_flags[c] = cflags;
+}
+
 // Completes the runs that cross chunk borders, in chunk order: tail of the run's first chunk, the full
 // chunks it covers, then the head of the chunk where it ends.
 template <int VEC>
@@ -782,7 +900,12 @@ static int launch_segment(SegArgs a, cudaStream_t st) {
     const int slots = (a.d + VEC - 1) / VEC;
     const int ns = (slots + 31) / 32;
     const int blocks = (int)((a.chunks + 3) / 4);
-    if (!GW && VEC == 4 && ns <= 4 && a.acc != nullptr) {
+    if (!GW && VEC == 4 && ns <= 1 && sizeof(GT) == 2 && a.acc != nullptr) {
+        // short bf16 rows (the scoring backward's 128-wide key rows): four chunks per warp (measured faster);
+        // wide fp32 rows keep one chunk per warp (measured faster there)
+        bb_rowsum4_kernel<GT, 4><<<(int)((a.chunks + 15) / 16), 128, 0, st>>>(a);
+        SMLM_LAUNCHED("bb_rowsum4_kernel");
+    } else if (!GW && VEC == 4 && ns <= 4 && a.acc != nullptr) {
         if (ns <= 1) bb_rowsum_kernel<GT, 1><<<blocks, 128, 0, st>>>(a);
         else if (ns == 2) bb_rowsum_kernel<GT, 2><<<blocks, 128, 0, st>>>(a);
         else if (ns == 3) bb_rowsum_kernel<GT, 3><<<blocks, 128, 0, st>>>(a);

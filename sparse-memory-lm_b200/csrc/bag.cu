@@ -670,7 +670,7 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a) {
                 float4* q = reinterpret_cast<float4*>(dst + col);
                 float4 x = accumulate ? *q : make_float4(0.f, 0.f, 0.f, 0.f);
                 x.x = x.x + sum[s][0]; x.y = x.y + sum[s][1]; x.z = x.z + sum[s][2]; x.w = x.w + sum[s][3];
-                *q = x;
+                __stcs(q, x);  // streaming store: the row is not read again until the optimizer step
                 sq = fmaf(x.x, x.x, sq); sq = fmaf(x.y, x.y, sq); sq = fmaf(x.z, x.z, sq); sq = fmaf(x.w, x.w, sq);
             }
         }

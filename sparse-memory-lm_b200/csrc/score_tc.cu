@@ -272,11 +272,23 @@ struct Epi {
     // Pre-pass: the maximum of 32 consecutive scores (columns >= nk excluded) is queued as a key; the merged list
     // then holds the 32 largest such group maxima, and its 32nd entry is a score reached by 32 distinct columns.
     __device__ __forceinline__ void group_max(const uint32_t (&v)[32], int col0, int nk) {
-        float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        float mx;
+        if (col0 + 32 <= nk) {  // warp-uniform: a full group, a plain max tree
+            float m[16];
 #pragma unroll
-        for (int i = 0; i < 32; i++)
-            if (col0 + i < nk) m[i & 3] = fmaxf(m[i & 3], __uint_as_float(v[i]));
-        const float mx = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+            for (int i = 0; i < 16; i++) m[i] = fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 16]));
+#pragma unroll
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
+            mx = m[0];
+        } else {
+            float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                if (col0 + i < nk) m[i & 3] = fmaxf(m[i & 3], __uint_as_float(v[i]));
+            mx = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+        }
         cand[cnt * EPI_THREADS + e] =
             mx == -INFINITY ? 0u : order_code16(__bfloat16_as_ushort(__float2bfloat16_rn(mx))) << 16;
         cnt++;
@@ -321,6 +333,17 @@ struct Epi {
     // filters them; survivors are queued, and merged once any lane has FLUSH_AT of them.
     __device__ __forceinline__ void take(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
         dump(v, col0, nk, dbg);
+        {
+            // quick reject: once the bound is high, whole chunks fall below it (a max tree, one vote)
+            float m[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) m[i] = fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 16]));
+#pragma unroll
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
+            if (__all_sync(FULL, !(m[0] >= bound))) return;  // no survivor in any lane (NaN never passes)
+        }
         uint32_t part[4] = {0u, 0u, 0u, 0u};  // four independent chains
 #pragma unroll
         for (int i = 0; i < 32; i++)

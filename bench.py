@@ -39,10 +39,9 @@ sys.path.insert(0, os.path.join(ROOT, "sparse-memory-lm_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "PKM layer tokens/s (fwd+bwd+opt) at 16.8M rows"
-# DRAM bytes (read + write) of one lazy Adam launch per touched row, from the ncu capture in
-# profiles/lazy_adam_kernel_pkm-layer-1m.md (6.651 GB for 621,697 touched rows); traffic scales with the
-# touched rows.
-ADAM_TRAFFIC_PER_ROW = 10698
+# DRAM bytes (read + write) of the fused row-sum + lazy Adam step per touched row, from the ncu capture in
+# profiles/lazy_adam_kernel_pkm-layer-1m.md; traffic scales with the touched rows (None: not measured).
+ADAM_TRAFFIC_PER_ROW = None
 D_MODEL, HEADS, KNN, K_DIM = 384, 4, 32, 256
 
 
@@ -296,19 +295,28 @@ def run_cuda(args, world, rank, local):
     peak_src = "measured" if hbm else "fallback"
     hbm = hbm or 6650.0
     adam_ms = statistics.mean(per_kernel["lazy_adam_step"])
-    # mask scan, row list, read p / m / v / acc, write p / m / v (the clean RowStore keeps consumed acc rows)
-    adam_bytes = rows * 1 + U * (4 + 4 + 1) + U * D_MODEL * 4 * 7
-    roof = {"kernel": "lazy_adam_step", "bound": "hbm", "achieved": adam_bytes / (adam_ms / 1e3) / 1e9,
+    M = N * HEADS * KNN
+    fused = mem.shard is None        # one backward per step on one GPU: the row sums go straight into the step
+    if fused:
+        # the fused step: read p / m / v and write them back for every touched row, clear its mark, read the
+        # sorted (row, position) pairs and weights and the output gradient rows (the accumulator is never used)
+        adam_bytes = U * D_MODEL * 4 * 6 + U + M * 12 + N * D_MODEL * 4
+    else:
+        # mask scan, row list, read p / m / v / acc, write p / m / v (the clean RowStore keeps consumed acc rows)
+        adam_bytes = rows * 1 + U * (4 + 4 + 1) + U * D_MODEL * 4 * 7
+    roof = {"kernel": "lazy_adam_step (fused with the deferred row sums)" if fused else "lazy_adam_step",
+            "bound": "hbm", "achieved": adam_bytes / (adam_ms / 1e3) / 1e9,
             "peak": hbm, "peak_source": peak_src, "unit": "GB/s",
             "traffic": round(ADAM_TRAFFIC_PER_ROW * U) if ADAM_TRAFFIC_PER_ROW else None,
             "traffic_source": "ncu dram bytes per touched row on a 1M-row capture, scaled by the measured rows",
             "algorithmic_bytes": adam_bytes, "unique_rows": U}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    M = N * HEADS * KNN
     kernel_bytes = {
         "bag_forward": M * (D_MODEL * 4 + 12) + N * D_MODEL * 4,
-        # table row once per run + accumulator row written (first touch of the step: not read) + sort + gw
-        "bag_backward_rows": U * D_MODEL * 4 * 2 + M * (8 * 4 + 4 + 4) + N * D_MODEL * 4,
+        # deferred (fused): each distinct table row once for the weight gradient, grad_out, sort, gw, the row
+        # norms and marks; otherwise also the accumulator rows written
+        "bag_backward_rows": (U * D_MODEL * 4 * (1 if fused else 2) + M * (8 * 4 + 4 + 4) + N * D_MODEL * 4
+                              + U * 5),
         "lazy_adam_step": adam_bytes,
         # row-sharded owner side: every rank's lookups scanned (8 B), this shard's ~M rows gathered, partials out
         "shard_bag_forward": world * M * 8 + M * D_MODEL * 4 + world * N * D_MODEL * 4,

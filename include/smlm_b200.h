@@ -58,6 +58,11 @@ extern "C" {
 /* flags of smlm_bag_backward_rows: rows whose touched byte is 0 are written, not accumulated (the caller
  * guarantees such rows count as zero, e.g. a RowStore whose untouched rows are never read as data) */
 #define SMLM_BWD_FIRST_TOUCH_WRITES 1
+/* flags of smlm_bag_backward_rows: deferred row sums (needs SMLM_BWD_FIRST_TOUCH_WRITES, touched and row_sqnorm;
+ * acc may be NULL). The call sorts the lookups, writes gw, the row norms and the touched marks, but not the rows:
+ * the sorted pairs stay in the workspace, and smlm_lazy_adam_deferred_step (or smlm_bag_rows_materialize) finish
+ * them later with the same grad_out, weights and sizes. */
+#define SMLM_BWD_DEFER_ROWS 2
 /* flags of the optimizer steps: leave the consumed accumulator rows unchanged instead of zeroing them (they
  * count as zero once their touched byte is cleared) */
 #define SMLM_STEP_KEEP_ACC 1
@@ -120,6 +125,13 @@ SMLM_API int smlm_bag_backward_rows(const void *grad_out, int grad_dtype, const 
                                     int64_t n, int64_t k, int64_t rows, int64_t d, void *workspace,
                                     size_t workspace_bytes, int *status, void *stream);
 
+/* Writes the rows of a deferred backward (SMLM_BWD_DEFER_ROWS; every row it touched counts as zero before):
+ * acc[row] = the row's sum, exactly what the backward would have written. Same grad_out, weights, sizes and
+ * workspace as that backward. No counterpart in the reference (its backward always writes the rows). */
+SMLM_API int smlm_bag_rows_materialize(const void *grad_out, int grad_dtype, const void *weights, int weights_dtype,
+                                       float *acc, int64_t n, int64_t k, int64_t rows, int64_t d, void *workspace,
+                                       size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------------- row-sparse optimizers */
 
 SMLM_API size_t smlm_touched_workspace(int64_t rows);
@@ -163,6 +175,19 @@ SMLM_API int smlm_lazy_adam_lowmem_step(float *param, void *exp_avg, void *exp_a
  *   p[r] -= (lr / denom) * g;  acc[r] = 0;  touched[r] = 0.
  * count may be NULL for SMLM_ROWADAGRAD. flags: SMLM_STEP_KEEP_ACC.
  * Replaces RowWiseOptimizer._masked (row_optim.py:179-201). */
+/* Lazy Adam fused with the row sums of a deferred backward: each row's sum (the gradient
+ * smlm_bag_rows_materialize would have written, in the same summation order) goes straight into the
+ * smlm_lazy_adam_step update of that row (same scalars, same operation order: the result is bit-identical to
+ * materialising and stepping), touched cleared; the accumulator is never written or read. Same grad_out,
+ * weights, sizes and workspace as the deferred backward. Replaces kernels.py:417-433 lazy_adam_step for a
+ * RowStore whose rows come from one backward since the last step. */
+SMLM_API int smlm_lazy_adam_deferred_step(float *param, float *exp_avg, float *exp_avg_sq, uint8_t *touched,
+                                          const void *grad_out, int grad_dtype, const void *weights, int weights_dtype,
+                                          const float *grad_scale_dev, float grad_scale, int64_t n, int64_t k,
+                                          int64_t rows, int64_t d, float one_minus_b1, float b2, float one_minus_b2,
+                                          float bc2_sqrt, float eps, float neg_step_size, void *value_copy,
+                                          int copy_dtype, void *workspace, size_t workspace_bytes, void *stream);
+
 SMLM_API int smlm_rowwise_step(float *param, float *acc, uint8_t *touched, float *v, int32_t *count,
                                const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d, int kind,
                                float b2, float eps, float lr, int flags, void *workspace, size_t workspace_bytes,

@@ -81,13 +81,7 @@ struct AdamArgs {
 
 // Element update in the reference C loop's order (host_rows.c:69-76), every operation rounded on its own.
 __device__ __forceinline__ void adam_elem(const AdamArgs& a, float scale, float& p, float& m, float& v, float g) {
-    const float gk = __fmul_rn(g, scale);
-    const float mk = __fadd_rn(m, __fmul_rn(a.one_minus_b1, __fsub_rn(gk, m)));
-    const float vk = __fadd_rn(__fmul_rn(v, a.b2), __fmul_rn(__fmul_rn(a.one_minus_b2, gk), gk));
-    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vk), a.bc2_sqrt), a.eps);
-    p = __fadd_rn(p, __fmul_rn(a.neg_step, __fdiv_rn(mk, denom)));
-    m = mk;
-    v = vk;
+    adam_update(AdamScalars{a.one_minus_b1, a.b2, a.one_minus_b2, a.bc2_sqrt, a.eps, a.neg_step}, scale, p, m, v, g);
 }
 
 template <int VEC>

@@ -352,7 +352,23 @@ struct SegArgs {
     int64_t m, rows;
     int k, d, P;
     int64_t chunks;
+    int all_fresh;      // every row counts as untouched (materialising a deferred backward)
 };
+
+// The fused optimizer pass over deferred row sums: each completed row sum goes straight into lazy Adam.
+struct RowAdam {
+    float *p, *m, *v;
+    const float* scale_dev;
+    float scale;
+    AdamScalars s;
+    void* copy;
+    int copy_dtype;
+};
+
+// What the row-sum pass does with a completed row sum x (= 0 + the run's sum for a first touch):
+constexpr int ROWS_WRITE = 0;  // acc[row] = x (or acc[row] + x), its squared norm, touched = 1
+constexpr int ROWS_NORM = 1;   // only its squared norm and touched = 1 (deferred backward: acc stays untouched)
+constexpr int ROWS_ADAM = 2;   // lazy Adam of the table row with gradient x, touched = 0
 
 // One warp per chunk of P sorted positions. Each run of equal rows is summed in position order; runs that
 // lie inside the chunk go straight into acc (they belong to this chunk alone: no atomics), the run that
@@ -616,8 +632,8 @@ static void launch_gw(GwArgs a, cudaStream_t st) {
 // with the next position's grad_out row in flight in a second register buffer, adds w * grad_out row to the
 // run's sum, and writes each finished run's row once (with its squared norm and touched flag). Same summation
 // order and results as bb_segment_kernel.
-template <typename GT, int NS>
-__global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a) {
+template <typename GT, int NS, int MODE>
+__global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
     const int lane = lane_id();
     const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (c >= a.chunks) return;
@@ -638,17 +654,22 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a) {
     const bool mid = head_cross && tail_cross && first_row == last_row;
     int cflags = 0;
     constexpr uint32_t FRESH = 0x80000000u;
+    const float scale = MODE == ROWS_ADAM ? (ad.scale_dev ? *ad.scale_dev : ad.scale) : 1.f;
 
     uint32_t cur = NO_ROW;
     bool cur_fresh = false;
     float sum[NS][4];
+    float pr[MODE == ROWS_ADAM ? NS : 1][4], mr[MODE == ROWS_ADAM ? NS : 1][4], vr[MODE == ROWS_ADAM ? NS : 1][4];
 #pragma unroll
     for (int s = 0; s < NS; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
 
+    auto is_direct = [&](uint32_t row) {
+        return !mid && !(head_cross && row == first_row) && !(tail_cross && row == last_row);
+    };
     auto flush = [&]() {
         if (cur == NO_ROW) return;
-        float* dst;
-        bool direct = false;
+        float* dst = nullptr;
+        const bool direct = is_direct(cur);
         if (mid) {
             dst = a.carry_head + c * a.d;
             cflags |= FLAG_MID;
@@ -657,29 +678,45 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a) {
         } else if (tail_cross && cur == last_row) {
             dst = a.carry_tail + c * a.d;
             cflags |= FLAG_TAIL;
-        } else {
+        } else if (MODE == ROWS_WRITE) {
             dst = a.acc + (int64_t)cur * a.d;
-            direct = true;
         }
-        const bool accumulate = direct && !cur_fresh;
+        const bool accumulate = MODE == ROWS_WRITE && direct && !cur_fresh;
         float sq = 0.f;
 #pragma unroll
         for (int s = 0; s < NS; s++) {
             const int col = (lane + 32 * s) * 4;
             if (col < a.d) {
-                float4* q = reinterpret_cast<float4*>(dst + col);
-                float4 x = accumulate ? *q : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (!direct) {  // a partial of a run that crosses chunks: the fix-up completes it
+                    *reinterpret_cast<float4*>(dst + col) = make_float4(sum[s][0], sum[s][1], sum[s][2], sum[s][3]);
+                    continue;
+                }
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (accumulate) x = *reinterpret_cast<float4*>(dst + col);
                 x.x = x.x + sum[s][0]; x.y = x.y + sum[s][1]; x.z = x.z + sum[s][2]; x.w = x.w + sum[s][3];
-                __stcs(q, x);  // streaming store: the row is not read again until the optimizer step
-                sq = fmaf(x.x, x.x, sq); sq = fmaf(x.y, x.y, sq); sq = fmaf(x.z, x.z, sq); sq = fmaf(x.w, x.w, sq);
+                if constexpr (MODE == ROWS_WRITE) {
+                    __stcs(reinterpret_cast<float4*>(dst + col), x);  // not read again until the optimizer step
+                } else if constexpr (MODE == ROWS_ADAM) {
+                    const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                    for (int i = 0; i < 4; i++) adam_update(ad.s, scale, pr[s][i], mr[s][i], vr[s][i], xs[i]);
+                    const int64_t o = (int64_t)cur * a.d + col;
+                    *reinterpret_cast<float4*>(ad.p + o) = make_float4(pr[s][0], pr[s][1], pr[s][2], pr[s][3]);
+                    *reinterpret_cast<float4*>(ad.m + o) = make_float4(mr[s][0], mr[s][1], mr[s][2], mr[s][3]);
+                    *reinterpret_cast<float4*>(ad.v + o) = make_float4(vr[s][0], vr[s][1], vr[s][2], vr[s][3]);
+                    if (ad.copy) store_out<4>(ad.copy, ad.copy_dtype, o, pr[s]);
+                }
+                if constexpr (MODE != ROWS_ADAM) {
+                    sq = fmaf(x.x, x.x, sq); sq = fmaf(x.y, x.y, sq); sq = fmaf(x.z, x.z, sq); sq = fmaf(x.w, x.w, sq);
+                }
             }
         }
         if (direct) {
-            if (a.sqnorm) {
+            if (MODE != ROWS_ADAM && a.sqnorm) {
                 sq = warp_sum(sq);
                 if (lane == 0) a.sqnorm[cur] = sq;
             }
-            if (lane == 0 && a.touched) a.touched[cur] = 1;
+            if (lane == 0 && a.touched) a.touched[cur] = MODE == ROWS_ADAM ? 0 : 1;
         }
     };
     auto load_g = [&](uint32_t tokf, float (&v)[NS][4]) {
@@ -697,6 +734,20 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a) {
             cur_fresh = (tokf & FRESH) != 0;
 #pragma unroll
             for (int s = 0; s < NS; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
+            if constexpr (MODE == ROWS_ADAM) {
+                if (is_direct(row)) {  // the row's parameters and moments, in flight while its run is summed
+                    const int64_t base = (int64_t)row * a.d;
+#pragma unroll
+                    for (int s = 0; s < NS; s++) {
+                        const int col = (lane + 32 * s) * 4;
+                        if (col < a.d) {
+                            Elt<float>::template load<4>(ad.p + base + col, pr[s]);
+                            Elt<float>::template load<4>(ad.m + base + col, mr[s]);
+                            Elt<float>::template load<4>(ad.v + base + col, vr[s]);
+                        }
+                    }
+                }
+            }
         }
 #pragma unroll
         for (int s = 0; s < NS; s++)
@@ -712,7 +763,8 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a) {
             my_key = a.keys[b + lane];
             if (my_key < valid_lim) {
                 const uint32_t p = a.pos[b + lane];
-                const bool fresh = a.first_writes && a.touched && a.touched[my_key] == 0;
+                const bool fresh = MODE == ROWS_WRITE &&
+                                   (a.all_fresh || (a.first_writes && a.touched && a.touched[my_key] == 0));
                 my_tokf = p / (uint32_t)a.k | (fresh ? FRESH : 0u);
                 my_w = load_weight(a.w, a.w_dtype, p);
             }
@@ -855,16 +907,19 @@ __global__ void __launch_bounds__(128) bb_rowsum4_kernel(SegArgs a) {
 }
 
 // Completes the runs that cross chunk borders, in chunk order: tail of the run's first chunk, the full
-// chunks it covers, then the head of the chunk where it ends.
-template <int VEC>
-__global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a) {
+// chunks it covers, then the head of the chunk where it ends; then does with the row what the row-sum pass does
+// with a direct row (MODE).
+template <int VEC, int MODE>
+__global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a, RowAdam ad) {
     const int lane = lane_id();
     const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (c >= a.chunks || a.acc == nullptr) return;
+    if (c >= a.chunks || (MODE == ROWS_WRITE && a.acc == nullptr)) return;
     if (!(a.chunk_flags[c] & FLAG_TAIL)) return;
     const int64_t end = min((c + 1) * a.P, a.m);
     const uint32_t row = a.keys[end - 1];
-    const bool accumulate = !(a.first_writes && a.touched && a.touched[row] == 0);
+    const bool accumulate = MODE == ROWS_WRITE && !a.all_fresh &&
+                            !(a.first_writes && a.touched && a.touched[row] == 0);
+    const float scale = MODE == ROWS_ADAM ? (ad.scale_dev ? *ad.scale_dev : ad.scale) : 1.f;
     float sq = 0.f;
     for (int col0 = lane * VEC; col0 < a.d; col0 += 32 * VEC) {
         float tot[VEC];
@@ -880,19 +935,47 @@ __global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a) {
 #pragma unroll
             for (int i = 0; i < VEC; i++) tot[i] = tot[i] + a.carry_head[c2 * a.d + col0 + i];
         }
-        float* dst = a.acc + (int64_t)row * a.d + col0;
+        const int64_t o = (int64_t)row * a.d + col0;
 #pragma unroll
         for (int i = 0; i < VEC; i++) {
-            const float x = (accumulate ? dst[i] : 0.f) + tot[i];
-            dst[i] = x;
-            sq = fmaf(x, x, sq);
+            const float x = (accumulate ? a.acc[o + i] : 0.f) + tot[i];
+            if constexpr (MODE == ROWS_WRITE) a.acc[o + i] = x;
+            if constexpr (MODE == ROWS_ADAM) {
+                float p = ad.p[o + i], m = ad.m[o + i], v = ad.v[o + i];
+                adam_update(ad.s, scale, p, m, v, x);
+                ad.p[o + i] = p;
+                ad.m[o + i] = m;
+                ad.v[o + i] = v;
+                if (ad.copy) {
+                    if (ad.copy_dtype == SMLM_BF16) static_cast<uint16_t*>(ad.copy)[o + i] = (uint16_t)f32_to_bf16_bits(p);
+                    else static_cast<float*>(ad.copy)[o + i] = p;
+                }
+            } else {
+                sq = fmaf(x, x, sq);
+            }
         }
     }
-    if (a.sqnorm) {
+    if (MODE != ROWS_ADAM && a.sqnorm) {
         sq = warp_sum(sq);
         if (lane == 0) a.sqnorm[row] = sq;
     }
-    if (lane == 0 && a.touched) a.touched[row] = 1;
+    if (lane == 0 && a.touched) a.touched[row] = MODE == ROWS_ADAM ? 0 : 1;
+}
+
+// The row-sum pass for a deferred backward (MODE ROWS_NORM) or the fused optimizer step (ROWS_ADAM): rows of
+// 16-byte-aligned float4 groups only, at most 512 wide (the caller checks).
+template <typename GT, int MODE>
+static int launch_rows_mode(SegArgs a, RowAdam ad, cudaStream_t st) {
+    const int ns = (a.d / 4 + 31) / 32;
+    const int blocks = (int)((a.chunks + 3) / 4);
+    if (ns <= 1) bb_rowsum_kernel<GT, 1, MODE><<<blocks, 128, 0, st>>>(a, ad);
+    else if (ns == 2) bb_rowsum_kernel<GT, 2, MODE><<<blocks, 128, 0, st>>>(a, ad);
+    else if (ns == 3) bb_rowsum_kernel<GT, 3, MODE><<<blocks, 128, 0, st>>>(a, ad);
+    else bb_rowsum_kernel<GT, 4, MODE><<<blocks, 128, 0, st>>>(a, ad);
+    SMLM_LAUNCHED("bb_rowsum_kernel");
+    bb_fixup_kernel<4, MODE><<<(int)((a.chunks + 7) / 8), 256, 0, st>>>(a, ad);
+    SMLM_LAUNCHED("bb_fixup_kernel");
+    return SMLM_OK;
 }
 
 template <typename TT, typename GT, bool GW, int VEC>
@@ -900,23 +983,24 @@ static int launch_segment(SegArgs a, cudaStream_t st) {
     const int slots = (a.d + VEC - 1) / VEC;
     const int ns = (slots + 31) / 32;
     const int blocks = (int)((a.chunks + 3) / 4);
+    const RowAdam none{};
     if (!GW && VEC == 4 && ns <= 1 && sizeof(GT) == 2 && a.acc != nullptr) {
         // short bf16 rows (the scoring backward's 128-wide key rows): four chunks per warp (measured faster);
         // wide fp32 rows keep one chunk per warp (measured faster there)
         bb_rowsum4_kernel<GT, 4><<<(int)((a.chunks + 15) / 16), 128, 0, st>>>(a);
         SMLM_LAUNCHED("bb_rowsum4_kernel");
     } else if (!GW && VEC == 4 && ns <= 4 && a.acc != nullptr) {
-        if (ns <= 1) bb_rowsum_kernel<GT, 1><<<blocks, 128, 0, st>>>(a);
-        else if (ns == 2) bb_rowsum_kernel<GT, 2><<<blocks, 128, 0, st>>>(a);
-        else if (ns == 3) bb_rowsum_kernel<GT, 3><<<blocks, 128, 0, st>>>(a);
-        else bb_rowsum_kernel<GT, 4><<<blocks, 128, 0, st>>>(a);
+        if (ns <= 1) bb_rowsum_kernel<GT, 1, ROWS_WRITE><<<blocks, 128, 0, st>>>(a, none);
+        else if (ns == 2) bb_rowsum_kernel<GT, 2, ROWS_WRITE><<<blocks, 128, 0, st>>>(a, none);
+        else if (ns == 3) bb_rowsum_kernel<GT, 3, ROWS_WRITE><<<blocks, 128, 0, st>>>(a, none);
+        else bb_rowsum_kernel<GT, 4, ROWS_WRITE><<<blocks, 128, 0, st>>>(a, none);
         SMLM_LAUNCHED("bb_rowsum_kernel");
     } else if (ns <= 1) bb_segment_kernel<TT, GT, GW, VEC, 1><<<blocks, 128, 0, st>>>(a);
     else if (ns == 2) bb_segment_kernel<TT, GT, GW, VEC, 2><<<blocks, 128, 0, st>>>(a);
     else if (ns == 3) bb_segment_kernel<TT, GT, GW, VEC, 3><<<blocks, 128, 0, st>>>(a);
     else bb_segment_kernel<TT, GT, GW, VEC, 4><<<blocks, 128, 0, st>>>(a);
     SMLM_LAUNCHED("bb_segment_kernel");
-    bb_fixup_kernel<VEC><<<(int)((a.chunks + 7) / 8), 256, 0, st>>>(a);
+    bb_fixup_kernel<VEC, ROWS_WRITE><<<(int)((a.chunks + 7) / 8), 256, 0, st>>>(a, none);
     SMLM_LAUNCHED("bb_fixup_kernel");
     return SMLM_OK;
 }
@@ -1084,11 +1168,18 @@ static int backward_impl(const char* fn, const void* grad_out, int grad_dtype, c
     SMLM_CHECK_ARG(n * k < (int64_t)0x7fffffff, "%s: n * k must be below 2^31", fn);
     SMLM_CHECK_ARG(rows < (int64_t)0xffffffff, "%s: rows must be below 2^32 - 1", fn);
     SMLM_CHECK_ARG(d < (1 << 30), "%s: d too large", fn);
-    SMLM_CHECK_ARG((flags & ~SMLM_BWD_FIRST_TOUCH_WRITES) == 0, "%s: unknown flags %d", fn, flags);
+    SMLM_CHECK_ARG((flags & ~(SMLM_BWD_FIRST_TOUCH_WRITES | SMLM_BWD_DEFER_ROWS)) == 0, "%s: unknown flags %d", fn,
+                   flags);
     SMLM_CHECK_ARG(!(flags & SMLM_BWD_FIRST_TOUCH_WRITES) || touched != nullptr,
                    "%s: first-touch writes need the touched mask", fn);
+    const bool defer = (flags & SMLM_BWD_DEFER_ROWS) != 0;
+    SMLM_CHECK_ARG(!defer || (touched && row_sqnorm && (flags & SMLM_BWD_FIRST_TOUCH_WRITES)),
+                   "%s: deferred row sums need first-touch writes, the touched mask and the row norms", fn);
+    SMLM_CHECK_ARG(!defer || (d % 4 == 0 && d <= 512 &&
+                              reinterpret_cast<uintptr_t>(grad_out) % (grad_dtype == SMLM_F32 ? 16 : 8) == 0),
+                   "%s: deferred row sums need d %% 4 == 0, d <= 512 and an aligned grad_out", fn);
     if (n == 0 || k == 0) return SMLM_OK;
-    SMLM_CHECK_ARG(grad_out && indices && weights && (table || !gw) && (gw || acc), "%s: null pointer", fn);
+    SMLM_CHECK_ARG(grad_out && indices && weights && (table || !gw) && (gw || acc || defer), "%s: null pointer", fn);
     if (d == 0 && gw) {
         SMLM_CUDA(cudaMemsetAsync(gw, 0, sizeof(float) * n * k, as_stream(stream)));
     }
@@ -1132,7 +1223,13 @@ static int backward_impl(const char* fn, const void* grad_out, int grad_dtype, c
         }
         SMLM_LAUNCHED("bb_gw_kernel");
         a.gw = nullptr;
-        if (acc == nullptr) return SMLM_OK;
+        if (acc == nullptr && !defer) return SMLM_OK;
+    }
+    if (defer) {
+        SMLM_CHECK_ARG(a.gw == nullptr, "%s: deferred row sums need an aligned table for the weight gradient", fn);
+        const RowAdam none{};
+        return grad_dtype == SMLM_F32 ? launch_rows_mode<float, ROWS_NORM>(a, none, st)
+                                      : launch_rows_mode<__nv_bfloat16, ROWS_NORM>(a, none, st);
     }
     if (table_dtype == SMLM_F32) return vec ? launch_segment_g<float, 4>(a, st) : launch_segment_g<float, 1>(a, st);
     return vec ? launch_segment_g<__nv_bfloat16, 4>(a, st) : launch_segment_g<__nv_bfloat16, 1>(a, st);
@@ -1160,4 +1257,71 @@ extern "C" int smlm_shard_bag_backward_rows(const void* grad_out, int grad_dtype
     return backward_impl("shard_bag_backward_rows", grad_out, grad_dtype, indices, index_dtype == SMLM_I32, row_base,
                          1, weights, weights_dtype, table_shard, table_dtype, acc, touched, row_sqnorm, flags, gw, n,
                          k, shard_rows, d, workspace, workspace_bytes, status, stream);
+}
+
+namespace smlm {
+// The sorted (row, position) pairs a deferred backward left in its workspace, for the passes that finish it.
+static int deferred_args(const char* fn, const void* grad_out, int grad_dtype, const void* weights, int weights_dtype,
+                         int64_t n, int64_t k, int64_t rows, int64_t d, void* workspace, size_t workspace_bytes,
+                         SegArgs* a) {
+    SMLM_CHECK_ARG(n >= 0 && k >= 0 && rows >= 0 && d % 4 == 0 && d > 0 && d <= 512, "%s: bad sizes", fn);
+    SMLM_CHECK_ARG(weights_dtype == SMLM_F32 || weights_dtype == SMLM_BF16, "%s: weights must be fp32 or bf16", fn);
+    SMLM_CHECK_ARG(grad_dtype == SMLM_F32 || grad_dtype == SMLM_BF16, "%s: grad_out must be fp32 or bf16", fn);
+    SMLM_CHECK_ARG(n * k < (int64_t)0x7fffffff && rows < (int64_t)0xffffffff, "%s: size too large", fn);
+    SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(grad_out) % (grad_dtype == SMLM_F32 ? 16 : 8) == 0,
+                   "%s: grad_out must be aligned", fn);
+    BackwardPlan p = plan_backward(n, k, rows);
+    BackwardBufs bb;
+    const size_t need = layout_backward(p, d, nullptr, &bb);
+    if (workspace == nullptr || workspace_bytes < need) {
+        set_error("%s: workspace too small (%zu < %zu)", fn, workspace_bytes, need);
+        return SMLM_ERR_WORKSPACE;
+    }
+    layout_backward(p, d, workspace, &bb);
+    *a = SegArgs{bb.keys_out, bb.pos_out, grad_out, grad_dtype, weights, weights_dtype, nullptr, nullptr, nullptr,
+                 nullptr, bb.carry_head, bb.carry_tail, bb.flags, nullptr, 1, p.m, rows, (int)k, (int)d, p.P,
+                 p.chunks, 1};
+    return SMLM_OK;
+}
+}  // namespace smlm
+
+extern "C" int smlm_bag_rows_materialize(const void* grad_out, int grad_dtype, const void* weights, int weights_dtype,
+                                         float* acc, int64_t n, int64_t k, int64_t rows, int64_t d, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+    SegArgs a;
+    int rc = deferred_args("bag_rows_materialize", grad_out, grad_dtype, weights, weights_dtype, n, k, rows, d,
+                           workspace, workspace_bytes, &a);
+    if (rc != SMLM_OK || n == 0 || k == 0) return rc;
+    SMLM_CHECK_ARG(acc && reinterpret_cast<uintptr_t>(acc) % 16 == 0, "bag_rows_materialize: acc must be aligned");
+    a.acc = acc;
+    const RowAdam none{};
+    cudaStream_t st = as_stream(stream);
+    return grad_dtype == SMLM_F32 ? launch_rows_mode<float, ROWS_WRITE>(a, none, st)
+                                  : launch_rows_mode<__nv_bfloat16, ROWS_WRITE>(a, none, st);
+}
+
+extern "C" int smlm_lazy_adam_deferred_step(float* param, float* exp_avg, float* exp_avg_sq, uint8_t* touched,
+                                            const void* grad_out, int grad_dtype, const void* weights,
+                                            int weights_dtype, const float* grad_scale_dev, float grad_scale,
+                                            int64_t n, int64_t k, int64_t rows, int64_t d, float one_minus_b1, float b2,
+                                            float one_minus_b2, float bc2_sqrt, float eps, float neg_step_size,
+                                            void* value_copy, int copy_dtype, void* workspace, size_t workspace_bytes,
+                                            void* stream) {
+    SegArgs a;
+    int rc = deferred_args("lazy_adam_deferred_step", grad_out, grad_dtype, weights, weights_dtype, n, k, rows, d,
+                           workspace, workspace_bytes, &a);
+    if (rc != SMLM_OK || n == 0 || k == 0) return rc;
+    SMLM_CHECK_ARG(param && exp_avg && exp_avg_sq && touched, "lazy_adam_deferred_step: null pointer");
+    SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(param) % 16 == 0 && reinterpret_cast<uintptr_t>(exp_avg) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(exp_avg_sq) % 16 == 0 &&
+                       (value_copy == nullptr || reinterpret_cast<uintptr_t>(value_copy) % 16 == 0),
+                   "lazy_adam_deferred_step: tables must be 16-byte aligned");
+    SMLM_CHECK_ARG(value_copy == nullptr || copy_dtype == SMLM_F32 || copy_dtype == SMLM_BF16,
+                   "lazy_adam_deferred_step: value copy must be fp32 or bf16");
+    a.touched = touched;
+    RowAdam ad{param, exp_avg, exp_avg_sq, grad_scale_dev, grad_scale,
+               AdamScalars{one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step_size}, value_copy, copy_dtype};
+    cudaStream_t st = as_stream(stream);
+    return grad_dtype == SMLM_F32 ? launch_rows_mode<float, ROWS_ADAM>(a, ad, st)
+                                  : launch_rows_mode<__nv_bfloat16, ROWS_ADAM>(a, ad, st);
 }

@@ -127,6 +127,21 @@ __device__ __forceinline__ void flag(int* status, int bit) {
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
+// Lazy Adam update of one element in the reference C loop's order (host_rows.c:69-76), every operation rounded
+// on its own: the one definition used by every Adam kernel of the library.
+struct AdamScalars {
+    float one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step;
+};
+__device__ __forceinline__ void adam_update(const AdamScalars& a, float scale, float& p, float& m, float& v, float g) {
+    const float gk = __fmul_rn(g, scale);
+    const float mk = __fadd_rn(m, __fmul_rn(a.one_minus_b1, __fsub_rn(gk, m)));
+    const float vk = __fadd_rn(__fmul_rn(v, a.b2), __fmul_rn(__fmul_rn(a.one_minus_b2, gk), gk));
+    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vk), a.bc2_sqrt), a.eps);
+    p = __fadd_rn(p, __fmul_rn(a.neg_step, __fdiv_rn(mk, denom)));
+    m = mk;
+    v = vk;
+}
+
 // Vector loads of VEC elements (fp32 or bf16) widened to fp32 (16-byte / 8-byte loads for VEC == 4).
 template <typename T>
 struct Elt;

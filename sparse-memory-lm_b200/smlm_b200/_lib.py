@@ -21,6 +21,7 @@ FLAG_INDEX_RANGE = 1
 FLAG_TIMEOUT = 4
 ROWRMS, ROWADAGRAD = 0, 1
 BWD_FIRST_TOUCH_WRITES = 1
+BWD_DEFER_ROWS = 2
 STEP_KEEP_ACC = 1
 SCORE_F32_EXACT, SCORE_BF16 = 0, 1
 
@@ -48,6 +49,9 @@ SIGNATURES = {
     "smlm_bag_backward_rows": (_i32, [_p, _i32, _p, _p, _i32, _p, _i32, _p, _p, _p, _i32, _p, _i64, _i64, _i64,
                                       _i64, _p, _sz, _p, _p]),
     "smlm_touched_workspace": (_sz, [_i64]),
+    "smlm_bag_rows_materialize": (_i32, [_p, _i32, _p, _i32, _p, _i64, _i64, _i64, _i64, _p, _sz, _p]),
+    "smlm_lazy_adam_deferred_step": (_i32, [_p, _p, _p, _p, _p, _i32, _p, _i32, _p, _f32, _i64, _i64, _i64, _i64,
+                                            _f32, _f32, _f32, _f32, _f32, _f32, _p, _i32, _p, _sz, _p]),
     "smlm_lazy_adam_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32,
                                    _p, _i32, _i32, _p, _sz, _p]),
     "smlm_lazy_adam_lowmem_step": (_i32, [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32,

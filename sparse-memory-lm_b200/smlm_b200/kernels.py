@@ -343,6 +343,79 @@ def slot_sum(x):
     return out
 
 
+class DeferredRows:
+    """The sorted lookups of a backward whose row sums were deferred (SMLM_BWD_DEFER_ROWS), with the tensors that
+    finish them: the workspace, grad_out and the weights (kept alive until the rows are written or stepped)."""
+
+    def __init__(self, ws, g, w, n, k, rows, d):
+        self.ws, self.g, self.w = ws, g, w
+        self.n, self.k, self.rows, self.d = n, k, rows, d
+
+
+def deferrable(table, acc):
+    """Whether bag_backward_deferred applies: float4 rows at most 512 wide, 16-byte aligned."""
+    D = table.shape[1]
+    return (D % 4 == 0 and D <= 512 and table.dtype in (torch.float32, torch.bfloat16) and acc.is_contiguous()
+            and table.data_ptr() % 16 == 0)
+
+
+def bag_backward_deferred(grad_out, indices, weights, table, touched, row_sqnorm):
+    """bag_backward_rows into a clean accumulator with the row sums deferred: returns the weight gradient and a
+    DeferredRows; the rows' squared norms and touched marks are written now, the rows themselves by
+    bag_rows_materialize or lazy_adam_deferred_step later."""
+    dev = L.require_cuda(grad_out, indices, weights, table, touched, row_sqnorm)
+    N, Kk = indices.shape
+    rows, D = table.shape
+    g = _contig(grad_out if grad_out.dtype in (torch.float32, torch.bfloat16) else grad_out.float())
+    if g.data_ptr() % 16:
+        g = g.clone()                       # the deferred passes read grad_out rows as aligned vectors
+    idx = _contig(indices.long())
+    w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
+    t = _contig(table)
+    gw = torch.empty(N, Kk, dtype=torch.float32, device=dev)
+    ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, Kk, rows, D), dev)
+    with L.timed("bag_backward_rows", L.backward_launches(rows)):
+        rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), L.ptr(w),
+                                            L.dtype_code(w.dtype), L.ptr(t), L.dtype_code(t.dtype), None,
+                                            L.ptr(touched), L.ptr(row_sqnorm),
+                                            L.BWD_FIRST_TOUCH_WRITES | L.BWD_DEFER_ROWS, L.ptr(gw), N, Kk, rows, D,
+                                            L.ptr(ws), ws.numel(), L.status_ptr(dev), L.stream(dev))
+    L.check(rc, "bag_backward_rows (deferred)")
+    L.after(dev, "bag_backward_rows")
+    return gw, DeferredRows(ws, g, w, N, Kk, rows, D)
+
+
+def bag_rows_materialize(pending, acc):
+    """Writes the deferred rows into acc (rows untouched before the deferred backward)."""
+    dev = L.require_cuda(acc)
+    p = pending
+    with L.timed("bag_rows_materialize", 2):
+        rc = L.lib().smlm_bag_rows_materialize(L.ptr(p.g), L.dtype_code(p.g.dtype), L.ptr(p.w), L.dtype_code(p.w.dtype),
+                                               L.ptr(acc), p.n, p.k, p.rows, p.d, L.ptr(p.ws), p.ws.numel(),
+                                               L.stream(dev))
+    L.check(rc, "bag_rows_materialize")
+
+
+def lazy_adam_deferred_step(param, exp_avg, exp_avg_sq, touched, pending, grad_scale, step, lr, beta1, beta2, eps,
+                            value_copy=None):
+    """lazy_adam_step fused with the deferred row sums: bit-identical to bag_rows_materialize + lazy_adam_step,
+    without writing or reading the accumulator."""
+    dev = L.require_cuda(param, exp_avg, exp_avg_sq, touched, value_copy)
+    p = pending
+    sp, sf, keep = _scale_args(grad_scale, dev)
+    bc1 = 1 - beta1 ** step
+    bc2 = 1 - beta2 ** step
+    with L.timed("lazy_adam_step", 2):
+        rc = L.lib().smlm_lazy_adam_deferred_step(
+            L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(touched), L.ptr(p.g), L.dtype_code(p.g.dtype),
+            L.ptr(p.w), L.dtype_code(p.w.dtype), sp, sf, p.n, p.k, p.rows, p.d, 1 - beta1, beta2, 1 - beta2,
+            math.sqrt(bc2), eps, -(lr / bc1), L.ptr(value_copy),
+            L.dtype_code(value_copy.dtype) if value_copy is not None else L.F32, L.ptr(p.ws), p.ws.numel(),
+            L.stream(dev))
+    L.check(rc, "lazy_adam_deferred_step")
+    del keep
+
+
 def quantize_q4(table, chunk=None):
     """table (rows, D) fp32 -> packed (rows, D/2) uint8, scales (rows,) fp16 (reference: kernels.py:280-294):
     per row d = half(w[argmax |w|] / -8) (1 if that is 0), codes clamp(round(w / d), -8, 7) + 8; byte i holds

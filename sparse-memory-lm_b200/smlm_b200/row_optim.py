@@ -51,9 +51,10 @@ class RowWiseOptimizer(torch.optim.Optimizer):
                 st = row_store(p)
                 state = self._state(p)
                 state["step"] += 1
+                st.materialize()
                 K.rowwise_step(p, st._acc, st._touched, state["v"], state.get("n"), st.grad_scale, group["lr"],
                                group["beta2"], group["eps"], self.kind, keep_acc=st.clean)
-                st.grad_scale = 1.0
+                st.stepped()
 
     def zero_grad(self, set_to_none=True):
         pass                                   # the accumulator is cleared in step(), as in LazyRowAdam

@@ -64,6 +64,8 @@ class CudaShardOps:
     def bag_backward(self, g, idx, w, table, base, store):
         if store is None:
             return K.shard_bag_backward_rows(g, idx, w, table, base, None, None)
+        store.materialize()
+        store.live = True
         return K.shard_bag_backward_rows(g, idx, w, table, base, store._acc, store._touched,
                                          row_sqnorm=store._sqnorm if store.clean else None,
                                          first_touch_writes=store.clean)
@@ -230,6 +232,8 @@ class _PeerBag(torch.autograd.Function):
                 t.shape[1], ctx.epoch, status, L.stream(dev))
         L.check(rc, "xchg_backward_gw")
         if store is not None and shard.count:
+            store.materialize()
+            store.live = True
             K.shard_bag_backward_rows(all_g, all_idx, all_w, t, shard.base, store._acc, store._touched,
                                       row_sqnorm=store._sqnorm if store.clean else None,
                                       first_touch_writes=store.clean, want_gw=False)

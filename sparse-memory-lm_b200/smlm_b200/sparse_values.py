@@ -43,6 +43,8 @@ class RowStore:
         self._sqnorm = torch.zeros(table.shape[0], dtype=torch.float32, device=table.device)
         self.grad_scale = 1.0           # set by clipping, applied in the optimizer step
         self.clean = True
+        self.live = False               # acc holds rows written since the last reset / step
+        self.pending = None             # a backward's deferred row sums (kernels.DeferredRows), not yet in acc
 
     @property
     def acc(self):
@@ -56,9 +58,21 @@ class RowStore:
 
     def expose(self):
         """Make `acc` an exact dense accumulator (stale untouched rows <- 0) before outside code reads it."""
+        self.materialize()
         if self.clean:
             K.zero_untouched(self._acc, self._touched)
             self.clean = False
+
+    def materialize(self):
+        """Write the deferred row sums of the last backward into acc (where that backward would have)."""
+        if self.pending is not None:
+            K.bag_rows_materialize(self.pending, self._acc)
+            self.pending = None
+            self.live = True
+
+    def can_defer(self, table):
+        """A backward may leave its row sums to the optimizer step: nothing else is in the store yet."""
+        return self.clean and not self.live and self.pending is None and K.deferrable(table, self._acc)
 
     def touched_rows(self):
         """Number of touched rows (synchronises; does not expose the store)."""
@@ -70,10 +84,19 @@ class RowStore:
                 self._acc.zero_()
             self._touched.zero_()
             self.clean = True           # every row is untouched and counts as zero
+            self.live = False
+            self.pending = None
         else:
+            self.materialize()
             if not self.clean:
                 self._acc.index_fill_(0, rows, 0.0)
             self._touched.index_fill_(0, rows, False)
+        self.grad_scale = 1.0
+
+    def stepped(self):
+        """The optimizer consumed every touched row (touched cleared, acc rows zeroed or left stale)."""
+        self.live = False
+        self.pending = None
         self.grad_scale = 1.0
 
     def norm(self):
@@ -111,10 +134,15 @@ class _RowSparseBag(torch.autograd.Function):
         w, indices = ctx.saved_tensors
         if store is None:
             gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
+        elif store.can_defer(table):
+            # the first backward into an empty store: its row sums go straight into the optimizer step
+            gw, store.pending = K.bag_backward_deferred(grad_out, indices, w, table, store._touched, store._sqnorm)
         else:
+            store.materialize()
             gw = K.bag_backward_rows(grad_out, indices, w, table, store._acc, store._touched,
                                      row_sqnorm=store._sqnorm if store.clean else None,
                                      first_touch_writes=store.clean)
+            store.live = True
         # drop the RowStore reference so that `del table.row_store` after training frees the accumulator
         ctx.table = ctx.store = None
         return gw.view(ctx.wshape).to(ctx.wdtype), None, None, None, None
@@ -229,16 +257,23 @@ class LazyRowAdam(torch.optim.Optimizer):
                 st = row_store(p)
                 state = self._state(p)
                 state["step"] += 1
-                if self.state_dtype == "fp32":
+                if self.state_dtype == "fp32" and st.pending is not None and not st.live:
+                    # rows of one deferred backward: summed and stepped in one pass, acc never written
+                    K.lazy_adam_deferred_step(p, state["exp_avg"], state["exp_avg_sq"], st._touched, st.pending,
+                                              st.grad_scale, int(state["step"]), group["lr"], b1, b2, group["eps"],
+                                              value_copy=getattr(p, "value_copy", None))
+                elif self.state_dtype == "fp32":
+                    st.materialize()
                     K.lazy_adam_step(p, state["exp_avg"], state["exp_avg_sq"], st._acc, st._touched,
                                      st.grad_scale, int(state["step"]), group["lr"], b1, b2, group["eps"],
                                      value_copy=getattr(p, "value_copy", None), keep_acc=st.clean)
                 else:
+                    st.materialize()
                     K.lazy_adam_lowmem_step(p, state["exp_avg"], state["exp_avg_sq"], state.get("exp_avg_scale"),
                                             state.get("exp_avg_sq_scale"), st._acc, st._touched, st.grad_scale,
                                             int(state["step"]), group["lr"], b1, b2, group["eps"],
                                             value_copy=getattr(p, "value_copy", None), keep_acc=st.clean)
-                st.grad_scale = 1.0         # the kernel has zeroed the read accumulator rows and the mask
+                st.stepped()                # touched rows consumed; grad_scale back to 1
 
     def zero_grad(self, set_to_none=True):
         # the accumulator is cleared in step(); rows accumulated by a backward without a following step stay in

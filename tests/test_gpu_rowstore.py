@@ -101,3 +101,80 @@ def test_clean_store_equals_exact_store_over_steps():
     # exposing the clean store yields the exact accumulator (all zero after the last step)
     st = row_store(mems[0].values.weight)
     assert torch.count_nonzero(st.acc) == 0 and not st.touched.any()
+
+
+def test_deferred_rows_materialize_and_fused_step_bit_exact():
+    """A deferred backward (row norms and touched marks now, rows later) materialises exactly the rows the
+    write path produces, and the fused sum-and-Adam step equals materialising then stepping, bit for bit;
+    hot rows make runs cross the 256-position work chunks."""
+    gen = torch.Generator().manual_seed(4)
+    rows, D, N, Kk = 20000, 384, 4096, 256                       # N K >= 2^20: 256-position chunks
+    table = torch.randn(rows, D, generator=gen) * D ** -0.5
+    idx = skewed_indices(rows, N, Kk, gen)
+    w = torch.softmax(torch.randn(N, Kk, generator=gen), -1)
+    g = torch.randn(N, D, generator=gen)
+    T, I, W, G = (x.to(DEV) for x in (table, idx, w, g))
+    # write path into a clean store
+    acc_w = torch.randn(rows, D, generator=gen).to(DEV)          # stale garbage: first-touch writes ignore it
+    t_w = torch.zeros(rows, dtype=torch.bool, device=DEV)
+    sq_w = torch.zeros(rows, device=DEV)
+    gw_w = K.bag_backward_rows(G, I, W, T, acc_w, t_w, row_sqnorm=sq_w, first_touch_writes=True)
+    # deferred path
+    t_d = torch.zeros(rows, dtype=torch.bool, device=DEV)
+    sq_d = torch.zeros(rows, device=DEV)
+    gw_d, pend = K.bag_backward_deferred(G, I, W, T, t_d, sq_d)
+    assert torch.equal(t_d, t_w) and torch.equal(sq_d[t_d], sq_w[t_w]) and torch.equal(gw_d, gw_w)
+    acc_d = torch.randn(rows, D, generator=gen).to(DEV)
+    K.bag_rows_materialize(pend, acc_d)
+    assert torch.equal(acc_d[t_d], acc_w[t_w])
+    # fused step == materialise + lazy Adam step, with a clip factor and a bf16 value copy
+    p0 = torch.randn(rows, D, generator=gen).to(DEV)
+    m0 = (torch.randn(rows, D, generator=gen) * 1e-3).to(DEV)
+    v0 = (torch.rand(rows, D, generator=gen) * 1e-5).to(DEV)
+    scale = torch.tensor(0.37, device=DEV)
+    outs = []
+    for fused in (False, True):
+        p, m, v = p0.clone(), m0.clone(), v0.clone()
+        copy = p0.bfloat16()
+        touched = t_w.clone()
+        if fused:
+            K.lazy_adam_deferred_step(p, m, v, touched, pend, scale, 3, 1e-2, 0.9, 0.98, 1e-8, value_copy=copy)
+        else:
+            K.lazy_adam_step(p, m, v, acc_w.clone(), touched, scale, 3, 1e-2, 0.9, 0.98, 1e-8, value_copy=copy,
+                             keep_acc=True)
+        assert not touched.any()
+        outs.append((p, m, v, copy))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    assert torch.equal(outs[1][0][~t_w], p0[~t_w])               # unread rows untouched
+
+
+def test_single_backward_steps_fused_equal_exact_store():
+    """One backward per step (the fused path: the accumulator is never written) against a store read from
+    outside after every backward (exact mode), three steps with clipping: tables and moments bit-identical."""
+    mems = []
+    for _ in range(2):
+        torch.manual_seed(0)
+        mems.append(ProductKeyMemory(64, 64, n_keys=64, heads=4, knn=16, k_dim=32, query_norm="none",
+                                     swilu=False, value_grad="row_sparse").to(DEV))
+    mems[1].load_state_dict(mems[0].state_dict())
+    opts = [LazyRowAdam([m.values.weight], lr=1e-2, betas=(0.9, 0.98)) for m in mems]
+    gen = torch.Generator().manual_seed(5)
+    for step in range(3):
+        x = torch.randn(300, 64, generator=gen).to(DEV)
+        g = torch.randn(300, 64, generator=gen).to(DEV)
+        for i, m in enumerate(mems):
+            m(x).backward(g)
+            if i == 1:
+                row_store(m.values.weight).acc                   # exact mode
+        assert row_store(mems[0].values.weight).pending is not None
+        norms = [float(clip_row_sparse([m.values.weight], 0.05)) for m in mems]
+        assert abs(norms[0] - norms[1]) <= 1e-5 * norms[1]
+        for m in mems:
+            row_store(m.values.weight).grad_scale = 0.5
+        for o in opts:
+            o.step()
+        assert row_store(mems[0].values.weight).pending is None
+        assert torch.equal(mems[0].values.weight, mems[1].values.weight)
+        for k in ("exp_avg", "exp_avg_sq"):
+            assert torch.equal(opts[0].state[mems[0].values.weight][k], opts[1].state[mems[1].values.weight][k])

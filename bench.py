@@ -296,7 +296,8 @@ def run_cuda(args, world, rank, local):
     hbm = hbm or 6650.0
     adam_ms = statistics.mean(per_kernel["lazy_adam_step"])
     M = N * HEADS * KNN
-    fused = mem.shard is None        # one backward per step on one GPU: the row sums go straight into the step
+    # one backward per step: the row sums go straight into the step (one GPU, or shards behind the peer exchange)
+    fused = mem.shard is None or mem.shard_exchange == "p2p"
     if fused:
         # the fused step: read p / m / v and write them back for every touched row, clear its mark, read the
         # sorted (row, position) pairs and weights and the output gradient rows (the accumulator is never used)
@@ -320,7 +321,8 @@ def run_cuda(args, world, rank, local):
         "lazy_adam_step": adam_bytes,
         # row-sharded owner side: every rank's lookups scanned (8 B), this shard's ~M rows gathered, partials out
         "shard_bag_forward": world * M * 8 + M * D_MODEL * 4 + world * N * D_MODEL * 4,
-        "shard_bag_backward_rows": U * D_MODEL * 4 * 2 + world * M * (8 * 4 + 8) + world * N * D_MODEL * 4,
+        "shard_bag_backward_rows": (U * D_MODEL * 4 * (0 if fused else 1) + world * M * (8 * 4 + 8)
+                                    + world * N * D_MODEL * 4 + U * 5),
     }
     breakdown = {}
     for name, t in sorted(per_kernel.items()):

@@ -385,6 +385,31 @@ def bag_backward_deferred(grad_out, indices, weights, table, touched, row_sqnorm
     return gw, DeferredRows(ws, g, w, N, Kk, rows, D)
 
 
+def shard_bag_backward_deferred(grad_out, indices, weights, table_shard, row_base, touched, row_sqnorm):
+    """shard_bag_backward_rows with the row sums deferred (no weight gradient): the shard's row norms and touched
+    marks now, a DeferredRows for the optimizer step (or bag_rows_materialize)."""
+    dev = L.require_cuda(grad_out, indices, weights, table_shard, touched, row_sqnorm)
+    N, Kk = indices.shape
+    rows, D = table_shard.shape
+    g = _contig(grad_out if grad_out.dtype in (torch.float32, torch.bfloat16) else grad_out.float())
+    if g.data_ptr() % 16:
+        g = g.clone()
+    idx = _contig(indices)
+    w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
+    t = _contig(table_shard)
+    ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, Kk, rows, D), dev)
+    with L.timed("shard_bag_backward_rows", L.backward_launches(rows)):
+        rc = L.lib().smlm_shard_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), _index_code(idx),
+                                                  int(row_base), L.ptr(w), L.dtype_code(w.dtype),
+                                                  L.ptr(t) if rows else None, L.dtype_code(t.dtype), None,
+                                                  L.ptr(touched), L.ptr(row_sqnorm),
+                                                  L.BWD_FIRST_TOUCH_WRITES | L.BWD_DEFER_ROWS, None, N, Kk, rows, D,
+                                                  L.ptr(ws), ws.numel(), L.status_ptr(dev), L.stream(dev))
+    L.check(rc, "shard_bag_backward_rows (deferred)")
+    L.after(dev, "shard_bag_backward_rows")
+    return DeferredRows(ws, g, w, N, Kk, rows, D)
+
+
 def bag_rows_materialize(pending, acc):
     """Writes the deferred rows into acc (rows untouched before the deferred backward)."""
     dev = L.require_cuda(acc)

@@ -232,11 +232,16 @@ class _PeerBag(torch.autograd.Function):
                 t.shape[1], ctx.epoch, status, L.stream(dev))
         L.check(rc, "xchg_backward_gw")
         if store is not None and shard.count:
-            store.materialize()
-            store.live = True
-            K.shard_bag_backward_rows(all_g, all_idx, all_w, t, shard.base, store._acc, store._touched,
-                                      row_sqnorm=store._sqnorm if store.clean else None,
-                                      first_touch_writes=store.clean, want_gw=False)
+            if store.can_defer(t):
+                # the shard's row sums go straight into the optimizer step (see RowStore)
+                store.pending = K.shard_bag_backward_deferred(all_g, all_idx, all_w, t, shard.base, store._touched,
+                                                              store._sqnorm)
+            else:
+                store.materialize()
+                store.live = True
+                K.shard_bag_backward_rows(all_g, all_idx, all_w, t, shard.base, store._acc, store._touched,
+                                          row_sqnorm=store._sqnorm if store.clean else None,
+                                          first_touch_writes=store.clean, want_gw=False)
         gw = torch.empty(N, Kk, dtype=torch.float32, device=dev)
         with L.timed("xchg_collect_gw", 1):
             rc = L.lib().smlm_xchg_collect_gw(L.ptr(x.peers), shard.rank, P, N, Kk, x.n_cap, t.shape[1],

@@ -56,9 +56,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows-per-half", type=int, default=1024)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
-    ap.add_argument("--case", choices=["layer", "scoring"], default="layer",
+    ap.add_argument("--case", choices=["layer", "scoring", "inference"], default="layer",
                     help="scoring: only the fused sub-key scoring + selection of the workload's layer (a small "
-                         "standalone case for profiler captures; prints its time per call)")
+                         "standalone case for profiler captures; prints its time per call); inference: only the "
+                         "B-16M prefill / decode measurement")
+    ap.add_argument("--no-inference", action="store_true", help="leave the inference measurement out of the line")
     return ap.parse_args()
 
 
@@ -350,6 +352,108 @@ def run_cuda(args, world, rank, local):
     return line
 
 
+# ------------------------------------------------------------------------------------------- inference
+def _event_ms(fn, reps):
+    """Device time of `reps` calls of fn (CUDA events on the current stream, synchronised on both sides)."""
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e)
+
+
+@torch.no_grad()
+def run_inference(args, local):
+    """The B-16M inference token loop (the metric's "B-16M decode tok/s"): the reference's B-16M model (12 layers,
+    d_model 384, 6 attention heads, SwiGLU 1024, vocab 50304, product-key memories in layers 2, 6 and 10 sharing
+    one 4096^2 = 16,777,216 x 384 fp32 value table, BatchNorm queries, swilu), random-init weights, eval mode,
+    bf16 autocast, through smlm_b200.model.Transformer. Measured like the reference's inference_benchmark
+    (smlm/train.py:283-315): prefill of 2048 uniform random token ids at batch 1 and 64 (full forward, logits of
+    every position), then 256 greedy decode steps from that prefill: decode_b* through smlm_b200.decode.GraphDecoder
+    (static KV cache, the whole step one CUDA graph), decode_b*_eager through the reference's loop (growing KV
+    cache, one-token memory layers replaying their own graphs). Plus the per-token product-key lookup latency: one memory layer
+    on one token (query projection, fused scoring + top-k + softmax, value bag with the swilu product) and the
+    lookup alone (fused scoring + selection, value bag), each as a CUDA-graph replay. All device-timed with CUDA
+    events."""
+    from smlm_b200 import kernels as K
+    from smlm_b200.decode import GraphDecoder
+    from smlm_b200.model import ModelConfig, Transformer
+    dev = torch.device("cuda", local)
+    prompt, new = 2048, 256
+    cfg = ModelConfig(mem_layers=[2, 6, 10], mem_n_keys=args.rows_per_half, mem_share_values=True,
+                      mem_value_grad="row_sparse", max_seq_len=prompt + new)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = Transformer(cfg)
+    model.eval()
+    model.set_memory_decode_graphs(True)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    res = {"model": "B-16M (12 layers, PKM in layers 2/6/10 sharing one table)" if args.rows_per_half == 4096
+           else f"B ({args.rows_per_half ** 2} rows)", "rows": args.rows_per_half ** 2, "prompt_len": prompt,
+           "new_tokens": new, "dtype": "bf16 autocast, fp32 value table", "data": "synthetic uniform token ids"}
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        for b in (1, 64):
+            ids = torch.randint(0, cfg.vocab_size, (b, prompt), device=dev, generator=gen)
+            model(ids)                                                     # warm-up
+            reps = 5 if b == 1 else 2
+            ms = _event_ms(lambda: model(ids), reps) / reps
+            res[f"prefill_b{b}_tok_s"] = round(b * prompt / (ms / 1e3), 1)
+            res[f"prefill_b{b}_ms"] = round(ms, 3)
+            for rep in range(2):                                           # rep 0: warm-up (graph capture)
+                caches = [dict() for _ in range(cfg.n_layers)]
+                logits = model(ids, kv_caches=caches, pos0=0)
+                state = {"nxt": logits[:, -1:].argmax(-1), "i": 0}
+                del logits
+                steps = 8 if rep == 0 else new
+
+                def decode_step():
+                    lg = model(state["nxt"], kv_caches=caches, pos0=prompt + state["i"])
+                    state["nxt"] = lg[:, -1:].argmax(-1)
+                    state["i"] += 1
+                ms = _event_ms(decode_step, steps)
+            res[f"decode_b{b}_eager_tok_s"] = round(b * new / (ms / 1e3), 1)
+            del caches, state
+            dec = GraphDecoder(model, b, max_len=prompt + new)
+            dec.prefill(ids)
+            dec.step()                                                     # capture
+            dec.prefill(ids)
+            ms = _event_ms(dec.step, new)
+            res[f"decode_b{b}_tok_s"] = round(b * new / (ms / 1e3), 1)
+            res[f"decode_b{b}_ms_per_step"] = round(ms / new, 4)
+            del dec, ids
+        # one memory layer, one token: the layer's decode graph
+        mem = model.memory_layers()[0]
+        x1 = torch.randn(1, cfg.d_model, device=dev, generator=gen)
+        for _ in range(3):
+            mem(x1)
+        res["pkm_layer_us_per_token"] = round(_event_ms(lambda: mem(x1), 200) / 200 * 1e3, 2)
+    # the lookup alone: fused scoring + top-k + softmax and the value bag of one token, captured once
+    q1 = torch.randn(1, mem.heads, mem.k_dim, device=dev, generator=gen).bfloat16()
+    keys = mem.keys.detach().bfloat16()
+    table = mem.values.weight.detach()
+
+    def lookup():
+        _, idx, w = K.score_select(q1, keys, mem.knn)
+        return K.bag_infer(idx.view(1, -1), w.view(1, -1), table, out_bf16=True)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            lookup()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        lookup()
+    for _ in range(3):
+        graph.replay()
+    res["pkm_lookup_us_per_token"] = round(_event_ms(graph.replay, 200) / 200 * 1e3, 2)
+    del graph, model
+    return res
+
+
 # ----------------------------------------------------------------------------------------- CPU reference
 def cpu_reference(n_keys, N, steps, warmup):
     """The reference's PyTorch path (oracle/torch_path.py) on the host cores: fwd + bwd + clip + lazy Adam
@@ -401,6 +505,9 @@ def main():
     if args.case == "scoring":
         run_scoring_case(args)
         return
+    if args.case == "inference":
+        print(json.dumps({"case": "inference", **run_inference(args, 0)}), flush=True)
+        return
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         if rank == 0:
@@ -420,6 +527,11 @@ def main():
             torch.distributed.destroy_process_group()
         return
     line = run_cuda(args, world, rank, local)
+    if world == 1 and not args.no_inference:
+        import gc
+        gc.collect()
+        torch.cuda.empty_cache()
+        line["inference"] = run_inference(args, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_reference(args.cpu_rows_per_half, args.cpu_tokens, 2, 1)
     if rank == 0:

@@ -167,10 +167,140 @@ static int launch_bag_vec(BagArgs a, cudaStream_t st) {
     return SMLM_OK;
 }
 
+// Few tokens (decoding, short prompts): one warp per (token, 512-byte column block). A warp-per-token gather
+// keeps only a few rows in flight, so a token's lookups would cost one memory round trip per few rows. Here
+// every valid lookup's slice of the column block is copied into shared memory with cp.async (16 bytes per lane,
+// L2-only), up to SMALL_STAGES chunks of 32 lookups in flight at once, and then summed in lookup order: the same
+// sequential fmaf chain per column as bag_gather_kernel, so the same bits. A lane reads back only the bytes it
+// copied itself; the chunk's weights and valid marks go through shared memory to the whole warp.
+constexpr int SMALL_STAGES = 4;
+constexpr int SMALL_ROW_BYTES = 512;  // 32 lanes x 16 bytes
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait(int pending) {  // wait until at most `pending` groups are in flight
+    if (pending <= 0) asm volatile("cp.async.wait_group 0;" ::: "memory");
+    else if (pending == 1) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else if (pending == 2) asm volatile("cp.async.wait_group 2;" ::: "memory");
+    else asm volatile("cp.async.wait_group 3;" ::: "memory");
+}
+
+template <typename TT>
+__global__ void __launch_bounds__(32) bag_small_kernel(BagArgs a, int stages) {
+    constexpr int VEC = 16 / sizeof(TT);
+    extern __shared__ __align__(16) uint8_t small_buf[];                      // [stages][32][512]
+    float* sw = reinterpret_cast<float*>(small_buf + stages * 32 * SMALL_ROW_BYTES);  // [stages][32] weights
+    uint32_t* svalid = reinterpret_cast<uint32_t*>(sw + stages * 32);                 // [stages] valid lookups
+    const int lane = threadIdx.x;
+    const int nblk = (a.d + 32 * VEC - 1) / (32 * VEC);
+    const int64_t n = blockIdx.x / nblk;
+    const int col = (int)(blockIdx.x % nblk) * 32 * VEC + lane * VEC;
+    const bool on = col < a.d;
+    const TT* table = static_cast<const TT*>(a.table);
+    const int nchunks = (a.k + 31) / 32;
+
+    auto issue = [&](int ch) {
+        const int slot = ch % stages;
+        const int j = ch * 32 + lane;
+        int64_t r = -1;
+        float w = 0.f;
+        if (j < a.k) {
+            r = load_index(a.idx, a.idx32, n * a.k + j) - a.row_base;
+            w = load_weight(a.w, a.w_dtype, n * a.k + j);
+            if (r < 0 || r >= a.rows) {
+                if (!a.skip_foreign) flag(a.status, SMLM_FLAG_INDEX_RANGE);
+                r = -1;
+            }
+        }
+        sw[slot * 32 + lane] = w;
+        const uint32_t valid = __ballot_sync(FULL, r >= 0);
+        if (lane == 0) svalid[slot] = valid;
+        const int cnt = min(32, a.k - ch * 32);
+        uint8_t* dst = small_buf + (size_t)slot * 32 * SMALL_ROW_BYTES + lane * 16;
+        for (int u = 0; u < cnt; u++) {
+            const int64_t ru = __shfl_sync(FULL, r, u);
+            if (ru >= 0 && on) cp_async16(dst + u * SMALL_ROW_BYTES, table + ru * a.d + col);
+        }
+        cp_async_commit();
+    };
+
+    float acc[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; i++) acc[i] = 0.f;
+    int issued = 0;
+    for (; issued < min(stages, nchunks); issued++) issue(issued);
+    for (int ch = 0; ch < nchunks; ch++) {
+        cp_async_wait(issued - ch - 1);
+        __syncwarp();
+        const int slot = ch % stages;
+        const int cnt = min(32, a.k - ch * 32);
+        const uint8_t* src = small_buf + (size_t)slot * 32 * SMALL_ROW_BYTES + lane * 16;
+        const uint32_t valid = svalid[slot];
+        for (int u = 0; u < cnt; u++) {
+            if (!((valid >> u) & 1u) || !on) continue;  // warp-uniform except for `on`
+            const float w = sw[slot * 32 + u];
+            float v[VEC];
+            if constexpr (sizeof(TT) == 4) {
+                const float4 x = *reinterpret_cast<const float4*>(src + u * SMALL_ROW_BYTES);
+                v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+            } else {
+                const uint4 x = *reinterpret_cast<const uint4*>(src + u * SMALL_ROW_BYTES);
+                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    v[2 * i] = bf16_bits_to_f32(xs[i] & 0xffffu);
+                    v[2 * i + 1] = bf16_bits_to_f32(xs[i] >> 16);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < VEC; i++) acc[i] = fmaf(w, v[i], acc[i]);
+        }
+        __syncwarp();  // the slot is free again
+        if (issued < nchunks) issue(issued++);
+    }
+    if (!on) return;
+    if (a.pre) {
+#pragma unroll
+        for (int i = 0; i < VEC; i++) {
+            const int64_t off = n * a.d + col + i;
+            const float p = a.pre_dtype == SMLM_F32 ? __ldg(static_cast<const float*>(a.pre) + off)
+                                                    : bf16_bits_to_f32(__ldg(static_cast<const uint16_t*>(a.pre) + off));
+            acc[i] = acc[i] * silu_bf16(p);
+        }
+    }
+    store_out<VEC>(a.out, a.out_dtype, n * a.d + col, acc);
+}
+
+// Token counts up to this take bag_small_kernel.
+constexpr int64_t BAG_SMALL_N = 256;
+
+template <typename TT>
+static int launch_bag_small(BagArgs a, cudaStream_t st) {
+    constexpr int VEC = 16 / sizeof(TT);
+    const int stages = (int)std::min<int64_t>(SMALL_STAGES, (a.k + 31) / 32);
+    const size_t smem = (size_t)stages * (32 * (SMALL_ROW_BYTES + 4) + 4);
+    if (smem > 48 * 1024) {
+        SMLM_CUDA(cudaFuncSetAttribute(bag_small_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    }
+    const int64_t blocks = a.n * ((a.d + 32 * VEC - 1) / (32 * VEC));
+    bag_small_kernel<TT><<<(unsigned)blocks, 32, smem, st>>>(a, stages);
+    SMLM_LAUNCHED("bag_small_kernel");
+    return SMLM_OK;
+}
+
 static int launch_bag(BagArgs a, int table_dtype, cudaStream_t st) {
     if (a.n == 0 || a.d == 0) return SMLM_OK;
     const uintptr_t tp = reinterpret_cast<uintptr_t>(a.table);
     const uintptr_t op = reinterpret_cast<uintptr_t>(a.out);
+    if (a.n <= BAG_SMALL_N && a.k > 0 && tp % 16 == 0 && (a.out_dtype != SMLM_F32 || op % 16 == 0) &&
+        (a.pre == nullptr || a.pre_dtype == SMLM_F32 || a.pre_dtype == SMLM_BF16)) {
+        if (table_dtype == SMLM_F32 && a.d % 4 == 0) return launch_bag_small<float>(a, st);
+        if (table_dtype == SMLM_BF16 && a.d % 8 == 0) return launch_bag_small<__nv_bfloat16>(a, st);
+    }
     const bool out_vec_ok = a.out_dtype != SMLM_F32 || (op % 16 == 0);
     if (table_dtype == SMLM_F32) {
         if (a.d % 4 == 0 && tp % 16 == 0 && out_vec_ok) return launch_bag_vec<float, 4>(a, st);

@@ -7,7 +7,11 @@
 // per-half top-k computes. A second small kernel (select.cu, pk_pairs_kernel) forms the knn x knn pairs and the
 // softmax from the two per-half lists.
 //
-// CTA = 10 warps, persistent over units (128-token tile, head); a unit runs half 0 then half 1:
+// CTA = 10 warps, persistent over units (128-token tile, head, key-range split); a unit runs half 0 then half 1.
+// With at least as many (tile, head) pairs as SMs there is one split (all key tiles); with fewer (decoding, short
+// prompts) the key tiles are divided among up to #SMs / #pairs splits, each writing its own per-half top lists
+// (a split of fewer than PRE_MIN_TILES key tiles skips the pre-pass described below):
+
 //   warp 0      TMA producer: Q tile (128 tokens x 128, two 64-wide 128B-swizzled boxes) and key tiles
 //               (128 keys x 128) through a 3-stage ring, completion by mbarrier transaction counts.
 //   warp 1      allocates 256 TMEM columns (two 128-column fp32 accumulators); lane 0 issues tcgen05.mma
@@ -36,8 +40,8 @@
 
 namespace smlm {
 
-int launch_pk_pairs(const uint32_t* lists, int64_t rows_nh, int nk, int knn, void* scores, int64_t* idx, float* w,
-                    cudaStream_t st);
+int launch_pk_pairs(const uint32_t* lists, int lists_per_half, int64_t rows_nh, int nk, int knn, void* scores,
+                    int64_t* idx, float* w, cudaStream_t st);
 
 namespace tc {
 
@@ -55,6 +59,7 @@ constexpr int ATOM_BYTES_A = BM * 128;
 constexpr int ATOM_BYTES_B = BN * 128;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr unsigned long long WAIT_NS = 1000000000ull;  // bound of every mbarrier wait
+constexpr int PRE_MIN_TILES = 16;  // key tiles a unit needs before the pre-pass can yield a bound
 
 // ------------------------------------------------------------------------------------------- PTX wrappers
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -370,7 +375,8 @@ struct Epi {
 
 struct Params {
     int n, heads, nk, atoms;  // atoms = half / 64
-    uint32_t* lists;          // [n][heads][2 halves][2 column sets][32]
+    int splits;               // key-range splits per (tile, head): 1, or more when there are few token tiles
+    uint32_t* lists;          // [n][heads][2 halves][splits][2 column sets][32]
     uint16_t* dbg1;           // optional bf16 scores [n][heads][nk], half 0
     uint16_t* dbg2;           // half 1
     int* status;
@@ -400,8 +406,17 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (P.n + BM - 1) / BM;
-    const int units = tiles_m * P.heads;
+    const int units = tiles_m * P.heads * P.splits;
     const int ntiles = (P.nk + BN - 1) / BN;
+    // unit u = ((tile * heads) + head) * splits + split; split s covers key tiles [kt0, kt1)
+    auto unit_tiles = [&](int u, int& kt0) {
+        const int s = u % P.splits;
+        kt0 = (int)((int64_t)s * ntiles / P.splits);
+        return (int)((int64_t)(s + 1) * ntiles / P.splits) - kt0;
+    };
+    // passes over a unit's key tiles: the pre-pass only yields a bound once a thread holds 32 group maxima (two
+    // per tile), so units of fewer than PRE_MIN_TILES tiles go straight to the selection pass
+    auto unit_passes = [](int nt) { return nt >= PRE_MIN_TILES ? 2 : 1; };
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; i++) {
@@ -435,7 +450,10 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
             uint32_t ph = 0;
             int a_iter = 0;
             for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-                const int tm = u / P.heads, h = u % P.heads;
+                const int tm = u / P.splits / P.heads, h = (u / P.splits) % P.heads;
+                int kt0;
+                const int nt = unit_tiles(u, kt0);
+                const int np = unit_passes(nt);
                 for (int half = 0; half < 2; half++) {
                     if (!mbar_wait(smem_addr(a_empty), (a_iter & 1) ^ 1, abort_flag)) break;
                     mbar_expect_tx(smem_addr(a_full), a_bytes);
@@ -443,8 +461,8 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                         tma_load_3d(smem_addr(sA + i * ATOM_BYTES_A), &tq, smem_addr(a_full), i * ATOM, h * 2 + half,
                                     tm * BM);
                     a_iter++;
-                    for (int t = 0; t < 2 * ntiles; t++) {  // pre-pass, then the selection pass
-                        const int kt = t < ntiles ? t : t - ntiles;
+                    for (int t = 0; t < np * nt; t++) {  // (pre-pass, then) the selection pass
+                        const int kt = kt0 + (t < nt ? t : t - nt);
                         if (!mbar_wait(smem_addr(&empty_b[s]), ph ^ 1, abort_flag)) break;
                         mbar_expect_tx(smem_addr(&full_b[s]), b_bytes);
                         for (int i = 0; i < P.atoms; i++)
@@ -463,11 +481,14 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
             uint32_t ph = 0;
             int a_iter = 0, t_iter = 0;
             for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+                int kt0;
+                const int nt = unit_tiles(u, kt0);
+                const int np = unit_passes(nt);
                 for (int half = 0; half < 2; half++) {
                     if (!mbar_wait(smem_addr(a_full), a_iter & 1, abort_flag)) break;
                     fence_after();
                     const uint32_t a_base = smem_addr(sA);
-                    for (int t = 0; t < 2 * ntiles; t++) {  // the same key tiles twice (pre-pass, selection)
+                    for (int t = 0; t < np * nt; t++) {  // the key tiles once per pass (pre-pass, selection)
                         if (!mbar_wait(smem_addr(&full_b[s]), ph, abort_flag)) break;
                         const int tb = t_iter & 1;
                         if (!mbar_wait(smem_addr(&t_empty[tb]), ((t_iter >> 1) & 1) ^ 1, abort_flag)) break;
@@ -509,7 +530,10 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
         int t_iter = 0;
         uint32_t pre_seq = 0;
         for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-            const int tm = u / P.heads, h = u % P.heads;
+            const int tm = u / P.splits / P.heads, h = (u / P.splits) % P.heads, split = u % P.splits;
+            int kt0;
+            const int nt = unit_tiles(u, kt0);
+            const int np = unit_passes(nt);
             const int64_t n = (int64_t)tm * BM + row;
             for (int half = 0; half < 2; half++) {
                 uint16_t* dbg = half ? P.dbg2 : P.dbg1;
@@ -518,7 +542,8 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                 bool ok = true;
                 ep.clear();
                 ep.floor = -INFINITY;
-                for (int t = 0; t < 2 * ntiles; t++) {
+                if (np == 1) ep.start_pass2(0u);
+                for (int t = 0; t < np * nt; t++) {
                     const int tb = t_iter & 1;
                     // warp-uniform outcome: the TMEM loads below are .sync.aligned
                     if (!__all_sync(FULL, mbar_wait(smem_addr(&t_full[tb]), (t_iter >> 1) & 1, abort_flag))) {
@@ -535,13 +560,13 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_addr(&t_empty[tb]));
                     t_iter++;
-                    if (t < ntiles) {
+                    if (np == 2 && t < nt) {
                         // pre-pass: group maxima of 32 columns, merged 16 at a time (every lane holds the same count)
-                        const int c0 = t * BN + cset * 64;
+                        const int c0 = (kt0 + t) * BN + cset * 64;
                         ep.group_max(v0, c0, P.nk);
                         ep.group_max(v1, c0 + 32, P.nk);
                         if (ep.cnt == BATCH) ep.flush();
-                        if (t == ntiles - 1) {
+                        if (t == nt - 1) {
                             if (ep.cnt) ep.flush();
                             // the better of the two column-set threads' bounds (both are valid for the union)
                             const uint32_t own = ep.top[31] >> 16;
@@ -549,7 +574,7 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                             ep.start_pass2(max(own, other));
                         }
                     } else {
-                        const int c0 = (t - ntiles) * BN + cset * 64;
+                        const int c0 = (kt0 + t - (np - 1) * nt) * BN + cset * 64;
                         ep.take(v0, c0, P.nk, dbg);
                         ep.take(v1, c0 + 32, P.nk, dbg);
                     }
@@ -557,7 +582,7 @@ __global__ void __launch_bounds__(THREADS, 1) score_topk_kernel(const __grid_con
                 if (!ok) break;
                 if (__any_sync(FULL, ep.cnt > 0)) ep.flush();
                 if (n < P.n) {
-                    uint32_t* dst = P.lists + (((n * P.heads + h) * 2 + half) * 2 + cset) * 32;
+                    uint32_t* dst = P.lists + ((((n * P.heads + h) * 2 + half) * P.splits + split) * 2 + cset) * 32;
 #pragma unroll
                     for (int i = 0; i < 32; i += 4)
                         *reinterpret_cast<uint4*>(dst + i) = make_uint4(ep.top[i], ep.top[i + 1], ep.top[i + 2], ep.top[i + 3]);
@@ -591,13 +616,26 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// Key-range splits per (token tile, head): with fewer (tile, head) units than SMs (decoding, short prefills) each
+// unit's key tiles are split over several CTAs, every split keeping its own per-half top lists, which the pair
+// kernel merges (exact: each list is the top of its keys, and the top knn of all keys lies in their union).
+// ntiles = 0: the upper bound over all key counts (what the workspace query sizes for).
+int score_splits(int64_t n, int64_t h, int64_t ntiles) {
+    const int64_t base = ((n + BM - 1) / BM) * h;
+    int64_t s = base >= sm_count() ? 1 : std::max<int64_t>(1, sm_count() / std::max<int64_t>(base, 1));
+    if (ntiles > 0) s = std::min(s, ntiles);
+    return (int)std::max<int64_t>(1, std::min<int64_t>(s, 512));
+}
+
 }  // namespace tc
 }  // namespace smlm
 
 using namespace smlm;
 
 extern "C" size_t smlm_score_select_workspace(int64_t n, int64_t h) {
-    return (size_t)std::max<int64_t>(n, 0) * std::max<int64_t>(h, 0) * 2 * 2 * 32 * sizeof(uint32_t) + 256;
+    n = std::max<int64_t>(n, 0);
+    h = std::max<int64_t>(h, 0);
+    return (size_t)n * h * 2 * tc::score_splits(n, std::max<int64_t>(h, 1), 0) * 2 * 32 * sizeof(uint32_t) + 256;
 }
 
 extern "C" int smlm_score_select(const void* q, const void* keys, int64_t n, int64_t h, int64_t nk, int64_t half,
@@ -614,7 +652,8 @@ extern "C" int smlm_score_select(const void* q, const void* keys, int64_t n, int
     SMLM_CHECK_ARG(q && keys && scores && indices && weights, "score_select: null pointer");
     SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(keys) % 16 == 0,
                    "score_select: q and keys must be 16-byte aligned");
-    const size_t need = smlm_score_select_workspace(n, h);
+    const int splits = tc::score_splits(n, h, (nk + tc::BN - 1) / tc::BN);
+    const size_t need = (size_t)n * h * 2 * splits * 2 * 32 * sizeof(uint32_t);
     if (workspace == nullptr || workspace_bytes < need) {
         set_error("score_select: workspace too small (%zu < %zu)", workspace_bytes, need);
         return SMLM_ERR_WORKSPACE;
@@ -656,13 +695,13 @@ extern "C" int smlm_score_select(const void* q, const void* keys, int64_t n, int
     const int atoms = (int)(half / tc::ATOM);
     const size_t smem = tc::smem_bytes(atoms);
     SMLM_CUDA(cudaFuncSetAttribute(tc::score_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int64_t units = ((n + tc::BM - 1) / tc::BM) * h;
+    const int64_t units = ((n + tc::BM - 1) / tc::BM) * h * splits;
     const int grid = (int)std::min<int64_t>(units, sm_count());
-    tc::Params P{(int)n, (int)h, (int)nk, atoms, lists, static_cast<uint16_t*>(s1_out), static_cast<uint16_t*>(s2_out),
-                 status};
+    tc::Params P{(int)n, (int)h, (int)nk, atoms, splits, lists, static_cast<uint16_t*>(s1_out),
+                 static_cast<uint16_t*>(s2_out), status};
     tc::score_topk_kernel<<<grid, tc::THREADS, smem, st>>>(tq, tk, P);
     SMLM_LAUNCHED("score_topk_kernel");
-    return launch_pk_pairs(lists, n * h, (int)nk, (int)knn, scores, indices, weights, st);
+    return launch_pk_pairs(lists, 2 * splits, n * h, (int)nk, (int)knn, scores, indices, weights, st);
 }
 
 // ------------------------------------------------------------------------------- allocation-free variant
@@ -757,8 +796,8 @@ extern "C" int smlm_score_select_noalloc(const void* q, const void* keys, int64_
     const int grid = (int)std::min<int64_t>(units, sm_count());
     // every (token, head) row of the lists is written by the scoring kernel before the pair kernel reads it,
     // so the previous call's contents need no clearing
-    tc::Params P{(int)n, (int)h, (int)nk, atoms, lists, nullptr, nullptr, status};
+    tc::Params P{(int)n, (int)h, (int)nk, atoms, 1, lists, nullptr, nullptr, status};
     tc::score_topk_kernel<<<grid, tc::THREADS, smem, st>>>(tq, tk, P);
     SMLM_LAUNCHED("score_topk_kernel");
-    return launch_pk_pairs(lists, n * h, (int)nk, (int)knn, scores, indices, weights, st);
+    return launch_pk_pairs(lists, 2, n * h, (int)nk, (int)knn, scores, indices, weights, st);
 }

@@ -289,11 +289,14 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) pk_select_kernel(const void* s
     }
 }
 
+constexpr int PAIR_BATCH = 16;  // top lists loaded together by the pair kernel
+
 // Pairs + softmax from per-half top lists of bf16 scores, as written by the fused scoring kernel:
-// lists[row][half][set] hold 32 keys (order code of the bf16 score << 16 | (0xffff - sub-key index)), sorted
-// descending, one list per column set; the two sets of a half are merged here.
-__global__ void __launch_bounds__(SEL_WARPS * 32) pk_pairs_kernel(const uint32_t* lists, int64_t rows_nh, int nk,
-                                                                   int knn, void* scores_out, int64_t* idx_out,
+// lists[row][half][list] hold 32 keys (order code of the bf16 score << 16 | (0xffff - sub-key index)), sorted
+// descending, one list per (key-range split, column set); the lists of a half are merged here.
+__global__ void __launch_bounds__(SEL_WARPS * 32) pk_pairs_kernel(const uint32_t* lists, int lists_per_half,
+                                                                   int64_t rows_nh, int nk, int knn,
+                                                                   void* scores_out, int64_t* idx_out,
                                                                    float* w_out) {
     __shared__ uint64_t sbuf[SEL_WARPS][SEL_CAP];
     __shared__ uint32_t sfix[SEL_WARPS][32];
@@ -304,13 +307,24 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) pk_pairs_kernel(const uint32_t
         uint32_t hk[2];
 #pragma unroll
         for (int half = 0; half < 2; half++) {
-            // two sorted lists (column sets) -> the bitonic max sequence -> one sorted list, across lanes
-            const uint32_t* l = lists + ((row * 2 + half) * 2) * 32;
-            uint32_t k = max(l[lane], l[32 + 31 - lane]);
+            // sorted list + next sorted list -> the bitonic max sequence -> one sorted list, across lanes
+            // (with key-range splits: many lists, loaded PAIR_BATCH at a time so their loads overlap)
+            const uint32_t* l = lists + ((row * 2 + half) * lists_per_half) * 32;
+            uint32_t k = l[lane];
+            for (int i0 = 1; i0 < lists_per_half; i0 += PAIR_BATCH) {
+                uint32_t nxt[PAIR_BATCH];
 #pragma unroll
-            for (int j = 16; j > 0; j >>= 1) {
-                const uint32_t x = __shfl_xor_sync(FULL, k, j);
-                k = (lane & j) ? min(k, x) : max(k, x);
+                for (int u = 0; u < PAIR_BATCH; u++) nxt[u] = i0 + u < lists_per_half ? l[(i0 + u) * 32 + 31 - lane] : 0u;
+#pragma unroll
+                for (int u = 0; u < PAIR_BATCH; u++) {
+                    if (i0 + u >= lists_per_half) break;
+                    k = max(k, nxt[u]);
+#pragma unroll
+                    for (int j = 16; j > 0; j >>= 1) {
+                        const uint32_t x = __shfl_xor_sync(FULL, k, j);
+                        k = (lane & j) ? min(k, x) : max(k, x);
+                    }
+                }
             }
             hk[half] = k;
         }
@@ -320,11 +334,11 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) pk_pairs_kernel(const uint32_t
     }
 }
 
-int launch_pk_pairs(const uint32_t* lists, int64_t rows_nh, int nk, int knn, void* scores, int64_t* idx, float* w,
-                    cudaStream_t st) {
+int launch_pk_pairs(const uint32_t* lists, int lists_per_half, int64_t rows_nh, int nk, int knn, void* scores,
+                    int64_t* idx, float* w, cudaStream_t st) {
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((rows_nh + SEL_WARPS - 1) / SEL_WARPS,
                                                                    (int64_t)sm_count() * 8));
-    pk_pairs_kernel<<<blocks, SEL_WARPS * 32, 0, st>>>(lists, rows_nh, nk, knn, scores, idx, w);
+    pk_pairs_kernel<<<blocks, SEL_WARPS * 32, 0, st>>>(lists, lists_per_half, rows_nh, nk, knn, scores, idx, w);
     SMLM_LAUNCHED("pk_pairs_kernel");
     return SMLM_OK;
 }

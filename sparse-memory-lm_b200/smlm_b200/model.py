@@ -11,6 +11,7 @@ from dataclasses import asdict, dataclass, field
 import torch
 import torch.nn.functional as F
 from torch import nn
+from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from .pkm import ProductKeyMemory
 
@@ -57,9 +58,14 @@ class RotaryEmbedding(nn.Module):
         self.register_buffer("sin", freqs.sin(), persistent=False)
 
     def forward(self, x, pos0=0):
+        """pos0: the first position (int), or a device tensor of the T positions (static-cache decoding)."""
         T = x.shape[-2]
-        cos = self.cos[pos0:pos0 + T].to(x.dtype)
-        sin = self.sin[pos0:pos0 + T].to(x.dtype)
+        if torch.is_tensor(pos0):
+            cos = self.cos.index_select(0, pos0).to(x.dtype)
+            sin = self.sin.index_select(0, pos0).to(x.dtype)
+        else:
+            cos = self.cos[pos0:pos0 + T].to(x.dtype)
+            sin = self.sin[pos0:pos0 + T].to(x.dtype)
         x1, x2 = x.chunk(2, dim=-1)
         return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
 
@@ -76,6 +82,8 @@ class Attention(nn.Module):
     def forward(self, x, kv_cache=None, pos0=0):
         B, T, C = x.shape
         q, k, v = self.wqkv(x).view(B, T, 3, self.n_heads, self.head_dim).permute(2, 0, 3, 1, 4)
+        if kv_cache is not None and "kbuf" in kv_cache:
+            return self.wo(self._static(q, k, v, kv_cache).transpose(1, 2).reshape(B, T, C))
         q, k = self.rope(q, pos0), self.rope(k, pos0)
         if kv_cache is not None:
             if kv_cache.get("k") is not None:
@@ -83,12 +91,43 @@ class Attention(nn.Module):
                 v = torch.cat([kv_cache["v"], v], dim=2)
             kv_cache["k"], kv_cache["v"] = k, v
         S = k.shape[2]
-        if T > 1 and S > T:
-            mask = torch.ones(T, S, dtype=torch.bool, device=q.device).tril(S - T)
-            y = F.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+        if kv_cache is not None:
+            # the cache grows by one position per decoding step: keep to the backends that need no per-shape
+            # plan (a backend that builds one per sequence length would re-plan on every step)
+            with sdpa_kernel(_CACHED_BACKENDS):
+                y = _attend(q, k, v, T, S)
         else:
-            y = F.scaled_dot_product_attention(q, k, v, is_causal=T > 1)
+            y = _attend(q, k, v, T, S)
         return self.wo(y.transpose(1, 2).reshape(B, T, C))
+
+
+    def _static(self, q, k, v, cache):
+        """Static KV cache (smlm_b200.decode.GraphDecoder): preallocated (B, heads, max_len, head_dim) buffers and
+        the tokens' positions as a device tensor, so a decoding step has fixed shapes and no host-side position
+        (it can be captured in one CUDA graph). The new keys / values are written at their positions; each query
+        attends to the cache positions up to its own."""
+        pos = cache["pos"]
+        q, k = self.rope(q, pos), self.rope(k, pos)
+        kbuf, vbuf = cache["kbuf"], cache["vbuf"]
+        kbuf.index_copy_(2, pos, k.to(kbuf.dtype))
+        vbuf.index_copy_(2, pos, v.to(vbuf.dtype))
+        mask = cache["arange"].view(1, -1) <= pos.view(-1, 1)
+        # one query for few (sequence, head) pairs (decoding at small batch): the plain matmul form spreads the
+        # cache length over the GPU, where a fused kernel would give each pair one CTA
+        small = q.shape[2] == 1 and q.shape[0] * q.shape[1] < 64
+        with sdpa_kernel([SDPBackend.MATH] if small else _MASKED_BACKENDS):
+            return F.scaled_dot_product_attention(q, kbuf.to(q.dtype), vbuf.to(q.dtype), attn_mask=mask)
+
+
+_CACHED_BACKENDS = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
+_MASKED_BACKENDS = [SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
+
+
+def _attend(q, k, v, T, S):
+    if T > 1 and S > T:
+        mask = torch.ones(T, S, dtype=torch.bool, device=q.device).tril(S - T)
+        return F.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+    return F.scaled_dot_product_attention(q, k, v, is_causal=T > 1)
 
 
 class SwiGLU(nn.Module):

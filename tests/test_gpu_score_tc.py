@@ -91,3 +91,16 @@ def test_score_select_backward_matches_unfused():
         torch.testing.assert_close(qa.grad.float(), qb.grad.float(), rtol=2 ** -7, atol=1e-3)
         torch.testing.assert_close(ka.grad.float(), kb.grad.float(), rtol=2 ** -7, atol=1e-3)
     assert qa.grad.abs().sum() > 0 and ka.grad.abs().sum() > 0
+
+
+@pytest.mark.parametrize("n_small", [1, 3, 64, 130, 600])
+def test_key_range_splits_match_full_sweep(n_small):
+    """Few token tiles (decoding, short prompts) split each (tile, head)'s key tiles over several CTAs, each with
+    its own top lists, merged by the pair kernel. A token's scores do not depend on the other tokens of its tile,
+    so the first n_small tokens alone (split sweep) select exactly what they select inside a batch of 37 tiles x
+    4 heads = 148 units (one unsplit sweep per unit)."""
+    q, keys = inputs(37 * 128, 4, 4096, 128, 11)
+    full = K.score_select(q, keys, 32)
+    part = K.score_select(q[:n_small].contiguous(), keys, 32)
+    for a, b in zip(part, full):
+        assert torch.equal(a, b[:n_small])

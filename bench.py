@@ -40,8 +40,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "PKM layer tokens/s (fwd+bwd+opt) at 16.8M rows"
 # DRAM bytes (read + write) of the fused row-sum + lazy Adam step per touched row, from the ncu capture in
-# profiles/lazy_adam_kernel_pkm-layer-1m.md; traffic scales with the touched rows (None: not measured).
-ADAM_TRAFFIC_PER_ROW = None
+# profiles/bb_rowsum_adam_kernel_pkm-layer-1m.md; traffic scales with the touched rows.
+ADAM_TRAFFIC_PER_ROW = 9575
+# the same for the plain lazy Adam step over a written accumulator (profiles/lazy_adam_kernel_pkm-layer-1m.md)
+ADAM_UNFUSED_TRAFFIC_PER_ROW = 10698
 D_MODEL, HEADS, KNN, K_DIM = 384, 4, 32, 256
 
 
@@ -310,7 +312,7 @@ def run_cuda(args, world, rank, local):
     roof = {"kernel": "lazy_adam_step (fused with the deferred row sums)" if fused else "lazy_adam_step",
             "bound": "hbm", "achieved": adam_bytes / (adam_ms / 1e3) / 1e9,
             "peak": hbm, "peak_source": peak_src, "unit": "GB/s",
-            "traffic": round(ADAM_TRAFFIC_PER_ROW * U) if ADAM_TRAFFIC_PER_ROW else None,
+            "traffic": round((ADAM_TRAFFIC_PER_ROW if fused else ADAM_UNFUSED_TRAFFIC_PER_ROW) * U),
             "traffic_source": "ncu dram bytes per touched row on a 1M-row capture, scaled by the measured rows",
             "algorithmic_bytes": adam_bytes, "unique_rows": U}
     roof["frac"] = roof["achieved"] / roof["peak"]

@@ -18,9 +18,13 @@ restatement under oracle/, the only oracle use in this file) on a bounded sample
 
 --impl reference times the reference's PyTorch path on the host cores instead (rank 0 only under torchrun).
 With --gpus N > 1 (torchrun, one process per GPU, NCCL) the 16.8M-row table and its optimizer state are
-row-sharded over the N GPUs and each GPU runs 32,768 tokens per step (weak scaling): the lookups, partial bags,
-output gradients and weight gradients cross NVLink through NCCL collectives, the replicated parameters'
-gradients are all-reduced.
+row-sharded over the N GPUs and each GPU runs 32,768 tokens per step (weak scaling): the lookups, partial bags
+and weight gradients cross NVLink through peer memory inside the owner kernels, the output gradients through an
+NCCL all-gather, the replicated parameters' gradients through an NCCL all-reduce.
+
+The default run also measures the B-16M inference token loop (`inference`: prefill and greedy decode of the
+B-16M model, per-token lookup latency). --case configs times BASELINE configs 1-3 as single layers (fwd / bwd /
+opt separately); --case scoring and --case inference run one part alone.
 """
 import argparse
 import json
@@ -58,10 +62,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows-per-half", type=int, default=1024)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
-    ap.add_argument("--case", choices=["layer", "scoring", "inference"], default="layer",
+    ap.add_argument("--case", choices=["layer", "scoring", "inference", "configs"], default="layer",
                     help="scoring: only the fused sub-key scoring + selection of the workload's layer (a small "
                          "standalone case for profiler captures; prints its time per call); inference: only the "
-                         "B-16M prefill / decode measurement")
+                         "B-16M prefill / decode measurement; configs: BASELINE configs 1-3 as single layers "
+                         "with fwd / bwd / opt timed separately")
     ap.add_argument("--no-inference", action="store_true", help="leave the inference measurement out of the line")
     return ap.parse_args()
 
@@ -354,6 +359,88 @@ def run_cuda(args, world, rank, local):
     return line
 
 
+# -------------------------------------------------------------------------------------- configs 1 - 3
+# (name, sub-keys per half, tokens per step, bf16 autocast, BatchNorm query + swilu, table optimizer)
+LAYER_CONFIGS = [
+    ("config1-layer-65k-fp32", 256, 2048, False, False, "adam"),
+    ("config2-b1m-layer", 1024, 32768, True, True, "adam"),
+    ("config2-b1m-layer-bf16-moments", 1024, 32768, True, True, "adam-bf16"),
+    ("config3-b4m-layer-rowrms", 2048, 65536, True, True, "rowrms"),
+]
+
+
+def run_configs(args):
+    """BASELINE configs 1-3 as single PKM layers on one GPU, each phase device-timed: config 1 (65,536 rows,
+    2,048 tokens, fp32 without autocast, no BatchNorm / swilu, LazyRowAdam), config 2 (the B-1M model's layer:
+    1,048,576 rows, 32 x 1024 tokens, bf16 autocast, BatchNorm query and swilu, LazyRowAdam with fp32 and with bf16
+    moments), config 3 (the B-4M layer: 4,194,304 rows, 64 x 1024 tokens, the row-wise rowrms optimizer). Seeded
+    synthetic inputs x, upstream gradient ~ N(0, 1). fwd = the layer's forward; bwd = backward + value / dense
+    clipping; opt = the table optimizer + fused AdamW on the dense parameters (with deferred row sums the table's
+    row sums run in opt, not in bwd)."""
+    from smlm_b200.pkm import ProductKeyMemory
+    from smlm_b200.row_optim import RowWiseOptimizer
+    from smlm_b200.sparse_values import LazyRowAdam, OptimizerSet, clip_row_sparse, row_store
+    dev = torch.device("cuda", 0)
+    out = []
+    for name, n_keys, N, autocast, bn, kind in LAYER_CONFIGS:
+        torch.manual_seed(0)
+        with torch.device(dev):
+            mem = ProductKeyMemory(D_MODEL, D_MODEL, n_keys=n_keys, heads=HEADS, knn=KNN, k_dim=K_DIM,
+                                   query_norm="batchnorm" if bn else "none", swilu=bn, value_grad="row_sparse")
+            if not bn:   # config-1 initialisation
+                with torch.no_grad():
+                    mem.query_proj.weight.normal_(0, 0.02)
+                    mem.keys.normal_(0, (K_DIM // 2) ** -0.5)
+        table = mem.values.weight
+        dense = [p for p in mem.parameters() if p is not table]
+        if kind == "rowrms":
+            topt = RowWiseOptimizer([table], lr=1e-3, kind="rowrms", beta2=0.98)
+        else:
+            topt = LazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98), eps=1e-8,
+                               state_dtype="bf16" if kind == "adam-bf16" else "fp32")
+        opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True), topt)
+        gen = torch.Generator(device=dev).manual_seed(1)
+        xs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(2)]
+        gs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(2)]
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+        uniq = []
+
+        def step(i, e=None):
+            if e:
+                e[0].record()
+            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+                o = mem(xs[i % 2])
+            if e:
+                e[1].record()
+            o.backward(gs[i % 2])
+            clip_row_sparse([table], 1.0)
+            torch.nn.utils.clip_grad_norm_([p for p in dense if p.grad is not None], 1.0, foreach=True)
+            if e:
+                e[2].record()
+            else:
+                uniq.append(row_store(table).touched_rows())
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+            if e:
+                e[3].record()
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            step(i, ev[i])
+        torch.cuda.synchronize()
+        ph = [sum(e[j].elapsed_time(e[j + 1]) for e in ev) / args.steps for j in range(3)]
+        out.append({"config": name, "rows": n_keys ** 2, "tokens": N, "autocast_bf16": autocast,
+                    "query_norm_swilu": bn, "optimizer": kind, "fwd_ms": round(ph[0], 4), "bwd_ms": round(ph[1], 4),
+                    "opt_ms": round(ph[2], 4), "tokens_per_s": round(N / (sum(ph) / 1e3), 1),
+                    "unique_rows_per_step": round(sum(uniq[1:]) / max(1, len(uniq) - 1))})
+        del mem, opt, topt, xs, gs
+        import gc
+        gc.collect()
+        torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------------------------------- inference
 def _event_ms(fn, reps):
     """Device time of `reps` calls of fn (CUDA events on the current stream, synchronised on both sides)."""
@@ -506,6 +593,10 @@ def main():
     args = parse()
     if args.case == "scoring":
         run_scoring_case(args)
+        return
+    if args.case == "configs":
+        print(json.dumps({"case": "configs", "steps": args.steps, "warmup": args.warmup,
+                          "configs": run_configs(args)}), flush=True)
         return
     if args.case == "inference":
         print(json.dumps({"case": "inference", **run_inference(args, 0)}), flush=True)

@@ -500,6 +500,12 @@ constexpr int ROWS_WRITE = 0;  // acc[row] = x (or acc[row] + x), its squared no
 constexpr int ROWS_NORM = 1;   // only its squared norm and touched = 1 (deferred backward: acc stays untouched)
 constexpr int ROWS_ADAM = 2;   // lazy Adam of the table row with gradient x, touched = 0
 
+// Parameters and moments of a touched row: read once and written once per step (streaming, evict-first).
+__device__ __forceinline__ void ld_stream4(const float* p, float (&v)[4]) {
+    const float4 x = __ldcs(reinterpret_cast<const float4*>(p));
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+}
+
 // One warp per chunk of P sorted positions. Each run of equal rows is summed in position order; runs that
 // lie inside the chunk go straight into acc (they belong to this chunk alone: no atomics), the run that
 // enters from the previous chunk goes to carry_head, the run that leaves to carry_tail (see fixup).
@@ -831,9 +837,9 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
 #pragma unroll
                     for (int i = 0; i < 4; i++) adam_update(ad.s, scale, pr[s][i], mr[s][i], vr[s][i], xs[i]);
                     const int64_t o = (int64_t)cur * a.d + col;
-                    *reinterpret_cast<float4*>(ad.p + o) = make_float4(pr[s][0], pr[s][1], pr[s][2], pr[s][3]);
-                    *reinterpret_cast<float4*>(ad.m + o) = make_float4(mr[s][0], mr[s][1], mr[s][2], mr[s][3]);
-                    *reinterpret_cast<float4*>(ad.v + o) = make_float4(vr[s][0], vr[s][1], vr[s][2], vr[s][3]);
+                    __stcs(reinterpret_cast<float4*>(ad.p + o), make_float4(pr[s][0], pr[s][1], pr[s][2], pr[s][3]));
+                    __stcs(reinterpret_cast<float4*>(ad.m + o), make_float4(mr[s][0], mr[s][1], mr[s][2], mr[s][3]));
+                    __stcs(reinterpret_cast<float4*>(ad.v + o), make_float4(vr[s][0], vr[s][1], vr[s][2], vr[s][3]));
                     if (ad.copy) store_out<4>(ad.copy, ad.copy_dtype, o, pr[s]);
                 }
                 if constexpr (MODE != ROWS_ADAM) {
@@ -871,9 +877,9 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
                     for (int s = 0; s < NS; s++) {
                         const int col = (lane + 32 * s) * 4;
                         if (col < a.d) {
-                            Elt<float>::template load<4>(ad.p + base + col, pr[s]);
-                            Elt<float>::template load<4>(ad.m + base + col, mr[s]);
-                            Elt<float>::template load<4>(ad.v + base + col, vr[s]);
+                            ld_stream4(ad.p + base + col, pr[s]);
+                            ld_stream4(ad.m + base + col, mr[s]);
+                            ld_stream4(ad.v + base + col, vr[s]);
                         }
                     }
                 }

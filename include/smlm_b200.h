@@ -339,6 +339,17 @@ SMLM_API int smlm_xchg_backward_gw(void *const *peers_dev, int rank, int world, 
 SMLM_API int smlm_xchg_collect_gw(void *const *peers_dev, int rank, int world, int64_t n, int64_t k, int64_t n_cap,
                                   int64_t d, float *gw, int64_t epoch, int *status, void *stream);
 
+/* ------------------------------------------------------------------------------------- Engram n-gram rows
+ * Row indices of an Engram module's lookups: for position t of sequence b and lookup (order o, head h), the XOR over
+ * i < orders[o] of c[b, history + t - i] * mult[o, h, i] (int64), then x ^= x >> 17, row = (x mod rows, floored)
+ * + (o * heads + h) * rows. c: (batch, history + t_len) int64 compressed token ids (the history positions first);
+ * mult: (n_orders, heads, max_order) int64 device array; orders: n_orders host ints, 1 <= orders[o] <= max_order,
+ * orders[o] <= history + 1, n_orders <= 8; out: (batch, t_len, n_orders * heads) int64.
+ * Replaces engram.py:63-75 NgramHash.forward (the table lookups themselves are smlm_bag_forward with k = 1). */
+SMLM_API int smlm_ngram_rows(const int64_t *c, int64_t batch, int64_t t_len, int history, const int64_t *mult,
+                             const int *orders, int n_orders, int heads, int max_order, int64_t rows, int64_t *out,
+                             void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -225,3 +225,21 @@ def ref_rowwise(p, acc, touched, v, count, grad_scale, kind, b2, eps, lr, thread
 def touched_norm(acc, touched):
     rows, d = acc.shape
     return lib().orc_touched_norm(_ptr(_c(acc, np.float32)), _ptr(_c(touched, np.uint8)), rows, d)
+
+
+def ngram_rows(c, history, mult, orders, heads, rows):
+    """Engram n-gram rows, restated in numpy int64 arithmetic from the reference's NgramHash.forward
+    (smlm/engram.py:63-75): per order o, the XOR over i < n of c[:, history + t - i] * mult[o, h, i], then
+    x ^= x >> 17 and row = x mod rows (floored) + (o * heads + h) * rows. c (B, history + T) int64 ->
+    (B, T, len(orders) * heads) int64."""
+    c = np.asarray(c, dtype=np.int64)
+    mult = np.asarray(mult, dtype=np.int64)
+    T = c.shape[1] - history
+    out = []
+    for o, n in enumerate(orders):
+        x = np.zeros((c.shape[0], T, heads), dtype=np.int64)
+        for i in range(n):
+            x ^= c[:, history - i:history - i + T, None] * mult[o, :, i][None, None, :]
+        x ^= x >> 17
+        out.append(np.mod(x, rows) + (o * heads + np.arange(heads, dtype=np.int64)) * rows)
+    return np.concatenate(out, -1)

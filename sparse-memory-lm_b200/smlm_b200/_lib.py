@@ -81,6 +81,7 @@ SIGNATURES = {
                                      _i64, _p, _p]),
     "smlm_xchg_collect_gw": (_i32, [_p, _i32, _i32, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "smlm_score_select_noalloc": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
+    "smlm_ngram_rows": (_i32, [_p, _i64, _i64, _i32, _p, _p, _i32, _i32, _i32, _i64, _p, _p]),
 }
 
 _LIB = None

@@ -22,6 +22,8 @@ from .model import Transformer
 class GraphDecoder:
     def __init__(self, model: Transformer, batch: int, max_len: int = None, dtype=None):
         cfg = model.cfg
+        if cfg.eng_layers:
+            raise ValueError("GraphDecoder: Engram memories keep growing caches (decode them with the KV-cache loop)")
         self.model = model
         self.batch = batch
         self.max_len = max_len or cfg.max_seq_len

@@ -607,3 +607,30 @@ def zero_untouched(acc, touched):
     with L.timed("zero_untouched", 1):
         rc = L.lib().smlm_zero_untouched(L.ptr(acc), L.ptr(touched), rows, D, L.stream(dev))
     L.check(rc, "zero_untouched")
+
+
+# ------------------------------------------------------------------------------------------ Engram rows
+def ngram_rows(c, history, mult, orders, heads, rows):
+    """Row indices of an Engram module's lookups (reference: engram.py:63-75 NgramHash.forward): c (B, history + T)
+    int64 compressed ids, mult (n_orders, heads, max_order) int64 -> (B, T, n_orders * heads) int64, lookup
+    (order o, head h) in rows [(o * heads + h) * rows, ... + rows)."""
+    import ctypes
+    dev = L.require_cuda(c, mult)
+    if c.dtype != torch.long or mult.dtype != torch.long:
+        raise ValueError("ngram_rows: c and mult must be int64")
+    B, W = c.shape
+    T = W - history
+    if T < 0:
+        raise ValueError(f"ngram_rows: {W} ids for a history of {history}")
+    n_orders, h, max_order = mult.shape
+    if h != heads or len(orders) != n_orders:
+        raise ValueError("ngram_rows: mult does not match orders / heads")
+    out = torch.empty(B, T, n_orders * heads, dtype=torch.long, device=dev)
+    c, mult = _contig(c), _contig(mult)
+    arr = (ctypes.c_int * n_orders)(*[int(o) for o in orders])
+    with L.timed("ngram_rows", 1):
+        rc = L.lib().smlm_ngram_rows(L.ptr(c), B, T, int(history), L.ptr(mult), ctypes.cast(arr, ctypes.c_void_p),
+                                     n_orders, heads, max_order, int(rows), L.ptr(out), L.stream(dev))
+    L.check(rc, "ngram_rows")
+    return out
+

@@ -2,8 +2,8 @@
 
 The dense parts (RMSNorm, RoPE attention, SwiGLU, tied LM head) are plain PyTorch; the memory layers are
 smlm_b200.pkm.ProductKeyMemory on the sm_100a kernels. ModelConfig keeps the reference's field names and
-defaults (mem_impl defaults to "cuda"); state_dict keys match the reference's, so checkpoints load across.
-Engram n-gram memories (reference smlm/engram.py) are not part of this build.
+defaults (mem_impl / eng_impl default to "cuda"); state_dict keys match the reference's, so checkpoints load
+across. Engram n-gram memories (eng_layers) are smlm_b200.engram.EngramMemory, as in the reference.
 """
 import math
 from dataclasses import asdict, dataclass, field
@@ -13,6 +13,7 @@ import torch.nn.functional as F
 from torch import nn
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
+from .engram import EngramMemory, NgramHash
 from .pkm import ProductKeyMemory
 
 
@@ -44,6 +45,14 @@ class ModelConfig:
     mem_value_grad: str = "dense"
     mem_impl: str = "cuda"
     eng_layers: list = field(default_factory=list)
+    eng_orders: list = field(default_factory=lambda: [2, 3])
+    eng_heads: int = 8
+    eng_head_dim: int = 24
+    eng_rows: int = 524287
+    eng_conv_kernel: int = 4
+    eng_hash_seed: int = 0
+    eng_impl: str = "cuda"
+    eng_value_grad: str = "row_sparse"
 
     def to_dict(self):
         return asdict(self)
@@ -165,8 +174,14 @@ class Block(nn.Module):
             self.ffn_norm_r2 = nn.RMSNorm(cfg.d_model, eps=cfg.norm_eps)
             self.ffn_r2 = _memory(cfg, shared_values)
         self.engram = None
+        if layer_id in cfg.eng_layers:
+            self.engram = EngramMemory(cfg.d_model, len(cfg.eng_orders) * cfg.eng_heads, cfg.eng_head_dim,
+                                       cfg.eng_rows, conv_kernel=cfg.eng_conv_kernel, dilation=max(cfg.eng_orders),
+                                       eps=cfg.norm_eps, impl=cfg.eng_impl, value_grad=cfg.eng_value_grad)
 
-    def forward(self, x, kv_cache=None, pos0=0):
+    def forward(self, x, kv_cache=None, pos0=0, eng_rows=None):
+        if self.engram is not None:
+            x = x + self.engram(x, eng_rows, kv_cache)
         x = x + self.attn(self.attn_norm(x), kv_cache, pos0)
         x = x + self.ffn(self.ffn_norm(x))
         if self.ffn_r2 is not None:
@@ -177,8 +192,6 @@ class Block(nn.Module):
 class Transformer(nn.Module):
     def __init__(self, cfg):
         super().__init__()
-        if cfg.eng_layers:
-            raise NotImplementedError("Engram memories (eng_layers) are not part of this build")
         self.cfg = cfg
         self.tok_emb = nn.Embedding(cfg.vocab_size, cfg.d_model)
         shared = None
@@ -186,6 +199,8 @@ class Transformer(nn.Module):
             v_dim = cfg.mem_v_dim if cfg.mem_v_dim > 0 else cfg.d_model
             shared = nn.Embedding(cfg.mem_n_keys ** 2, v_dim)
         self.layers = nn.ModuleList([Block(cfg, i, shared) for i in range(cfg.n_layers)])
+        self.ngram = (NgramHash(cfg.vocab_size, cfg.eng_orders, cfg.eng_heads, cfg.eng_rows, cfg.eng_hash_seed)
+                      if cfg.eng_layers else None)
         self.norm = nn.RMSNorm(cfg.d_model, eps=cfg.norm_eps)
         self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False)
         self.lm_head.weight = self.tok_emb.weight
@@ -205,7 +220,7 @@ class Transformer(nn.Module):
     def set_dormant(self, layers):
         for i in layers:
             blk = self.layers[i]
-            if blk.is_memory:
+            if blk.is_memory or blk.engram is not None:
                 raise ValueError(f"block {i} reads a table; only plain blocks can grow in")
             blk.dormant = True
 
@@ -236,7 +251,7 @@ class Transformer(nn.Module):
         return out
 
     def engram_layers(self):
-        return []
+        return [b.engram for b in self.layers if b.engram is not None]
 
     def set_memory_decode_graphs(self, enabled=True):
         for m in self.memory_layers():
@@ -265,10 +280,21 @@ class Transformer(nn.Module):
 
     def forward(self, idx, targets=None, kv_caches=None, pos0=0, fused_ce=False, ce_chunk_size=1024):
         x = self.tok_emb(idx)
+        rows = None
+        if self.ngram is not None:
+            # n-gram rows need the last tokens before this chunk: pad at the start, else from the cache
+            c = self.ngram.canon[idx]
+            hist = kv_caches[0].get("eng_hist") if kv_caches is not None else None
+            if hist is None:
+                hist = torch.full((c.shape[0], self.ngram.history), self.ngram.pad, dtype=c.dtype, device=c.device)
+            c = torch.cat([hist, c], 1)
+            if kv_caches is not None:
+                kv_caches[0]["eng_hist"] = c[:, -self.ngram.history:]
+            rows = self.ngram(c)
         for i, blk in enumerate(self.layers):
             if blk.dormant:
                 continue
-            x = blk(x, None if kv_caches is None else kv_caches[i], pos0)
+            x = blk(x, None if kv_caches is None else kv_caches[i], pos0, rows)
         logits = self.lm_head(self.norm(x))
         if targets is None:
             return logits
@@ -277,14 +303,15 @@ class Transformer(nn.Module):
 
     def param_counts(self):
         emb = self.tok_emb.weight.numel()
-        tables = {id(m.values.weight): m.values.weight.numel() for m in self.memory_layers()}
+        tables = {id(m.values.weight): m.values.weight.numel() for m in self.memory_layers() + self.engram_layers()}
         values = sum(tables.values())
         total = sum(p.numel() for p in self.parameters())
         buffers = sum(b.numel() for n, b in self.named_buffers() if "running" in n)
         return {"total": total, "embedding": emb, "non_embedding": total - emb, "memory_values": values,
                 "dense_body": total - emb - values,
                 "active_non_embedding_per_token": total - emb - values + sum(
-                    m.heads * m.knn * m.v_dim for m in self.memory_layers()),
+                    m.heads * m.knn * m.v_dim for m in self.memory_layers()) + sum(
+                    m.n_lookups * m.head_dim for m in self.engram_layers()),
                 "bn_running_stats": buffers}
 
     def macs_per_token(self, context_len=None):
@@ -293,6 +320,8 @@ class Transformer(nn.Module):
         d = c.d_model
         out = {"attn_proj": 0, "attn_scores": 0, "ffn": 0, "memory": 0, "engram": 0, "lm_head": d * c.vocab_size}
         for blk in self.layers:
+            if blk.engram is not None:
+                out["engram"] += blk.engram.macs_per_token()
             out["attn_proj"] += 4 * d * d
             out["attn_scores"] += 2 * d * (T / 2)
             if blk.is_memory:

@@ -24,17 +24,18 @@ def build_optimizer(model, lr, value_lr, weight_decay, betas=(0.9, 0.95), eps=1e
         raise ValueError(f"Unknown optimizer: {optimizer!r} (this build routes AdamW only)")
     sparse_tables = row_sparse_tables(model)
     sparse_ids = {id(t) for t in sparse_tables}
-    decay, no_decay, values = [], [], []
+    engram_ids = {id(m.values.weight) for m in model.modules() if getattr(m, "is_engram", False)}
+    decay, no_decay, values, eng_values = [], [], [], []
     for n, p in model.named_parameters():
         if not p.requires_grad or id(p) in sparse_ids:
             continue
         if getattr(p, "pk_value_param", False):
-            values.append(p)
+            (eng_values if id(p) in engram_ids else values).append(p)
         elif p.dim() >= 2 and not getattr(p, "no_weight_decay", False):
             decay.append(p)
         else:
             no_decay.append(p)
-    if values and value_state != "fp32":
+    if (values or eng_values) and value_state != "fp32":
         raise ValueError("value_state requires row_sparse gradients for every trainable value table")
     groups = [
         {"params": decay, "weight_decay": weight_decay, "base_lr": lr, "name": "decay"},
@@ -42,19 +43,30 @@ def build_optimizer(model, lr, value_lr, weight_decay, betas=(0.9, 0.95), eps=1e
     ]
     if values:
         groups.append({"params": values, "weight_decay": 0.0, "base_lr": value_lr, "name": "memory_values"})
+    if eng_values:                  # dense Engram tables (eng_value_grad="dense"): their own learning rate
+        groups.append({"params": eng_values, "weight_decay": 0.0, "base_lr": eng_value_lr or value_lr,
+                       "name": "engram_values"})
     for g in groups:
         g["lr"] = g["base_lr"]
     fused = all(p.is_cuda for g in groups for p in g["params"]) or None
     opt = torch.optim.AdamW(groups, betas=betas, eps=eps, fused=fused)
     if sparse_tables:
-        if value_optim != "adam":
-            from .row_optim import RowWiseOptimizer
-            lazy = RowWiseOptimizer(sparse_tables, lr=value_lr, kind=value_optim, beta2=betas[1], eps=eps,
-                                    name="memory_values")
-        else:
-            lazy = LazyRowAdam(sparse_tables, lr=value_lr, betas=betas, eps=eps, state_dtype=value_state,
-                               name="memory_values")
-        return OptimizerSet(opt, lazy)
+        # one table optimizer for the product-key table(s), one for the Engram tables (learning rate
+        # eng_value_lr, default value_lr); clipping stays one global norm over all of them (clip_grads)
+        owners = {id(m.values.weight): m for m in model.modules() if getattr(m, "value_grad", None) == "row_sparse"}
+        lazy = []
+        for engram in (False, True):
+            tabs = [t for t in sparse_tables if getattr(owners[id(t)], "is_engram", False) == engram]
+            if not tabs:
+                continue
+            tlr = (eng_value_lr or value_lr) if engram else value_lr
+            name = "engram_values" if engram else "memory_values"
+            if value_optim != "adam":
+                from .row_optim import RowWiseOptimizer
+                lazy.append(RowWiseOptimizer(tabs, lr=tlr, kind=value_optim, beta2=betas[1], eps=eps, name=name))
+            else:
+                lazy.append(LazyRowAdam(tabs, lr=tlr, betas=betas, eps=eps, state_dtype=value_state, name=name))
+        return OptimizerSet(opt, *lazy)
     return opt
 
 

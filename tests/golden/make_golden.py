@@ -1,7 +1,7 @@
 """Generates the golden fixtures in this directory by running the REFERENCE implementation
 (re133/sparse-memory-lm, imported read-only from a local checkout) on seeded inputs.
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [/path/to/reference]
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [/path/to/reference] [fixture names ...]
 
 The Triton kernels of the reference run in Triton's CPU interpreter (TRITON_INTERPRET=1), its PyTorch path on the
 CPU. Each .npz holds the inputs and the reference's outputs; the tests pin the CPU oracle (oracle/) to them and
@@ -290,14 +290,53 @@ def gen_layer():
     save("layer.npz", **arrays)
 
 
+def gen_engram():
+    """Engram (reference smlm/engram.py, impl="torch", value_grad="row_sparse", fp32 on the CPU): NgramHash's
+    multipliers and rows, one EngramMemory forward / backward (head_dim 8 and 24, a non-zero convolution) and one
+    LazyRowAdam step of its table. Token compression needs the GPT-2 vocabulary through tiktoken, which is not
+    reachable offline, so the fixture replaces canonical_ids by the identity map (the hash, the module and the
+    training step take the compressed ids as given)."""
+    import smlm.engram as RE
+    RE.canonical_ids = lambda vocab: (torch.arange(vocab, dtype=torch.int64), vocab)
+    arrays = {}
+    for v, head_dim in enumerate((8, 24)):
+        ng = RE.NgramHash(512, orders=(2, 3), heads=2, rows=101, seed=v)
+        gen = torch.Generator().manual_seed(20 + v)
+        B, T, d = 2, 17, 32
+        c = torch.randint(0, 512, (B, ng.history + T), generator=gen)
+        c[:, :ng.history] = ng.pad
+        rows = ng(c)
+        torch.manual_seed(30 + v)
+        e = RE.EngramMemory(d, ng.n_lookups, head_dim, 101, conv_kernel=4, dilation=max(ng.orders), impl="torch",
+                            value_grad="row_sparse")
+        with torch.no_grad():
+            e.conv.weight.normal_(std=0.3)
+        x = torch.randn(B, T, d, generator=gen).requires_grad_()
+        g = torch.randn(B, T, d, generator=gen)
+        state0 = {k: t.detach().clone() for k, t in e.state_dict().items()}
+        y = e(x, rows)
+        y.backward(g)
+        st = row_store(e.values.weight)
+        pre = f"v{v}_"
+        for k, t in state0.items():
+            arrays[pre + "param_" + k] = t
+        arrays.update({pre + "c": c, pre + "mult": ng.mult, pre + "rows": rows, pre + "x": x.detach(), pre + "g": g,
+                       pre + "y": y.detach(), pre + "x_grad": x.grad, pre + "wk_grad": e.w_k.weight.grad,
+                       pre + "wv_grad": e.w_v.weight.grad, pre + "conv_grad": e.conv.weight.grad,
+                       pre + "hnorm_grad": e.h_norm.weight.grad, pre + "acc": st.acc.clone(),
+                       pre + "touched": st.touched.clone(), pre + "head_dim": np.array(head_dim)})
+        opt = LazyRowAdam([e.values.weight], lr=1e-3, betas=(0.9, 0.98), eps=1e-8, impl="torch")
+        opt.step()
+        arrays[pre + "values_after"] = e.values.weight.detach().clone()
+    save("engram.npz", **arrays)
+
+
+GENERATORS = {"select_bf16": gen_select_bf16, "select_f32": gen_select_f32, "select_backward": gen_select_backward,
+              "bag": gen_bag, "lazy_adam": gen_lazy_adam, "lazy_adam_lowmem": gen_lazy_adam_lowmem,
+              "rowwise": gen_rowwise, "infer": gen_infer, "layer": gen_layer, "engram": gen_engram}
+
 if __name__ == "__main__":
+    # python make_golden.py [reference path] [fixture names ...]: all fixtures by default
     torch.set_num_threads(4)
-    gen_select_bf16()
-    gen_select_f32()
-    gen_select_backward()
-    gen_bag()
-    gen_lazy_adam()
-    gen_lazy_adam_lowmem()
-    gen_rowwise()
-    gen_infer()
-    gen_layer()
+    for name in (sys.argv[2:] or list(GENERATORS)):
+        GENERATORS[name]()

@@ -284,3 +284,20 @@ def test_oracle_select_equals_bruteforce_product_search():
         bf, bi = full.reshape(50, H, -1).topk(knn, dim=-1)
         assert np.array_equal(sc, bf.numpy())
         assert np.array_equal(np.sort(idx, -1), np.sort(bi.numpy(), -1))
+
+
+def test_engram_hash_oracle_and_multipliers_match_reference():
+    """Engram: the oracle's n-gram hash gives the reference NgramHash's rows, and this build's NgramHash draws the
+    reference's multipliers (same seed -> same rows -> checkpoints and tables stay compatible)."""
+    import smlm_b200.engram as E
+    g = golden("engram.npz")
+    real = E.canonical_ids
+    E.canonical_ids = lambda vocab: (torch.arange(vocab, dtype=torch.int64), vocab)   # GPT-2 vocabulary offline
+    try:
+        for v in (0, 1):
+            ng = E.NgramHash(512, orders=(2, 3), heads=2, rows=101, seed=v)
+            assert np.array_equal(ng.mult.numpy(), g[f"v{v}_mult"])
+            rows = O.ngram_rows(g[f"v{v}_c"], ng.history, g[f"v{v}_mult"], [2, 3], 2, 101)
+            assert np.array_equal(rows, g[f"v{v}_rows"])
+    finally:
+        E.canonical_ids = real

@@ -193,6 +193,17 @@ SMLM_API int smlm_rowwise_step(float *param, float *acc, uint8_t *touched, float
                                float b2, float eps, float lr, int flags, void *workspace, size_t workspace_bytes,
                                void *stream);
 
+/* The row-wise step fused with the row sums of a deferred backward: each row's sum (the gradient
+ * smlm_bag_rows_materialize would have written, same summation order) goes straight into the smlm_rowwise_step
+ * update of that row (same formulas and rounding: bit-identical to materialising and stepping), touched cleared;
+ * no accumulator is written or read. Same grad_out, weights, sizes and workspace as the deferred backward.
+ * Replaces RowWiseOptimizer._masked (row_optim.py:179-201) for a RowStore whose rows come from one backward. */
+SMLM_API int smlm_rowwise_deferred_step(float *param, uint8_t *touched, float *v, int32_t *count, const void *grad_out,
+                                        int grad_dtype, const void *weights, int weights_dtype,
+                                        const float *grad_scale_dev, float grad_scale, int64_t n, int64_t k,
+                                        int64_t rows, int64_t d, int kind, float b2, float eps, float lr,
+                                        void *workspace, size_t workspace_bytes, void *stream);
+
 /* L2 norm of the accumulator over the touched rows, written to *norm_out (device fp32): the reference's
  * acc.norm() (sparse_values.py:143) for an accumulator whose untouched rows count as zero. With row_sqnorm
  * (the per-row squared norms the backward wrote) only 4 bytes per touched row are read, else the rows of acc.

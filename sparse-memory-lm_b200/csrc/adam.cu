@@ -300,7 +300,6 @@ __global__ void __launch_bounds__(256) rowwise_kernel(RowArgs a) {
     const int n = *a.count;
     const float scale = a.scale_dev ? *a.scale_dev : a.scale;
     const int warps = gridDim.x * (blockDim.x >> 5);
-    const float one_minus_b2 = __fsub_rn(1.0f, a.b2);
     for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
         const int64_t r = a.list[i];
         const int64_t base = r * a.d;
@@ -313,23 +312,7 @@ __global__ void __launch_bounds__(256) rowwise_kernel(RowArgs a) {
             }
         }
         q = warp_sum_d(q) / (double)a.d;
-        float denom;
-        if (a.kind == SMLM_ROWRMS) {
-            const float vr = __fadd_rn(__fmul_rn(a.b2, a.v[r]), __fmul_rn(one_minus_b2, (float)q));
-            const int32_t cnt = a.count_state[r] + 1;
-            denom = __fadd_rn(__fsqrt_rn((float)((double)vr / (1.0 - pow((double)a.b2, (double)cnt)))), a.eps);
-            __syncwarp();
-            if (lane == 0) {
-                a.v[r] = vr;
-                a.count_state[r] = cnt;
-            }
-        } else {
-            const float vr = __fadd_rn(a.v[r], (float)q);
-            denom = __fadd_rn(__fsqrt_rn(vr), a.eps);
-            __syncwarp();
-            if (lane == 0) a.v[r] = vr;
-        }
-        const float step = __fdiv_rn(a.lr, denom);
+        const float step = rowwise_state_step(a.kind, a.b2, a.eps, a.lr, a.v, a.count_state, r, q, lane);
         for (int c = lane * VEC; c < a.d; c += 32 * VEC) {
 #pragma unroll
             for (int t = 0; t < VEC; t++) {

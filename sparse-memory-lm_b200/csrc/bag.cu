@@ -493,12 +493,18 @@ struct RowAdam {
     AdamScalars s;
     void* copy;
     int copy_dtype;
+    // the fused row-wise step (ROWS_ROWWISE): per-row state, kind and scalars (p, scale_dev and scale above)
+    float* row_v;
+    int32_t* row_count;
+    int rw_kind;
+    float rw_b2, rw_eps, rw_lr;
 };
 
 // What the row-sum pass does with a completed row sum x (= 0 + the run's sum for a first touch):
 constexpr int ROWS_WRITE = 0;  // acc[row] = x (or acc[row] + x), its squared norm, touched = 1
 constexpr int ROWS_NORM = 1;   // only its squared norm and touched = 1 (deferred backward: acc stays untouched)
 constexpr int ROWS_ADAM = 2;   // lazy Adam of the table row with gradient x, touched = 0
+constexpr int ROWS_ROWWISE = 3;  // the row-wise (rowrms / rowadagrad) step of the table row with gradient x
 
 // Parameters and moments of a touched row: read once and written once per step (streaming, evict-first).
 __device__ __forceinline__ void ld_stream4(const float* p, float (&v)[4]) {
@@ -790,12 +796,13 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
     const bool mid = head_cross && tail_cross && first_row == last_row;
     int cflags = 0;
     constexpr uint32_t FRESH = 0x80000000u;
-    const float scale = MODE == ROWS_ADAM ? (ad.scale_dev ? *ad.scale_dev : ad.scale) : 1.f;
+    constexpr bool STEP = MODE == ROWS_ADAM || MODE == ROWS_ROWWISE;  // an optimizer step on the table row
+    const float scale = STEP ? (ad.scale_dev ? *ad.scale_dev : ad.scale) : 1.f;
 
     uint32_t cur = NO_ROW;
     bool cur_fresh = false;
     float sum[NS][4];
-    float pr[MODE == ROWS_ADAM ? NS : 1][4], mr[MODE == ROWS_ADAM ? NS : 1][4], vr[MODE == ROWS_ADAM ? NS : 1][4];
+    float pr[STEP ? NS : 1][4], mr[MODE == ROWS_ADAM ? NS : 1][4], vr[MODE == ROWS_ADAM ? NS : 1][4];
 #pragma unroll
     for (int s = 0; s < NS; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
 
@@ -818,6 +825,40 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
             dst = a.acc + (int64_t)cur * a.d;
         }
         const bool accumulate = MODE == ROWS_WRITE && direct && !cur_fresh;
+        if constexpr (MODE == ROWS_ROWWISE) {
+            if (direct) {
+                // the gradient x = 0 + the run's sum, scaled; q = mean of its squares in the rowwise kernel's
+                // order (slot by slot, summed in double), then the row's state and the parameter update
+                double q = 0.0;
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    if ((lane + 32 * s) * 4 < a.d) {
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            sum[s][i] = __fmul_rn(__fadd_rn(0.f, sum[s][i]), scale);
+                            q = fma((double)sum[s][i], (double)sum[s][i], q);
+                        }
+                    }
+                }
+                q = warp_sum_d(q) / (double)a.d;
+                const float step = rowwise_state_step(ad.rw_kind, ad.rw_b2, ad.rw_eps, ad.rw_lr, ad.row_v,
+                                                      ad.row_count, cur, q, lane);
+#pragma unroll
+                for (int s = 0; s < NS; s++) {
+                    const int col = (lane + 32 * s) * 4;
+                    if (col < a.d) {
+                        float4 pn;
+                        pn.x = __fsub_rn(pr[s][0], __fmul_rn(step, sum[s][0]));
+                        pn.y = __fsub_rn(pr[s][1], __fmul_rn(step, sum[s][1]));
+                        pn.z = __fsub_rn(pr[s][2], __fmul_rn(step, sum[s][2]));
+                        pn.w = __fsub_rn(pr[s][3], __fmul_rn(step, sum[s][3]));
+                        __stcs(reinterpret_cast<float4*>(ad.p + (int64_t)cur * a.d + col), pn);
+                    }
+                }
+                if (lane == 0 && a.touched) a.touched[cur] = 0;
+                return;
+            }
+        }
         float sq = 0.f;
 #pragma unroll
         for (int s = 0; s < NS; s++) {
@@ -842,17 +883,17 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
                     __stcs(reinterpret_cast<float4*>(ad.v + o), make_float4(vr[s][0], vr[s][1], vr[s][2], vr[s][3]));
                     if (ad.copy) store_out<4>(ad.copy, ad.copy_dtype, o, pr[s]);
                 }
-                if constexpr (MODE != ROWS_ADAM) {
+                if constexpr (!STEP) {
                     sq = fmaf(x.x, x.x, sq); sq = fmaf(x.y, x.y, sq); sq = fmaf(x.z, x.z, sq); sq = fmaf(x.w, x.w, sq);
                 }
             }
         }
         if (direct) {
-            if (MODE != ROWS_ADAM && a.sqnorm) {
+            if (!STEP && a.sqnorm) {
                 sq = warp_sum(sq);
                 if (lane == 0) a.sqnorm[cur] = sq;
             }
-            if (lane == 0 && a.touched) a.touched[cur] = MODE == ROWS_ADAM ? 0 : 1;
+            if (lane == 0 && a.touched) a.touched[cur] = STEP ? 0 : 1;
         }
     };
     auto load_g = [&](uint32_t tokf, float (&v)[NS][4]) {
@@ -870,16 +911,18 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
             cur_fresh = (tokf & FRESH) != 0;
 #pragma unroll
             for (int s = 0; s < NS; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
-            if constexpr (MODE == ROWS_ADAM) {
-                if (is_direct(row)) {  // the row's parameters and moments, in flight while its run is summed
+            if constexpr (STEP) {
+                if (is_direct(row)) {  // the row's parameters (and moments), in flight while its run is summed
                     const int64_t base = (int64_t)row * a.d;
 #pragma unroll
                     for (int s = 0; s < NS; s++) {
                         const int col = (lane + 32 * s) * 4;
                         if (col < a.d) {
                             ld_stream4(ad.p + base + col, pr[s]);
-                            ld_stream4(ad.m + base + col, mr[s]);
-                            ld_stream4(ad.v + base + col, vr[s]);
+                            if constexpr (MODE == ROWS_ADAM) {
+                                ld_stream4(ad.m + base + col, mr[s]);
+                                ld_stream4(ad.v + base + col, vr[s]);
+                            }
                         }
                     }
                 }
@@ -1055,10 +1098,9 @@ __global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a, RowAdam ad) {
     const uint32_t row = a.keys[end - 1];
     const bool accumulate = MODE == ROWS_WRITE && !a.all_fresh &&
                             !(a.first_writes && a.touched && a.touched[row] == 0);
-    const float scale = MODE == ROWS_ADAM ? (ad.scale_dev ? *ad.scale_dev : ad.scale) : 1.f;
-    float sq = 0.f;
-    for (int col0 = lane * VEC; col0 < a.d; col0 += 32 * VEC) {
-        float tot[VEC];
+    const float scale = (MODE == ROWS_ADAM || MODE == ROWS_ROWWISE) ? (ad.scale_dev ? *ad.scale_dev : ad.scale) : 1.f;
+    // the row's total over its chunks, columns col0 .. col0 + VEC - 1, in chunk order
+    auto total = [&](int col0, float (&tot)[VEC]) {
 #pragma unroll
         for (int i = 0; i < VEC; i++) tot[i] = a.carry_tail[c * a.d + col0 + i];
         int64_t c2 = c + 1;
@@ -1071,6 +1113,37 @@ __global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a, RowAdam ad) {
 #pragma unroll
             for (int i = 0; i < VEC; i++) tot[i] = tot[i] + a.carry_head[c2 * a.d + col0 + i];
         }
+    };
+    if constexpr (MODE == ROWS_ROWWISE) {
+        // two passes over the row: the mean square q first (rowwise kernel order), then the parameter update
+        double q = 0.0;
+        for (int col0 = lane * VEC; col0 < a.d; col0 += 32 * VEC) {
+            float tot[VEC];
+            total(col0, tot);
+#pragma unroll
+            for (int i = 0; i < VEC; i++) {
+                const float gk = __fmul_rn(__fadd_rn(0.f, tot[i]), scale);
+                q = fma((double)gk, (double)gk, q);
+            }
+        }
+        q = warp_sum_d(q) / (double)a.d;
+        const float step = rowwise_state_step(ad.rw_kind, ad.rw_b2, ad.rw_eps, ad.rw_lr, ad.row_v, ad.row_count,
+                                              row, q, lane);
+        for (int col0 = lane * VEC; col0 < a.d; col0 += 32 * VEC) {
+            float tot[VEC];
+            total(col0, tot);
+            const int64_t o = (int64_t)row * a.d + col0;
+#pragma unroll
+            for (int i = 0; i < VEC; i++)
+                ad.p[o + i] = __fsub_rn(ad.p[o + i], __fmul_rn(step, __fmul_rn(__fadd_rn(0.f, tot[i]), scale)));
+        }
+        if (lane == 0 && a.touched) a.touched[row] = 0;
+        return;
+    }
+    float sq = 0.f;
+    for (int col0 = lane * VEC; col0 < a.d; col0 += 32 * VEC) {
+        float tot[VEC];
+        total(col0, tot);
         const int64_t o = (int64_t)row * a.d + col0;
 #pragma unroll
         for (int i = 0; i < VEC; i++) {
@@ -1460,4 +1533,33 @@ extern "C" int smlm_lazy_adam_deferred_step(float* param, float* exp_avg, float*
     cudaStream_t st = as_stream(stream);
     return grad_dtype == SMLM_F32 ? launch_rows_mode<float, ROWS_ADAM>(a, ad, st)
                                   : launch_rows_mode<__nv_bfloat16, ROWS_ADAM>(a, ad, st);
+}
+
+extern "C" int smlm_rowwise_deferred_step(float* param, uint8_t* touched, float* v, int32_t* count,
+                                          const void* grad_out, int grad_dtype, const void* weights,
+                                          int weights_dtype, const float* grad_scale_dev, float grad_scale,
+                                          int64_t n, int64_t k, int64_t rows, int64_t d, int kind, float b2,
+                                          float eps, float lr, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+    SegArgs a;
+    int rc = deferred_args("rowwise_deferred_step", grad_out, grad_dtype, weights, weights_dtype, n, k, rows, d,
+                           workspace, workspace_bytes, &a);
+    if (rc != SMLM_OK || n == 0 || k == 0) return rc;
+    SMLM_CHECK_ARG(kind == SMLM_ROWRMS || kind == SMLM_ROWADAGRAD, "rowwise_deferred_step: unknown kind %d", kind);
+    SMLM_CHECK_ARG(param && touched && v && (count || kind == SMLM_ROWADAGRAD), "rowwise_deferred_step: null pointer");
+    SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(param) % 16 == 0, "rowwise_deferred_step: table must be 16-byte aligned");
+    a.touched = touched;
+    RowAdam ad{};
+    ad.p = param;
+    ad.scale_dev = grad_scale_dev;
+    ad.scale = grad_scale;
+    ad.row_v = v;
+    ad.row_count = count;
+    ad.rw_kind = kind;
+    ad.rw_b2 = b2;
+    ad.rw_eps = eps;
+    ad.rw_lr = lr;
+    cudaStream_t st = as_stream(stream);
+    return grad_dtype == SMLM_F32 ? launch_rows_mode<float, ROWS_ROWWISE>(a, ad, st)
+                                  : launch_rows_mode<__nv_bfloat16, ROWS_ROWWISE>(a, ad, st);
 }

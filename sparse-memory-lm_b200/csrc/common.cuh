@@ -142,6 +142,32 @@ __device__ __forceinline__ void adam_update(const AdamScalars& a, float scale, f
     v = vk;
 }
 
+// Row-wise optimizer state update of row r from q = mean of the row's squared gradient (the reference C loop's
+// formulas and rounding, host_rows.c:84-117; fp32 state, the bias correction in double): returns the step size
+// lr / denom; lane 0 writes the row's state (call with the whole warp, after q is reduced). The one definition used
+// by every row-wise kernel of the library.
+__device__ __forceinline__ float rowwise_state_step(int kind, float b2, float eps, float lr, float* v, int32_t* count,
+                                                    int64_t r, double q, int lane) {
+    float denom;
+    if (kind == SMLM_ROWRMS) {
+        const float one_minus_b2 = __fsub_rn(1.0f, b2);
+        const float vr = __fadd_rn(__fmul_rn(b2, v[r]), __fmul_rn(one_minus_b2, (float)q));
+        const int32_t cnt = count[r] + 1;
+        denom = __fadd_rn(__fsqrt_rn((float)((double)vr / (1.0 - pow((double)b2, (double)cnt)))), eps);
+        __syncwarp();
+        if (lane == 0) {
+            v[r] = vr;
+            count[r] = cnt;
+        }
+    } else {
+        const float vr = __fadd_rn(v[r], (float)q);
+        denom = __fadd_rn(__fsqrt_rn(vr), eps);
+        __syncwarp();
+        if (lane == 0) v[r] = vr;
+    }
+    return __fdiv_rn(lr, denom);
+}
+
 // Vector loads of VEC elements (fp32 or bf16) widened to fp32 (16-byte / 8-byte loads for VEC == 4).
 template <typename T>
 struct Elt;

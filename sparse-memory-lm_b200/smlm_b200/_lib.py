@@ -58,6 +58,8 @@ SIGNATURES = {
                                           _f32, _f32, _f32, _f32, _p, _i32, _i32, _p, _sz, _p]),
     "smlm_rowwise_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _i32, _f32, _f32, _f32, _i32, _p, _sz,
                                  _p]),
+    "smlm_rowwise_deferred_step": (_i32, [_p, _p, _p, _p, _p, _i32, _p, _i32, _p, _f32, _i64, _i64, _i64, _i64,
+                                          _i32, _f32, _f32, _f32, _p, _sz, _p]),
     "smlm_touched_norm": (_i32, [_p, _p, _p, _i64, _i64, _p, _p, _sz, _p]),
     "smlm_zero_untouched": (_i32, [_p, _p, _i64, _i64, _p]),
     "smlm_pk_select": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),

@@ -582,6 +582,22 @@ def rowwise_step(param, acc, touched, v, n, grad_scale, lr, beta2, eps, kind, ke
     del keep
 
 
+def rowwise_deferred_step(param, touched, v, n, pending, grad_scale, lr, beta2, eps, kind):
+    """rowwise_step fused with the deferred row sums: bit-identical to bag_rows_materialize + rowwise_step, without
+    writing or reading the accumulator."""
+    dev = L.require_cuda(param, touched, v, n)
+    p = pending
+    code = {"rowrms": L.ROWRMS, "rowadagrad": L.ROWADAGRAD}[kind]
+    sp, sf, keep = _scale_args(grad_scale, dev)
+    with L.timed("rowwise_step", 2):
+        rc = L.lib().smlm_rowwise_deferred_step(
+            L.ptr(param), L.ptr(touched), L.ptr(v), L.ptr(n), L.ptr(p.g), L.dtype_code(p.g.dtype), L.ptr(p.w),
+            L.dtype_code(p.w.dtype), sp, sf, p.n, p.k, p.rows, p.d, code, beta2, eps, lr, L.ptr(p.ws), p.ws.numel(),
+            L.stream(dev))
+    L.check(rc, "rowwise_deferred_step")
+    del keep
+
+
 def touched_norm(acc, touched, row_sqnorm=None):
     """L2 norm (0-d fp32 tensor on the device) of the accumulator rows marked in `touched`; equals acc.norm()
     for an accumulator whose untouched rows count as zero (reference: sparse_values.py:143). With row_sqnorm (as

@@ -51,9 +51,14 @@ class RowWiseOptimizer(torch.optim.Optimizer):
                 st = row_store(p)
                 state = self._state(p)
                 state["step"] += 1
-                st.materialize()
-                K.rowwise_step(p, st._acc, st._touched, state["v"], state.get("n"), st.grad_scale, group["lr"],
-                               group["beta2"], group["eps"], self.kind, keep_acc=st.clean)
+                if st.pending is not None and not st.live:
+                    # rows of one deferred backward: summed and stepped in one pass, acc never written
+                    K.rowwise_deferred_step(p, st._touched, state["v"], state.get("n"), st.pending, st.grad_scale,
+                                            group["lr"], group["beta2"], group["eps"], self.kind)
+                else:
+                    st.materialize()
+                    K.rowwise_step(p, st._acc, st._touched, state["v"], state.get("n"), st.grad_scale, group["lr"],
+                                   group["beta2"], group["eps"], self.kind, keep_acc=st.clean)
                 st.stepped()
 
     def zero_grad(self, set_to_none=True):

@@ -149,6 +149,45 @@ def test_deferred_rows_materialize_and_fused_step_bit_exact():
     assert torch.equal(outs[1][0][~t_w], p0[~t_w])               # unread rows untouched
 
 
+@pytest.mark.parametrize("kind", ["rowrms", "rowadagrad"])
+def test_deferred_rowwise_step_bit_exact(kind):
+    """The row-wise step fused with a deferred backward's row sums equals materialising the rows and running
+    rowwise_step, bit for bit (parameters, row state, step counts), with a clip factor; hot rows make runs cross
+    the 256-position work chunks (the fix-up pass); unread rows and their state stay as they were."""
+    gen = torch.Generator().manual_seed(6)
+    rows, D, N, Kk = 20000, 384, 4096, 256
+    table = torch.randn(rows, D, generator=gen) * D ** -0.5
+    idx = skewed_indices(rows, N, Kk, gen)
+    w = torch.softmax(torch.randn(N, Kk, generator=gen), -1)
+    g = torch.randn(N, D, generator=gen)
+    T, I, W, G = (x.to(DEV) for x in (table, idx, w, g))
+    t_d = torch.zeros(rows, dtype=torch.bool, device=DEV)
+    sq_d = torch.zeros(rows, device=DEV)
+    _, pend = K.bag_backward_deferred(G, I, W, T, t_d, sq_d)
+    acc = torch.zeros(rows, D, device=DEV)
+    K.bag_rows_materialize(pend, acc)
+    p0 = torch.randn(rows, D, generator=gen).to(DEV)
+    v0 = (torch.rand(rows, generator=gen) * 1e-3).to(DEV)
+    n0 = torch.randint(0, 5, (rows,), generator=gen, dtype=torch.int32).to(DEV)
+    scale = torch.tensor(0.61, device=DEV)
+    outs = []
+    for fused in (False, True):
+        p, v, n = p0.clone(), v0.clone(), n0.clone()
+        touched = t_d.clone()
+        if fused:
+            K.rowwise_deferred_step(p, touched, v, n if kind == "rowrms" else None, pend, scale, 1e-2, 0.95, 1e-8,
+                                    kind)
+        else:
+            K.rowwise_step(p, acc.clone(), touched, v, n if kind == "rowrms" else None, scale, 1e-2, 0.95, 1e-8,
+                           kind, keep_acc=True)
+        assert not touched.any()
+        outs.append((p, v, n))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    assert torch.equal(outs[1][0][~t_d], p0[~t_d]) and torch.equal(outs[1][1][~t_d], v0[~t_d])
+    assert not torch.equal(outs[1][0][t_d], p0[t_d])
+
+
 def test_single_backward_steps_fused_equal_exact_store():
     """One backward per step (the fused path: the accumulator is never written) against a store read from
     outside after every backward (exact mode), three steps with clipping: tables and moments bit-identical."""

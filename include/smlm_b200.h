@@ -63,6 +63,9 @@ extern "C" {
  * the sorted pairs stay in the workspace, and smlm_lazy_adam_deferred_step (or smlm_bag_rows_materialize) finish
  * them later with the same grad_out, weights and sizes. */
 #define SMLM_BWD_DEFER_ROWS 2
+/* widest row (values per table row) the row-sparse backward and its optimizer steps take; wider rows return
+ * SMLM_ERR_INVALID (the forward bag has no limit) */
+#define SMLM_MAX_ROW_WIDTH 512
 /* flags of the optimizer steps: leave the consumed accumulator rows unchanged instead of zeroing them (they
  * count as zero once their touched byte is cleared) */
 #define SMLM_STEP_KEEP_ACC 1

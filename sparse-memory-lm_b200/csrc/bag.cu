@@ -1187,6 +1187,12 @@ static int launch_rows_mode(SegArgs a, RowAdam ad, cudaStream_t st) {
     return SMLM_OK;
 }
 
+static int invalid_width(int64_t d) {
+    set_error("row-sparse backward: rows of %lld values are wider than the supported %d", (long long)d,
+              SMLM_MAX_ROW_WIDTH);
+    return SMLM_ERR_INVALID;
+}
+
 template <typename TT, typename GT, bool GW, int VEC>
 static int launch_segment(SegArgs a, cudaStream_t st) {
     const int slots = (a.d + VEC - 1) / VEC;
@@ -1207,7 +1213,17 @@ static int launch_segment(SegArgs a, cudaStream_t st) {
     } else if (ns <= 1) bb_segment_kernel<TT, GT, GW, VEC, 1><<<blocks, 128, 0, st>>>(a);
     else if (ns == 2) bb_segment_kernel<TT, GT, GW, VEC, 2><<<blocks, 128, 0, st>>>(a);
     else if (ns == 3) bb_segment_kernel<TT, GT, GW, VEC, 3><<<blocks, 128, 0, st>>>(a);
-    else bb_segment_kernel<TT, GT, GW, VEC, 4><<<blocks, 128, 0, st>>>(a);
+    else if (ns == 4) bb_segment_kernel<TT, GT, GW, VEC, 4><<<blocks, 128, 0, st>>>(a);
+    else {
+        // scalar rows (widths that are not a multiple of 4, or unaligned data) up to SMLM_MAX_ROW_WIDTH
+        if constexpr (VEC == 1) {
+            if (ns <= 8) bb_segment_kernel<TT, GT, GW, 1, 8><<<blocks, 128, 0, st>>>(a);
+            else if (ns <= 16) bb_segment_kernel<TT, GT, GW, 1, 16><<<blocks, 128, 0, st>>>(a);
+            else return invalid_width(a.d);
+        } else {
+            return invalid_width(a.d);
+        }
+    }
     SMLM_LAUNCHED("bb_segment_kernel");
     bb_fixup_kernel<VEC, ROWS_WRITE><<<(int)((a.chunks + 7) / 8), 256, 0, st>>>(a, none);
     SMLM_LAUNCHED("bb_fixup_kernel");
@@ -1376,7 +1392,8 @@ static int backward_impl(const char* fn, const void* grad_out, int grad_dtype, c
     SMLM_CHECK_ARG(grad_dtype == SMLM_F32 || grad_dtype == SMLM_BF16, "%s: grad_out must be fp32 or bf16", fn);
     SMLM_CHECK_ARG(n * k < (int64_t)0x7fffffff, "%s: n * k must be below 2^31", fn);
     SMLM_CHECK_ARG(rows < (int64_t)0xffffffff, "%s: rows must be below 2^32 - 1", fn);
-    SMLM_CHECK_ARG(d < (1 << 30), "%s: d too large", fn);
+    SMLM_CHECK_ARG(d <= SMLM_MAX_ROW_WIDTH, "%s: rows of %lld values are wider than the supported %d", fn,
+                   (long long)d, SMLM_MAX_ROW_WIDTH);
     SMLM_CHECK_ARG((flags & ~(SMLM_BWD_FIRST_TOUCH_WRITES | SMLM_BWD_DEFER_ROWS)) == 0, "%s: unknown flags %d", fn,
                    flags);
     SMLM_CHECK_ARG(!(flags & SMLM_BWD_FIRST_TOUCH_WRITES) || touched != nullptr,
@@ -1479,6 +1496,7 @@ static int deferred_args(const char* fn, const void* grad_out, int grad_dtype, c
     SMLM_CHECK_ARG(n * k < (int64_t)0x7fffffff && rows < (int64_t)0xffffffff, "%s: size too large", fn);
     SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(grad_out) % (grad_dtype == SMLM_F32 ? 16 : 8) == 0,
                    "%s: grad_out must be aligned", fn);
+    if (n == 0 || k == 0) return SMLM_OK;  // an empty backward left nothing to sum (the callers return here too)
     BackwardPlan p = plan_backward(n, k, rows);
     BackwardBufs bb;
     const size_t need = layout_backward(p, d, nullptr, &bb);

@@ -24,6 +24,7 @@ from .sharded import RowShard, sharded_embedding_bag
 from .sparse_values import row_sparse_embedding_bag
 
 IMPLS = ("cuda", "triton", "torch")
+MAX_ROW_WIDTH = 512        # SMLM_MAX_ROW_WIDTH: widest value row of the row-sparse backward
 
 
 class ProductKeyMemory(nn.Module):
@@ -52,6 +53,9 @@ class ProductKeyMemory(nn.Module):
             raise ValueError(f"the CUDA selection needs 1 <= knn <= 32 and n_keys <= 65536, got n_keys={n_keys}, "
                              f"knn={knn}")
         self.impl = "cuda"
+        if value_grad == "row_sparse" and (v_dim if v_dim > 0 else d_out) > MAX_ROW_WIDTH:
+            raise ValueError(f"row-sparse value gradients support rows of at most {MAX_ROW_WIDTH} values, got "
+                             f"{v_dim if v_dim > 0 else d_out}")
         self.score_scale_init = score_scale_init
 
         self.keys = nn.Parameter(torch.empty(heads, 2, n_keys, k_dim // 2))
@@ -220,9 +224,11 @@ class ProductKeyMemory(nn.Module):
             # bf16 cast fused (reference: pkm.py:213-224)
             pre = self.swilu_proj(x)
             t = getattr(self.values, "infer_table", None) or (self.values.weight, None)
-            out = K.bag_infer(indices.view(N, -1), weights.view(N, -1), t[0], t[1], pre=pre, out_bf16=True)
+            K_ = self.heads * self.knn
+            out = K.bag_infer(indices.view(N, K_), weights.view(N, K_), t[0], t[1], pre=pre, out_bf16=True)
             return self.value_proj(out)
-        out = self.read_values(indices.view(N, -1), weights.view(N, -1))
+        K_ = self.heads * self.knn
+        out = self.read_values(indices.view(N, K_), weights.view(N, K_))
         if self.swilu:
             out = self.value_proj(out * F.silu(self.swilu_proj(x)).to(out.dtype))
         return out

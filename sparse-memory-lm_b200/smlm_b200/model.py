@@ -116,16 +116,32 @@ class Attention(nn.Module):
         (it can be captured in one CUDA graph). The new keys / values are written at their positions; each query
         attends to the cache positions up to its own."""
         pos = cache["pos"]
-        q, k = self.rope(q, pos), self.rope(k, pos)
+        # per-step values every layer shares (the rotary tables are the same in all layers): computed once
+        shared = cache.get("step")
+        if shared is None:
+            shared = {}
+        rope = shared.get("rope")
+        if rope is None or rope[0].dtype != q.dtype:
+            rope = shared["rope"] = (self.rope.cos.index_select(0, pos).to(q.dtype),
+                                     self.rope.sin.index_select(0, pos).to(q.dtype))
+        q, k = _rotate(q, *rope), _rotate(k, *rope)
         kbuf, vbuf = cache["kbuf"], cache["vbuf"]
         kbuf.index_copy_(2, pos, k.to(kbuf.dtype))
         vbuf.index_copy_(2, pos, v.to(vbuf.dtype))
-        mask = cache["arange"].view(1, -1) <= pos.view(-1, 1)
+        mask = shared.get("mask")
+        if mask is None:
+            mask = shared["mask"] = cache["arange"].view(1, -1) <= pos.view(-1, 1)
         # one query for few (sequence, head) pairs (decoding at small batch): the plain matmul form spreads the
         # cache length over the GPU, where a fused kernel would give each pair one CTA
         small = q.shape[2] == 1 and q.shape[0] * q.shape[1] < 64
         with sdpa_kernel([SDPBackend.MATH] if small else _MASKED_BACKENDS):
             return F.scaled_dot_product_attention(q, kbuf.to(q.dtype), vbuf.to(q.dtype), attn_mask=mask)
+
+
+def _rotate(x, cos, sin):
+    """RotaryEmbedding.forward with the position tables already selected."""
+    x1, x2 = x.chunk(2, dim=-1)
+    return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
 
 
 _CACHED_BACKENDS = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]

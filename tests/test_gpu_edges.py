@@ -126,3 +126,26 @@ def test_smallest_tables_select_all_keys():
     from util import bits_of_bf16
     osc, oidx, ow = O.select(bits_of_bf16(s1), bits_of_bf16(s2), 8, bf16=True)
     assert np.array_equal(idx.cpu().numpy(), oidx) and np.array_equal(bits_of_bf16(sc), osc)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_small_batch_bag_ring_wraps(dtype):
+    """Few tokens with many lookups: the small-batch bag's four in-flight chunks of 32 lookups wrap around its
+    ring (K = 300: ten chunks, the last one partial), rows out of range in between are skipped and flagged."""
+    gen = torch.Generator().manual_seed(12)
+    rows, D, N, Kk = 5000, 64, 7, 300
+    table = torch.randn(rows, D, generator=gen) * D ** -0.5
+    idx = torch.randint(0, rows, (N, Kk), generator=gen)
+    w = torch.rand(N, Kk, generator=gen)
+    t = table.to(dtype)
+    out = K.bag_forward(idx.to(DEV), w.to(DEV), t.to(DEV)).cpu()
+    from util import bits_of_bf16
+    if dtype == torch.bfloat16:
+        ref, _ = O.bag_forward(idx.numpy(), w.numpy(), bits_of_bf16(t), bf16=True)
+    else:
+        ref, _ = O.bag_forward(idx.numpy(), w.numpy(), table.numpy())
+    assert torch.equal(out, torch.from_numpy(ref))
+    bad = idx.clone()
+    bad[3, 100] = rows
+    with pytest.raises(IndexError, match="out of range"):
+        K.bag_forward(bad.to(DEV), w.to(DEV), t.to(DEV))

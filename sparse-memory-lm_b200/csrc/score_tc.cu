@@ -338,17 +338,6 @@ struct Epi {
     // filters them; survivors are queued, and merged once any lane has FLUSH_AT of them.
     __device__ __forceinline__ void take(const uint32_t (&v)[32], int col0, int nk, uint16_t* dbg) {
         dump(v, col0, nk, dbg);
-        {
-            // quick reject: once the bound is high, whole chunks fall below it (a max tree, one vote)
-            float m[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) m[i] = fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 16]));
-#pragma unroll
-            for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-                for (int i = 0; i < w; i++) m[i] = fmaxf(m[i], m[i + w]);
-            if (__all_sync(FULL, !(m[0] >= bound))) return;  // no survivor in any lane (NaN never passes)
-        }
         uint32_t part[4] = {0u, 0u, 0u, 0u};  // four independent chains
 #pragma unroll
         for (int i = 0; i < 32; i++)

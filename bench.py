@@ -323,10 +323,11 @@ def run_cuda(args, world, rank, local):
     roof["frac"] = roof["achieved"] / roof["peak"]
     kernel_bytes = {
         "bag_forward": M * (D_MODEL * 4 + 12) + N * D_MODEL * 4,
-        # deferred (fused): each distinct table row once for the weight gradient, grad_out, sort, gw, the row
-        # norms and marks; otherwise also the accumulator rows written
-        "bag_backward_rows": (U * D_MODEL * 4 * (1 if fused else 2) + M * (8 * 4 + 4 + 4) + N * D_MODEL * 4
-                              + U * 5),
+        # the weight gradient alone: every lookup's table row, its index and weight, grad_out, gw written
+        "bag_weight_grad": M * (D_MODEL * 4 + 8 + 4 + 4) + N * D_MODEL * 4,
+        # the rest of the backward: key build and sort (2 passes of keys and positions), then the norm pass
+        # (sorted pairs, weights, grad_out, row norms and marks); without the fused step also the rows written
+        "bag_backward_rows": M * (8 * 4 + 4) + N * D_MODEL * 4 + U * 5 + (0 if fused else U * D_MODEL * 4),
         "lazy_adam_step": adam_bytes,
         # row-sharded owner side: every rank's lookups scanned (8 B), this shard's ~M rows gathered, partials out
         "shard_bag_forward": world * M * 8 + M * D_MODEL * 4 + world * N * D_MODEL * 4,

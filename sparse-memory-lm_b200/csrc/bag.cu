@@ -1417,6 +1417,24 @@ static int backward_impl(const char* fn, const void* grad_out, int grad_dtype, c
         return SMLM_ERR_WORKSPACE;
     }
     layout_backward(p, d, workspace, &bb);
+    {
+        // the weight gradient alone (no accumulator, no deferred rows): the gather-shaped kernel, no sort
+        const uintptr_t tp = reinterpret_cast<uintptr_t>(table), gp = reinterpret_cast<uintptr_t>(grad_out);
+        if (!defer && acc == nullptr && gw && d > 0 && d <= 512 && d % 4 == 0 &&
+            gp % (grad_dtype == SMLM_F32 ? 16 : 8) == 0 && tp % (table_dtype == SMLM_F32 ? 16 : 8) == 0) {
+            GwArgs ga{grad_out, indices, idx32, row_base, table, gw, n, rows, (int)k, (int)d};
+            cudaStream_t s0 = as_stream(stream);
+            if (table_dtype == SMLM_F32) {
+                if (grad_dtype == SMLM_F32) launch_gw<float, float>(ga, s0);
+                else launch_gw<float, __nv_bfloat16>(ga, s0);
+            } else {
+                if (grad_dtype == SMLM_F32) launch_gw<__nv_bfloat16, float>(ga, s0);
+                else launch_gw<__nv_bfloat16, __nv_bfloat16>(ga, s0);
+            }
+            SMLM_LAUNCHED("bb_gw_kernel");
+            return SMLM_OK;
+        }
+    }
     uint32_t *keys_in = bb.keys_in, *keys_out = bb.keys_out, *pos_in = bb.pos_in, *pos_out = bb.pos_out;
     void* sort_tmp = bb.sort_tmp;
     float *carry_head = bb.carry_head, *carry_tail = bb.carry_tail;

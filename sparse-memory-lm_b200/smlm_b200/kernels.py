@@ -266,7 +266,8 @@ def bag_backward_rows(grad_out, indices, weights, table, acc, touched, row_sqnor
     flags = L.BWD_FIRST_TOUCH_WRITES if first_touch_writes else 0
     ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, K, rows, D), dev)
     t_code = L.dtype_code(table.dtype) if table is not None else L.F32
-    with L.timed("bag_backward_rows", L.backward_launches(rows)):
+    gw_only = acc is None and touched is None and want_gw
+    with L.timed("bag_weight_grad" if gw_only else "bag_backward_rows", 1 if gw_only else L.backward_launches(rows)):
         rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), L.ptr(w),
                                             L.dtype_code(w.dtype), L.ptr(table), t_code, L.ptr(acc), L.ptr(touched),
                                             L.ptr(row_sqnorm), flags, L.ptr(gw), N, K, rows, D, L.ptr(ws),
@@ -350,6 +351,7 @@ class DeferredRows:
     def __init__(self, ws, g, w, n, k, rows, d):
         self.ws, self.g, self.w = ws, g, w
         self.n, self.k, self.rows, self.d = n, k, rows, d
+        self.ready = None                   # event of a side stream still writing them (overlap=True)
 
 
 def deferrable(table, acc):
@@ -359,10 +361,24 @@ def deferrable(table, acc):
             and table.data_ptr() % 16 == 0)
 
 
-def bag_backward_deferred(grad_out, indices, weights, table, touched, row_sqnorm):
-    """bag_backward_rows into a clean accumulator with the row sums deferred: returns the weight gradient and a
-    DeferredRows; the rows' squared norms and touched marks are written now, the rows themselves by
-    bag_rows_materialize or lazy_adam_deferred_step later."""
+_SIDE = {}
+
+
+def side_stream(dev):
+    """A second stream per device for work that may overlap the caller's stream (created on first use)."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _SIDE.get(idx)
+    if st is None:
+        st = _SIDE[idx] = torch.cuda.Stream(device=dev)
+    return st
+
+
+def bag_backward_deferred(grad_out, indices, weights, table, touched, row_sqnorm, want_gw=True, overlap=False):
+    """bag_backward_rows into a clean accumulator with the row sums deferred: returns the weight gradient (None
+    with want_gw=False) and a DeferredRows; the rows' squared norms and touched marks are written now, the rows
+    themselves by bag_rows_materialize or lazy_adam_deferred_step later. overlap=True (with want_gw=False): the
+    key build, sort and norm pass run on a side stream, overlapping the caller's next kernels; the DeferredRows
+    then carries the event (`ready`) that readers of touched, the norms or the rows wait for (RowStore does)."""
     dev = L.require_cuda(grad_out, indices, weights, table, touched, row_sqnorm)
     N, Kk = indices.shape
     rows, D = table.shape
@@ -372,17 +388,28 @@ def bag_backward_deferred(grad_out, indices, weights, table, touched, row_sqnorm
     idx = _contig(indices.long())
     w = _contig(weights if weights.dtype in (torch.float32, torch.bfloat16) else weights.float())
     t = _contig(table)
-    gw = torch.empty(N, Kk, dtype=torch.float32, device=dev)
+    gw = torch.empty(N, Kk, dtype=torch.float32, device=dev) if want_gw else None
     ws = L.workspace(L.lib().smlm_bag_backward_workspace(N, Kk, rows, D), dev)
-    with L.timed("bag_backward_rows", L.backward_launches(rows)):
-        rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), L.ptr(w),
-                                            L.dtype_code(w.dtype), L.ptr(t), L.dtype_code(t.dtype), None,
-                                            L.ptr(touched), L.ptr(row_sqnorm),
-                                            L.BWD_FIRST_TOUCH_WRITES | L.BWD_DEFER_ROWS, L.ptr(gw), N, Kk, rows, D,
-                                            L.ptr(ws), ws.numel(), L.status_ptr(dev), L.stream(dev))
-    L.check(rc, "bag_backward_rows (deferred)")
-    L.after(dev, "bag_backward_rows")
-    return gw, DeferredRows(ws, g, w, N, Kk, rows, D)
+    main = torch.cuda.current_stream(dev)
+    side = side_stream(dev) if overlap and not want_gw else main
+    if side is not main:
+        side.wait_stream(main)
+        for x in (g, idx, w, t, ws, touched, row_sqnorm):
+            x.record_stream(side)           # the caching allocator keeps them until the side stream is done
+    with torch.cuda.stream(side):
+        with L.timed("bag_backward_rows", L.backward_launches(rows) - (0 if want_gw else 1)):
+            rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), L.ptr(w),
+                                                L.dtype_code(w.dtype), L.ptr(t), L.dtype_code(t.dtype), None,
+                                                L.ptr(touched), L.ptr(row_sqnorm),
+                                                L.BWD_FIRST_TOUCH_WRITES | L.BWD_DEFER_ROWS, L.ptr(gw), N, Kk, rows,
+                                                D, L.ptr(ws), ws.numel(), L.status_ptr(dev), L.stream(dev))
+        L.check(rc, "bag_backward_rows (deferred)")
+        L.after(dev, "bag_backward_rows")
+    rows_ = DeferredRows(ws, g, w, N, Kk, rows, D)
+    if side is not main:
+        rows_.ready = torch.cuda.Event()
+        rows_.ready.record(side)
+    return gw, rows_
 
 
 def shard_bag_backward_deferred(grad_out, indices, weights, table_shard, row_base, touched, row_sqnorm):

@@ -49,6 +49,7 @@ class RowWiseOptimizer(torch.optim.Optimizer):
         for group in self.param_groups:
             for p in group["params"]:
                 st = row_store(p)
+                st.sync()
                 state = self._state(p)
                 state["step"] += 1
                 if st.pending is not None and not st.live:

@@ -56,6 +56,13 @@ class RowStore:
         self.expose()
         return self._touched
 
+    def sync(self):
+        """Order the current stream after a backward whose norm pass still runs on a side stream (overlap)."""
+        p = self.pending
+        if p is not None and p.ready is not None:
+            torch.cuda.current_stream(self._touched.device).wait_event(p.ready)
+            p.ready = None
+
     def expose(self):
         """Make `acc` an exact dense accumulator (stale untouched rows <- 0) before outside code reads it."""
         self.materialize()
@@ -65,6 +72,7 @@ class RowStore:
 
     def materialize(self):
         """Write the deferred row sums of the last backward into acc (where that backward would have)."""
+        self.sync()
         if self.pending is not None:
             K.bag_rows_materialize(self.pending, self._acc)
             self.pending = None
@@ -76,9 +84,11 @@ class RowStore:
 
     def touched_rows(self):
         """Number of touched rows (synchronises; does not expose the store)."""
+        self.sync()
         return int(self._touched.sum())
 
     def reset(self, rows=None):
+        self.sync()
         if rows is None:
             if not self.clean:
                 self._acc.zero_()
@@ -102,6 +112,7 @@ class RowStore:
     def norm(self):
         """acc.norm() (reference: sparse_values.py:143): from the per-row squared norms of the touched rows when
         clean, over the whole exposed accumulator otherwise."""
+        self.sync()
         if self.clean:
             return K.touched_norm(self._acc, self._touched, row_sqnorm=self._sqnorm)
         return self._acc.norm()
@@ -135,8 +146,12 @@ class _RowSparseBag(torch.autograd.Function):
         if store is None:
             gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
         elif store.can_defer(table):
-            # the first backward into an empty store: its row sums go straight into the optimizer step
-            gw, store.pending = K.bag_backward_deferred(grad_out, indices, w, table, store._touched, store._sqnorm)
+            # the first backward into an empty store: its row sums go straight into the optimizer step. The weight
+            # gradient (which the scoring backward needs next) comes first; the sort and the norm pass (which only
+            # the clip and the step need) run on a side stream meanwhile
+            gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
+            _, store.pending = K.bag_backward_deferred(grad_out, indices, w, table, store._touched, store._sqnorm,
+                                                       want_gw=False, overlap=True)
         else:
             store.materialize()
             gw = K.bag_backward_rows(grad_out, indices, w, table, store._acc, store._touched,
@@ -255,6 +270,7 @@ class LazyRowAdam(torch.optim.Optimizer):
             b1, b2 = group["betas"]
             for p in group["params"]:
                 st = row_store(p)
+                st.sync()
                 state = self._state(p)
                 state["step"] += 1
                 if self.state_dtype == "fp32" and st.pending is not None and not st.live:

@@ -397,7 +397,7 @@ def bag_backward_deferred(grad_out, indices, weights, table, touched, row_sqnorm
         for x in (g, idx, w, t, ws, touched, row_sqnorm):
             x.record_stream(side)           # the caching allocator keeps them until the side stream is done
     with torch.cuda.stream(side):
-        with L.timed("bag_backward_rows", L.backward_launches(rows) - (0 if want_gw else 1)):
+        with L.timed("bag_backward_rows", L.backward_launches(rows) + (1 if want_gw else 0)):
             rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), L.ptr(w),
                                                 L.dtype_code(w.dtype), L.ptr(t), L.dtype_code(t.dtype), None,
                                                 L.ptr(touched), L.ptr(row_sqnorm),

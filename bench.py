@@ -205,16 +205,20 @@ def train_step(mem, opt, x, g):
 
 
 def timed_loop(fn, steps, world):
+    """Device time (CUDA events around exactly `steps` calls, synchronised on both sides) and the host time the
+    loop took to enqueue them (ms). Host time close to device time means the loop is host-bound."""
     barrier(world)
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
+    t0 = time.perf_counter()
     for i in range(steps):
         fn(i)
+    host = (time.perf_counter() - t0) * 1e3
     e.record()
     torch.cuda.synchronize()
     barrier(world)
-    return s.elapsed_time(e)
+    return s.elapsed_time(e), host
 
 
 def run_cuda(args, world, rank, local):
@@ -247,9 +251,13 @@ def run_cuda(args, world, rank, local):
         opt.zero_grad(set_to_none=True)
     U = sum(uniq) / len(uniq)
 
-    L.PROFILE = []
     with Clocks(local) as clocks:
-        ms = timed_loop(lambda i: train_step(mem, opt, xs[i % n_batches], gs[i % n_batches]), args.steps, world)
+        ms, host_ms = timed_loop(lambda i: train_step(mem, opt, xs[i % n_batches], gs[i % n_batches]), args.steps,
+                                 world)
+    # per-kernel timings: the same number of further steps with CUDA events recorded around every library call
+    # on the stream it launches on (kept out of the headline loop, whose host work they would add to)
+    L.PROFILE = []
+    timed_loop(lambda i: train_step(mem, opt, xs[i % n_batches], gs[i % n_batches]), args.steps, world)
     prof, L.PROFILE = L.PROFILE, None
     ms = max_over_ranks(ms, world)
     ms_step = ms / args.steps
@@ -291,7 +299,7 @@ def run_cuda(args, world, rank, local):
         v = train_step(mem, opt, bufs[b][0], bufs[b][1])
         consumed[b].record(torch.cuda.current_stream(dev))
         out_host[i % n_batches].copy_(v, non_blocking=True)
-    ms_e2e = max_over_ranks(timed_loop(e2e_step, args.steps, world), world)
+    ms_e2e = max_over_ranks(timed_loop(e2e_step, args.steps, world)[0], world)
     e2e_tok_s = N * world / (ms_e2e / args.steps / 1e3)
 
     # roofline of the dominant kernel: lazy Adam over the U touched rows of a (rows, 384) fp32 table
@@ -356,7 +364,9 @@ def run_cuda(args, world, rank, local):
                        "unique_rows_per_step_per_gpu": round(U)},
             "e2e": {"value": round(e2e_tok_s, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 2 * N * D_MODEL * 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": launches, "roofline": roof, "kernels": breakdown, "clocks": clocks.summary()}
+            "gpu_launches": launches, "host_ms_per_step": round(host_ms / args.steps, 4),
+            "kernel_timing": "per-call CUDA events on the launching stream over K further identical steps",
+            "roofline": roof, "kernels": breakdown, "clocks": clocks.summary()}
     return line
 
 

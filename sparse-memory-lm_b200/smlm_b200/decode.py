@@ -24,6 +24,8 @@ class GraphDecoder:
         cfg = model.cfg
         if cfg.eng_layers:
             raise ValueError("GraphDecoder: Engram memories keep growing caches (decode them with the KV-cache loop)")
+        if model.training:
+            raise ValueError("GraphDecoder: put the model in eval mode first (BatchNorm uses its running statistics)")
         self.model = model
         self.batch = batch
         self.max_len = max_len or cfg.max_seq_len

@@ -68,6 +68,8 @@ def parse():
                          "B-16M prefill / decode measurement; configs: BASELINE configs 1-3 as single layers "
                          "with fwd / bwd / opt timed separately")
     ap.add_argument("--no-inference", action="store_true", help="leave the inference measurement out of the line")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the step as eager calls (default on one GPU: the step captured as one CUDA graph)")
     return ap.parse_args()
 
 
@@ -167,7 +169,7 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------------ layer
-def build_layer(n_keys, device, world=1):
+def build_layer(n_keys, device, world=1, capturable=False):
     from smlm_b200.pkm import ProductKeyMemory
     from smlm_b200.sparse_values import LazyRowAdam, OptimizerSet
     torch.manual_seed(0)
@@ -184,8 +186,9 @@ def build_layer(n_keys, device, world=1):
         broadcast_replicated(mem, group)
     table = mem.values.weight
     dense = [p for p in mem.parameters() if p is not table]
-    opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True),
-                       LazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98), eps=1e-8))
+    opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True,
+                                         capturable=capturable),
+                       LazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98), eps=1e-8, capturable=capturable))
     return mem, opt
 
 
@@ -225,14 +228,25 @@ def run_cuda(args, world, rank, local):
     from smlm_b200 import _lib as L
     dev = torch.device("cuda", local)
     N, n_keys = args.tokens, args.rows_per_half
-    mem, opt = build_layer(n_keys, dev, world)
+    # one GPU: the step is also captured as one CUDA graph (smlm_b200.graph_step), which takes the host out of the
+    # step (the headline figures); the row-sharded exchange keeps host-side epochs, so N > 1 stays eager
+    graphed = world == 1 and not args.eager
+    mem, opt = build_layer(n_keys, dev, world, capturable=graphed)
     rows = mem.values.weight.shape[0]           # this GPU's rows (all of them on one GPU)
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     n_batches = 4
     xs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(n_batches)]
     gs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(n_batches)]
-    for i in range(args.warmup):
-        train_step(mem, opt, xs[i % n_batches], gs[i % n_batches])
+    if graphed:
+        # captured before any eager step: the warm-up steps run inside GraphedStep on its side stream (autograd
+        # ties each parameter's gradient accumulation to the stream of its first backward, and the legacy
+        # default stream cannot join a capture)
+        from smlm_b200.graph_step import GraphedStep
+        gstep = GraphedStep(lambda x, g: train_step(mem, opt, x, g), [xs[0], gs[0]], opt.opts,
+                            warmup=args.warmup)
+    else:
+        for i in range(args.warmup):
+            train_step(mem, opt, xs[i % n_batches], gs[i % n_batches])
     torch.cuda.synchronize()
 
     # unique rows per step (U) for the algorithmic byte counts: measured on untimed steps
@@ -251,14 +265,19 @@ def run_cuda(args, world, rank, local):
         opt.zero_grad(set_to_none=True)
     U = sum(uniq) / len(uniq)
 
-    with Clocks(local) as clocks:
-        ms, host_ms = timed_loop(lambda i: train_step(mem, opt, xs[i % n_batches], gs[i % n_batches]), args.steps,
-                                 world)
-    # per-kernel timings: the same number of further steps with CUDA events recorded around every library call
-    # on the stream it launches on (kept out of the headline loop, whose host work they would add to)
+    eager_ms, eager_host_ms = timed_loop(lambda i: train_step(mem, opt, xs[i % n_batches], gs[i % n_batches]),
+                                         args.steps, world)
+    # per-kernel timings: the same number of further eager steps with CUDA events recorded around every library
+    # call on the stream it launches on (kept out of the timed loops, whose host work they would add to)
     L.PROFILE = []
     timed_loop(lambda i: train_step(mem, opt, xs[i % n_batches], gs[i % n_batches]), args.steps, world)
     prof, L.PROFILE = L.PROFILE, None
+    eager_ms = max_over_ranks(eager_ms, world)
+    step_fn = lambda i, x, g: train_step(mem, opt, x, g)  # noqa: E731
+    if graphed:
+        step_fn = lambda i, x, g: gstep(x, g)  # noqa: E731
+    with Clocks(local) as clocks:
+        ms, host_ms = timed_loop(lambda i: step_fn(i, xs[i % n_batches], gs[i % n_batches]), args.steps, world)
     ms = max_over_ranks(ms, world)
     ms_step = ms / args.steps
     tokens_per_s = N * world / (ms_step / 1e3)
@@ -296,7 +315,7 @@ def run_cuda(args, world, rank, local):
             prefetch(i + 1)
         b = i % 2
         torch.cuda.current_stream(dev).wait_event(loaded[b])
-        v = train_step(mem, opt, bufs[b][0], bufs[b][1])
+        v = step_fn(i, bufs[b][0], bufs[b][1])
         consumed[b].record(torch.cuda.current_stream(dev))
         out_host[i % n_batches].copy_(v, non_blocking=True)
     ms_e2e = max_over_ranks(timed_loop(e2e_step, args.steps, world)[0], world)
@@ -365,7 +384,12 @@ def run_cuda(args, world, rank, local):
             "e2e": {"value": round(e2e_tok_s, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 2 * N * D_MODEL * 4, "d2h_bytes_per_step": 4},
             "gpu_launches": launches, "host_ms_per_step": round(host_ms / args.steps, 4),
-            "kernel_timing": "per-call CUDA events on the launching stream over K further identical steps",
+            "step_mode": ("one CUDA graph per step (smlm_b200.graph_step.GraphedStep; inputs copied into its static "
+                          "buffers every step)" if graphed else "eager calls"),
+            "eager": {"ms_per_step": round(eager_ms / args.steps, 4),
+                      "host_ms_per_step": round(eager_host_ms / args.steps, 4),
+                      "tokens_per_s": round(N * world / (eager_ms / args.steps / 1e3), 1)},
+            "kernel_timing": "per-call CUDA events on the launching stream over K further identical eager steps",
             "roofline": roof, "kernels": breakdown, "clocks": clocks.summary()}
     return line
 

@@ -191,6 +191,17 @@ SMLM_API int smlm_lazy_adam_deferred_step(float *param, float *exp_avg, float *e
                                           float bc2_sqrt, float eps, float neg_step_size, void *value_copy,
                                           int copy_dtype, void *workspace, size_t workspace_bytes, void *stream);
 
+/* smlm_lazy_adam_deferred_step with the six step scalars read from device memory when the kernels run:
+ * scalars_dev[0..5] = one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step_size (fp32). For a training step
+ * captured in a CUDA graph: the caller writes each step's scalars (computed as for the by-value call, so the
+ * results are the same bits) into that buffer before replaying. No counterpart in the reference. */
+SMLM_API int smlm_lazy_adam_deferred_step_dev(float *param, float *exp_avg, float *exp_avg_sq, uint8_t *touched,
+                                              const void *grad_out, int grad_dtype, const void *weights,
+                                              int weights_dtype, const float *grad_scale_dev, float grad_scale,
+                                              int64_t n, int64_t k, int64_t rows, int64_t d, const float *scalars_dev,
+                                              void *value_copy, int copy_dtype, void *workspace,
+                                              size_t workspace_bytes, void *stream);
+
 SMLM_API int smlm_rowwise_step(float *param, float *acc, uint8_t *touched, float *v, int32_t *count,
                                const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d, int kind,
                                float b2, float eps, float lr, int flags, void *workspace, size_t workspace_bytes,

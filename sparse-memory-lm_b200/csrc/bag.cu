@@ -498,7 +498,15 @@ struct RowAdam {
     int32_t* row_count;
     int rw_kind;
     float rw_b2, rw_eps, rw_lr;
+    // lazy Adam's six scalars in device memory instead of `s` (one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps,
+    // neg_step): a step replayed from a CUDA graph reads that step's values, written before the replay
+    const float* s_dev;
 };
+
+__device__ __forceinline__ AdamScalars adam_scalars(const RowAdam& ad) {
+    if (ad.s_dev == nullptr) return ad.s;
+    return AdamScalars{ad.s_dev[0], ad.s_dev[1], ad.s_dev[2], ad.s_dev[3], ad.s_dev[4], ad.s_dev[5]};
+}
 
 // What the row-sum pass does with a completed row sum x (= 0 + the run's sum for a first touch):
 constexpr int ROWS_WRITE = 0;  // acc[row] = x (or acc[row] + x), its squared norm, touched = 1
@@ -798,6 +806,7 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
     constexpr uint32_t FRESH = 0x80000000u;
     constexpr bool STEP = MODE == ROWS_ADAM || MODE == ROWS_ROWWISE;  // an optimizer step on the table row
     const float scale = STEP ? (ad.scale_dev ? *ad.scale_dev : ad.scale) : 1.f;
+    const AdamScalars asc = MODE == ROWS_ADAM ? adam_scalars(ad) : AdamScalars{};
 
     uint32_t cur = NO_ROW;
     bool cur_fresh = false;
@@ -876,7 +885,7 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
                 } else if constexpr (MODE == ROWS_ADAM) {
                     const float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-                    for (int i = 0; i < 4; i++) adam_update(ad.s, scale, pr[s][i], mr[s][i], vr[s][i], xs[i]);
+                    for (int i = 0; i < 4; i++) adam_update(asc, scale, pr[s][i], mr[s][i], vr[s][i], xs[i]);
                     const int64_t o = (int64_t)cur * a.d + col;
                     __stcs(reinterpret_cast<float4*>(ad.p + o), make_float4(pr[s][0], pr[s][1], pr[s][2], pr[s][3]));
                     __stcs(reinterpret_cast<float4*>(ad.m + o), make_float4(mr[s][0], mr[s][1], mr[s][2], mr[s][3]));
@@ -1099,6 +1108,7 @@ __global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a, RowAdam ad) {
     const bool accumulate = MODE == ROWS_WRITE && !a.all_fresh &&
                             !(a.first_writes && a.touched && a.touched[row] == 0);
     const float scale = (MODE == ROWS_ADAM || MODE == ROWS_ROWWISE) ? (ad.scale_dev ? *ad.scale_dev : ad.scale) : 1.f;
+    const AdamScalars asc = MODE == ROWS_ADAM ? adam_scalars(ad) : AdamScalars{};
     // the row's total over its chunks, columns col0 .. col0 + VEC - 1, in chunk order
     auto total = [&](int col0, float (&tot)[VEC]) {
 #pragma unroll
@@ -1151,7 +1161,7 @@ __global__ void __launch_bounds__(256) bb_fixup_kernel(SegArgs a, RowAdam ad) {
             if constexpr (MODE == ROWS_WRITE) a.acc[o + i] = x;
             if constexpr (MODE == ROWS_ADAM) {
                 float p = ad.p[o + i], m = ad.m[o + i], v = ad.v[o + i];
-                adam_update(ad.s, scale, p, m, v, x);
+                adam_update(asc, scale, p, m, v, x);
                 ad.p[o + i] = p;
                 ad.m[o + i] = m;
                 ad.v[o + i] = v;
@@ -1545,13 +1555,12 @@ extern "C" int smlm_bag_rows_materialize(const void* grad_out, int grad_dtype, c
                                   : launch_rows_mode<__nv_bfloat16, ROWS_WRITE>(a, none, st);
 }
 
-extern "C" int smlm_lazy_adam_deferred_step(float* param, float* exp_avg, float* exp_avg_sq, uint8_t* touched,
-                                            const void* grad_out, int grad_dtype, const void* weights,
-                                            int weights_dtype, const float* grad_scale_dev, float grad_scale,
-                                            int64_t n, int64_t k, int64_t rows, int64_t d, float one_minus_b1, float b2,
-                                            float one_minus_b2, float bc2_sqrt, float eps, float neg_step_size,
-                                            void* value_copy, int copy_dtype, void* workspace, size_t workspace_bytes,
-                                            void* stream) {
+namespace smlm {
+static int lazy_adam_deferred_impl(float* param, float* exp_avg, float* exp_avg_sq, uint8_t* touched,
+                                   const void* grad_out, int grad_dtype, const void* weights, int weights_dtype,
+                                   const float* grad_scale_dev, float grad_scale, int64_t n, int64_t k, int64_t rows,
+                                   int64_t d, AdamScalars sc, const float* scalars_dev, void* value_copy,
+                                   int copy_dtype, void* workspace, size_t workspace_bytes, void* stream) {
     SegArgs a;
     int rc = deferred_args("lazy_adam_deferred_step", grad_out, grad_dtype, weights, weights_dtype, n, k, rows, d,
                            workspace, workspace_bytes, &a);
@@ -1564,11 +1573,39 @@ extern "C" int smlm_lazy_adam_deferred_step(float* param, float* exp_avg, float*
     SMLM_CHECK_ARG(value_copy == nullptr || copy_dtype == SMLM_F32 || copy_dtype == SMLM_BF16,
                    "lazy_adam_deferred_step: value copy must be fp32 or bf16");
     a.touched = touched;
-    RowAdam ad{param, exp_avg, exp_avg_sq, grad_scale_dev, grad_scale,
-               AdamScalars{one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step_size}, value_copy, copy_dtype};
+    RowAdam ad{param, exp_avg, exp_avg_sq, grad_scale_dev, grad_scale, sc, value_copy, copy_dtype};
+    ad.s_dev = scalars_dev;
     cudaStream_t st = as_stream(stream);
     return grad_dtype == SMLM_F32 ? launch_rows_mode<float, ROWS_ADAM>(a, ad, st)
                                   : launch_rows_mode<__nv_bfloat16, ROWS_ADAM>(a, ad, st);
+}
+}  // namespace smlm
+
+extern "C" int smlm_lazy_adam_deferred_step(float* param, float* exp_avg, float* exp_avg_sq, uint8_t* touched,
+                                            const void* grad_out, int grad_dtype, const void* weights,
+                                            int weights_dtype, const float* grad_scale_dev, float grad_scale,
+                                            int64_t n, int64_t k, int64_t rows, int64_t d, float one_minus_b1, float b2,
+                                            float one_minus_b2, float bc2_sqrt, float eps, float neg_step_size,
+                                            void* value_copy, int copy_dtype, void* workspace, size_t workspace_bytes,
+                                            void* stream) {
+    return smlm::lazy_adam_deferred_impl(param, exp_avg, exp_avg_sq, touched, grad_out, grad_dtype, weights,
+                                         weights_dtype, grad_scale_dev, grad_scale, n, k, rows, d,
+                                         smlm::AdamScalars{one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps,
+                                                           neg_step_size},
+                                         nullptr, value_copy, copy_dtype, workspace, workspace_bytes, stream);
+}
+
+extern "C" int smlm_lazy_adam_deferred_step_dev(float* param, float* exp_avg, float* exp_avg_sq, uint8_t* touched,
+                                                const void* grad_out, int grad_dtype, const void* weights,
+                                                int weights_dtype, const float* grad_scale_dev, float grad_scale,
+                                                int64_t n, int64_t k, int64_t rows, int64_t d,
+                                                const float* scalars_dev, void* value_copy, int copy_dtype,
+                                                void* workspace, size_t workspace_bytes, void* stream) {
+    SMLM_CHECK_ARG(scalars_dev != nullptr, "lazy_adam_deferred_step_dev: null scalars");
+    return smlm::lazy_adam_deferred_impl(param, exp_avg, exp_avg_sq, touched, grad_out, grad_dtype, weights,
+                                         weights_dtype, grad_scale_dev, grad_scale, n, k, rows, d,
+                                         smlm::AdamScalars{}, scalars_dev, value_copy, copy_dtype, workspace,
+                                         workspace_bytes, stream);
 }
 
 extern "C" int smlm_rowwise_deferred_step(float* param, uint8_t* touched, float* v, int32_t* count,

@@ -52,6 +52,8 @@ SIGNATURES = {
     "smlm_bag_rows_materialize": (_i32, [_p, _i32, _p, _i32, _p, _i64, _i64, _i64, _i64, _p, _sz, _p]),
     "smlm_lazy_adam_deferred_step": (_i32, [_p, _p, _p, _p, _p, _i32, _p, _i32, _p, _f32, _i64, _i64, _i64, _i64,
                                             _f32, _f32, _f32, _f32, _f32, _f32, _p, _i32, _p, _sz, _p]),
+    "smlm_lazy_adam_deferred_step_dev": (_i32, [_p, _p, _p, _p, _p, _i32, _p, _i32, _p, _f32, _i64, _i64, _i64, _i64,
+                                                _p, _p, _i32, _p, _sz, _p]),
     "smlm_lazy_adam_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32,
                                    _p, _i32, _i32, _p, _sz, _p]),
     "smlm_lazy_adam_lowmem_step": (_i32, [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32,

@@ -394,8 +394,9 @@ def bag_backward_deferred(grad_out, indices, weights, table, touched, row_sqnorm
     side = side_stream(dev) if overlap and not want_gw else main
     if side is not main:
         side.wait_stream(main)
-        for x in (g, idx, w, t, ws, touched, row_sqnorm):
-            x.record_stream(side)           # the caching allocator keeps them until the side stream is done
+        if not torch.cuda.is_current_stream_capturing():  # (a captured graph's memory lives as long as the graph)
+            for x in (g, idx, w, t, ws, touched, row_sqnorm):
+                x.record_stream(side)       # the caching allocator keeps them until the side stream is done
     with torch.cuda.stream(side):
         with L.timed("bag_backward_rows", L.backward_launches(rows) + (1 if want_gw else 0)):
             rc = L.lib().smlm_bag_backward_rows(L.ptr(g), L.dtype_code(g.dtype), L.ptr(idx), L.ptr(w),
@@ -449,21 +450,28 @@ def bag_rows_materialize(pending, acc):
 
 
 def lazy_adam_deferred_step(param, exp_avg, exp_avg_sq, touched, pending, grad_scale, step, lr, beta1, beta2, eps,
-                            value_copy=None):
+                            value_copy=None, scalars_dev=None):
     """lazy_adam_step fused with the deferred row sums: bit-identical to bag_rows_materialize + lazy_adam_step,
-    without writing or reading the accumulator."""
-    dev = L.require_cuda(param, exp_avg, exp_avg_sq, touched, value_copy)
+    without writing or reading the accumulator. scalars_dev: a (6,) fp32 device buffer holding the step's scalars
+    (1 - beta1, beta2, 1 - beta2, sqrt(1 - beta2^step), eps, -lr / (1 - beta1^step)), read when the kernels run
+    (for a step captured in a CUDA graph); step / lr / betas / eps are then not used."""
+    dev = L.require_cuda(param, exp_avg, exp_avg_sq, touched, value_copy, scalars_dev)
     p = pending
     sp, sf, keep = _scale_args(grad_scale, dev)
-    bc1 = 1 - beta1 ** step
-    bc2 = 1 - beta2 ** step
+    cp = L.dtype_code(value_copy.dtype) if value_copy is not None else L.F32
     with L.timed("lazy_adam_step", 2):
-        rc = L.lib().smlm_lazy_adam_deferred_step(
-            L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(touched), L.ptr(p.g), L.dtype_code(p.g.dtype),
-            L.ptr(p.w), L.dtype_code(p.w.dtype), sp, sf, p.n, p.k, p.rows, p.d, 1 - beta1, beta2, 1 - beta2,
-            math.sqrt(bc2), eps, -(lr / bc1), L.ptr(value_copy),
-            L.dtype_code(value_copy.dtype) if value_copy is not None else L.F32, L.ptr(p.ws), p.ws.numel(),
-            L.stream(dev))
+        if scalars_dev is not None:
+            rc = L.lib().smlm_lazy_adam_deferred_step_dev(
+                L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(touched), L.ptr(p.g),
+                L.dtype_code(p.g.dtype), L.ptr(p.w), L.dtype_code(p.w.dtype), sp, sf, p.n, p.k, p.rows, p.d,
+                L.ptr(scalars_dev), L.ptr(value_copy), cp, L.ptr(p.ws), p.ws.numel(), L.stream(dev))
+        else:
+            bc1 = 1 - beta1 ** step
+            bc2 = 1 - beta2 ** step
+            rc = L.lib().smlm_lazy_adam_deferred_step(
+                L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(touched), L.ptr(p.g), L.dtype_code(p.g.dtype),
+                L.ptr(p.w), L.dtype_code(p.w.dtype), sp, sf, p.n, p.k, p.rows, p.d, 1 - beta1, beta2, 1 - beta2,
+                math.sqrt(bc2), eps, -(lr / bc1), L.ptr(value_copy), cp, L.ptr(p.ws), p.ws.numel(), L.stream(dev))
     L.check(rc, "lazy_adam_deferred_step")
     del keep
 

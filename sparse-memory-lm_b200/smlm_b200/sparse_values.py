@@ -12,6 +12,8 @@ Same API and semantics as re133/sparse-memory-lm smlm/sparse_values.py:
 The only implementation is "cuda" (libsmlm_b200.so); the reference's "torch" / "triton" values are accepted
 as aliases so that configurations carry over, and CPU tables raise.
 """
+import math
+
 import torch
 
 from . import kernels as K
@@ -225,10 +227,15 @@ class LazyRowAdam(torch.optim.Optimizer):
 
     value_copy_dtype=torch.bfloat16 keeps a bf16 copy of each table (`table.value_copy`) that the step refreshes
     for the updated rows: the forward can read the copy (half the gather bytes) while the fp32 table stays the
-    master."""
+    master.
+
+    capturable=True (no counterpart in the reference) lets a training step that ends in this optimizer be captured
+    in a CUDA graph (smlm_b200.graph_step): the step's bias-correction scalars are read from a small device buffer,
+    which prepare_replay() advances and fills (computed as the eager step computes them, so the same bits) before
+    every replay. Captured steps must take the fused deferred path (fp32 moments, one backward per step)."""
 
     def __init__(self, params, lr, betas=(0.9, 0.95), eps=1e-8, name="memory_values", impl="cuda",
-                 state_dtype="fp32", value_copy_dtype=None):
+                 state_dtype="fp32", value_copy_dtype=None, capturable=False):
         params = list(params)
         _check_impl(impl)
         if state_dtype not in ("fp32", "bf16", "int8"):
@@ -246,6 +253,10 @@ class LazyRowAdam(torch.optim.Optimizer):
         self.impl = "cuda"
         self.state_dtype = state_dtype
         self.value_copy_dtype = value_copy_dtype
+        if capturable and state_dtype != "fp32":
+            raise ValueError("capturable=True needs fp32 moments")
+        self.capturable = capturable
+        self._scal = {}                 # capturable: per table, its step scalars on the device, (6,) fp32
         if value_copy_dtype is not None:
             for p in params:
                 p.value_copy = p.detach().to(value_copy_dtype)
@@ -264,14 +275,63 @@ class LazyRowAdam(torch.optim.Optimizer):
                 state["exp_avg_sq_scale"] = torch.zeros(p.shape[0], dtype=torch.float32, device=p.device)
         return state
 
+    @staticmethod
+    def _scalars(step, lr, b1, b2, eps):
+        """The fused step's six scalars for `step`, as smlm_lazy_adam_deferred_step takes them."""
+        bc1 = 1 - b1 ** step
+        bc2 = 1 - b2 ** step
+        return [1 - b1, b2, 1 - b2, math.sqrt(bc2), eps, -(lr / bc1)]
+
+    def _write_scalars(self, p, group):
+        """capturable: this table's scalars for its current step count, copied to the device buffer on the
+        current stream."""
+        b1, b2 = group["betas"]
+        dev_buf = self._scal.get(p)
+        if dev_buf is None:
+            dev_buf = self._scal[p] = torch.zeros(6, dtype=torch.float32, device=p.device)
+        # a fresh pinned staging tensor per write: the host allocator keeps it until its copy has run, so a host
+        # that runs steps ahead never overwrites scalars a queued step still has to read
+        host = torch.tensor(self._scalars(int(self.state[p]["step"]), group["lr"], b1, b2, group["eps"]),
+                            dtype=torch.float32).pin_memory()
+        dev_buf.copy_(host, non_blocking=True)
+        return dev_buf
+
+    def prepare_replay(self):
+        """capturable: advance every table's step count and write its scalars, before replaying a captured step."""
+        for group in self.param_groups:
+            for p in group["params"]:
+                state = self._state(p)
+                state["step"] += 1
+                self._write_scalars(p, group)
+
     @torch.no_grad()
     def step(self):
+        capturing = torch.cuda.is_current_stream_capturing()
+        if capturing and not self.capturable:
+            raise RuntimeError("LazyRowAdam: capturing a step needs LazyRowAdam(capturable=True)")
         for group in self.param_groups:
             b1, b2 = group["betas"]
             for p in group["params"]:
                 st = row_store(p)
                 st.sync()
                 state = self._state(p)
+                if self.capturable and self.state_dtype == "fp32" and st.pending is not None and not st.live:
+                    # the scalars come from the device buffer: written now for an eager step, by prepare_replay()
+                    # before every replay of a captured one
+                    if not capturing:
+                        state["step"] += 1
+                        self._write_scalars(p, group)
+                    elif p not in self._scal:
+                        raise RuntimeError("LazyRowAdam(capturable=True): run one eager step before capturing")
+                    K.lazy_adam_deferred_step(p, state["exp_avg"], state["exp_avg_sq"], st._touched, st.pending,
+                                              st.grad_scale, 1, group["lr"], b1, b2, group["eps"],
+                                              value_copy=getattr(p, "value_copy", None),
+                                              scalars_dev=self._scal[p])
+                    st.stepped()
+                    continue
+                if capturing:
+                    raise RuntimeError("LazyRowAdam: only the fused deferred step (one backward per step into an "
+                                       "empty row store) can be captured")
                 state["step"] += 1
                 if self.state_dtype == "fp32" and st.pending is not None and not st.live:
                     # rows of one deferred backward: summed and stepped in one pass, acc never written

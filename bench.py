@@ -11,7 +11,9 @@ keys / query), value clipping, LazyRowAdam on the table + fused AdamW on the den
 public API (smlm_b200.pkm.ProductKeyMemory, smlm_b200.sparse_values).
 
 `value` is device-timed with the inputs resident (CUDA events on the launching stream, barrier + synchronize
-around exactly K steps, max over ranks). `e2e` repeats the K steps with each step's inputs copied from pinned
+around exactly K steps, max over ranks); on one GPU the step is captured once as a CUDA graph
+(smlm_b200.graph_step.GraphedStep) and replayed, so the host does not limit it (the eager step is reported beside
+it under `eager`). `e2e` repeats the K steps with each step's inputs copied from pinned
 host memory and a scalar read back inside the timed region. `roofline` is the dominant kernel (the lazy Adam
 step) against the measured HBM copy bandwidth. `cpu_baseline` times the reference's PyTorch CPU path (a
 restatement under oracle/, the only oracle use in this file) on a bounded sample.

@@ -22,7 +22,8 @@ restatement under oracle/, the only oracle use in this file) on a bounded sample
 With --gpus N > 1 (torchrun, one process per GPU, NCCL) the 16.8M-row table and its optimizer state are
 row-sharded over the N GPUs and each GPU runs 32,768 tokens per step (weak scaling): the lookups, partial bags
 and weight gradients cross NVLink through peer memory inside the owner kernels, the output gradients through an
-NCCL all-gather, the replicated parameters' gradients through an NCCL all-reduce.
+NCCL all-gather, the replicated parameters' gradients through an NCCL all-reduce; the line's `exchange` key gives
+the exchange calls' NVLink and HBM bytes against the measured peer-copy and HBM bandwidths.
 
 The default run also measures the B-16M inference token loop (`inference`: prefill and greedy decode of the
 B-16M model, per-token lookup latency). --case configs times BASELINE configs 1-3 as single layers (fwd / bwd /
@@ -51,6 +52,8 @@ ADAM_TRAFFIC_PER_ROW = 9575
 # the same for the plain lazy Adam step over a written accumulator (profiles/lazy_adam_kernel_pkm-layer-1m.md)
 ADAM_UNFUSED_TRAFFIC_PER_ROW = 10698
 D_MODEL, HEADS, KNN, K_DIM = 384, 4, 32, 256
+# peer copy bandwidth per direction per GPU measured over NVLink on this pool's B200s (nominal 900 GB/s)
+NVLINK_PEER_GBS = 770.0
 
 
 def parse():
@@ -207,6 +210,40 @@ def train_step(mem, opt, x, g):
     opt.step()
     opt.zero_grad(set_to_none=True)
     return vnorm
+
+
+def exchange_rooflines(per_kernel_ms, world, n, k, d, hbm_gbs, table_bytes=4):
+    """Roofline of the row-sharded exchange calls of one rank and step (the owner kernels that read and write the
+    other ranks' memory over NVLink), from their mean CUDA-event times `per_kernel_ms` (name -> ms); None on one
+    GPU. n tokens per rank, k lookups per token (m = n k), d values per row; lookups spread evenly over the shards.
+      xchg_forward      NVLink: the P-1 peers' lookups read (8 B each), a partial bag per peer token written
+                        (d x 4 B); HBM: this shard's ~m table rows, every rank's lookups copied locally, the P
+                        partial slots summed into the output
+      xchg_backward_gw  NVLink: the weight gradient of each remote in-shard lookup stored into its rank (4 B);
+                        HBM: the all-gathered output gradients, this shard's ~m table rows, every rank's lookups
+    Each call's target time is the slower of its NVLink bytes at NVLINK_PEER_GBS and its HBM bytes at hbm_gbs;
+    frac = target / measured."""
+    if world < 2:
+        return None
+    m = n * k
+    calls = {
+        "xchg_forward": ((world - 1) * n * (k * 8 + d * 4),
+                         m * d * table_bytes + world * n * k * 8 + (world + 2) * n * d * 4),
+        "xchg_backward_gw": ((world - 1) * m * 4 // world,
+                             m * d * table_bytes + world * n * d * 4 + world * n * k * 4),
+    }
+    out = {}
+    for name, (nv, hb) in calls.items():
+        ms = per_kernel_ms.get(name)
+        if not ms:
+            continue
+        t_nv, t_hbm = nv / (NVLINK_PEER_GBS * 1e9) * 1e3, hb / (hbm_gbs * 1e9) * 1e3
+        nv_gbs, hb_gbs = nv / (ms / 1e3) / 1e9, hb / (ms / 1e3) / 1e9
+        out[name] = {"ms": round(ms, 4), "nvlink_bytes": nv, "nvlink_GB/s": round(nv_gbs, 1),
+                     "nvlink_frac": round(nv_gbs / NVLINK_PEER_GBS, 3), "hbm_bytes": hb, "hbm_GB/s": round(hb_gbs, 1),
+                     "hbm_frac": round(hb_gbs / hbm_gbs, 3), "bound": "nvlink" if t_nv >= t_hbm else "hbm",
+                     "target_ms": round(max(t_nv, t_hbm), 4), "frac": round(max(t_nv, t_hbm) / ms, 3)}
+    return out
 
 
 def timed_loop(fn, steps, world):
@@ -393,6 +430,13 @@ def run_cuda(args, world, rank, local):
                       "tokens_per_s": round(N * world / (eager_ms / args.steps / 1e3), 1)},
             "kernel_timing": "per-call CUDA events on the launching stream over K further identical eager steps",
             "roofline": roof, "kernels": breakdown, "clocks": clocks.summary()}
+    if world > 1:
+        xr = exchange_rooflines({name: statistics.mean(t) for name, t in per_kernel.items()}, world, N,
+                                HEADS * KNN, D_MODEL, hbm)
+        line["exchange"] = {"peak_nvlink_gbs": NVLINK_PEER_GBS,
+                            "peak_source": "measured peer copy per direction per GPU on this pool (nominal 900)",
+                            "calls": xr,
+                            "nccl_allgather_bytes_in_per_step": (world - 1) * N * D_MODEL * 4}
     return line
 
 

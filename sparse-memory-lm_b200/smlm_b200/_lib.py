@@ -6,6 +6,10 @@ and scratch memory is a torch uint8 buffer sized by the library's own *_workspac
 
 SMLM_B200_CHECK=1 turns on checked mode: after every call the stream is synchronised and the device status
 word (out-of-range row indices) is read; a set flag raises IndexError.
+
+SMLM_B200_NVTX=1 wraps every library call in an NVTX range named "smlm:<call>" (score_select, bag_forward,
+bag_backward_rows, lazy_adam_step, xchg_forward, ...), so a profiler timeline shows the layer's stages; off by
+default (a range costs host time on every call).
 """
 import ctypes
 import os
@@ -163,15 +167,20 @@ _STATUS = {}
 # Optional per-call timing for benchmarks: set PROFILE to a list and every kernel entry appends
 # (name, start_event, end_event, kernel_launches) recorded on the current stream around the call.
 PROFILE = None
+NVTX = os.environ.get("SMLM_B200_NVTX", "0") == "1"
 
 
 class timed:
-    """Context manager recording CUDA events around one entry-point call when PROFILE is a list."""
+    """Context manager around one entry-point call: CUDA events when PROFILE is a list, an NVTX range when NVTX is
+    on."""
 
     def __init__(self, name, launches):
         self.name, self.launches = name, launches
 
     def __enter__(self):
+        self.nvtx = NVTX
+        if self.nvtx:
+            torch.cuda.nvtx.range_push(f"smlm:{self.name}")
         if PROFILE is not None:
             self.s = torch.cuda.Event(enable_timing=True)
             self.s.record()
@@ -182,6 +191,8 @@ class timed:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
             PROFILE.append((self.name, self.s, e, self.launches))
+        if self.nvtx:
+            torch.cuda.nvtx.range_pop()
         return False
 
 

@@ -108,3 +108,22 @@ def test_lazy_adam_argument_validation(mode):
             LazyRowAdam([P(torch.zeros(4, 7))], state_dtype=mode, **dict({"lr": 0.01}, **options))
     with pytest.raises(ValueError, match="state_dtype"):
         LazyRowAdam([P(torch.zeros(4, 7))], lr=0.01, state_dtype="fp16")
+
+
+def test_nvtx_ranges_balanced(monkeypatch):
+    """SMLM_B200_NVTX: every library call opens one NVTX range named after it and closes it, also on an error."""
+    from smlm_b200 import _lib as L
+    log = []
+    monkeypatch.setattr(L, "NVTX", True)
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda name: log.append(("push", name)))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: log.append(("pop",)))
+    with L.timed("bag_forward", 1):
+        pass
+    with pytest.raises(ValueError):
+        with L.timed("lazy_adam_step", 2):
+            raise ValueError("argument check")
+    assert log == [("push", "smlm:bag_forward"), ("pop",), ("push", "smlm:lazy_adam_step"), ("pop",)]
+    monkeypatch.setattr(L, "NVTX", False)
+    with L.timed("bag_forward", 1):
+        pass
+    assert len(log) == 4

@@ -601,6 +601,24 @@ def lazy_adam_lowmem_step(param, exp_avg, exp_avg_sq, exp_avg_scale, exp_avg_sq_
     del keep
 
 
+def lazy_adam_step_lowmem(param, exp_avg, exp_avg_sq, acc, touched, grad_scale, step, lr, beta1, beta2, eps,
+                          state_dtype, exp_avg_scale=None, exp_avg_sq_scale=None):
+    """The reference's name and argument order for the compact-moment step (kernels.py:493-515): state_dtype
+    "bf16" (bf16 exp_avg / exp_avg_sq) or "int8" (int8 / uint8 codes with their fp32 row scales). Same effects as
+    lazy_adam_lowmem_step: touched rows updated, their accumulator rows zeroed, touched cleared."""
+    if state_dtype not in ("bf16", "int8"):
+        raise ValueError("low-memory Adam state_dtype must be 'bf16' or 'int8'")
+    int8 = state_dtype == "int8"
+    if int8 and (exp_avg_scale is None or exp_avg_sq_scale is None):
+        raise ValueError("int8 Adam needs exp_avg_scale and exp_avg_sq_scale")
+    want = (torch.int8, torch.uint8) if int8 else (torch.bfloat16, torch.bfloat16)
+    if (exp_avg.dtype, exp_avg_sq.dtype) != want:
+        raise ValueError(f"state_dtype {state_dtype!r} needs moments of {want[0]} / {want[1]}, got "
+                         f"{exp_avg.dtype} / {exp_avg_sq.dtype}")
+    lazy_adam_lowmem_step(param, exp_avg, exp_avg_sq, exp_avg_scale if int8 else None,
+                          exp_avg_sq_scale if int8 else None, acc, touched, grad_scale, step, lr, beta1, beta2, eps)
+
+
 def rowwise_step(param, acc, touched, v, n, grad_scale, lr, beta2, eps, kind, keep_acc=False):
     """Row-wise rowrms / rowadagrad step over the touched rows, in place; accumulator rows zeroed, mask cleared
     (reference: row_optim.py:168-201, formulas of host_rows.c:84-117)."""

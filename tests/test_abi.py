@@ -127,3 +127,21 @@ def test_nvtx_ranges_balanced(monkeypatch):
     with L.timed("bag_forward", 1):
         pass
     assert len(log) == 4
+
+
+def test_reference_named_lowmem_step_validates_before_launch():
+    """kernels.lazy_adam_step_lowmem (the reference's signature) refuses a bad state_dtype, missing int8 scales,
+    mismatched moment dtypes and CPU tensors with ValueError, before any launch."""
+    p = torch.zeros(4, 8)
+    acc, touched = torch.zeros(4, 8), torch.zeros(4, dtype=torch.bool)
+    bf = torch.zeros(4, 8, dtype=torch.bfloat16)
+    args = (acc, touched, 1.0, 1, 1e-3, 0.9, 0.98, 1e-8)
+    with pytest.raises(ValueError, match="'bf16' or 'int8'"):
+        K.lazy_adam_step_lowmem(p, bf, bf, *args, "fp16")
+    with pytest.raises(ValueError, match="scale"):
+        K.lazy_adam_step_lowmem(p, torch.zeros(4, 8, dtype=torch.int8), torch.zeros(4, 8, dtype=torch.uint8),
+                                *args, "int8")
+    with pytest.raises(ValueError, match="needs moments"):
+        K.lazy_adam_step_lowmem(p, bf, bf, *args, "int8", torch.zeros(4), torch.zeros(4))
+    with pytest.raises(ValueError, match="CUDA"):
+        K.lazy_adam_step_lowmem(p, bf, bf, *args, "bf16")

@@ -73,6 +73,45 @@ def test_matches_oracle_and_reference_kernel(mode, dim):
     assert np.array_equal(p, g[f"{t}_p11"])
 
 
+@pytest.mark.parametrize("mode", ["bf16", "int8"])
+def test_reference_named_entry_point(mode):
+    """kernels.lazy_adam_step_lowmem (the reference's name and argument order, kernels.py:493-515) equals
+    lazy_adam_lowmem_step bit for bit over three steps, and consumes the rows (touched cleared, acc rows zeroed)."""
+    gen = torch.Generator().manual_seed(11)
+    R, D = 300, 384
+    i8 = mode == "int8"
+    p0 = torch.randn(R, D, generator=gen).to(DEV)
+    p1 = p0.clone()
+
+    def moments():
+        return (torch.zeros(R, D, dtype=torch.int8 if i8 else torch.bfloat16, device=DEV),
+                torch.zeros(R, D, dtype=torch.uint8 if i8 else torch.bfloat16, device=DEV),
+                torch.zeros(R, device=DEV) if i8 else None, torch.zeros(R, device=DEV) if i8 else None)
+    sa, sb = moments(), moments()
+    for step in range(1, 4):
+        rows = torch.randperm(R, generator=gen)[:100].to(DEV)
+        grad = torch.randn(100, D, generator=gen).to(DEV)
+        accs, marks = [], []
+        for _ in range(2):
+            acc = torch.zeros(R, D, device=DEV)
+            acc[rows] = grad
+            mark = torch.zeros(R, dtype=torch.bool, device=DEV)
+            mark[rows] = True
+            accs.append(acc)
+            marks.append(mark)
+        K.lazy_adam_step_lowmem(p0, sa[0], sa[1], accs[0], marks[0], 0.5, step, 1e-2, 0.9, 0.98, 1e-8, mode,
+                                exp_avg_scale=sa[2], exp_avg_sq_scale=sa[3])
+        K.lazy_adam_lowmem_step(p1, sb[0], sb[1], sb[2], sb[3], accs[1], marks[1], 0.5, step, 1e-2, 0.9, 0.98, 1e-8)
+        assert same_bits(p0, p1), f"values, step {step}"
+        for a, b in zip(sa, sb):
+            if a is not None:
+                assert same_bits(a, b), f"state, step {step}"
+        assert not marks[0].any() and not accs[0].any()
+    with pytest.raises(ValueError):
+        K.lazy_adam_step_lowmem(p0, sa[0], sa[1], accs[0], marks[0], 1.0, 4, 1e-2, 0.9, 0.98, 1e-8,
+                                "int8" if not i8 else "bf16")
+
+
 @pytest.mark.parametrize("mode", MODES)
 def test_unread_rows_preserve_every_state_tensor(mode):
     gen = torch.Generator().manual_seed(71)

@@ -3,7 +3,9 @@
 Each function below stands in for the function of the same name in re133/sparse-memory-lm smlm/kernels.py
 (file:line given per function) and calls libsmlm_b200.so through its C ABI (include/smlm_b200.h). All tensors
 must be CUDA tensors; nothing here has a CPU path. Kernels run on the current CUDA stream without host
-synchronisation, so every function can be captured in a CUDA graph.
+synchronisation, so every function can be captured in a CUDA graph. The reference's Triton launch-shape arguments
+(ch, num_warps, block_j, block_d, P, rows_per_program) are accepted by the same names and have no effect: the
+CUDA kernels choose their own launch shapes.
 """
 import math
 
@@ -17,7 +19,7 @@ def _contig(t):
 
 
 # ------------------------------------------------------------------------------------------ selection
-def pk_select(s1, s2, knn):
+def pk_select(s1, s2, knn, ch=None, num_warps=None):
     """s1, s2 (N, H, n_keys) bf16 or fp32 sub-key scores -> scores (N, H, knn) (same dtype), indices (N, H, knn)
     int64 into the n_keys^2 table, softmax weights (N, H, knn) fp32 (reference: kernels.py:214-226).
 
@@ -219,7 +221,7 @@ class ScoreSelect(torch.autograd.Function):
 
 
 # ------------------------------------------------------------------------------------------ value bag
-def bag_forward(indices, weights, table, out_dtype=torch.float32, name="bag_forward"):
+def bag_forward(indices, weights, table, out_dtype=torch.float32, name="bag_forward", *, block_j=None, block_d=None):
     """out[n] = sum_k weights[n, k] * table[indices[n, k]] (fp32 accumulation); table fp32 / bf16
     (reference: kernels.py:229-237)."""
     dev = L.require_cuda(indices, weights, table)
@@ -239,7 +241,7 @@ def bag_forward(indices, weights, table, out_dtype=torch.float32, name="bag_forw
 
 
 def bag_backward_rows(grad_out, indices, weights, table, acc, touched, row_sqnorm=None, first_touch_writes=False,
-                      want_gw=True):
+                      want_gw=True, *, P=None, block_d=None, num_warps=None):
     """grad_out (N, D) fp32 / bf16, indices / weights (N, K) -> per-sample-weight gradient (N, K) fp32;
     acc[indices[n, k]] += weights[n, k] * grad_out[n] and touched[indices] = True, in place
     (reference: kernels.py:73-88). Deterministic: sorted rows, no float atomics.
@@ -499,7 +501,7 @@ def dequantize_q4(packed, scales):
     return torch.cat([lo, hi], dim=1) * scales.float()[:, None]
 
 
-def bag_infer(indices, weights, table, scales=None, pre=None, out_bf16=False):
+def bag_infer(indices, weights, table, scales=None, pre=None, out_bf16=False, block_j=None, block_d=None):
     """Inference value bag (reference: kernels.py:364-378). table fp32 / bf16 (scales None) or q4-packed uint8
     (rows, D/2) with fp16 scales. pre: optional (N, D) swilu pre-activation -> out = bag * bf16(silu(pre)).
     Returns (N, D) fp32, or bf16 with out_bf16."""
@@ -540,7 +542,7 @@ def _scale_args(grad_scale, device):
 
 
 def lazy_adam_step(param, exp_avg, exp_avg_sq, acc, touched, grad_scale, step, lr, beta1, beta2, eps,
-                   value_copy=None, keep_acc=False):
+                   value_copy=None, keep_acc=False, *, rows_per_program=None, block_d=None):
     """In-place lazy Adam step over the touched rows (reference: kernels.py:417-433): torch's Adam formula, global
     step for the bias correction, no weight decay; the touched accumulator rows are zeroed and the mask cleared.
     grad_scale: 0-d tensor (clip factor) or float; step: the step number after this update (1 for the first).

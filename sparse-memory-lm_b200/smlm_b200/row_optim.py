@@ -68,6 +68,11 @@ class RowWiseOptimizer(torch.optim.Optimizer):
     def _params(self):
         return [p for g in self.param_groups for p in g["params"]]
 
+    def flush(self):
+        """The reference writes the state of GPU-cached hot rows of a host-RAM table back into the per-row state
+        (row_optim.py:209-217); tables here live on the GPU whole and their state is always in the per-row tensors,
+        so there is nothing to write back."""
+
     def state_dict(self):
         params = self._params()
         return {"format": "smlm.row_wise.v1", "kind": self.kind, "shapes": [list(p.shape) for p in params],

@@ -145,3 +145,24 @@ def test_reference_named_lowmem_step_validates_before_launch():
         K.lazy_adam_step_lowmem(p, bf, bf, *args, "int8", torch.zeros(4), torch.zeros(4))
     with pytest.raises(ValueError, match="CUDA"):
         K.lazy_adam_step_lowmem(p, bf, bf, *args, "bf16")
+
+
+def test_reference_launch_arguments_accepted():
+    """The reference's Triton launch-shape arguments are accepted by name (no TypeError); the call then reaches the
+    usual argument checks (CPU tensors: ValueError, no CPU path)."""
+    t = torch.zeros(4, 8)
+    idx = torch.zeros(2, 3, dtype=torch.int64)
+    w = torch.zeros(2, 3)
+    s = torch.zeros(2, 4, 16)
+    calls = [
+        lambda: K.pk_select(s, s, 4, ch=128, num_warps=4),
+        lambda: K.bag_forward(idx, w, t, block_j=32, block_d=128),
+        lambda: K.bag_infer(idx, w, t, block_j=64, block_d=None),
+        lambda: K.bag_backward_rows(torch.zeros(2, 8), idx, w, t, torch.zeros(4, 8),
+                                    torch.zeros(4, dtype=torch.bool), P=32, block_d=64, num_warps=2),
+        lambda: K.lazy_adam_step(t, t, t, t, torch.zeros(4, dtype=torch.bool), 1.0, 1, 1e-3, 0.9, 0.98, 1e-8,
+                                 rows_per_program=8, block_d=128),
+    ]
+    for call in calls:
+        with pytest.raises(ValueError):
+            call()

@@ -1,4 +1,4 @@
-"""Host logic of the row-sharded value table on CPU ranks (gloo, 2 and 3 processes): row ranges, the all-gather /
+"""Host logic of the row-sharded value table on CPU ranks (gloo, 2, 3 and 4 processes): row ranges, the all-gather /
 all-to-all routing of lookups, partial bags and weight gradients, the owner-order sums, the sharded clip norm and
 the replicated-gradient all-reduce. The owner-side compute is a plain torch stand-in here (the CUDA kernels are
 covered by the GPU tests); the result of P ranks must equal one rank over the concatenated batches."""
@@ -125,7 +125,7 @@ def worker(rank, world, port, R, D, N, Kk, errors):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,R", [(2, 1000), (3, 50), (3, 4)])
+@pytest.mark.parametrize("world,R", [(2, 1000), (3, 50), (3, 4), (4, 130)])
 def test_sharded_bag_equals_one_rank(world, R):
     ctx = mp.get_context("spawn")
     errors = ctx.Queue()

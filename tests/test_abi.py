@@ -166,3 +166,42 @@ def test_reference_launch_arguments_accepted():
     for call in calls:
         with pytest.raises(ValueError):
             call()
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """The header is plain C11 (gcc -std=c11 -pedantic -Werror), every declaration links by name against
+    libsmlm_b200.so, and a C caller gets the size queries, the host-side argument checks and the error text
+    without a GPU (no call below reaches a launch)."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    names = declared()
+    src = tmp_path / "abi_caller.c"
+    src.write_text("\n".join([
+        "#include <stdio.h>",
+        "#include <string.h>",
+        '#include "smlm_b200.h"',
+        "typedef void (*fn_t)(void);",
+        "static const fn_t every_entry_point[] = {" + ", ".join(f"(fn_t){n}" for n in names) + "};",
+        "int main(void) {",
+        "    void *s = (void *)0x1000; /* never dereferenced: the checks fail before any launch */",
+        "    if (smlm_version() < 100) return 1;",
+        "    if (smlm_bag_backward_workspace(1024, 128, 1 << 20, 384) == 0) return 2;",
+        "    if (smlm_touched_workspace(1 << 20) == 0) return 3;",
+        "    if (smlm_pk_select(s, s, SMLM_BF16, 4, 2, 64, 33, s, s, s, NULL) != SMLM_ERR_INVALID) return 4;",
+        '    if (strstr(smlm_last_error(), "knn") == NULL) return 5;',
+        "    if (smlm_bag_forward(NULL, NULL, SMLM_F32, NULL, SMLM_F32, 0, 8, 16, 32, NULL, SMLM_F32, NULL, NULL)",
+        "        != SMLM_OK) return 6;",
+        '    printf("ok %zu\\n", sizeof(every_entry_point) / sizeof(every_entry_point[0]));',
+        "    return 0;",
+        "}",
+    ]) + "\n")
+    lib_dir = os.path.dirname(L.LIB_PATH)
+    exe = tmp_path / "abi_caller"
+    subprocess.run([gcc, "-std=c11", "-pedantic", "-Wall", "-Wextra", "-Werror", "-I", os.path.dirname(HEADER),
+                    str(src), "-o", str(exe), "-L", lib_dir, "-lsmlm_b200", f"-Wl,-rpath,{lib_dir}"], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, (out.returncode, out.stderr)
+    assert out.stdout.strip() == f"ok {len(names)}"

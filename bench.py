@@ -400,12 +400,19 @@ def run_cuda(args, world, rank, local):
         "shard_bag_backward_rows": (U * D_MODEL * 4 * (0 if fused else 1) + world * M * (8 * 4 + 8)
                                     + world * N * D_MODEL * 4 + U * 5),
     }
+    # the fused scoring + selection: its sub-key contraction on the tensor cores (algorithmic FLOPs) against the
+    # measured bf16 GEMM burst peak; the selection in its epilogue and the pair kernel share the same time
+    kernel_flops = {"score_select": 2 * N * HEADS * 2 * n_keys * (K_DIM // 2)}
+    tc_peak = peaks.get("bf16_tflops") or 1590.0
     breakdown = {}
     for name, t in sorted(per_kernel.items()):
         entry = {"ms": round(statistics.mean(t), 4), "calls_per_step": len(t) / args.steps}
         if name in kernel_bytes:
             gbs = kernel_bytes[name] / (statistics.mean(t) / 1e3) / 1e9
             entry.update({"GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3)})
+        if name in kernel_flops:
+            tfs = kernel_flops[name] / (statistics.mean(t) / 1e3) / 1e12
+            entry.update({"TFLOP/s": round(tfs, 1), "tensor_frac": round(tfs / tc_peak, 3)})
         breakdown[name] = entry
 
     line = {"metric": METRIC, "value": round(tokens_per_s, 1), "unit": "tokens/s", "n_gpus": world,

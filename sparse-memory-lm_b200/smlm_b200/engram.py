@@ -49,9 +49,15 @@ class NgramHash(nn.Module):
     """Row indices of all hash heads for every position (reference: engram.py:44-75). One set of indices serves
     every Engram module of a model; each module has its own tables."""
 
-    def __init__(self, vocab_size, orders=(2, 3), heads=8, rows=524287, seed=0):
+    def __init__(self, vocab_size, orders=(2, 3), heads=8, rows=524287, seed=0, canon=None):
+        """canon (no counterpart in the reference): the token compression as (int64 ids of vocab_size entries,
+        number of distinct ids), for callers that bring their own table or feed already-compressed ids (the
+        identity map); by default it is computed from the GPT-2 vocabulary as the reference does."""
         super().__init__()
-        canon, n_canon = canonical_ids(vocab_size)
+        canon, n_canon = canonical_ids(vocab_size) if canon is None else canon
+        canon = torch.as_tensor(canon, dtype=torch.int64)
+        if canon.shape != (vocab_size,) or not 0 < int(n_canon) < 2 ** 16:
+            raise ValueError(f"canon must map {vocab_size} token ids to fewer than 65,536 compressed ids")
         self.register_buffer("canon", canon, persistent=False)
         self.pad = n_canon                                   # compressed id of the positions before a sequence
         self.orders, self.heads, self.rows = list(orders), heads, rows

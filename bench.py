@@ -27,7 +27,7 @@ the exchange calls' NVLink and HBM bytes against the measured peer-copy and HBM 
 
 The default run also measures the B-16M inference token loop (`inference`: prefill and greedy decode of the
 B-16M model, per-token lookup latency). --case configs times BASELINE configs 1-3 as single layers (fwd / bwd /
-opt separately); --case scoring and --case inference run one part alone.
+opt separately); --case scoring and --case inference run one part alone; --case engram times the Engram n-gram memory module.
 """
 import argparse
 import json
@@ -67,11 +67,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows-per-half", type=int, default=1024)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
-    ap.add_argument("--case", choices=["layer", "scoring", "inference", "configs"], default="layer",
+    ap.add_argument("--case", choices=["layer", "scoring", "inference", "configs", "engram"], default="layer",
                     help="scoring: only the fused sub-key scoring + selection of the workload's layer (a small "
                          "standalone case for profiler captures; prints its time per call); inference: only the "
                          "B-16M prefill / decode measurement; configs: BASELINE configs 1-3 as single layers "
-                         "with fwd / bwd / opt timed separately")
+                         "with fwd / bwd / opt timed separately; engram: the reference's default Engram module "
+                         "(hash, one-lookup bags, backward, lazy Adam) per step")
     ap.add_argument("--no-inference", action="store_true", help="leave the inference measurement out of the line")
     ap.add_argument("--eager", action="store_true",
                     help="time the step as eager calls (default on one GPU: the step captured as one CUDA graph)")
@@ -533,6 +534,71 @@ def run_configs(args):
     return out
 
 
+# ------------------------------------------------------------------------------------------------ engram
+def run_engram(args):
+    """The reference's default Engram n-gram memory module on one GPU (orders 2 and 3, 8 hash heads each, rows of
+    24 values, 524,287 rows per head: a 8,388,592 x 24 fp32 table), d_model 384, 32 x 1024 seeded uniform token
+    ids per step (used as compressed ids: the GPT-2 token compression needs tiktoken's vocabulary, not available
+    offline), hidden states and upstream gradient ~ N(0, 1). One step = the hash of every position (ngram_rows),
+    the module's forward (16 one-lookup value bags, gating, RMSNorms, depthwise convolution), backward into the
+    row store, value clipping, LazyRowAdam on the table and fused AdamW on the dense parts. Device-timed with CUDA
+    events (whole step, and per library call over as many further steps)."""
+    from smlm_b200 import _lib as L
+    from smlm_b200.engram import EngramMemory, NgramHash
+    from smlm_b200.sparse_values import LazyRowAdam, OptimizerSet, clip_row_sparse
+    dev = torch.device("cuda", 0)
+    B, T, vocab = 32, 1024, 32768
+    orders, heads, hd, rows = (2, 3), 8, 24, 524287
+    torch.manual_seed(0)
+    ng = NgramHash(vocab, orders, heads, rows, seed=0, canon=(torch.arange(vocab), vocab)).to(dev)
+    with torch.device(dev):
+        mod = EngramMemory(D_MODEL, ng.n_lookups, hd, rows, conv_kernel=4, dilation=max(orders))
+    table = mod.values.weight
+    dense = [p for p in mod.parameters() if p is not table]
+    opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True),
+                       LazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98), eps=1e-8))
+    gen = torch.Generator(device=dev).manual_seed(3)
+    ids = [torch.randint(0, vocab, (B, ng.history + T), device=dev, generator=gen) for _ in range(2)]
+    hs = [torch.randn(B, T, D_MODEL, device=dev, generator=gen) for _ in range(2)]
+    gs = [torch.randn(B, T, D_MODEL, device=dev, generator=gen) for _ in range(2)]
+
+    def step(i):
+        r = ng(ids[i % 2])
+        y = mod(hs[i % 2], r)
+        y.backward(gs[i % 2])
+        clip_row_sparse([table], 1.0)
+        torch.nn.utils.clip_grad_norm_([p for p in dense if p.grad is not None], 1.0, foreach=True)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+
+    for i in range(args.warmup):
+        step(i)
+    uniq = int(torch.unique(ng(ids[0])).numel())                    # distinct rows one step reads
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        step(i)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    L.PROFILE = []
+    for i in range(args.steps):
+        step(i)
+    torch.cuda.synchronize()
+    prof, L.PROFILE = L.PROFILE, None
+    per = {}
+    for name, a, b, _ in prof:
+        per.setdefault(name, []).append(a.elapsed_time(b))
+    lookups = B * T * ng.n_lookups
+    return {"case": "engram", "module": "EngramMemory(d_model 384, orders 2/3 x 8 heads, 24-value rows, "
+                                       "524,287 rows per head)", "table_rows": table.shape[0], "tokens": B * T,
+            "lookups_per_step": lookups, "unique_rows_per_step": uniq, "steps": args.steps,
+            "ms_per_step": round(ms, 4), "tokens_per_s": round(B * T / (ms / 1e3), 1),
+            "kernels": {k: {"ms": round(statistics.mean(v), 4), "calls_per_step": len(v) / args.steps}
+                        for k, v in sorted(per.items())}}
+
+
 # ------------------------------------------------------------------------------------------- inference
 def _event_ms(fn, reps):
     """Device time of `reps` calls of fn (CUDA events on the current stream, synchronised on both sides)."""
@@ -689,6 +755,9 @@ def main():
     if args.case == "configs":
         print(json.dumps({"case": "configs", "steps": args.steps, "warmup": args.warmup,
                           "configs": run_configs(args)}), flush=True)
+        return
+    if args.case == "engram":
+        print(json.dumps(run_engram(args)), flush=True)
         return
     if args.case == "inference":
         print(json.dumps({"case": "inference", **run_inference(args, 0)}), flush=True)

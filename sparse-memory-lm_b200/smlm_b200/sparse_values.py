@@ -145,24 +145,30 @@ class _RowSparseBag(torch.autograd.Function):
     def backward(ctx, grad_out):
         table, store = ctx.table, ctx.store
         w, indices = ctx.saved_tensors
+        # the per-sample-weight gradient only when the weights need one (constant weights, e.g. the one-lookup
+        # bags of an Engram table, skip its kernel; the row sums are the same either way)
+        want_gw = ctx.needs_input_grad[0]
+        gw = None
         if store is None:
-            gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
+            if want_gw:
+                gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
         elif store.can_defer(table):
             # the first backward into an empty store: its row sums go straight into the optimizer step. The weight
             # gradient (which the scoring backward needs next) comes first; the sort and the norm pass (which only
             # the clip and the step need) run on a side stream meanwhile
-            gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
+            if want_gw:
+                gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
             _, store.pending = K.bag_backward_deferred(grad_out, indices, w, table, store._touched, store._sqnorm,
                                                        want_gw=False, overlap=True)
         else:
             store.materialize()
             gw = K.bag_backward_rows(grad_out, indices, w, table, store._acc, store._touched,
                                      row_sqnorm=store._sqnorm if store.clean else None,
-                                     first_touch_writes=store.clean)
+                                     first_touch_writes=store.clean, want_gw=want_gw)
             store.live = True
         # drop the RowStore reference so that `del table.row_store` after training frees the accumulator
         ctx.table = ctx.store = None
-        return gw.view(ctx.wshape).to(ctx.wdtype), None, None, None, None
+        return (gw.view(ctx.wshape).to(ctx.wdtype) if gw is not None else None), None, None, None, None
 
 
 def row_sparse_embedding_bag(indices, weights, table, impl="cuda"):

@@ -31,7 +31,6 @@ opt separately); --case scoring and --case inference run one part alone; --case 
 """
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess

@@ -1,14 +1,12 @@
 """The RowStore's clean mode (untouched rows count as zero, first touches are written, the step leaves consumed
 rows alone, clip norms from per-row squared norms) gives exactly what the exact, reference-semantics mode gives."""
-import numpy as np
 import pytest
 import torch
 
-from oracle import oracle as O
 from smlm_b200 import kernels as K
 from smlm_b200.pkm import ProductKeyMemory
 from smlm_b200.sparse_values import LazyRowAdam, clip_row_sparse, row_store
-from util import close, skewed_indices
+from util import skewed_indices
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"

@@ -13,7 +13,6 @@ import os
 import time
 
 import pytest
-import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 

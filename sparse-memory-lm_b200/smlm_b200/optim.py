@@ -86,6 +86,11 @@ def value_table_memory(model, value_state="fp32", *, host=None, value_optim="ada
         if not p.requires_grad:
             continue
         sparse = id(p) in sparse_ids
+        # compact moments exist only for row-sparse fp32 tables (LazyRowAdam(state_dtype=...)): refused otherwise
+        if value_state != "fp32" and not sparse:
+            raise ValueError(f"value_state {value_state!r} needs row-sparse gradients on every trainable value table")
+        if value_state != "fp32" and p.dtype != torch.float32:
+            raise ValueError(f"value_state {value_state!r} needs fp32 value tables")
         out["gradient_bytes"] += n * (max(4, size) if sparse else size)
         if sparse and value_optim != "adam":
             from .row_optim import state_bytes

@@ -331,9 +331,41 @@ def gen_engram():
     save("engram.npz", **arrays)
 
 
+def gen_budget():
+    """Host arithmetic of the optimizer module (reference smlm/optim.py): value_table_memory of small models (one
+    row-sparse memory layer; two layers sharing one table; a dense-gradient table) for every value_state /
+    value_optim, and lr_multiplier over a warmup + cosine schedule. Written as JSON (errors as their type name)."""
+    import json
+    from smlm import optim as RO
+    from smlm.model import ModelConfig, Transformer
+    base = dict(vocab_size=256, d_model=64, n_layers=3, n_heads=4, ffn_hidden=128, mem_n_keys=64, max_seq_len=64)
+    models = {"one_sparse": dict(base, mem_layers=[1], mem_value_grad="row_sparse"),
+              "shared_sparse": dict(base, mem_layers=[0, 2], mem_share_values=True, mem_value_grad="row_sparse"),
+              "dense": dict(base, mem_layers=[1], mem_value_grad="dense")}
+    out = {"models": models, "memory": {}, "lr": []}
+    for name, kw in models.items():
+        torch.manual_seed(0)
+        m = Transformer(ModelConfig(**kw))
+        for vs in ("fp32", "bf16", "int8"):
+            for vo in ("adam", "rowrms", "rowadagrad"):
+                try:
+                    r = RO.value_table_memory(m, vs, value_optim=vo)
+                except ValueError as e:
+                    r = {"error": type(e).__name__}
+                out["memory"][f"{name}/{vs}/{vo}"] = r
+    for total, warm, mn in ((100, 10, 0.1), (1000, 0, 0.0), (7, 3, 0.5)):
+        out["lr"].append({"total": total, "warmup": warm, "min_ratio": mn,
+                          "mult": [RO.lr_multiplier(s, total, warm, mn) for s in range(total + 2)]})
+    path = os.path.join(OUT, "budget.json")
+    with open(path, "w") as f:
+        json.dump(out, f, indent=0, sort_keys=True)
+    print(f"budget.json: {os.path.getsize(path)} bytes")
+
+
 GENERATORS = {"select_bf16": gen_select_bf16, "select_f32": gen_select_f32, "select_backward": gen_select_backward,
               "bag": gen_bag, "lazy_adam": gen_lazy_adam, "lazy_adam_lowmem": gen_lazy_adam_lowmem,
-              "rowwise": gen_rowwise, "infer": gen_infer, "layer": gen_layer, "engram": gen_engram}
+              "rowwise": gen_rowwise, "infer": gen_infer, "layer": gen_layer, "engram": gen_engram,
+              "budget": gen_budget}
 
 if __name__ == "__main__":
     # python make_golden.py [reference path] [fixture names ...]: all fixtures by default

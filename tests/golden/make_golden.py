@@ -362,10 +362,38 @@ def gen_budget():
     print(f"budget.json: {os.path.getsize(path)} bytes")
 
 
+def gen_model_structure():
+    """The reference model's checkpoint layout (smlm/model.py): state_dict keys, shapes and dtypes, param_counts()
+    and macs_per_token() of small Transformers (one memory layer; two sharing a table; Engram layers; no BatchNorm /
+    swilu; learned score scale). Engram's token compression uses the identity map (tiktoken's vocabulary is not
+    reachable offline). Written as JSON."""
+    import json
+    import smlm.engram as RE
+    from smlm.model import ModelConfig, Transformer
+    RE.canonical_ids = lambda vocab: (torch.arange(vocab, dtype=torch.int64), vocab)
+    base = dict(vocab_size=256, d_model=64, n_layers=4, n_heads=4, ffn_hidden=128, mem_n_keys=64, max_seq_len=64)
+    models = {"sparse": dict(base, mem_layers=[1], mem_value_grad="row_sparse"),
+              "shared": dict(base, mem_layers=[0, 2], mem_share_values=True, mem_value_grad="row_sparse"),
+              "engram": dict(base, mem_layers=[1], eng_layers=[0, 3], eng_rows=31, eng_heads=2, eng_head_dim=8),
+              "no_bn_swilu": dict(base, mem_layers=[2], mem_query_norm="none", mem_swilu=False),
+              "score_scale": dict(base, mem_layers=[2], mem_score_scale="learned")}
+    out = {}
+    for name, kw in models.items():
+        torch.manual_seed(0)
+        m = Transformer(ModelConfig(**kw))
+        out[name] = {"config": kw, "state_dict": [[k, list(v.shape), str(v.dtype)] for k, v in m.state_dict().items()],
+                     "param_counts": m.param_counts(), "macs_per_token": m.macs_per_token(),
+                     "macs_per_token_64": m.macs_per_token(64)}
+    path = os.path.join(OUT, "model_structure.json")
+    with open(path, "w") as f:
+        json.dump(out, f, indent=0, sort_keys=True)
+    print(f"model_structure.json: {os.path.getsize(path)} bytes")
+
+
 GENERATORS = {"select_bf16": gen_select_bf16, "select_f32": gen_select_f32, "select_backward": gen_select_backward,
               "bag": gen_bag, "lazy_adam": gen_lazy_adam, "lazy_adam_lowmem": gen_lazy_adam_lowmem,
               "rowwise": gen_rowwise, "infer": gen_infer, "layer": gen_layer, "engram": gen_engram,
-              "budget": gen_budget}
+              "budget": gen_budget, "model_structure": gen_model_structure}
 
 if __name__ == "__main__":
     # python make_golden.py [reference path] [fixture names ...]: all fixtures by default

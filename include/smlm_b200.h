@@ -79,6 +79,8 @@ extern "C" {
 #define SMLM_SCORE_BF16 1      /* bf16 operands, fp32 accumulate, scores rounded to bf16 (autocast path) */
 
 /* Library version (major * 10000 + minor * 100 + patch) and the last error of this thread. */
+/* Interface version (100 for this header) and the text of the calling thread's last error. No counterpart in the
+ * reference: its Python kernel layer raises exceptions where these entry points return a code. */
 SMLM_API int smlm_version(void);
 SMLM_API const char *smlm_last_error(void);
 
@@ -107,6 +109,9 @@ SMLM_API int smlm_quantize_q4(const float *table, int64_t rows, int64_t d, uint8
 
 /* ------------------------------------------------------------------------ value bag backward (row-sparse) */
 
+/* Scratch bytes of smlm_bag_backward_rows / smlm_shard_bag_backward_rows for these sizes (sort keys and positions,
+ * chunk carries), host arithmetic only. The reference's bag_backward_rows (kernels.py:73-88) takes its sort
+ * temporaries from the torch allocator; here the caller passes them in. */
 SMLM_API size_t smlm_bag_backward_workspace(int64_t n, int64_t k, int64_t rows, int64_t d);
 
 /* Row-sparse backward of the value bag:
@@ -137,6 +142,9 @@ SMLM_API int smlm_bag_rows_materialize(const void *grad_out, int grad_dtype, con
 
 /* ------------------------------------------------------------------------------- row-sparse optimizers */
 
+/* Scratch bytes of the touched-row compaction that the optimizer steps and smlm_touched_norm run first (the list
+ * of touched rows), host arithmetic only. No counterpart in the reference: its steps scan the whole mask
+ * (kernels.py:417-433, row_optim.py:179-201). */
 SMLM_API size_t smlm_touched_workspace(int64_t rows);
 
 /* Lazy Adam on the rows with touched[r] != 0 (the only rows loaded): with g = acc[r] * scale,
@@ -202,6 +210,11 @@ SMLM_API int smlm_lazy_adam_deferred_step_dev(float *param, float *exp_avg, floa
                                               void *value_copy, int copy_dtype, void *workspace,
                                               size_t workspace_bytes, void *stream);
 
+/* Row-wise optimizer step over the touched rows (kind SMLM_ROWRMS or SMLM_ROWADAGRAD): g = acc row * clip factor,
+ * q = mean of g^2 (summed in double), rowrms v = b2 v + (1 - b2) q with a per-row step count, rowadagrad v += q,
+ * then the parameter update; touched rows consumed, others bit-unchanged. Replaces RowWiseOptimizer.step's GPU
+ * path (row_optim.py:52-71, 179-201) with the formulas of host_rows.c:82-117. Workspace:
+ * smlm_touched_workspace(rows). */
 SMLM_API int smlm_rowwise_step(float *param, float *acc, uint8_t *touched, float *v, int32_t *count,
                                const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d, int kind,
                                float b2, float eps, float lr, int flags, void *workspace, size_t workspace_bytes,
@@ -226,7 +239,8 @@ SMLM_API int smlm_touched_norm(const float *acc, const float *row_sqnorm, const 
                                int64_t d, float *norm_out, void *workspace, size_t workspace_bytes, void *stream);
 
 /* acc rows whose touched byte is 0 are set to zero: turns "untouched rows count as zero" into actual zeros
- * before an accumulator is handed to code that reads it as a dense tensor (RowStore.acc). */
+ * before an accumulator is handed to code that reads it as a dense tensor (RowStore.acc). No counterpart in the
+ * reference, whose accumulator is always dense (sparse_values.py:26-41). */
 SMLM_API int smlm_zero_untouched(float *acc, const uint8_t *touched, int64_t rows, int64_t d, void *stream);
 
 /* ------------------------------------------------------------------------- product-key scoring / select */
@@ -268,6 +282,8 @@ SMLM_API int smlm_select_grad_entries(const int64_t *indices, const float *weigh
 SMLM_API int smlm_subkey_scores_f32(const float *q, const float *keys, int64_t n, int64_t h, int64_t nk, int64_t half,
                            float *s1, float *s2, void *stream);
 
+/* Scratch bytes of smlm_score_select (the per-half top lists of every (token, head)), host arithmetic only. No
+ * counterpart in the reference, whose einsum + pk_select path (pkm.py:195-201) allocates through torch. */
 SMLM_API size_t smlm_score_select_workspace(int64_t n, int64_t h);
 
 /* Fused scoring + selection under bf16 (the autocast path): q (n, h, 2 half) bf16, keys (h, 2, nk, half) bf16.
@@ -326,7 +342,8 @@ SMLM_API int smlm_shard_bag_backward_rows(const void *grad_out, int grad_dtype, 
 SMLM_API int smlm_slot_sum(const float *src, int64_t slots, int64_t count, float *dst, void *stream);
 
 /* ----------------------------------------------- row-sharded exchange through peer memory (NVLink, CUDA IPC)
- * The same exchange as the NCCL collectives above, fused into the owner's kernels: every rank owns one exchange
+ * No counterpart in the reference (one device there). The same exchange as the NCCL collectives above, fused
+ * into the owner's kernels: every rank owns one exchange
  * block in its HBM (flags, its lookups, a receive area for the owners' partial bags and one for the weight
  * gradients), mapped into the other ranks' processes with CUDA IPC (no multicast objects anywhere). The owner's
  * forward kernel reads each rank's lookups over NVLink and stores that rank's partial bag straight into its

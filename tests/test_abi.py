@@ -205,3 +205,23 @@ def test_header_compiles_as_c_and_links(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert out.returncode == 0, (out.returncode, out.stderr)
     assert out.stdout.strip() == f"ok {len(names)}"
+
+
+def test_every_declaration_cites_its_reference_interface():
+    """Each entry point of the header names the reference interface it replaces (file:line) or says that it has no
+    counterpart there: in the comment above it, above its group of adjacent declarations, or in its section's
+    heading comment."""
+    text = open(HEADER).read()
+    cite = re.compile(r"\.(py|c):\d+|[Nn]o counterpart")
+    uncited = []
+    for sec in re.split(r"/\* -{10,}", text):
+        heading = re.match(r"[^\n]*\n?((?: \*[^\n]*\n)*)", sec).group(0)
+        covered = bool(cite.search(heading))
+        prev, prev_ok = 0, False
+        for m in re.finditer(r"SMLM_API\s+[\w\s\*]*?\b(smlm_\w+)\s*\(", sec):
+            between = sec[prev:m.start()]
+            ok = covered or bool(cite.search(between)) or (prev > 0 and not between.strip() and prev_ok)
+            if not ok:
+                uncited.append(m.group(1))
+            prev, prev_ok = sec.index(";", m.end()) + 1, ok
+    assert not uncited, f"declarations without a reference citation: {uncited}"

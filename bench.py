@@ -45,10 +45,10 @@ sys.path.insert(0, os.path.join(ROOT, "sparse-memory-lm_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "PKM layer tokens/s (fwd+bwd+opt) at 16.8M rows"
-# DRAM bytes (read + write) of the fused row-sum + lazy Adam step per touched row, from the ncu capture in
-# profiles/bb_rowsum_adam_kernel_pkm-layer-1m.md; traffic scales with the touched rows.
+# DRAM bytes (read + write) of the fused row-sum + lazy Adam step per touched row, from the ncu capture of that
+# kernel on a 1M-row layer; traffic scales with the touched rows.
 ADAM_TRAFFIC_PER_ROW = 9575
-# the same for the plain lazy Adam step over a written accumulator (profiles/lazy_adam_kernel_pkm-layer-1m.md)
+# the same for the plain lazy Adam step over a written accumulator (ncu capture of lazy_adam_kernel, 1M rows)
 ADAM_UNFUSED_TRAFFIC_PER_ROW = 10698
 D_MODEL, HEADS, KNN, K_DIM = 384, 4, 32, 256
 # peer copy bandwidth per direction per GPU measured over NVLink on this pool's B200s (nominal 900 GB/s)
@@ -428,7 +428,10 @@ def run_cuda(args, world, rank, local):
                              "table + moments (77 GB resident), inputs cycle over 4 batches",
                        "unique_rows_per_step_per_gpu": round(U)},
             "e2e": {"value": round(e2e_tok_s, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": 2 * N * D_MODEL * 4, "d2h_bytes_per_step": 4},
+                    "h2d_bytes_per_step": 2 * N * D_MODEL * 4, "d2h_bytes_per_step": 4,
+                    "note": "a training step: the inputs (activations and upstream gradient) go in every step; "
+                            "only the step's scalar (the value clip norm) comes back, the layer output and the "
+                            "updated rows stay on the device"},
             "gpu_launches": launches, "host_ms_per_step": round(host_ms / args.steps, 4),
             "step_mode": ("one CUDA graph per step (smlm_b200.graph_step.GraphedStep; inputs copied into its static "
                           "buffers every step)" if graphed else "eager calls"),
@@ -701,49 +704,102 @@ def run_inference(args, local):
 
 
 # ----------------------------------------------------------------------------------------- CPU reference
-def cpu_reference(n_keys, N, steps, warmup):
-    """The reference's PyTorch path (oracle/torch_path.py) on the host cores: fwd + bwd + clip + lazy Adam
-    (the reference's full-table fp32 Adam with unread rows restored) + AdamW on the dense parameters."""
+REF_PKG = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _cpu_name():
+    try:
+        return [ln.split(":", 1)[1].strip() for ln in open("/proc/cpuinfo") if ln.startswith("model name")][0]
+    except (OSError, IndexError):
+        return "unknown"
+
+
+def reference_modules():
+    """The reference's own modules: its smlm package as vendored, unmodified, into baseline/_ref by
+    __graft_entry__.build() (kind "reference"); without it, the restatement under oracle/ (kind "port")."""
+    if os.path.isfile(os.path.join(REF_PKG, "smlm", "pkm.py")):
+        if REF_PKG not in sys.path:
+            sys.path.insert(0, REF_PKG)
+        from smlm.pkm import ProductKeyMemory
+        from smlm.sparse_values import LazyRowAdam, clip_row_sparse
+        return "reference", "the reference's smlm package (baseline/_ref/smlm, unmodified)", \
+            (lambda **kw: ProductKeyMemory(impl="torch", **kw)), \
+            (lambda params, **kw: LazyRowAdam(params, impl="torch", **kw)), clip_row_sparse
     from oracle import torch_path as TP
-    threads = os.cpu_count() or 1
+    return "port", "the reference's PyTorch path restated in oracle/torch_path.py", \
+        (lambda **kw: TP.TorchPKM(canonical=False, **kw)), TP.TorchLazyRowAdam, TP.clip_row_sparse
+
+
+def cpu_reference(n_keys, N, steps, warmup, threads=None):
+    """The reference's PyTorch path on the host cores, one PKM layer step as the GPU arm's (config-1 layer without
+    BatchNorm / swilu, fp32: the reference scores in fp32 off CUDA): forward, backward into its RowStore, value
+    clipping, its LazyRowAdam (impl="torch": a full-table fused Adam with the unread rows restored) and AdamW on
+    the dense parameters. Median of `steps` timed steps after `warmup`."""
+    kind, what, PKM, LRA, clip = reference_modules()
+    threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
     torch.manual_seed(0)
-    mem = TP.TorchPKM(D_MODEL, D_MODEL, n_keys=n_keys, heads=HEADS, knn=KNN, k_dim=K_DIM, query_norm="none",
-                      swilu=False, canonical=False)
-    TP.init_like_reference(mem, 0)
+    mem = PKM(d_in=D_MODEL, d_out=D_MODEL, n_keys=n_keys, heads=HEADS, knn=KNN, k_dim=K_DIM, query_norm="none",
+              swilu=False, value_grad="row_sparse")
+    with torch.no_grad():                                  # config-1 initialisation
+        mem.query_proj.weight.normal_(0, 0.02)
+        mem.query_proj.bias.zero_()
+        mem.keys.normal_(0, (K_DIM // 2) ** -0.5)
+        mem.values.weight.normal_(0, D_MODEL ** -0.5)
     table = mem.values.weight
     dense = [p for p in mem.parameters() if p is not table]
     adamw = torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0)
-    lazy = TP.TorchLazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98))
+    lazy = LRA([table], lr=1e-3, betas=(0.9, 0.98))
     gen = torch.Generator().manual_seed(1)
-    x = torch.randn(N, D_MODEL, generator=gen)
-    g = torch.randn(N, D_MODEL, generator=gen)
+    xs = [torch.randn(N, D_MODEL, generator=gen) for _ in range(2)]
+    gs = [torch.randn(N, D_MODEL, generator=gen) for _ in range(2)]
 
-    def step():
-        out = mem(x)
-        out.backward(g)
-        TP.clip_row_sparse([table], 1.0)
+    def step(i):
+        out = mem(xs[i % 2])
+        out.backward(gs[i % 2])
+        clip([table], 1.0)
         torch.nn.utils.clip_grad_norm_(dense, 1.0)
         adamw.step()
         lazy.step()
         adamw.zero_grad(set_to_none=True)
 
-    for _ in range(warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        step()
-    dt = (time.perf_counter() - t0) / steps
-    try:
-        cpu = [ln.split(":", 1)[1].strip() for ln in open("/proc/cpuinfo") if ln.startswith("model name")][0]
-    except (OSError, IndexError):
-        cpu = "unknown"
-    return {"value": round(N / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"reference PyTorch path (oracle/torch_path.py) on {cpu}: one PKM layer with "
-                      f"{n_keys}^2 = {n_keys ** 2} rows (the 16.8M-row table scaled down to fit host RAM; the "
-                      f"reference's full-table Adam makes larger tables slower), {N} tokens per step, "
-                      f"{steps} timed steps after {warmup} warm-up, {threads} threads",
-            "ms_per_step": round(dt * 1e3, 2)}
+    for i in range(warmup):
+        step(i)
+    times = []
+    for i in range(steps):
+        t0 = time.perf_counter()
+        step(i)
+        times.append(time.perf_counter() - t0)
+    dt = statistics.median(times)
+    return {"value": round(N / dt, 1), "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{what} on {_cpu_name()}: one PKM layer step with {n_keys}^2 = {n_keys ** 2} rows x "
+                      f"{D_MODEL} (the 16.8M-row table scaled down to fit a bounded CPU run; the reference's "
+                      f"full-table Adam makes larger tables slower), {N} tokens per step, median of {steps} timed "
+                      f"steps after {warmup} warm-up, {threads} threads",
+            "ms_per_step": round(dt * 1e3, 2), "rows": n_keys ** 2, "tokens_per_step": N}
+
+
+def run_reference_arm(args, world, rank):
+    """--impl reference: rank 0 times the reference's CPU path with every host thread on the arm's workload, as a
+    bounded sample (a 1M-row table, 4,096 tokens per step), --steps timed steps after --warmup; it also times
+    BASELINE config 1 exactly (65,536 rows, 2,048 tokens). Other ranks exit at once without touching a GPU."""
+    if rank != 0:
+        return None
+    base = cpu_reference(args.cpu_rows_per_half, args.cpu_tokens, args.steps, args.warmup)
+    c1 = cpu_reference(256, 2048, max(3, min(args.steps, 10)), 2)
+    return {"metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "pkm-layer-b16m", "sample": f"pkm-layer-{base['rows']}-rows-cpu-sample",
+                       "rows": base["rows"], "tokens_per_step": base["tokens_per_step"], "v_dim": D_MODEL,
+                       "heads": HEADS, "knn": KNN, "k_dim": K_DIM,
+                       "note": "the B-16M layer step on the host cores, on a bounded sample: see cpu_baseline"},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "config1_cpu": {"rows": c1["rows"], "tokens_per_step": c1["tokens_per_step"], "value": c1["value"],
+                            "unit": "tokens/s", "ms_per_step": c1["ms_per_step"], "kind": c1["kind"],
+                            "cores": c1["cores"]},
+            "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
@@ -761,24 +817,13 @@ def main():
     if args.case == "inference":
         print(json.dumps({"case": "inference", **run_inference(args, 0)}), flush=True)
         return
-    world, rank, local = dist_setup(args)
     if args.impl == "reference":
-        if rank == 0:
-            base = cpu_reference(args.cpu_rows_per_half, args.cpu_tokens, max(1, min(args.steps, 3)),
-                                 min(args.warmup, 1))
-            line = {"metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": world,
-                    "steps": max(1, min(args.steps, 3)), "warmup": min(args.warmup, 1),
-                    "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-                    "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-                    "config": {"workload": "pkm-layer-b16m", "rows": args.cpu_rows_per_half ** 2,
-                               "tokens_per_step": args.cpu_tokens, "note": "CPU sample, see cpu_baseline.sample"},
-                    "cpu_baseline": base,
-                    "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                            "d2h_bytes_per_step": 0}}
+        # the CPU path needs no process group and no GPU: ranks other than 0 leave at once
+        line = run_reference_arm(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        if line is not None:
             print(json.dumps(line), flush=True)
-        if world > 1:
-            torch.distributed.destroy_process_group()
         return
+    world, rank, local = dist_setup(args)
     line = run_cuda(args, world, rank, local)
     if world == 1 and not args.no_inference:
         import gc
@@ -786,7 +831,8 @@ def main():
         torch.cuda.empty_cache()
         line["inference"] = run_inference(args, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_reference(args.cpu_rows_per_half, args.cpu_tokens, 2, 1)
+        base = cpu_reference(args.cpu_rows_per_half, args.cpu_tokens, 3, 1)
+        line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

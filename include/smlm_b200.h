@@ -305,9 +305,13 @@ SMLM_API int smlm_score_select(const void *q, const void *keys, int64_t n, int64
  * No counterpart in the reference. Its scratch is a static device array inside the library, sized for at most
  * SMLM_NOALLOC_MAX_ROWS (token, head) rows (n * h; 8 MiB, held by every GPU that loads the library until the
  * process exits); larger calls return SMLM_ERR_INVALID. The first call on a device looks up that array's device
- * address (cudaGetSymbolAddress) with the device current; make that first call before any stream capture. All
- * calls share the one array, so calls that overlap on the GPU (other streams, other threads) race: serialise
- * them. The call allocates nothing: no cudaMalloc / cudaFree, no allocating library routine. */
+ * address (cudaGetSymbolAddress) with the device current; make that first call before any stream capture (a
+ * first call on a capturing stream returns SMLM_ERR_INVALID). All calls share the one array, so calls that
+ * overlap on the GPU (other streams, other threads) race: serialise them. The key range is split over several
+ * CTAs per (token tile, head) as the workspace entry point does, but only as far as the array holds the splits'
+ * lists (n * h * splits <= SMLM_NOALLOC_MAX_ROWS): near the row limit the call runs unsplit, so a few hundred
+ * tokens at most use fewer SMs than smlm_score_select would. The call allocates nothing: no cudaMalloc /
+ * cudaFree, no allocating library routine. */
 #define SMLM_NOALLOC_MAX_ROWS 16384
 SMLM_API int smlm_score_select_noalloc(const void *q, const void *keys, int64_t n, int64_t h, int64_t nk,
                                        int64_t half, int64_t knn, void *scores, int64_t *indices, float *weights,

@@ -36,6 +36,8 @@ def lib():
         L.orc_bag_forward.argtypes = [_p, _p, _p, _i32, _i64, _i64, _i64, _i64, _p]
         L.orc_bag_forward.restype = _i64
         L.orc_bag_backward.argtypes = [_p, _p, _p, _p, _i32, _p, _p, _p, _i64, _i64, _i64, _i64, _i64]
+        L.orc_bag_rows_subset.argtypes = [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p]
+        L.orc_bag_rows_subset.restype = _i64
         L.orc_quantize_q4.argtypes = [_p, _i64, _i64, _p, _p]
         L.orc_bag_infer.argtypes = [_p, _p, _p, _i32, _p, _p, _i32, _i64, _i64, _i64, _i64, _p, _i32]
         L.orc_lazy_adam.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32, _f32]
@@ -144,6 +146,21 @@ def bag_backward(g, idx, w, table, acc, touched, bf16=False, chunk=0):
     lib().orc_bag_backward(_ptr(g), _ptr(idx), _ptr(w), _ptr(table), int(bf16), _ptr(acc), _ptr(touched), _ptr(gw),
                            n, k, rows, d, chunk)
     return gw
+
+
+def bag_rows_subset(g, idx, w, rows, sample, chunk=0):
+    """The row sums bag_backward would add into a zeroed acc, for the rows in `sample` only (int64 array of
+    distinct rows), in that order: (len(sample), d) fp32. Same sorted order and chunk pieces as bag_backward over
+    all lookups; needs no table (for steps whose table does not fit host memory)."""
+    g, idx, w = _c(g, np.float32), _c(idx, np.int64), _c(w, np.float32)
+    n, k = idx.shape
+    d = g.shape[1]
+    sample = _c(sample, np.int64)
+    slot = np.full(rows, -1, np.int32)
+    slot[sample] = np.arange(sample.size, dtype=np.int32)
+    out = np.zeros((sample.size, d), np.float32)
+    lib().orc_bag_rows_subset(_ptr(g), _ptr(idx), _ptr(w), n, k, rows, d, chunk, _ptr(slot), _ptr(out))
+    return out
 
 
 def quantize_q4(table):

@@ -226,6 +226,52 @@ void orc_bag_backward(const float *g, const int64_t *idx, const float *w, const 
     free(rp); free(sum); free(part);
 }
 
+/* The row sums of orc_bag_backward (same sorted order, same chunk pieces over ALL valid lookups) for a subset of
+ * the rows only: rows with slot[r] >= 0 get 0 + their sum in out[slot[r]] (what orc_bag_backward leaves in a
+ * zeroed acc); the others are skipped. No table, no weight gradients: lets a test check sampled rows of a step
+ * whose table does not fit host memory. Returns the number of valid lookups. */
+int64_t orc_bag_rows_subset(const float *g, const int64_t *idx, const float *w, int64_t n, int64_t k,
+                            int64_t rows, int64_t d, int64_t chunk, const int32_t *slot, float *out) {
+    const int64_t m = n * k;
+    rowpos_t *rp = malloc(sizeof(rowpos_t) * (size_t)(m ? m : 1));
+    float *sum = malloc(sizeof(float) * (size_t)(d ? d : 1)), *part = malloc(sizeof(float) * (size_t)(d ? d : 1));
+    int64_t mv = 0;
+    for (int64_t p = 0; p < m; p++) {
+        const int64_t r = idx[p];
+        if (r < 0 || r >= rows) continue;
+        rp[mv].row = r;
+        rp[mv].pos = p;
+        mv++;
+    }
+    qsort(rp, (size_t)mv, sizeof(rowpos_t), by_row_then_pos);
+    for (int64_t s = 0; s < mv;) {
+        int64_t e = s;
+        while (e < mv && rp[e].row == rp[s].row) e++;
+        const int32_t o = slot[rp[s].row];
+        if (o >= 0) {
+            for (int64_t c = 0; c < d; c++) sum[c] = 0.0f;
+            int first = 1;
+            for (int64_t a = s; a < e;) {
+                int64_t b = e;
+                if (chunk > 0) { int64_t lim = (a / chunk + 1) * chunk; if (lim < b) b = lim; }
+                for (int64_t c = 0; c < d; c++) part[c] = 0.0f;
+                for (int64_t q = a; q < b; q++) {
+                    const int64_t p = rp[q].pos;
+                    const float wv = w[p];
+                    for (int64_t c = 0; c < d; c++) part[c] = fmaf(wv, g[(p / k) * d + c], part[c]);
+                }
+                for (int64_t c = 0; c < d; c++) sum[c] = first ? part[c] : sum[c] + part[c];
+                first = 0;
+                a = b;
+            }
+            for (int64_t c = 0; c < d; c++) out[(int64_t)o * d + c] = 0.0f + sum[c];
+        }
+        s = e;
+    }
+    free(rp); free(sum); free(part);
+    return mv;
+}
+
 /* ------------------------------------------------------------------------------------ inference bag, q4 */
 static float half_to_f32(uint16_t hb) { _Float16 x; memcpy(&x, &hb, 2); return (float)x; }
 static uint16_t f32_to_half(float f) { _Float16 x = (_Float16)f; uint16_t b; memcpy(&b, &x, 2); return b; }

@@ -707,7 +707,7 @@ namespace tc {
 
 // Device address of g_noalloc_lists on the current device, looked up once per device (host code only sees a
 // host-side stand-in under that name, which must never reach a kernel).
-static int noalloc_scratch(uint32_t** out) {
+static int noalloc_scratch(cudaStream_t stream, uint32_t** out) {
     static std::mutex mu;
     static uint32_t* addr[64] = {};
     int dev = 0;
@@ -715,6 +715,13 @@ static int noalloc_scratch(uint32_t** out) {
     SMLM_CHECK_ARG(dev >= 0 && dev < 64, "score_select_noalloc: device index %d out of range", dev);
     std::lock_guard<std::mutex> lock(mu);
     if (addr[dev] == nullptr) {
+        // the lookup may load the module, which a capturing stream does not allow: say so instead of failing
+        // with a bare CUDA error
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        SMLM_CUDA(cudaStreamIsCapturing(stream, &cap));
+        SMLM_CHECK_ARG(cap == cudaStreamCaptureStatusNone,
+                       "score_select_noalloc: the first call on device %d must come before any stream capture "
+                       "(it looks up the static scratch's device address)", dev);
         void* p = nullptr;
         SMLM_CUDA(cudaGetSymbolAddress(&p, g_noalloc_lists));
         addr[dev] = static_cast<uint32_t*>(p);
@@ -730,10 +737,11 @@ extern "C" int smlm_score_select_noalloc(const void* q, const void* keys, int64_
                                          int64_t half, int64_t knn, void* scores, int64_t* indices, float* weights,
                                          int* status, void* stream) {
     SMLM_CHECK_ARG(n >= 0 && h > 0, "score_select_noalloc: bad n / heads");
-    SMLM_CHECK_ARG(n * h <= SMLM_NOALLOC_MAX_ROWS,
-                   "score_select_noalloc: n * heads = %lld exceeds the static scratch (SMLM_NOALLOC_MAX_ROWS = %d); "
-                   "split the call or use smlm_score_select with a workspace",
-                   (long long)(n * h), SMLM_NOALLOC_MAX_ROWS);
+    // compared without forming n * h, which could wrap for absurd n
+    SMLM_CHECK_ARG(n <= SMLM_NOALLOC_MAX_ROWS / h,
+                   "score_select_noalloc: n = %lld tokens x %lld heads exceeds the static scratch "
+                   "(SMLM_NOALLOC_MAX_ROWS = %d rows); split the call or use smlm_score_select with a workspace",
+                   (long long)n, (long long)h, SMLM_NOALLOC_MAX_ROWS);
     SMLM_CHECK_ARG(half == 64 || half == 128, "score_select_noalloc: the half dimension must be 64 or 128, got %lld",
                    (long long)half);
     SMLM_CHECK_ARG(knn >= 1 && knn <= 32, "score_select_noalloc: knn must be in [1, 32]");
@@ -744,8 +752,9 @@ extern "C" int smlm_score_select_noalloc(const void* q, const void* keys, int64_
     SMLM_CHECK_ARG(q && keys && scores && indices && weights, "score_select_noalloc: null pointer");
     SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(keys) % 16 == 0,
                    "score_select_noalloc: q and keys must be 16-byte aligned");
+    cudaStream_t st = as_stream(stream);
     uint32_t* lists = nullptr;
-    int rc = tc::noalloc_scratch(&lists);
+    int rc = tc::noalloc_scratch(st, &lists);
     if (rc != SMLM_OK) return rc;
     auto encode = tc::encode_fn();
     if (!encode) {
@@ -777,16 +786,19 @@ extern "C" int smlm_score_select_noalloc(const void* q, const void* keys, int64_
             return SMLM_ERR_CUDA;
         }
     }
-    cudaStream_t st = as_stream(stream);
     const int atoms = (int)(half / tc::ATOM);
     const size_t smem = tc::smem_bytes(atoms);
     SMLM_CUDA(cudaFuncSetAttribute(tc::score_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int64_t units = ((n + tc::BM - 1) / tc::BM) * h;
+    // key-range splits as the workspace entry point chooses them, as far as the static lists hold them (each
+    // split keeps its own lists per row): small calls, decoding among them, still spread over the SMs
+    const int splits = (int)std::max<int64_t>(
+        1, std::min<int64_t>(tc::score_splits(n, h, (nk + tc::BN - 1) / tc::BN), SMLM_NOALLOC_MAX_ROWS / (n * h)));
+    const int64_t units = ((n + tc::BM - 1) / tc::BM) * h * splits;
     const int grid = (int)std::min<int64_t>(units, sm_count());
-    // every (token, head) row of the lists is written by the scoring kernel before the pair kernel reads it,
-    // so the previous call's contents need no clearing
-    tc::Params P{(int)n, (int)h, (int)nk, atoms, 1, lists, nullptr, nullptr, status};
+    // every (token, head, split) row of the lists is written by the scoring kernel before the pair kernel reads
+    // it, so the previous call's contents need no clearing
+    tc::Params P{(int)n, (int)h, (int)nk, atoms, splits, lists, nullptr, nullptr, status};
     tc::score_topk_kernel<<<grid, tc::THREADS, smem, st>>>(tq, tk, P);
     SMLM_LAUNCHED("score_topk_kernel");
-    return launch_pk_pairs(lists, 2, n * h, (int)nk, (int)knn, scores, indices, weights, st);
+    return launch_pk_pairs(lists, 2 * splits, n * h, (int)nk, (int)knn, scores, indices, weights, st);
 }

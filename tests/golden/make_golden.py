@@ -1,7 +1,9 @@
 """Generates the golden fixtures in this directory by running the REFERENCE implementation
 (re133/sparse-memory-lm, imported read-only from a local checkout) on seeded inputs.
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [/path/to/reference] [fixture names ...]
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /path/to/reference [fixture names ...]
+
+(or with the reference checkout's path in SMLM_REFERENCE and "-" as the first argument)
 
 The Triton kernels of the reference run in Triton's CPU interpreter (TRITON_INTERPRET=1), its PyTorch path on the
 CPU. Each .npz holds the inputs and the reference's outputs; the tests pin the CPU oracle (oracle/) to them and
@@ -11,7 +13,11 @@ import os
 import sys
 
 os.environ["TRITON_INTERPRET"] = "1"            # before triton is imported
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) < 2:
+    sys.exit("usage: make_golden.py /path/to/reference|- [fixture names ...]")
+REF = os.environ.get("SMLM_REFERENCE", "") if sys.argv[1] == "-" else sys.argv[1]
+if not os.path.isdir(os.path.join(REF, "smlm")):
+    sys.exit(f"make_golden.py: no reference checkout (smlm/) at {REF!r}")
 sys.path.insert(0, REF)
 OUT = os.path.dirname(os.path.abspath(__file__))
 

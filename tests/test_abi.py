@@ -47,6 +47,11 @@ def test_host_side_argument_checks_return_invalid():
                                  None)
     assert rc == L.ERR_INVALID and b"flags" in lib.smlm_last_error()
     assert rc == L.ERR_INVALID
+    # the allocation-free scoring refuses calls beyond its static scratch without forming n * heads (2^62 x 4
+    # would wrap to 0)
+    for n in (1 << 62, 16384 // 4 + 1):
+        rc = lib.smlm_score_select_noalloc(s, s, n, 4, 1024, 128, 32, s, s, s, None, None)
+        assert rc == L.ERR_INVALID and b"SMLM_NOALLOC_MAX_ROWS" in lib.smlm_last_error()
     with pytest.raises(ValueError, match="knn"):
         L.check(lib.smlm_pk_select(s, s, L.BF16, 4, 2, 64, 0, s, s, s, None), "pk_select")
     # empty inputs are fine and launch nothing

@@ -27,7 +27,7 @@ def test_exchange_rooflines():
 
 def test_reference_arm_line(tmp_path):
     """bench.py --impl reference (the reference's PyTorch path on the host cores) prints one JSON line with the
-    keys the driver reads; here on a tiny sample."""
+    keys the driver reads and the --steps / --warmup it was given; here on a tiny sample."""
     import json
     import os
     import subprocess
@@ -42,7 +42,10 @@ def test_reference_arm_line(tmp_path):
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["metric"] == bench.METRIC and d["unit"] == "tokens/s"
     assert d["value"] > 0 and d["higher_is_better"] is True and d["n_gpus"] == 1
-    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    # the reference's own package when build() vendored it into baseline/_ref, else the restatement under oracle/
+    want = "reference" if os.path.isfile(os.path.join(root, "baseline", "_ref", "smlm", "pkm.py")) else "port"
+    assert d["cpu_baseline"]["kind"] == want and d["cpu_baseline"]["cores"] >= 1
+    assert d["steps"] == 1 and d["warmup"] == 1
     assert d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 

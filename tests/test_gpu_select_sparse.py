@@ -8,7 +8,7 @@ import torch
 
 from oracle import oracle as O
 from smlm_b200 import kernels as K
-from util import close
+from util import close, exact_contractions, within_bf16
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -54,29 +54,6 @@ def test_entries_carry_the_dense_gradients(dtype):
     # each sub-key's gradient sits on its first occurrence, bit for bit the dense value
     d1, d2 = scatter_entries(rows, ew, N, H, NK)
     assert torch.equal(d1, ds1) and torch.equal(d2, ds2)
-
-
-def exact_contractions(ds1, ds2, q, keys):
-    """float64 dq, dkeys and the magnitudes sum |term| of the dense contractions."""
-    half = keys.shape[-1]
-    d1, d2 = ds1.double(), ds2.double()
-    qd, kd = q.double(), keys.double()
-    dq = torch.cat([torch.einsum("nhk,hkd->nhd", d1, kd[:, 0]), torch.einsum("nhk,hkd->nhd", d2, kd[:, 1])], -1)
-    mq = torch.cat([torch.einsum("nhk,hkd->nhd", d1.abs(), kd[:, 0].abs()),
-                    torch.einsum("nhk,hkd->nhd", d2.abs(), kd[:, 1].abs())], -1)
-    dk = torch.stack([torch.einsum("nhk,nhd->hkd", d1, qd[..., :half]),
-                      torch.einsum("nhk,nhd->hkd", d2, qd[..., half:])], 1)
-    mk = torch.stack([torch.einsum("nhk,nhd->hkd", d1.abs(), qd[..., :half].abs()),
-                      torch.einsum("nhk,nhd->hkd", d2.abs(), qd[..., half:].abs())], 1)
-    return dq, mq, dk, mk
-
-
-def within_bf16(ours, exact, mag, what):
-    """|ours - exact| <= one bf16 rounding of the result + fp32 accumulation error (2^-16 of sum |term|)."""
-    err = (ours.double() - exact).abs()
-    bound = exact.abs() * 2.0 ** -8 + mag * 2.0 ** -16 + 1e-30
-    bad = err > bound
-    assert not bool(bad.any()), f"{what}: {int(bad.sum())} entries off, max err {float(err.max())}"
 
 
 @pytest.mark.parametrize("N,H,NK,half", [(1024, 4, 256, 64), (4096, 4, 4096, 128)])

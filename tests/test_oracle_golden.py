@@ -301,3 +301,22 @@ def test_engram_hash_oracle_and_multipliers_match_reference():
             assert np.array_equal(rows, g[f"v{v}_rows"])
     finally:
         E.canonical_ids = real
+
+
+def test_bag_rows_subset_equals_full_backward():
+    """oracle.bag_rows_subset (the sums of sampled rows only, for steps whose table does not fit host memory)
+    equals the rows bag_backward leaves in a zeroed accumulator, for every chunk schedule, with padding lookups
+    and hot rows whose runs cross chunks."""
+    rng = np.random.default_rng(3)
+    rows, d, n, k = 700, 24, 400, 48
+    idx = rng.integers(0, rows, (n, k))
+    idx[rng.random((n, k)) < 0.2] = 11                    # one hot row spanning many chunks
+    idx[0, :7] = -1
+    w = rng.standard_normal((n, k)).astype(np.float32)
+    g = rng.standard_normal((n, d)).astype(np.float32)
+    table = rng.standard_normal((rows, d)).astype(np.float32)
+    sample = np.array([11, 0, 699, 350, 5])
+    for chunk in (0, 64, 256):
+        acc = np.zeros((rows, d), np.float32)
+        O.bag_backward(g, idx, w, table, acc, np.zeros(rows, np.uint8), chunk=chunk)
+        assert np.array_equal(O.bag_rows_subset(g, idx, w, rows, sample, chunk=chunk), acc[sample])

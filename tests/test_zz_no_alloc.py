@@ -31,17 +31,28 @@ def noalloc(q, keys, knn):
 
 def test_noalloc_equals_workspace_entry_point_on_two_calls():
     for call, (N, H, NK, knn) in enumerate([(3000, 4, 1024, 32), (777, 2, 512, 8)]):
-        gen = torch.Generator().manual_seed(100 + call)
-        q = torch.randn(N, H, 256, generator=gen).bfloat16().to(DEV)
-        keys = (torch.randn(H, 2, NK, 128, generator=gen) * 128 ** -0.5).bfloat16().to(DEV)
-        rc, sc, idx, w, status = noalloc(q, keys, knn)
-        assert rc == L.OK, L.lib().smlm_last_error()
-        torch.cuda.synchronize()
-        assert int(status.item()) == 0
-        rsc, ridx, rw = K.score_select(q, keys, knn)
-        assert torch.equal(idx, ridx)
-        assert torch.equal(sc, rsc)
-        torch.testing.assert_close(w, rw, rtol=0, atol=1e-6)
+        check_against_workspace_entry_point(N, H, NK, knn, 100 + call)
+
+
+def test_noalloc_at_its_row_limit_and_for_one_token():
+    """n * heads exactly SMLM_NOALLOC_MAX_ROWS (the last rows of the static array written and read, one key-range
+    split), then one token (a decoding call: the key range split over many CTAs inside the same array)."""
+    check_against_workspace_entry_point(MAX_ROWS // 4, 4, 4096, 32, 7)
+    check_against_workspace_entry_point(1, 4, 4096, 32, 8)
+
+
+def check_against_workspace_entry_point(N, H, NK, knn, seed):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(N, H, 256, generator=gen).bfloat16().to(DEV)
+    keys = (torch.randn(H, 2, NK, 128, generator=gen) * 128 ** -0.5).bfloat16().to(DEV)
+    rc, sc, idx, w, status = noalloc(q, keys, knn)
+    assert rc == L.OK, L.lib().smlm_last_error()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    rsc, ridx, rw = K.score_select(q, keys, knn)
+    assert torch.equal(idx, ridx)
+    assert torch.equal(sc, rsc)
+    torch.testing.assert_close(w, rw, rtol=0, atol=1e-6)
 
 
 def test_noalloc_rejects_calls_beyond_its_scratch():

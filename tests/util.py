@@ -59,3 +59,26 @@ def tie_free_rows(s1, s2, knn, bf16):
     h1 = (s1.view(N * H, NK) == a1.reshape(N * H, knn)[:, -1:]).sum(-1) > 1
     h2 = (s2.view(N * H, NK) == a2.reshape(N * H, knn)[:, -1:]).sum(-1) > 1
     return ((n_eq_total == n_eq_sel) & ~h1 & ~h2).numpy()
+
+
+def exact_contractions(ds1, ds2, q, keys):
+    """float64 dq, dkeys and the magnitudes sum |term| of the dense contractions."""
+    half = keys.shape[-1]
+    d1, d2 = ds1.double(), ds2.double()
+    qd, kd = q.double(), keys.double()
+    dq = torch.cat([torch.einsum("nhk,hkd->nhd", d1, kd[:, 0]), torch.einsum("nhk,hkd->nhd", d2, kd[:, 1])], -1)
+    mq = torch.cat([torch.einsum("nhk,hkd->nhd", d1.abs(), kd[:, 0].abs()),
+                    torch.einsum("nhk,hkd->nhd", d2.abs(), kd[:, 1].abs())], -1)
+    dk = torch.stack([torch.einsum("nhk,nhd->hkd", d1, qd[..., :half]),
+                      torch.einsum("nhk,nhd->hkd", d2, qd[..., half:])], 1)
+    mk = torch.stack([torch.einsum("nhk,nhd->hkd", d1.abs(), qd[..., :half].abs()),
+                      torch.einsum("nhk,nhd->hkd", d2.abs(), qd[..., half:].abs())], 1)
+    return dq, mq, dk, mk
+
+
+def within_bf16(ours, exact, mag, what):
+    """|ours - exact| <= one bf16 rounding of the result + fp32 accumulation error (2^-16 of sum |term|)."""
+    err = (ours.double() - exact).abs()
+    bound = exact.abs() * 2.0 ** -8 + mag * 2.0 ** -16 + 1e-30
+    bad = err > bound
+    assert not bool(bad.any()), f"{what}: {int(bad.sum())} entries off, max err {float(err.max())}"

@@ -26,8 +26,10 @@ NCCL all-gather, the replicated parameters' gradients through an NCCL all-reduce
 the exchange calls' NVLink and HBM bytes against the measured peer-copy and HBM bandwidths.
 
 The default run also measures the B-16M inference token loop (`inference`: prefill and greedy decode of the
-B-16M model, per-token lookup latency). --case configs times BASELINE configs 1-3 as single layers (fwd / bwd /
-opt separately); --case scoring and --case inference run one part alone; --case engram times the Engram n-gram memory module.
+B-16M model, per-token lookup latency). --case configs times BASELINE configs 1-4 as single layers (fwd / bwd /
+opt separately; config 2 also with the forward reading a bf16 copy of the fp32 table, config 4 with its inputs from a
+uniform + Zipf(1.1) token mix); --case model times BASELINE config 2 as stated, the B-1M model's training step;
+--case scoring and --case inference run one part alone; --case engram times the Engram n-gram memory module.
 """
 import argparse
 import json
@@ -66,12 +68,14 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows-per-half", type=int, default=1024)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
-    ap.add_argument("--case", choices=["layer", "scoring", "inference", "configs", "engram"], default="layer",
+    ap.add_argument("--case", choices=["layer", "scoring", "inference", "configs", "engram", "model"],
+                    default="layer",
                     help="scoring: only the fused sub-key scoring + selection of the workload's layer (a small "
                          "standalone case for profiler captures; prints its time per call); inference: only the "
-                         "B-16M prefill / decode measurement; configs: BASELINE configs 1-3 as single layers "
-                         "with fwd / bwd / opt timed separately; engram: the reference's default Engram module "
-                         "(hash, one-lookup bags, backward, lazy Adam) per step")
+                         "B-16M prefill / decode measurement; configs: BASELINE configs 1-4 as single layers "
+                         "with fwd / bwd / opt timed separately (config 4 with a uniform + Zipf token mix); "
+                         "model: BASELINE config 2, the B-1M model's training step; engram: the reference's "
+                         "default Engram module (hash, one-lookup bags, backward, lazy Adam) per step")
     ap.add_argument("--no-inference", action="store_true", help="leave the inference measurement out of the line")
     ap.add_argument("--eager", action="store_true",
                     help="time the step as eager calls (default on one GPU: the step captured as one CUDA graph)")
@@ -454,30 +458,57 @@ def run_cuda(args, world, rank, local):
     return line
 
 
-# -------------------------------------------------------------------------------------- configs 1 - 3
-# (name, sub-keys per half, tokens per step, bf16 autocast, BatchNorm query + swilu, table optimizer)
+# -------------------------------------------------------------------------------------- configs 1 - 4
+# name, sub-keys per half, tokens per step, bf16 autocast, BatchNorm query + swilu, table optimizer, layer input
+# ("gauss": x ~ N(0, 1); "zipf": x = a random N(0, 1) embedding of token ids drawn half uniform, half Zipf(1.1)
+# over a 50,304-id vocabulary, so that frequent tokens make hot rows), bf16 value copy read by the forward
 LAYER_CONFIGS = [
-    ("config1-layer-65k-fp32", 256, 2048, False, False, "adam"),
-    ("config2-b1m-layer", 1024, 32768, True, True, "adam"),
-    ("config2-b1m-layer-bf16-moments", 1024, 32768, True, True, "adam-bf16"),
-    ("config3-b4m-layer-rowrms", 2048, 65536, True, True, "rowrms"),
+    ("config1-layer-65k-fp32", 256, 2048, False, False, "adam", "gauss", False),
+    ("config2-b1m-layer", 1024, 32768, True, True, "adam", "gauss", False),
+    ("config2-b1m-layer-bf16-values", 1024, 32768, True, True, "adam", "gauss", True),
+    ("config2-b1m-layer-bf16-moments", 1024, 32768, True, True, "adam-bf16", "gauss", False),
+    ("config3-b4m-layer-rowrms", 2048, 65536, True, True, "rowrms", "gauss", False),
+    ("config4-b16m-layer-zipf", 4096, 32768, True, False, "adam", "zipf", False),
+    ("config4-b16m-layer-zipf-bf16-values", 4096, 32768, True, False, "adam", "zipf", True),
 ]
+ZIPF_VOCAB, ZIPF_S = 50304, 1.1
+
+
+def zipf_mix_tokens(n, gen, device):
+    """n token ids: half uniform over ZIPF_VOCAB, half Zipf(ZIPF_S) over the ranks (id = rank - 1), shuffled."""
+    rank = torch.arange(1, ZIPF_VOCAB + 1, dtype=torch.float64, device=device)
+    p = rank ** -ZIPF_S
+    zipf = torch.multinomial((p / p.sum()).float(), n - n // 2, replacement=True, generator=gen)
+    uni = torch.randint(0, ZIPF_VOCAB, (n // 2,), device=device, generator=gen)
+    mix = torch.cat([uni, zipf])
+    return mix[torch.randperm(n, device=device, generator=gen)]
+
+
+def layer_inputs(kind, N, gen, device):
+    if kind == "gauss":
+        return torch.randn(N, D_MODEL, device=device, generator=gen)
+    emb = getattr(layer_inputs, "emb", None)
+    if emb is None or emb.device != device:
+        emb = layer_inputs.emb = torch.randn(ZIPF_VOCAB, D_MODEL, device=device, generator=gen)
+    return emb[zipf_mix_tokens(N, gen, device)]
 
 
 def run_configs(args):
-    """BASELINE configs 1-3 as single PKM layers on one GPU, each phase device-timed: config 1 (65,536 rows,
+    """BASELINE configs 1-4 as single PKM layers on one GPU, each phase device-timed: config 1 (65,536 rows,
     2,048 tokens, fp32 without autocast, no BatchNorm / swilu, LazyRowAdam), config 2 (the B-1M model's layer:
-    1,048,576 rows, 32 x 1024 tokens, bf16 autocast, BatchNorm query and swilu, LazyRowAdam with fp32 and with bf16
-    moments), config 3 (the B-4M layer: 4,194,304 rows, 64 x 1024 tokens, the row-wise rowrms optimizer). Seeded
-    synthetic inputs x, upstream gradient ~ N(0, 1). fwd = the layer's forward; bwd = backward + value / dense
-    clipping; opt = the table optimizer + fused AdamW on the dense parameters (with deferred row sums the table's
-    row sums run in opt, not in bwd)."""
+    1,048,576 rows, 32 x 1024 tokens, bf16 autocast, BatchNorm query and swilu, LazyRowAdam with fp32 moments, with
+    the forward reading a bf16 copy of the fp32 master (the config's "values bf16 with fp32 master"), and with bf16
+    moments), config 3 (the B-4M layer: 4,194,304 rows, 64 x 1024 tokens, the row-wise rowrms optimizer), config 4
+    (the B-16M layer, 32 x 1024 tokens per GPU, its inputs embeddings of a uniform + Zipf(1.1) token mix: hot
+    rows). Seeded synthetic inputs, upstream gradient ~ N(0, 1). fwd = the layer's forward; bwd = backward +
+    value / dense clipping; opt = the table optimizer + fused AdamW on the dense parameters (with deferred row sums
+    the table's row sums run in opt, not in bwd)."""
     from smlm_b200.pkm import ProductKeyMemory
     from smlm_b200.row_optim import RowWiseOptimizer
     from smlm_b200.sparse_values import LazyRowAdam, OptimizerSet, clip_row_sparse, row_store
     dev = torch.device("cuda", 0)
     out = []
-    for name, n_keys, N, autocast, bn, kind in LAYER_CONFIGS:
+    for name, n_keys, N, autocast, bn, kind, inputs, copy in LAYER_CONFIGS:
         torch.manual_seed(0)
         with torch.device(dev):
             mem = ProductKeyMemory(D_MODEL, D_MODEL, n_keys=n_keys, heads=HEADS, knn=KNN, k_dim=K_DIM,
@@ -492,10 +523,11 @@ def run_configs(args):
             topt = RowWiseOptimizer([table], lr=1e-3, kind="rowrms", beta2=0.98)
         else:
             topt = LazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98), eps=1e-8,
-                               state_dtype="bf16" if kind == "adam-bf16" else "fp32")
+                               state_dtype="bf16" if kind == "adam-bf16" else "fp32",
+                               value_copy_dtype=torch.bfloat16 if copy else None)
         opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True), topt)
         gen = torch.Generator(device=dev).manual_seed(1)
-        xs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(2)]
+        xs = [layer_inputs(inputs, N, gen, dev) for _ in range(2)]
         gs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(2)]
         ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
         uniq = []
@@ -525,15 +557,119 @@ def run_configs(args):
             step(i, ev[i])
         torch.cuda.synchronize()
         ph = [sum(e[j].elapsed_time(e[j + 1]) for e in ev) / args.steps for j in range(3)]
-        out.append({"config": name, "rows": n_keys ** 2, "tokens": N, "autocast_bf16": autocast,
-                    "query_norm_swilu": bn, "optimizer": kind, "fwd_ms": round(ph[0], 4), "bwd_ms": round(ph[1], 4),
-                    "opt_ms": round(ph[2], 4), "tokens_per_s": round(N / (sum(ph) / 1e3), 1),
-                    "unique_rows_per_step": round(sum(uniq[1:]) / max(1, len(uniq) - 1))})
+        entry = {"config": name, "rows": n_keys ** 2, "tokens": N, "autocast_bf16": autocast,
+                 "query_norm_swilu": bn, "optimizer": kind, "inputs": inputs,
+                 "values_read": "bf16 copy of the fp32 master" if copy else "fp32 table",
+                 "fwd_ms": round(ph[0], 4), "bwd_ms": round(ph[1], 4), "opt_ms": round(ph[2], 4),
+                 "tokens_per_s": round(N / (sum(ph) / 1e3), 1),
+                 "unique_rows_per_step": round(sum(uniq[1:]) / max(1, len(uniq) - 1))}
+        if inputs == "zipf":
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                mem.record = True
+                mem(xs[0])
+                mem.record = False
+            _, counts = torch.unique(mem.last_indices, return_counts=True)
+            entry["max_lookups_per_row"] = int(counts.max())
+            entry["lookups_on_rows_read_over_64_times"] = round(float(counts[counts > 64].sum() / counts.sum()), 4)
+        out.append(entry)
         del mem, opt, topt, xs, gs
         import gc
         gc.collect()
         torch.cuda.empty_cache()
     return out
+
+
+# ------------------------------------------------------------------------------------------- config 2 model
+def run_model_case(args):
+    """BASELINE configs[1], the B-1M training step on one GPU: a 6-layer model (d_model 384, 6 attention heads,
+    SwiGLU 1024, vocab 32,768 with the embedding tied to the LM head, RMSNorm, RoPE), the product-key memory in
+    place of the feed-forward of layer 3 (0-based: the fourth block; 1024 sub-keys per half, 1,048,576 rows x 384,
+    BatchNorm query and swilu), values bf16 with an fp32 master (the forward reads the bf16 copy), 32 x 1024 tokens
+    uniform over the vocabulary per step, next-token cross entropy, bf16 autocast, clipping as the reference's
+    training loop does (values and the rest separately to 1.0), LazyRowAdam on the table and fused AdamW (weight
+    decay 0.1) on the rest. Random-init weights, seeded synthetic tokens. Timed as the whole step replayed as one
+    CUDA graph and as eager calls with fwd / bwd / opt separated (CUDA events)."""
+    from smlm_b200.graph_step import GraphedStep
+    from smlm_b200.model import ModelConfig, Transformer
+    from smlm_b200.optim import build_optimizer, clip_grads
+    from smlm_b200.sparse_values import row_sparse_tables, row_store
+    dev = torch.device("cuda", 0)
+    B, T, vocab = 32, 1024, 32768
+    cfg = ModelConfig(vocab_size=vocab, d_model=D_MODEL, n_layers=6, n_heads=6, ffn_hidden=1024, max_seq_len=T,
+                      mem_layers=[3], mem_n_keys=1024, mem_value_grad="row_sparse")
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = Transformer(cfg)
+    opt = build_optimizer(model, lr=1e-3, value_lr=1e-3, weight_decay=0.1, betas=(0.9, 0.95),
+                          value_copy_dtype=torch.bfloat16, capturable=True)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    seqs = [torch.randint(0, vocab, (B, T + 1), device=dev, generator=gen) for _ in range(4)]
+    batches = [(s[:, :-1].contiguous(), s[:, 1:].contiguous()) for s in seqs]
+
+    def forward(ids, tgt):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            _, loss = model(ids, targets=tgt)
+        return loss
+
+    def finish(loss):
+        loss.backward()
+        clip_grads(model, 1.0)
+
+    def step(ids, tgt):
+        loss = forward(ids, tgt)
+        finish(loss)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss.detach()
+
+    # captured first (autograd binds each parameter's gradient accumulation to the stream of its first backward)
+    gstep = GraphedStep(step, list(batches[0]), opt.opts, warmup=max(3, args.warmup))
+    for i in range(args.warmup):
+        gstep(*batches[i % 4])
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(0) as clocks:
+        s.record()
+        for i in range(args.steps):
+            gstep(*batches[i % 4])
+        e.record()
+        torch.cuda.synchronize()
+    graph_ms = s.elapsed_time(e) / args.steps
+    loss_now = float(gstep.outputs)
+    # eager phases (the optimizers keep stepping: same work per step); LazyRowAdam(capturable=True) runs its
+    # eager steps through the same fused kernel
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    table = row_sparse_tables(model)[0]
+    uniq = []
+    for i in range(args.steps + 1):
+        e4 = ev[i - 1] if i else None
+        ids, tgt = batches[i % 4]
+        if e4:
+            e4[0].record()
+        loss = forward(ids, tgt)
+        if e4:
+            e4[1].record()
+        finish(loss)
+        if e4:
+            e4[2].record()
+        else:
+            uniq.append(row_store(table).touched_rows())
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        if e4:
+            e4[3].record()
+    torch.cuda.synchronize()
+    ph = [sum(x[j].elapsed_time(x[j + 1]) for x in ev) / args.steps for j in range(3)]
+    return {"case": "model", "config": "config2-b1m-model",
+            "model": "6 layers, d_model 384, 6 heads, SwiGLU 1024, vocab 32768 tied, PKM (1024^2 rows x 384, "
+                     "BatchNorm query, swilu) in place of the FFN of layer 3 (0-based)",
+            "values": "bf16 copy read by the forward, fp32 master and fp32 Adam moments (LazyRowAdam)",
+            "tokens_per_step": B * T, "steps": args.steps, "warmup": args.warmup,
+            "graph_ms_per_step": round(graph_ms, 4), "tokens_per_s": round(B * T / (graph_ms / 1e3), 1),
+            "eager": {"fwd_ms": round(ph[0], 4), "bwd_ms": round(ph[1], 4), "opt_ms": round(ph[2], 4),
+                      "tokens_per_s": round(B * T / (sum(ph) / 1e3), 1)},
+            "loss_after_warmup_and_timed_steps": round(loss_now, 4),
+            "unique_rows_per_step": uniq[0] if uniq else None, "clocks": clocks.summary()}
 
 
 # ------------------------------------------------------------------------------------------------ engram
@@ -813,6 +949,9 @@ def main():
         return
     if args.case == "engram":
         print(json.dumps(run_engram(args)), flush=True)
+        return
+    if args.case == "model":
+        print(json.dumps(run_model_case(args)), flush=True)
         return
     if args.case == "inference":
         print(json.dumps({"case": "inference", **run_inference(args, 0)}), flush=True)

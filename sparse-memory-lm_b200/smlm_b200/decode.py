@@ -49,10 +49,8 @@ class GraphDecoder:
         self._key = None
 
     def _set_pos(self, pos):
-        shared = {}                          # per-step values the layers share (rotary tables, mask)
         for c in self.caches:
             c["pos"] = pos
-            c["step"] = shared
 
     @torch.no_grad()
     def prefill(self, ids):

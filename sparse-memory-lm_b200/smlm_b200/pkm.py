@@ -21,10 +21,37 @@ from torch import nn
 
 from . import kernels as K
 from .sharded import RowShard, sharded_embedding_bag
-from .sparse_values import row_sparse_embedding_bag
+from .sparse_values import read_table, row_sparse_embedding_bag
 
 IMPLS = ("cuda", "triton", "torch")
 MAX_ROW_WIDTH = 512        # SMLM_MAX_ROW_WIDTH: widest value row of the row-sparse backward
+
+
+class _DecodeGraph:
+    """A captured forward with a static input and output. Warmed up twice on a side stream before capture (the
+    autocast cache off, so no cast is captured from a stale cache)."""
+
+    def __init__(self, fn, x, key):
+        self.key = key
+        self.x = x.clone()
+        dtype = key[2]
+        mode = (torch.autocast("cuda", dtype=dtype, cache_enabled=False) if dtype is not None
+                else torch.autocast("cuda", enabled=False))
+        here = torch.cuda.current_stream()
+        side = torch.cuda.Stream()
+        side.wait_stream(here)
+        with torch.cuda.stream(side), mode:
+            fn(self.x)
+            fn(self.x)
+        here.wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), mode:
+            self.out = fn(self.x)
+
+    def run(self, x):
+        self.x.copy_(x)
+        self.graph.replay()
+        return self.out.clone()
 
 
 class ProductKeyMemory(nn.Module):
@@ -166,30 +193,17 @@ class ProductKeyMemory(nn.Module):
         return self._forward(x).view(*shape[:-1], self.d_out)
 
     def _graph_forward(self, x):
-        """One-token decoding without grad: replays a CUDA graph of _forward captured for this shape (same
-        kernels as the eager path, so bit-identical; it removes the per-launch host overhead)."""
+        """One-token no-grad forward as a CUDA-graph replay (reference: pkm.py:159-184): the graph of _forward
+        for this input's shape, dtype, autocast state and inference table is captured on first use (and again
+        when any of them changes), then replayed with the token copied into its static input. Same kernels as
+        the eager path, so the same bits, without the per-launch host work."""
         ac = torch.is_autocast_enabled("cuda")
-        key = (tuple(x.shape), x.dtype, ac, torch.get_autocast_dtype("cuda") if ac else None,
+        key = (tuple(x.shape), x.dtype, torch.get_autocast_dtype("cuda") if ac else None,
                id(getattr(self.values, "infer_table", None)))
-        g = getattr(self, "_graph", None)
-        if g is None or g[0] != key:
-            static_x = x.clone()
-            ctx = (torch.autocast("cuda", dtype=key[3], cache_enabled=False) if ac
-                   else torch.autocast("cuda", enabled=False))
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s), ctx:
-                for _ in range(2):
-                    self._forward(static_x)
-            torch.cuda.current_stream().wait_stream(s)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph), ctx:
-                static_out = self._forward(static_x)
-            g = self._graph = (key, graph, static_x, static_out)
-        _, graph, static_x, static_out = g
-        static_x.copy_(x)
-        graph.replay()
-        return static_out.clone()
+        dg = getattr(self, "_graph", None)
+        if dg is None or dg.key != key:
+            dg = self._graph = _DecodeGraph(self._forward, x, key)
+        return dg.run(x)
 
     def _select(self, q, autocast_bf16):
         """q (N, heads, k_dim) -> scores, indices, weights (N, heads, knn). Under bf16 autocast the fused
@@ -223,7 +237,7 @@ class ProductKeyMemory(nn.Module):
             # inference: value bag on the inference table (fp32 / bf16 / q4) with the swilu product and the
             # bf16 cast fused (reference: pkm.py:213-224)
             pre = self.swilu_proj(x)
-            t = getattr(self.values, "infer_table", None) or (self.values.weight, None)
+            t = getattr(self.values, "infer_table", None) or (read_table(self.values.weight), None)
             K_ = self.heads * self.knn
             out = K.bag_infer(indices.view(N, K_), weights.view(N, K_), t[0], t[1], pre=pre, out_bf16=True)
             return self.value_proj(out)

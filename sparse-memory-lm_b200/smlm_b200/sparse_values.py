@@ -131,43 +131,61 @@ def row_store(table):
     return st
 
 
+def read_table(table):
+    """The tensor a value bag reads for `table`: its bf16 copy when LazyRowAdam(value_copy_dtype=bf16) keeps one
+    (half the gather bytes; the fp32 table stays the master that the optimizer updates), else the table itself.
+    The optimizer's kernels refresh the copy's rows as they update them; a change made to the table through
+    torch (load_state_dict, an in-place op) shows in the table's version counter, and then the whole copy is
+    refreshed here before it is read."""
+    copy = getattr(table, "value_copy", None)
+    if copy is None or copy.shape != table.shape or copy.device != table.device:
+        return table
+    if getattr(table, "value_copy_version", None) != table._version:
+        with torch.no_grad():
+            copy.copy_(table)
+        table.value_copy_version = table._version
+    return copy
+
+
 class _RowSparseBag(torch.autograd.Function):
     @staticmethod
     def forward(ctx, weights, indices, table, store, impl="cuda"):
         n, j = indices.shape
         w = weights.reshape(n, j).to(table.dtype)
-        out = K.bag_forward(indices, w, table, out_dtype=table.dtype)
+        src = read_table(table)
+        out = K.bag_forward(indices, w, src, out_dtype=table.dtype)
         ctx.save_for_backward(w, indices)
-        ctx.table, ctx.store, ctx.wshape, ctx.wdtype = table, store, weights.shape, weights.dtype
+        ctx.table, ctx.src, ctx.store, ctx.wshape, ctx.wdtype = table, src, store, weights.shape, weights.dtype
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        table, store = ctx.table, ctx.store
+        table, src, store = ctx.table, ctx.src, ctx.store
         w, indices = ctx.saved_tensors
         # the per-sample-weight gradient only when the weights need one (constant weights, e.g. the one-lookup
         # bags of an Engram table, skip its kernel; the row sums are the same either way)
         want_gw = ctx.needs_input_grad[0]
         gw = None
+        # the weight gradient reads the rows the forward read (the bf16 copy when there is one)
         if store is None:
             if want_gw:
-                gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
+                gw = K.bag_backward_rows(grad_out, indices, w, src, None, None)
         elif store.can_defer(table):
             # the first backward into an empty store: its row sums go straight into the optimizer step. The weight
             # gradient (which the scoring backward needs next) comes first; the sort and the norm pass (which only
             # the clip and the step need) run on a side stream meanwhile
             if want_gw:
-                gw = K.bag_backward_rows(grad_out, indices, w, table, None, None)
+                gw = K.bag_backward_rows(grad_out, indices, w, src, None, None)
             _, store.pending = K.bag_backward_deferred(grad_out, indices, w, table, store._touched, store._sqnorm,
                                                        want_gw=False, overlap=True)
         else:
             store.materialize()
-            gw = K.bag_backward_rows(grad_out, indices, w, table, store._acc, store._touched,
+            gw = K.bag_backward_rows(grad_out, indices, w, src, store._acc, store._touched,
                                      row_sqnorm=store._sqnorm if store.clean else None,
                                      first_touch_writes=store.clean, want_gw=want_gw)
             store.live = True
         # drop the RowStore reference so that `del table.row_store` after training frees the accumulator
-        ctx.table = ctx.store = None
+        ctx.table = ctx.src = ctx.store = None
         return (gw.view(ctx.wshape).to(ctx.wdtype) if gw is not None else None), None, None, None, None
 
 
@@ -176,7 +194,7 @@ def row_sparse_embedding_bag(indices, weights, table, impl="cuda"):
     (reference: sparse_values.py:110-123)."""
     _check_impl(impl)
     if not torch.is_grad_enabled():
-        return K.bag_forward(indices, weights.to(table.dtype), table, out_dtype=table.dtype)
+        return K.bag_forward(indices, weights.to(table.dtype), read_table(table), out_dtype=table.dtype)
     if not table.requires_grad:
         # frozen table: gradient for the weights only, no row accumulator
         return _RowSparseBag.apply(weights, indices, table, None, impl)
@@ -232,8 +250,8 @@ class LazyRowAdam(torch.optim.Optimizer):
     fp32 scale per row each (exp_avg_scale, exp_avg_sq_scale); the update runs in fp32 on the decoded moments.
 
     value_copy_dtype=torch.bfloat16 keeps a bf16 copy of each table (`table.value_copy`) that the step refreshes
-    for the updated rows: the forward can read the copy (half the gather bytes) while the fp32 table stays the
-    master.
+    for the updated rows: the value bag and its weight gradient read the copy (half the gather bytes; read_table)
+    while the fp32 table stays the master that the step updates ("values bf16 with fp32 master").
 
     capturable=True (no counterpart in the reference) lets a training step that ends in this optimizer be captured
     in a CUDA graph (smlm_b200.graph_step): the step's bias-correction scalars are read from a small device buffer,
@@ -264,8 +282,11 @@ class LazyRowAdam(torch.optim.Optimizer):
         self.capturable = capturable
         self._scal = {}                 # capturable: per table, its step scalars on the device, (6,) fp32
         if value_copy_dtype is not None:
+            if value_copy_dtype != torch.bfloat16:
+                raise ValueError(f"value_copy_dtype must be torch.bfloat16, got {value_copy_dtype}")
             for p in params:
                 p.value_copy = p.detach().to(value_copy_dtype)
+                p.value_copy_version = p._version
 
     def _state(self, p):
         state = self.state[p]

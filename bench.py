@@ -271,9 +271,9 @@ def run_cuda(args, world, rank, local):
     from smlm_b200 import _lib as L
     dev = torch.device("cuda", local)
     N, n_keys = args.tokens, args.rows_per_half
-    # one GPU: the step is also captured as one CUDA graph (smlm_b200.graph_step), which takes the host out of the
-    # step (the headline figures); the row-sharded exchange keeps host-side epochs, so N > 1 stays eager
-    graphed = world == 1 and not args.eager
+    # the step is captured as one CUDA graph (smlm_b200.graph_step), which takes the host out of the step (the
+    # headline figures); on N > 1 GPUs the graph holds the peer exchange (device-side epochs) and the NCCL calls
+    graphed = not args.eager
     mem, opt = build_layer(n_keys, dev, world, capturable=graphed)
     rows = mem.values.weight.shape[0]           # this GPU's rows (all of them on one GPU)
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
@@ -455,6 +455,13 @@ def run_cuda(args, world, rank, local):
         except (KeyError, TypeError, ValueError, ZeroDivisionError) as exc:
             # a report of the measured calls: its failure is shown in the line, the measurement stands
             line["exchange"] = {"error": repr(exc)}
+    if graphed:
+        del gstep, step_fn                  # a graph holding NCCL calls is released before the process group
+    if world > 1:
+        torch.cuda.synchronize(dev)
+        x = getattr(mem.values.weight, "peer_exchange", None)
+        if x is not None:
+            x.close()
     return line
 
 
@@ -751,18 +758,20 @@ def _event_ms(fn, reps):
 
 
 @torch.no_grad()
-def run_inference(args, local):
-    """The B-16M inference token loop (the metric's "B-16M decode tok/s"): the reference's B-16M model (12 layers,
-    d_model 384, 6 attention heads, SwiGLU 1024, vocab 50304, product-key memories in layers 2, 6 and 10 sharing
-    one 4096^2 = 16,777,216 x 384 fp32 value table, BatchNorm queries, swilu), random-init weights, eval mode,
-    bf16 autocast, through smlm_b200.model.Transformer. Measured like the reference's inference_benchmark
-    (smlm/train.py:283-315): prefill of 2048 uniform random token ids at batch 1 and 64 (full forward, logits of
-    every position), then 256 greedy decode steps from that prefill: decode_b* through smlm_b200.decode.GraphDecoder
-    (static KV cache, the whole step one CUDA graph), decode_b*_eager through the reference's loop (growing KV
-    cache, one-token memory layers replaying their own graphs). Plus the per-token product-key lookup latency: one memory layer
-    on one token (query projection, fused scoring + top-k + softmax, value bag with the swilu product) and the
-    lookup alone (fused scoring + selection, value bag), each as a CUDA-graph replay. All device-timed with CUDA
-    events."""
+def run_inference(args, local, world=1):
+    """The B-16M inference token loop (the metric's "B-16M decode tok/s"): the reference's B-16M
+    model (12 layers, d_model 384, 6 attention heads, SwiGLU 1024, vocab 50304, product-key memories in layers 2,
+    6 and 10 sharing one 4096^2 = 16,777,216 x 384 fp32 value table, BatchNorm queries, swilu), random-init
+    weights, eval mode, bf16 autocast, through smlm_b200.model.Transformer. Measured like the reference's
+    inference_benchmark (smlm/train.py:283-315): prefill of 2048 uniform random token ids at batch 1 and 64 (full
+    forward, logits of every position), then 256 greedy decode steps from that prefill: decode_b* through
+    smlm_b200.decode.GraphDecoder (static KV cache, the whole step one CUDA graph), decode_b*_eager (one GPU only)
+    through the reference's loop (growing KV cache, one-token memory layers replaying their own graphs). Plus the
+    per-token product-key lookup latency: one memory layer on one token (query projection, fused scoring + top-k
+    + softmax, value bag with the swilu product) and, on one GPU, the lookup alone (fused scoring + selection,
+    value bag), each as a CUDA-graph replay. On N > 1 GPUs the table is row-sharded over them (peer exchange, the
+    swilu product fused into its sum), every rank runs its own prompts (batch b per rank) and the tokens/s are
+    whole-job figures (N x b sequences) over the slowest rank's time. All device-timed with CUDA events."""
     from smlm_b200 import kernels as K
     from smlm_b200.decode import GraphDecoder
     from smlm_b200.model import ModelConfig, Transformer
@@ -771,42 +780,54 @@ def run_inference(args, local):
     cfg = ModelConfig(mem_layers=[2, 6, 10], mem_n_keys=args.rows_per_half, mem_share_values=True,
                       mem_value_grad="row_sparse", max_seq_len=prompt + new)
     torch.manual_seed(0)
+    group = torch.distributed.group.WORLD if world > 1 else None
     with torch.device(dev):
-        model = Transformer(cfg)
+        model = Transformer(cfg, shard_group=group)
+    if world > 1:
+        from smlm_b200.sharded import broadcast_replicated
+        broadcast_replicated(model, group)
     model.eval()
     model.set_memory_decode_graphs(True)
-    gen = torch.Generator(device=dev).manual_seed(7)
+    rank = torch.distributed.get_rank() if world > 1 else 0
+    gen = torch.Generator(device=dev).manual_seed(7 + rank)
     res = {"model": "B-16M (12 layers, PKM in layers 2/6/10 sharing one table)" if args.rows_per_half == 4096
            else f"B ({args.rows_per_half ** 2} rows)", "rows": args.rows_per_half ** 2, "prompt_len": prompt,
-           "new_tokens": new, "dtype": "bf16 autocast, fp32 value table", "data": "synthetic uniform token ids"}
+           "new_tokens": new, "dtype": "bf16 autocast, fp32 value table", "data": "synthetic uniform token ids",
+           "gpus": world, "table": "one GPU" if world == 1 else f"row-sharded over {world} GPUs (peer exchange)",
+           "batch_is_per_gpu": True}
+
+    def timed(fn, reps):
+        return max_over_ranks(_event_ms(fn, reps), world)
+
     with torch.autocast("cuda", dtype=torch.bfloat16):
         for b in (1, 64):
             ids = torch.randint(0, cfg.vocab_size, (b, prompt), device=dev, generator=gen)
             model(ids)                                                     # warm-up
             reps = 5 if b == 1 else 2
-            ms = _event_ms(lambda: model(ids), reps) / reps
-            res[f"prefill_b{b}_tok_s"] = round(b * prompt / (ms / 1e3), 1)
+            ms = timed(lambda: model(ids), reps) / reps
+            res[f"prefill_b{b}_tok_s"] = round(world * b * prompt / (ms / 1e3), 1)
             res[f"prefill_b{b}_ms"] = round(ms, 3)
-            for rep in range(2):                                           # rep 0: warm-up (graph capture)
-                caches = [dict() for _ in range(cfg.n_layers)]
-                logits = model(ids, kv_caches=caches, pos0=0)
-                state = {"nxt": logits[:, -1:].argmax(-1), "i": 0}
-                del logits
-                steps = 8 if rep == 0 else new
+            if world == 1:
+                for rep in range(2):                                       # rep 0: warm-up (graph capture)
+                    caches = [dict() for _ in range(cfg.n_layers)]
+                    logits = model(ids, kv_caches=caches, pos0=0)
+                    state = {"nxt": logits[:, -1:].argmax(-1), "i": 0}
+                    del logits
+                    steps = 8 if rep == 0 else new
 
-                def decode_step():
-                    lg = model(state["nxt"], kv_caches=caches, pos0=prompt + state["i"])
-                    state["nxt"] = lg[:, -1:].argmax(-1)
-                    state["i"] += 1
-                ms = _event_ms(decode_step, steps)
-            res[f"decode_b{b}_eager_tok_s"] = round(b * new / (ms / 1e3), 1)
-            del caches, state
+                    def decode_step():
+                        lg = model(state["nxt"], kv_caches=caches, pos0=prompt + state["i"])
+                        state["nxt"] = lg[:, -1:].argmax(-1)
+                        state["i"] += 1
+                    ms = _event_ms(decode_step, steps)
+                res[f"decode_b{b}_eager_tok_s"] = round(b * new / (ms / 1e3), 1)
+                del caches, state
             dec = GraphDecoder(model, b, max_len=prompt + new)
             dec.prefill(ids)
             dec.step()                                                     # capture
             dec.prefill(ids)
-            ms = _event_ms(dec.step, new)
-            res[f"decode_b{b}_tok_s"] = round(b * new / (ms / 1e3), 1)
+            ms = timed(dec.step, new)
+            res[f"decode_b{b}_tok_s"] = round(world * b * new / (ms / 1e3), 1)
             res[f"decode_b{b}_ms_per_step"] = round(ms / new, 4)
             del dec, ids
         # one memory layer, one token: the layer's decode graph
@@ -814,28 +835,37 @@ def run_inference(args, local):
         x1 = torch.randn(1, cfg.d_model, device=dev, generator=gen)
         for _ in range(3):
             mem(x1)
-        res["pkm_layer_us_per_token"] = round(_event_ms(lambda: mem(x1), 200) / 200 * 1e3, 2)
-    # the lookup alone: fused scoring + top-k + softmax and the value bag of one token, captured once
-    q1 = torch.randn(1, mem.heads, mem.k_dim, device=dev, generator=gen).bfloat16()
-    keys = mem.keys.detach().bfloat16()
-    table = mem.values.weight.detach()
+        res["pkm_layer_us_per_token"] = round(timed(lambda: mem(x1), 200) / 200 * 1e3, 2)
+    if world == 1:
+        # the lookup alone: fused scoring + top-k + softmax and the value bag of one token, captured once
+        q1 = torch.randn(1, mem.heads, mem.k_dim, device=dev, generator=gen).bfloat16()
+        keys = mem.keys.detach().bfloat16()
+        table = mem.values.weight.detach()
 
-    def lookup():
-        _, idx, w = K.score_select(q1, keys, mem.knn)
-        return K.bag_infer(idx.view(1, -1), w.view(1, -1), table, out_bf16=True)
-    s = torch.cuda.Stream(dev)
-    s.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(s):
-        for _ in range(2):
+        def lookup():
+            _, idx, w = K.score_select(q1, keys, mem.knn)
+            return K.bag_infer(idx.view(1, -1), w.view(1, -1), table, out_bf16=True)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                lookup()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
             lookup()
-    torch.cuda.current_stream(dev).wait_stream(s)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        lookup()
-    for _ in range(3):
-        graph.replay()
-    res["pkm_lookup_us_per_token"] = round(_event_ms(graph.replay, 200) / 200 * 1e3, 2)
-    del graph, model
+        for _ in range(3):
+            graph.replay()
+        res["pkm_lookup_us_per_token"] = round(_event_ms(graph.replay, 200) / 200 * 1e3, 2)
+        del graph
+    else:
+        x = getattr(mem.values.weight, "peer_exchange", None)
+        torch.cuda.synchronize(dev)
+        for m in model.memory_layers():
+            m._graph = None
+        if x is not None:
+            x.close()
+    del model
     return res
 
 
@@ -964,11 +994,11 @@ def main():
         return
     world, rank, local = dist_setup(args)
     line = run_cuda(args, world, rank, local)
-    if world == 1 and not args.no_inference:
+    if not args.no_inference:
         import gc
         gc.collect()
         torch.cuda.empty_cache()
-        line["inference"] = run_inference(args, local)
+        line["inference"] = run_inference(args, local, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = cpu_reference(args.cpu_rows_per_half, args.cpu_tokens, 3, 1)
         line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}

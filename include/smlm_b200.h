@@ -348,16 +348,19 @@ SMLM_API int smlm_slot_sum(const float *src, int64_t slots, int64_t count, float
 /* ----------------------------------------------- row-sharded exchange through peer memory (NVLink, CUDA IPC)
  * No counterpart in the reference (one device there). The same exchange as the NCCL collectives above, fused
  * into the owner's kernels: every rank owns one exchange
- * block in its HBM (flags, its lookups, a receive area for the owners' partial bags and one for the weight
- * gradients), mapped into the other ranks' processes with CUDA IPC (no multicast objects anywhere). The owner's
- * forward kernel reads each rank's lookups over NVLink and stores that rank's partial bag straight into its
- * receive area; the weight-gradient kernel stores each in-shard lookup's gradient straight into the requesting
- * rank's area. Ranks announce progress by writing an epoch (one per forward, > 0, the same on every rank) into
- * each other's flags after a system-scope fence; every wait is bounded (10 s of %globaltimer) and a timeout
- * raises SMLM_FLAG_TIMEOUT in *status (required) and ends every later wait at once. One forward may be
- * outstanding per exchange (its backward runs before the next forward). All ranks call the same entries with the
- * same n, k, n_cap, d. The block is allocated once by smlm_xchg_alloc (the library's only device allocation,
- * made at setup, not per step). */
+ * block in its HBM (flags, an epoch counter, its lookups bucketed by owner, a receive area for the owners' partial
+ * bags and one for the weight gradients), mapped into the other ranks' processes with CUDA IPC (no multicast
+ * objects anywhere). Each rank sorts its lookups into per-owner buckets (a counting sort by owner, slot order kept)
+ * in its own block; the owner's forward kernel reads only its bucket of each rank over NVLink and stores that
+ * rank's partial bag straight into its receive area; the weight-gradient kernel stores each in-shard lookup's
+ * gradient straight into the requesting rank's area. Ranks announce progress by writing an epoch into each other's
+ * flags after a system-scope fence: the caller's (> 0, the same on every rank), or with epoch 0 the block's own
+ * counter, which the forward advances on the device and the backward reuses, so a step captured in a CUDA graph
+ * gets a new epoch on every replay. Every wait is bounded (10 s of %globaltimer) and a timeout raises
+ * SMLM_FLAG_TIMEOUT in *status (required) and ends every later wait at once. One forward may be outstanding per
+ * exchange (its backward runs before the next forward). All ranks call the same entries with the same n, k, n_cap,
+ * d, at most 64 ranks. The block is allocated once by smlm_xchg_alloc (the library's only device allocation, made
+ * at setup, not per step). */
 SMLM_API size_t smlm_xchg_bytes(int world, int64_t n_cap, int64_t k, int64_t d);
 /* cudaMalloc of the block (zeroed) and its IPC handle (cudaIpcMemHandle_t, 64 bytes) for the other ranks */
 SMLM_API int smlm_xchg_alloc(size_t bytes, void **block, void *ipc_handle);
@@ -366,15 +369,18 @@ SMLM_API int smlm_xchg_open(const void *ipc_handle, void **block);
 SMLM_API int smlm_xchg_close(void *block);
 SMLM_API int smlm_xchg_free(void *block);
 
-/* Forward of the sharded bag: publishes this rank's lookups (idx int32 global rows and fp32 weights, (n, k)),
- * computes this shard's partial bags of every rank's tokens into their receive areas, waits for every owner and
- * writes out (n, d) fp32 = the partials summed in owner order. all_idx / all_w ((world n, k)) receive every
- * rank's lookups (for the backward). peers_dev: device array of world block pointers (this rank's own included).
- * d % 4 == 0, d <= 512, table and out 16-byte aligned. */
+/* Forward of the sharded bag: buckets and publishes this rank's lookups (idx int32 global rows, -1 for padding,
+ * and fp32 weights, (n, k); the owner of row r is r / rows_per_rank), computes this shard's partial bags of every
+ * rank's tokens into their receive areas, waits for every owner and writes out (n, d) = the partials summed in
+ * owner order, times silu(pre) when pre ((n, d) fp32 / bf16, the swilu projection) is given, as fp32 or bf16
+ * (out_dtype). all_idx / all_w ((world n, k), both or neither): the lookups this shard served, in the layout of
+ * every rank's lookups stacked (the others -1), for the backward. peers_dev: device array of world block pointers
+ * (this rank's own included). d % 4 == 0, d <= 512, table, pre and out 16-byte aligned. */
 SMLM_API int smlm_xchg_forward(void *const *peers_dev, void *my_block, int rank, int world, const int32_t *idx,
-                               const float *weights, int64_t n, int64_t k, int64_t n_cap, const void *table_shard,
-                               int table_dtype, int64_t row_base, int64_t shard_rows, int64_t d, int32_t *all_idx,
-                               float *all_w, float *out, int64_t epoch, int *status, void *stream);
+                               const float *weights, int64_t n, int64_t k, int64_t n_cap, int64_t rows_per_rank,
+                               const void *table_shard, int table_dtype, int64_t row_base, int64_t shard_rows,
+                               int64_t d, int32_t *all_idx, float *all_w, const void *pre, int pre_dtype, void *out,
+                               int out_dtype, int64_t epoch, int *status, void *stream);
 /* Backward, owner side: weight gradients of this shard's lookups of every rank (grad_all: the all-gathered
  * output gradients (world n, d), fp32 / bf16) into the requesting ranks' areas. */
 SMLM_API int smlm_xchg_backward_gw(void *const *peers_dev, int rank, int world, const void *grad_all, int grad_dtype,

@@ -33,7 +33,6 @@ __device__ __forceinline__ void store_out(void* out, int dtype, int64_t off, con
     }
 }
 
-__device__ __forceinline__ float silu_bf16(float p) { return round_bf16(p / (1.0f + expf(-p))); }
 
 // ---------------------------------------------------------------------------------------------- bag gather
 // Lookup indices: int64 or int32 global rows; the table holds rows [row_base, row_base + rows). Rows outside

@@ -86,6 +86,8 @@ __device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
     return (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
 }
 __device__ __forceinline__ float round_bf16(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+// silu(p) = p * sigmoid(p) as the swilu product's factor, rounded to bf16 as the reference's autocast computes it
+__device__ __forceinline__ float silu_bf16(float p) { return round_bf16(p / (1.0f + expf(-p))); }
 
 // Order-preserving unsigned codes: a larger code means a larger value; -0 is mapped onto +0 so that the two
 // zeros tie (and the tie goes to the lower index, as for any other equal scores).

@@ -83,8 +83,8 @@ SIGNATURES = {
     "smlm_xchg_open": (_i32, [_p, _p]),
     "smlm_xchg_close": (_i32, [_p]),
     "smlm_xchg_free": (_i32, [_p]),
-    "smlm_xchg_forward": (_i32, [_p, _p, _i32, _i32, _p, _p, _i64, _i64, _i64, _p, _i32, _i64, _i64, _i64, _p, _p,
-                                 _p, _i64, _p, _p]),
+    "smlm_xchg_forward": (_i32, [_p, _p, _i32, _i32, _p, _p, _i64, _i64, _i64, _i64, _p, _i32, _i64, _i64, _i64,
+                                 _p, _p, _p, _i32, _p, _i32, _i64, _p, _p]),
     "smlm_xchg_backward_gw": (_i32, [_p, _i32, _i32, _p, _i32, _p, _i64, _i64, _i64, _p, _i32, _i64, _i64, _i64,
                                      _i64, _p, _p]),
     "smlm_xchg_collect_gw": (_i32, [_p, _i32, _i32, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),

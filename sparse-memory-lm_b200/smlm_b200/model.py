@@ -185,34 +185,36 @@ class SwiGLU(nn.Module):
 
 
 # ----------------------------------------------------------------------------------------------- blocks
-def _product_key_memory(cfg, shared_values):
-    """A memory layer as ModelConfig's mem_* fields describe it."""
+def _product_key_memory(cfg, shared_values, shard=None):
+    """A memory layer as ModelConfig's mem_* fields describe it; shard: (process group, exchange) to row-shard its
+    table over (no counterpart in the reference)."""
+    group, exchange = shard if shard is not None else (None, "p2p")
     return ProductKeyMemory(
         cfg.d_model, cfg.d_model, n_keys=cfg.mem_n_keys, heads=cfg.mem_heads, knn=cfg.mem_knn,
         k_dim=cfg.mem_k_dim, v_dim=cfg.mem_v_dim, query_norm=cfg.mem_query_norm, swilu=cfg.mem_swilu,
         value_impl=cfg.mem_value_impl, keys_weight_decay=cfg.mem_keys_weight_decay,
         score_scale=cfg.mem_score_scale, score_scale_init=cfg.mem_score_scale_init, shared_values=shared_values,
-        value_grad=cfg.mem_value_grad, impl=cfg.mem_impl)
+        value_grad=cfg.mem_value_grad, impl=cfg.mem_impl, shard_group=group, shard_exchange=exchange)
 
 
 class Block(nn.Module):
     """Residual branches in order: [Engram memory], attention, feed-forward or memory read, [second read]."""
 
-    def __init__(self, cfg, layer_id, shared_values=None):
+    def __init__(self, cfg, layer_id, shared_values=None, shard=None):
         super().__init__()
         self.is_memory = layer_id in cfg.mem_layers
         self.dormant = False                  # a block that grows in later (set_dormant / wake): skipped
         self.attn_norm = nn.RMSNorm(cfg.d_model, eps=cfg.norm_eps)
         self.attn = Attention(cfg)
         self.ffn_norm = nn.RMSNorm(cfg.d_model, eps=cfg.norm_eps)
-        self.ffn = (_product_key_memory(cfg, shared_values) if self.is_memory
+        self.ffn = (_product_key_memory(cfg, shared_values, shard) if self.is_memory
                     else SwiGLU(cfg.d_model, cfg.ffn_hidden))
         self.ffn_r2 = None
         if layer_id in cfg.mem_round_layers:
             if not (self.is_memory and shared_values is not None):
                 raise ValueError(f"layer {layer_id}: a second memory read needs a memory layer with a shared table")
             self.ffn_norm_r2 = nn.RMSNorm(cfg.d_model, eps=cfg.norm_eps)
-            self.ffn_r2 = _product_key_memory(cfg, shared_values)
+            self.ffn_r2 = _product_key_memory(cfg, shared_values, shard)
         self.engram = None
         if layer_id in cfg.eng_layers:
             self.engram = EngramMemory(cfg.d_model, len(cfg.eng_orders) * cfg.eng_heads, cfg.eng_head_dim,
@@ -237,13 +239,23 @@ class Block(nn.Module):
 
 # ---------------------------------------------------------------------------------------------- the model
 class Transformer(nn.Module):
-    def __init__(self, cfg):
+    def __init__(self, cfg, shard_group=None, shard_exchange="p2p"):
+        """shard_group (no counterpart in the reference): a torch.distributed process group over which the
+        product-key value tables are row-sharded (one process per GPU, each holding its rows; see
+        smlm_b200.sharded), shard_exchange "p2p" or "nccl"; everything else stays replicated. Needs
+        mem_value_grad="row_sparse"."""
         super().__init__()
         self.cfg = cfg
         self.tok_emb = nn.Embedding(cfg.vocab_size, cfg.d_model)
-        shared = (nn.Embedding(cfg.mem_n_keys ** 2, cfg.value_dim)
-                  if cfg.mem_share_values and cfg.mem_layers else None)
-        self.layers = nn.ModuleList(Block(cfg, i, shared) for i in range(cfg.n_layers))
+        shard = None
+        rows = cfg.mem_n_keys ** 2
+        if shard_group is not None and torch.distributed.get_world_size(shard_group) > 1:
+            from .sharded import RowShard
+            shard = (shard_group, shard_exchange)
+            rows = RowShard(rows, torch.distributed.get_world_size(shard_group),
+                            torch.distributed.get_rank(shard_group)).count
+        shared = nn.Embedding(rows, cfg.value_dim) if cfg.mem_share_values and cfg.mem_layers else None
+        self.layers = nn.ModuleList(Block(cfg, i, shared, shard) for i in range(cfg.n_layers))
         self.ngram = (NgramHash(cfg.vocab_size, cfg.eng_orders, cfg.eng_heads, cfg.eng_rows, cfg.eng_hash_seed)
                       if cfg.eng_layers else None)
         self.norm = nn.RMSNorm(cfg.d_model, eps=cfg.norm_eps)

@@ -20,7 +20,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from . import kernels as K
-from .sharded import RowShard, sharded_embedding_bag
+from .sharded import RowShard, sharded_bag_infer, sharded_embedding_bag
 from .sparse_values import read_table, row_sparse_embedding_bag
 
 IMPLS = ("cuda", "triton", "torch")
@@ -104,15 +104,19 @@ class ProductKeyMemory(nn.Module):
             raise ValueError(query_norm)
         self.shard = self.shard_group = None
         if shard_group is not None and dist.get_world_size(shard_group) > 1:
-            if value_grad != "row_sparse" or shared_values is not None:
-                raise ValueError("a row-sharded value table needs value_grad='row_sparse' and its own values")
+            if value_grad != "row_sparse":
+                raise ValueError("a row-sharded value table needs value_grad='row_sparse'")
             if shard_exchange not in ("p2p", "nccl"):
                 raise ValueError(f"unknown shard_exchange {shard_exchange!r}")
             self.shard = RowShard(self.size, dist.get_world_size(shard_group), dist.get_rank(shard_group))
             self.shard_group = shard_group
             self.shard_exchange = shard_exchange
         if shared_values is not None:
-            assert shared_values.weight.shape == (self.size, self.v_dim)
+            # a table shared by several layers (this rank's rows of it when row-sharded)
+            rows = self.shard.count if self.shard is not None else self.size
+            if tuple(shared_values.weight.shape) != (rows, self.v_dim):
+                raise ValueError(f"shared value table of shape {tuple(shared_values.weight.shape)}, expected "
+                                 f"{(rows, self.v_dim)}")
             self.values = shared_values
         else:
             self.values = nn.Embedding(self.shard.count if self.shard else self.size, self.v_dim)
@@ -188,7 +192,7 @@ class ProductKeyMemory(nn.Module):
         if not x.is_cuda:
             raise ValueError("ProductKeyMemory of smlm_b200 runs on CUDA only (no CPU fallback)")
         if (getattr(self, "decode_graph", False) and x.shape[0] == 1 and not self.record
-                and not torch.is_grad_enabled() and self.shard is None):
+                and not torch.is_grad_enabled() and (self.shard is None or self.shard_exchange == "p2p")):
             return self._graph_forward(x).view(*shape[:-1], self.d_out)
         return self._forward(x).view(*shape[:-1], self.d_out)
 
@@ -233,6 +237,14 @@ class ProductKeyMemory(nn.Module):
             self.last_indices = indices.detach()
             self.last_scores = scores.detach()
             self.last_weights = weights.detach()
+        if (not torch.is_grad_enabled() and self.swilu and autocast_bf16 and self.shard is not None
+                and self.shard_exchange == "p2p"):
+            # inference over a row-sharded table: the swilu product and the bf16 cast fused into the peer
+            # exchange's final sum of the owners' partial bags
+            K_ = self.heads * self.knn
+            out = sharded_bag_infer(indices.view(N, K_), weights.view(N, K_), self.values.weight, self.shard,
+                                    self.shard_group, pre=self.swilu_proj(x), out_bf16=True)
+            return self.value_proj(out)
         if not torch.is_grad_enabled() and self.swilu and autocast_bf16 and self.shard is None:
             # inference: value bag on the inference table (fp32 / bf16 / q4) with the swilu product and the
             # bf16 cast fused (reference: pkm.py:213-224)

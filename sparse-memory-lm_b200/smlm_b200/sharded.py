@@ -15,11 +15,21 @@ keys, the query projection and everything else stay replicated and data-parallel
   clip      the squared norm of every rank's accumulator rows is all-gathered and summed in rank order.
   step      each rank's LazyRowAdam updates its own rows only.
 
+That is the NCCL exchange (shard_exchange="nccl"). The default, shard_exchange="p2p" (PeerExchange), fuses the
+exchange into the kernels through peer memory over NVLink: each rank buckets its lookups by owner (a counting sort
+in its own exchange block), each owner reads only its bucket of every rank, gathers its rows and stores the
+partial bags straight into the requesting ranks' memory, which sum them in owner order (for inference with the
+swilu product fused); in the backward the owner stores each lookup's weight gradient straight into its
+requester's memory, and only the output gradients are all-gathered over NCCL. Its epochs live on the device, so
+a whole row-sharded step can be captured in one CUDA graph and replayed.
+
 A P-rank step over batches x_0 .. x_{P-1} is the one-rank step over their concatenation (row gradients summed over
 all tokens; the replicated parameters' gradients summed with allreduce_replicated_grads); only the fp32 summation
 order of the bag (owner partials) and of the row sums differ. Every rank must pass the same number of tokens.
-Data-path exchange volume per rank and step (N tokens, K lookups, D columns, P ranks): lookups 8 N K P,
-partial bags and output gradients 2 x 4 N D P, weight gradients 4 N K P bytes received.
+Data-path exchange volume per rank and step (N tokens, K lookups, D columns, P ranks), NCCL exchange: lookups
+8 N K P, partial bags and output gradients 2 x 4 N D P, weight gradients 4 N K P bytes received; peer exchange:
+lookups about 12 N K read by each owner (its buckets), partial bags and output gradients 2 x 4 N D P, weight
+gradients 4 N K.
 """
 import ctypes
 
@@ -123,9 +133,10 @@ class _ShardedBag(torch.autograd.Function):
 
 class PeerExchange:
     """The exchange blocks of every rank mapped into this process (CUDA IPC over NVLink) for the fused exchange:
-    the owner's kernels read the other ranks' lookups and write their partial bags and weight gradients through
-    peer pointers, with epoch flags and bounded waits (smlm_xchg_* in the C ABI). Collective to build and to
-    close; sized for up to n_cap tokens per rank."""
+    each rank buckets its lookups by owner in its own block, the owners' kernels read their buckets and write
+    partial bags and weight gradients through peer pointers, with epoch flags and bounded waits (smlm_xchg_* in
+    the C ABI). The epochs live on the device (advanced by every forward), so exchanges can be captured in a CUDA
+    graph and replayed. Collective to build and to close; sized for up to n_cap tokens per rank."""
 
     def __init__(self, shard, group, n_cap, k, d, device):
         lib = L.lib()
@@ -151,11 +162,28 @@ class PeerExchange:
                 self.opened.append(peer.value)
                 ptrs.append(peer.value)
         self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
-        self.epoch = 0
 
-    def next_epoch(self):
-        self.epoch += 1
-        return self.epoch
+    def forward(self, idx, w, table, n, pre=None, out_dtype=torch.float32, dense=True):
+        """One exchange forward (smlm_xchg_forward, device epoch): this rank's tokens' bags (n, d) over the whole
+        table, times silu(pre) with `pre`; with dense, also the lookups this shard served, stacked over the ranks
+        ((world n, k) int32 global rows, -1 for other shards' lookups, and fp32 weights) for the backward."""
+        shard, dev = self.shard, self.device
+        P, Kk = shard.world, self.k
+        all_idx = torch.empty(P * n, Kk, dtype=torch.int32, device=dev) if dense else None
+        all_w = torch.empty(P * n, Kk, dtype=torch.float32, device=dev) if dense else None
+        out = torch.empty(n, self.d, dtype=out_dtype, device=dev)
+        t = table.detach()
+        pre_c = pre.contiguous() if pre is not None else None
+        with L.timed("xchg_forward", 6):
+            rc = L.lib().smlm_xchg_forward(
+                L.ptr(self.peers), ctypes.c_void_p(self.block), shard.rank, P, L.ptr(idx), L.ptr(w), n, Kk,
+                self.n_cap, shard.per, L.ptr(t) if shard.count else None, L.dtype_code(t.dtype), shard.base,
+                shard.count, self.d, L.ptr(all_idx), L.ptr(all_w), L.ptr(pre_c),
+                L.dtype_code(pre_c.dtype) if pre_c is not None else L.F32, L.ptr(out), L.dtype_code(out_dtype), 0,
+                L.status_ptr(dev), L.stream(dev))
+        L.check(rc, "xchg_forward")
+        L.after(dev, "xchg_forward")
+        return out, all_idx, all_w
 
     def close(self):
         """Unmaps the peers' blocks and frees this rank's (collective: no rank may touch a block after)."""
@@ -176,6 +204,8 @@ def peer_exchange(table, shard, group, n, k):
     """The table's PeerExchange, built on first use or rebuilt (collectively) when n outgrows its capacity."""
     x = getattr(table, "peer_exchange", None)
     if x is None or x.n_cap < n or x.k != k or x.d != table.shape[1]:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the row-sharded exchange must be set up (one eager step of this shape) before capture")
         if x is not None:
             x.close()
         x = PeerExchange(shard, group, n, k, table.shape[1], table.device)
@@ -189,26 +219,15 @@ class _PeerBag(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, weights, indices, table, store, shard, group):
-        P = shard.world
+        from .sparse_values import read_table
         N, Kk = indices.shape
         x = peer_exchange(table, shard, group, N, Kk)
-        dev = table.device
         idx = indices.to(torch.int32).contiguous()
         w = weights.reshape(N, Kk).float().contiguous()
-        all_idx = torch.empty(P * N, Kk, dtype=torch.int32, device=dev)
-        all_w = torch.empty(P * N, Kk, dtype=torch.float32, device=dev)
-        out = torch.empty(N, table.shape[1], dtype=torch.float32, device=dev)
-        epoch = x.next_epoch()
-        t = table.detach()
-        with L.timed("xchg_forward", 3):
-            rc = L.lib().smlm_xchg_forward(
-                L.ptr(x.peers), ctypes.c_void_p(x.block), shard.rank, P, L.ptr(idx), L.ptr(w), N, Kk, x.n_cap,
-                L.ptr(t) if shard.count else None, L.dtype_code(t.dtype), shard.base, shard.count, t.shape[1],
-                L.ptr(all_idx), L.ptr(all_w), L.ptr(out), epoch, L.status_ptr(dev), L.stream(dev))
-        L.check(rc, "xchg_forward")
-        L.after(dev, "xchg_forward")
+        src = read_table(table)
+        out, all_idx, all_w = x.forward(idx, w, src, N)
         ctx.save_for_backward(all_idx, all_w)
-        ctx.table, ctx.store, ctx.shard, ctx.group, ctx.x, ctx.epoch = table, store, shard, group, x, epoch
+        ctx.table, ctx.src, ctx.store, ctx.shard, ctx.group, ctx.x = table, src, store, shard, group, x
         ctx.wshape, ctx.wdtype = weights.shape, weights.dtype
         return out.to(table.dtype)
 
@@ -223,13 +242,13 @@ class _PeerBag(torch.autograd.Function):
         if g.dtype not in (torch.float32, torch.bfloat16):
             g = g.float()
         all_g = _all_gather(g, ctx.group, P)
-        t = ctx.table.detach()
+        t, src = ctx.table.detach(), ctx.src.detach()
         status = L.status_ptr(dev)
         with L.timed("xchg_backward_gw", 1):
             rc = L.lib().smlm_xchg_backward_gw(
                 L.ptr(x.peers), shard.rank, P, L.ptr(all_g), L.dtype_code(all_g.dtype), L.ptr(all_idx), N, Kk,
-                x.n_cap, L.ptr(t) if shard.count else None, L.dtype_code(t.dtype), shard.base, shard.count,
-                t.shape[1], ctx.epoch, status, L.stream(dev))
+                x.n_cap, L.ptr(src) if shard.count else None, L.dtype_code(src.dtype), shard.base, shard.count,
+                src.shape[1], 0, status, L.stream(dev))
         L.check(rc, "xchg_backward_gw")
         if store is not None and shard.count:
             if store.can_defer(t):
@@ -245,11 +264,28 @@ class _PeerBag(torch.autograd.Function):
         gw = torch.empty(N, Kk, dtype=torch.float32, device=dev)
         with L.timed("xchg_collect_gw", 1):
             rc = L.lib().smlm_xchg_collect_gw(L.ptr(x.peers), shard.rank, P, N, Kk, x.n_cap, t.shape[1],
-                                              L.ptr(gw), ctx.epoch, status, L.stream(dev))
+                                              L.ptr(gw), 0, status, L.stream(dev))
         L.check(rc, "xchg_collect_gw")
         L.after(dev, "xchg_collect_gw")
-        ctx.table = ctx.store = ctx.x = None
+        ctx.table = ctx.src = ctx.store = ctx.x = None
         return gw.view(ctx.wshape).to(ctx.wdtype), None, None, None, None, None
+
+
+def sharded_bag_infer(indices, weights, table, shard, group, pre=None, out_bf16=False):
+    """No-grad sharded value bag over the peer exchange for inference (prefill, decoding): the bags of this rank's
+    tokens over the whole row-sharded table, with the swilu product silu(pre) and the bf16 cast fused into the
+    exchange's final sum (reference: the inference bag of pkm.py:213-224 on one device). Collective: every rank
+    calls it with the same token count. Reads the table's bf16 copy when it has one."""
+    from .sparse_values import read_table
+    if indices.ndim != 2 or table.shape[0] != shard.count:
+        raise ValueError("sharded_bag_infer: indices (N, K) and this rank's table shard expected")
+    N, Kk = indices.shape
+    with torch.no_grad():
+        x = peer_exchange(table, shard, group, N, Kk)
+        out, _, _ = x.forward(indices.to(torch.int32).contiguous(), weights.reshape(N, Kk).float().contiguous(),
+                              read_table(table), N, pre=pre, out_dtype=torch.bfloat16 if out_bf16 else torch.float32,
+                              dense=False)
+    return out
 
 
 def sharded_embedding_bag(indices, weights, table, shard, group, ops=None, store=None, exchange="nccl"):
@@ -267,8 +303,7 @@ def sharded_embedding_bag(indices, weights, table, shard, group, ops=None, store
         if store is None and torch.is_grad_enabled() and table.requires_grad:
             store = row_store(table)
         if not torch.is_grad_enabled():
-            with torch.no_grad():
-                return _PeerBag.forward(_NoCtx(), weights, indices, table, None, shard, group)
+            return sharded_bag_infer(indices, weights, table, shard, group).to(table.dtype)
         return _PeerBag.apply(weights, indices, table, store, shard, group)
     ops = ops or CUDA_OPS
     if indices.ndim != 2 or weights.shape[:1] != indices.shape[:1]:

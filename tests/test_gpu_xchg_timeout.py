@@ -34,9 +34,10 @@ def test_missing_peer_times_out_with_status():
         out = torch.empty(n, d, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
         t0 = time.time()
+        # rows per rank 50: rank 0 holds rows 0 .. 49 (the table), rank 1 rows 50 .. 99
         rc = lib.smlm_xchg_forward(L.ptr(peers), ctypes.c_void_p(blocks[0]), 0, world, L.ptr(idx), L.ptr(w), n, k, n,
-                                   L.ptr(table), L.F32, 0, 50, d, L.ptr(all_idx), L.ptr(all_w), L.ptr(out), 1,
-                                   L.ptr(status), L.stream(dev))
+                                   50, L.ptr(table), L.F32, 0, 50, d, L.ptr(all_idx), L.ptr(all_w), None, L.F32,
+                                   L.ptr(out), L.F32, 1, L.ptr(status), L.stream(dev))
         assert rc == L.OK
         torch.cuda.synchronize()
         elapsed = time.time() - t0
@@ -46,8 +47,8 @@ def test_missing_peer_times_out_with_status():
         assert float(torch.ones(4, device=dev).sum()) == 4.0
         # a missing status word is refused on the host, before any launch
         rc = lib.smlm_xchg_forward(L.ptr(peers), ctypes.c_void_p(blocks[0]), 0, world, L.ptr(idx), L.ptr(w), n, k, n,
-                                   L.ptr(table), L.F32, 0, 50, d, L.ptr(all_idx), L.ptr(all_w), L.ptr(out), 2, None,
-                                   L.stream(dev))
+                                   50, L.ptr(table), L.F32, 0, 50, d, L.ptr(all_idx), L.ptr(all_w), None, L.F32,
+                                   L.ptr(out), L.F32, 2, None, L.stream(dev))
         assert rc == L.ERR_INVALID
     finally:
         torch.cuda.synchronize()

@@ -220,9 +220,10 @@ def exchange_rooflines(per_kernel_ms, world, n, k, d, hbm_gbs, table_bytes=4):
     """Roofline of the row-sharded exchange calls of one rank and step (the owner kernels that read and write the
     other ranks' memory over NVLink), from their mean CUDA-event times `per_kernel_ms` (name -> ms); None on one
     GPU. n tokens per rank, k lookups per token (m = n k), d values per row; lookups spread evenly over the shards.
-      xchg_forward      NVLink: the P-1 peers' lookups read (8 B each), a partial bag per peer token written
-                        (d x 4 B); HBM: this shard's ~m table rows, every rank's lookups copied locally, the P
-                        partial slots summed into the output
+      xchg_forward      NVLink: this owner's buckets of the P-1 peers' lookups read (m / P entries of 12 B each),
+                        a partial bag per peer token written (d x 4 B); HBM: this rank's lookups bucketed (read 8 B,
+                        written 12 B each), this shard's ~m table rows, the dense local copy of the served lookups
+                        (P m x 4 B cleared, m x 8 B written), the P partial slots summed into the output
       xchg_backward_gw  NVLink: the weight gradient of each remote in-shard lookup stored into its rank (4 B);
                         HBM: the all-gathered output gradients, this shard's ~m table rows, every rank's lookups
     Each call's target time is the slower of its NVLink bytes at NVLINK_PEER_GBS and its HBM bytes at hbm_gbs;
@@ -231,8 +232,8 @@ def exchange_rooflines(per_kernel_ms, world, n, k, d, hbm_gbs, table_bytes=4):
         return None
     m = n * k
     calls = {
-        "xchg_forward": ((world - 1) * n * (k * 8 + d * 4),
-                         m * d * table_bytes + world * n * k * 8 + (world + 2) * n * d * 4),
+        "xchg_forward": ((world - 1) * (m // world) * 12 + (world - 1) * n * d * 4,
+                         m * 20 + m * d * table_bytes + world * m * 4 + m * 8 + (world + 1) * n * d * 4),
         "xchg_backward_gw": ((world - 1) * m * 4 // world,
                              m * d * table_bytes + world * n * d * 4 + world * n * k * 4),
     }

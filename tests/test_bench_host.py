@@ -11,8 +11,9 @@ def test_exchange_rooflines():
                                  d, hbm)
     assert set(r) == {"xchg_forward", "xchg_backward_gw"}
     f = r["xchg_forward"]
-    assert f["nvlink_bytes"] == 7 * n * (k * 8 + d * 4)
-    assert f["hbm_bytes"] == n * k * d * 4 + world * n * k * 8 + (world + 2) * n * d * 4
+    m = n * k
+    assert f["nvlink_bytes"] == 7 * (m // 8) * 12 + 7 * n * d * 4
+    assert f["hbm_bytes"] == m * 20 + m * d * 4 + world * m * 4 + m * 8 + (world + 1) * n * d * 4
     assert f["nvlink_GB/s"] == pytest.approx(f["nvlink_bytes"] / 2e-3 / 1e9, rel=1e-3)
     t_nv = f["nvlink_bytes"] / (bench.NVLINK_PEER_GBS * 1e9) * 1e3
     t_hbm = f["hbm_bytes"] / (hbm * 1e9) * 1e3

@@ -391,6 +391,45 @@ SMLM_API int smlm_xchg_backward_gw(void *const *peers_dev, int rank, int world, 
 SMLM_API int smlm_xchg_collect_gw(void *const *peers_dev, int rank, int world, int64_t n, int64_t k, int64_t n_cap,
                                   int64_t d, float *gw, int64_t epoch, int *status, void *stream);
 
+/* ------------------------------------------------------------------------------------- host-RAM value tables
+ * Tables too large for the GPUs' memory stay in host RAM with their gradient accumulator and optimizer state
+ * (reference: smlm/host_values.py, smlm/host_optim.py, smlm/host_rows.c). Here those host tensors are page-locked
+ * and mapped into the device's address space, and kernels work on the rows a step reads directly over the host
+ * link: no CPU loop and no staging copy through the CPU. smlm_lazy_adam_step, smlm_lazy_adam_lowmem_step and
+ * smlm_rowwise_step take mapped host pointers for the table, the accumulator, the touched mask and the state as
+ * they are; the calls below add what the host path needs besides. d % 4 == 0 (16-byte row accesses). */
+
+/* Page-locks [ptr, ptr + bytes) of host memory and maps it into the current device's address space
+ * (cudaHostRegister, mapped and portable); *device_ptr receives the address kernels use. The memory must stay
+ * allocated until smlm_host_unregister. No counterpart in the reference (its host rows are read by C loops). */
+SMLM_API int smlm_host_register(void *ptr, size_t bytes, void **device_ptr);
+SMLM_API int smlm_host_unregister(void *ptr);
+
+/* out[i] (device, (n, d) fp32) = hot[slot[i]] when slot (device int32, may be NULL) has slot[i] >= 0 (the row's
+ * HOT copy on the device), else table[rows[i]] (table: a mapped host table of table_rows rows; rows: device int64,
+ * distinct). Out-of-range rows give zeros and SMLM_FLAG_INDEX_RANGE. Replaces HostEmbedding.gather's staging
+ * (host_values.py:82-119: indices to the host, a C gather into pinned memory, a copy to the device). */
+SMLM_API int smlm_host_rows_gather(const float *table, int64_t table_rows, const int64_t *rows, const int32_t *slot,
+                                   const float *hot, int64_t n, int64_t d, float *out, int *status, void *stream);
+
+/* acc[rows[i]] = acc[rows[i]] + grads[i] and touched[rows[i]] = 1 (acc / touched: mapped host tensors of
+ * table_rows rows; grads device (n, d) fp32; rows device int64, distinct), skipping the rows whose skip[i] >= 0
+ * (skip may be NULL; HOT rows keep their own accumulator on the device). Replaces HostEmbedding.accumulate's copy
+ * to the host and C scatter-add (host_values.py:121-150, host_rows.c host_rows_add). */
+SMLM_API int smlm_host_rows_add(float *acc, uint8_t *touched, int64_t table_rows, const int64_t *rows,
+                                const float *grads, const int32_t *skip, int64_t n, int64_t d, int *status,
+                                void *stream);
+
+/* The row-wise step (kind SMLM_ROWRMS / SMLM_ROWADAGRAD; smlm_rowwise_step's formulas, order and rounding) of the
+ * distinct rows rows[i] (device int64) with gradient grads[i] (device (n, d) fp32, e.g. a step's row sums kept on
+ * the GPU), times the clip factor (*grad_scale_dev when given, else grad_scale); param, v and count may be mapped
+ * host memory. Replaces RowWiseOptimizer._step_gacc's chunked copies to the host and C loop
+ * (row_optim.py:73-135, host_rows.c host_rows_rowwise). */
+SMLM_API int smlm_rows_rowwise_step(float *param, int64_t table_rows, const int64_t *rows, const float *grads,
+                                    int64_t n, int64_t d, float *v, int32_t *count, int kind, float beta2, float eps,
+                                    float lr, const float *grad_scale_dev, float grad_scale, int *status,
+                                    void *stream);
+
 /* ------------------------------------------------------------------------------------- Engram n-gram rows
  * Row indices of an Engram module's lookups: for position t of sequence b and lookup (order o, head h), the XOR over
  * i < orders[o] of c[b, history + t - i] * mult[o, h, i] (int64), then x ^= x >> 17, row = (x mod rows, floored)

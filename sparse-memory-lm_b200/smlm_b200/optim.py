@@ -10,8 +10,8 @@ tables:
 
 Dense parameters go to one fused AdamW; row-sparse value tables go to a table optimizer on the sm_100a kernels
 (LazyRowAdam, or RowWiseOptimizer for value_optim "rowrms" / "rowadagrad"), one for the product-key tables and
-one for the Engram tables, returned together as one OptimizerSet. Muon (optimizer="muon") and host-RAM tables are
-not part of this build and are refused.
+one for the Engram tables (host-RAM tables under Adam get a HostLazyRowAdam of their own), returned together as
+one OptimizerSet. Muon (optimizer="muon") is not part of this build and is refused.
 """
 import math
 
@@ -92,8 +92,8 @@ def build_optimizer(model, lr, value_lr, weight_decay, betas=(0.9, 0.95), eps=1e
         mine = [t for t in tables if (id(t) in engram) == (name == "engram_values")]
         if mine:
             copy = value_copy_dtype if name == "memory_values" else None
-            table_opts.append(_table_optimizer(mine, lrs[lr_key], betas, eps, value_state, value_optim, name, copy,
-                                               capturable))
+            table_opts += _table_optimizers(mine, lrs[lr_key], betas, eps, value_state, value_optim, name, copy,
+                                            capturable)
     return OptimizerSet(dense, *table_opts)
 
 
@@ -104,6 +104,25 @@ def _table_optimizer(tables, lr, betas, eps, value_state, value_optim, name, val
                            value_copy_dtype=value_copy_dtype, capturable=capturable)
     from .row_optim import RowWiseOptimizer
     return RowWiseOptimizer(tables, lr=lr, kind=value_optim, beta2=betas[1], eps=eps, name=name)
+
+
+def _table_optimizers(tables, lr, betas, eps, value_state, value_optim, name, value_copy_dtype, capturable):
+    """The table optimizer(s) of one group of row-sparse tables: host-RAM tables under Adam get a HostLazyRowAdam
+    of their own, the rest (and every table under a row-wise optimizer) one optimizer (reference: optim.py:66-90)."""
+    host = [t for t in tables if getattr(t, "host_values", False)]
+    rest = [t for t in tables if not getattr(t, "host_values", False)]
+    out = []
+    if host and value_optim == "adam":
+        if value_copy_dtype is not None or capturable:
+            raise ValueError("value_copy_dtype / capturable do not apply to host-RAM tables")
+        from .host_optim import HostLazyRowAdam
+        out.append(HostLazyRowAdam(host, lr=lr, betas=betas, eps=eps, state_dtype=value_state, name=name))
+    else:
+        rest = tables
+    if rest:
+        out.append(_table_optimizer(rest, lr, betas, eps, value_state, value_optim, name, value_copy_dtype,
+                                    capturable))
+    return out
 
 
 # Persistent optimizer state of one trainable value table, by (gradient kind, table optimizer, moment storage):

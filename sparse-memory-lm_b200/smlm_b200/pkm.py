@@ -177,6 +177,8 @@ class ProductKeyMemory(nn.Module):
     def read_values(self, indices, weights):
         """indices, weights (N, heads*knn) -> (N, v_dim) (reference: pkm.py:138-148)."""
         w = self.values.weight
+        if getattr(w, "host_values", False):
+            return self.values.bag(indices, weights, self.impl)        # table in host RAM (host_values.py)
         if self.shard is not None:
             return sharded_embedding_bag(indices, weights, w, self.shard, self.shard_group,
                                          exchange=self.shard_exchange)
@@ -192,7 +194,8 @@ class ProductKeyMemory(nn.Module):
         if not x.is_cuda:
             raise ValueError("ProductKeyMemory of smlm_b200 runs on CUDA only (no CPU fallback)")
         if (getattr(self, "decode_graph", False) and x.shape[0] == 1 and not self.record
-                and not torch.is_grad_enabled() and (self.shard is None or self.shard_exchange == "p2p")):
+                and not torch.is_grad_enabled() and (self.shard is None or self.shard_exchange == "p2p")
+                and not getattr(self.values.weight, "host_values", False)):
             return self._graph_forward(x).view(*shape[:-1], self.d_out)
         return self._forward(x).view(*shape[:-1], self.d_out)
 
@@ -245,7 +248,8 @@ class ProductKeyMemory(nn.Module):
             out = sharded_bag_infer(indices.view(N, K_), weights.view(N, K_), self.values.weight, self.shard,
                                     self.shard_group, pre=self.swilu_proj(x), out_bf16=True)
             return self.value_proj(out)
-        if not torch.is_grad_enabled() and self.swilu and autocast_bf16 and self.shard is None:
+        if (not torch.is_grad_enabled() and self.swilu and autocast_bf16 and self.shard is None
+                and not getattr(self.values.weight, "host_values", False)):
             # inference: value bag on the inference table (fp32 / bf16 / q4) with the swilu product and the
             # bf16 cast fused (reference: pkm.py:213-224)
             pre = self.swilu_proj(x)

@@ -1,5 +1,6 @@
 """Row-wise optimizers for row-sparse value tables: one state number per row instead of Adam's two moments per
-value, on the sm_100a kernels (reference: re133/sparse-memory-lm smlm/row_optim.py).
+value, on the sm_100a kernels (reference: re133/sparse-memory-lm smlm/row_optim.py), for tables on the GPU or in
+host RAM (smlm_b200.host_values: mapped host memory, HOT rows, GACC).
 
 Only the rows read since the last step change; rows that were not read keep their values and their state
 exactly. g = a row's accumulated gradient times the clip factor, q = the mean of g^2 over the row.
@@ -25,8 +26,8 @@ class RowWiseOptimizer(torch.optim.Optimizer):
             raise ValueError(f"unknown row-wise optimizer: {kind}")
         if any(p.dtype != torch.float32 or p.ndim != 2 or not p.is_contiguous() or p.shape[1] == 0 for p in params):
             raise ValueError("row-wise optimizers require contiguous fp32 tables with nonzero width")
-        if any(not p.is_cuda for p in params):
-            raise ValueError("row-wise optimizers of this build run on CUDA tables only")
+        if any(not p.is_cuda and not getattr(p, "host_values", False) for p in params):
+            raise ValueError("row-wise optimizers of this build run on CUDA tables or host-RAM tables only")
         if not 0 <= lr or not 0 <= eps or not 0 <= beta2 < 1:
             raise ValueError("invalid learning rate, epsilon or beta2")
         super().__init__(params, dict(lr=lr, beta2=beta2, eps=eps, weight_decay=0.0))
@@ -52,6 +53,9 @@ class RowWiseOptimizer(torch.optim.Optimizer):
                 st.sync()
                 state = self._state(p)
                 state["step"] += 1
+                if getattr(p, "host_values", False):
+                    self._step_host(group, p, st, state)
+                    continue
                 if st.pending is not None and not st.live:
                     # rows of one deferred backward: summed and stepped in one pass, acc never written
                     K.rowwise_deferred_step(p, st._touched, state["v"], state.get("n"), st.pending, st.grad_scale,
@@ -62,6 +66,65 @@ class RowWiseOptimizer(torch.optim.Optimizer):
                                    group["beta2"], group["eps"], self.kind, keep_acc=st.clean)
                 st.stepped()
 
+    @torch.no_grad()
+    def _step_host(self, group, p, st, state):
+        """A table in host RAM (smlm_b200.host_values; reference: row_optim.py:58-157): its HOT rows' state lives
+        on the GPU in slot order and they step there; the other rows step in place in host RAM through the mapped
+        table, accumulator and state (smlm_rowwise_step), or, with GACC, from the step's row sums on the GPU
+        (smlm_rows_rowwise_step), overflow rows included."""
+        from . import _lib as L
+        from .host_values import mapped
+        hot = getattr(st, "hot", None)
+        sr = getattr(st, "steprows", None)
+        if hot is not None:
+            dev = hot.values.device
+        elif sr is not None:
+            dev = sr.acc.device
+        else:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        kind = L.ROWRMS if self.kind == "rowrms" else L.ROWADAGRAD
+        scale = st.grad_scale
+        if hot is not None:
+            if "hot_v" not in state:
+                state["hot_v"] = state["v"].index_select(0, hot.rows.cpu()).to(dev)
+                if "n" in state:
+                    state["hot_n"] = state["n"].index_select(0, hot.rows.cpu()).to(dev)
+            K.rowwise_step(hot.values, hot.acc, hot.touched, state["hot_v"], state.get("hot_n"), scale, group["lr"],
+                           group["beta2"], group["eps"], self.kind)
+        sp, sf, keep = None, 1.0, None
+        if torch.is_tensor(scale):
+            keep = scale.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+            sp = L.ptr(keep)
+        else:
+            sf = float(scale)
+        count = state.get("n")
+        with torch.cuda.device(dev):
+            if sr is not None:
+                parts = []
+                if sr.n:
+                    parts.append((sr.rows[:sr.n], sr.acc[:sr.n]))
+                spilled = sr.spilled()
+                if spilled is not None:   # rows read after every slot was taken: summed on the host, never in a slot
+                    parts.append((spilled[0].to(dev), spilled[1].to(dev)))
+                for rows, g in parts:
+                    rc = L.lib().smlm_rows_rowwise_step(
+                        mapped(p.detach()), p.shape[0], L.ptr(rows), L.ptr(g.contiguous()), rows.numel(), p.shape[1],
+                        mapped(state["v"]), mapped(count) if count is not None else None, kind, group["beta2"],
+                        group["eps"], group["lr"], sp, sf, L.status_ptr(dev), L.stream(dev))
+                    L.check(rc, "rows_rowwise_step")
+                torch.cuda.current_stream(dev).synchronize()
+                sr.reset()
+            elif bool(st.touched.any()):
+                ws = L.workspace(L.lib().smlm_touched_workspace(p.shape[0]), dev)
+                rc = L.lib().smlm_rowwise_step(
+                    mapped(p.detach()), mapped(st.acc), mapped(st.touched), mapped(state["v"]),
+                    mapped(count) if count is not None else None, sp, sf, p.shape[0], p.shape[1], kind,
+                    group["beta2"], group["eps"], group["lr"], 0, L.ptr(ws), ws.numel(), L.stream(dev))
+                L.check(rc, "rowwise_step (host table)")
+                torch.cuda.current_stream(dev).synchronize()
+        del keep
+        st.grad_scale = 1.0
+
     def zero_grad(self, set_to_none=True):
         pass                                   # the accumulator is cleared in step(), as in LazyRowAdam
 
@@ -69,15 +132,23 @@ class RowWiseOptimizer(torch.optim.Optimizer):
         return [p for g in self.param_groups for p in g["params"]]
 
     def flush(self):
-        """The reference writes the state of GPU-cached hot rows of a host-RAM table back into the per-row state
-        (row_optim.py:209-217); tables here live on the GPU whole and their state is always in the per-row tensors,
-        so there is nothing to write back."""
+        """Writes the state of the HOT rows of host-RAM tables (on the GPU, in slot order) back into the per-row
+        state of the whole table (reference: row_optim.py:209-217); tables on the GPU have nothing to write back."""
+        for p in self._params():
+            state, hot = self.state[p], getattr(row_store(p), "hot", None)
+            if hot is not None and "hot_v" in state:
+                rows = hot.rows.cpu()
+                state["v"].index_copy_(0, rows, state["hot_v"].cpu())
+                if "hot_n" in state:
+                    state["n"].index_copy_(0, rows, state["hot_n"].cpu())
 
     def state_dict(self):
+        """Every row's state in table order (HOT rows written back first), so it loads with or without HOT."""
+        self.flush()
         params = self._params()
         return {"format": "smlm.row_wise.v1", "kind": self.kind, "shapes": [list(p.shape) for p in params],
                 "param_groups": [{k: v for k, v in g.items() if k != "params"} for g in self.param_groups],
-                "state": [dict(self.state[p]) for p in params]}
+                "state": [{k: v for k, v in self.state[p].items() if not k.startswith("hot_")} for p in params]}
 
     def load_state_dict(self, state_dict):
         if state_dict.get("format") != "smlm.row_wise.v1" or state_dict.get("kind") != self.kind:

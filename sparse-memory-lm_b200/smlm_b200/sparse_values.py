@@ -121,9 +121,14 @@ class RowStore:
 
 
 def row_store(table):
-    """The RowStore attached to a (possibly shared) table parameter; created on first use."""
+    """The RowStore attached to a (possibly shared) table parameter; created on first use. A table in host RAM
+    (smlm_b200.host_values) gets a HostRowStore, or keeps the StepStore of its GACC step accumulator."""
     if getattr(table, "host_values", False):
-        raise NotImplementedError("host-RAM value tables (smlm/host_values.py) are not part of this build")
+        st = getattr(table, "row_store", None)
+        if st is None or (getattr(st, "steprows", None) is None and tuple(st.acc.shape) != tuple(table.shape)):
+            from .host_optim import HostRowStore
+            st = table.row_store = HostRowStore(table)
+        return st
     st = getattr(table, "row_store", None)
     if st is None or st._acc.device != table.device or st._acc.shape != table.shape:
         st = RowStore(table)

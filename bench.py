@@ -29,7 +29,8 @@ The default run also measures the B-16M inference token loop (`inference`: prefi
 B-16M model, per-token lookup latency). --case configs times BASELINE configs 1-4 as single layers (fwd / bwd /
 opt separately; config 2 also with the forward reading a bf16 copy of the fp32 table, config 4 with its inputs from a
 uniform + Zipf(1.1) token mix); --case model times BASELINE config 2 as stated, the B-1M model's training step;
---case scoring and --case inference run one part alone; --case engram times the Engram n-gram memory module.
+--case scoring and --case inference run one part alone; --case engram times the Engram n-gram memory module;
+--case host times the B-16M layer with its table in host RAM against the reference's own host-table path.
 """
 import argparse
 import json
@@ -68,14 +69,16 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows-per-half", type=int, default=1024)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
-    ap.add_argument("--case", choices=["layer", "scoring", "inference", "configs", "engram", "model"],
+    ap.add_argument("--case", choices=["layer", "scoring", "inference", "configs", "engram", "model", "host"],
                     default="layer",
                     help="scoring: only the fused sub-key scoring + selection of the workload's layer (a small "
                          "standalone case for profiler captures; prints its time per call); inference: only the "
                          "B-16M prefill / decode measurement; configs: BASELINE configs 1-4 as single layers "
                          "with fwd / bwd / opt timed separately (config 4 with a uniform + Zipf token mix); "
                          "model: BASELINE config 2, the B-1M model's training step; engram: the reference's "
-                         "default Engram module (hash, one-lookup bags, backward, lazy Adam) per step")
+                         "default Engram module (hash, one-lookup bags, backward, lazy Adam) per step; host: the "
+                         "B-16M layer with its table in host RAM, this build against the reference's own host "
+                         "path, per configuration (Adam, rowrms, rowrms + GACC, rowrms + HOT 5% + GACC)")
     ap.add_argument("--no-inference", action="store_true", help="leave the inference measurement out of the line")
     ap.add_argument("--eager", action="store_true",
                     help="time the step as eager calls (default on one GPU: the step captured as one CUDA graph)")
@@ -745,6 +748,229 @@ def run_engram(args):
                         for k, v in sorted(per.items())}}
 
 
+# ------------------------------------------------------------------------------------------- host-RAM tables
+# (name, table optimizer, GACC, HOT fraction): the reference's host-table configurations (its step-21 benchmark)
+HOST_CONFIGS = (("adam", "adam", False, 0.0), ("rowrms", "rowrms", False, 0.0), ("rowrms+gacc", "rowrms", True, 0.0),
+                ("rowrms+hot5%+gacc", "rowrms", True, 0.05))
+
+
+def _mem_available():
+    try:
+        return [int(ln.split()[1]) * 1024 for ln in open("/proc/meminfo") if ln.startswith("MemAvailable")][0]
+    except (OSError, IndexError):
+        return 0
+
+
+def _host_link_gbs(dev, nbytes=1 << 30):
+    """Pinned host <-> device copy bandwidth (GB/s) of this box, each direction: the denominators of the host path."""
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = {}
+    for name, fn in (("h2d", lambda: d.copy_(h, non_blocking=True)), ("d2h", lambda: h.copy_(d, non_blocking=True))):
+        fn()
+        out[name] = round(3 * nbytes / 1e9 / (_event_ms(fn, 3) / 1e3), 1)
+    return out
+
+
+def _host_layer(PKM, n_keys, table):
+    """The B-16M layer (config-1 layer: no BatchNorm / swilu) built on the meta device, its dense parameters then
+    materialised on the CPU with the config-1 initialisation (seed 0) and its value table set to `table` (a host
+    tensor shared by every configuration, so the 25.8 GB table is filled once)."""
+    from torch import nn
+    with torch.device("meta"):
+        mem = PKM(d_in=D_MODEL, d_out=D_MODEL, n_keys=n_keys, heads=HEADS, knn=KNN, k_dim=K_DIM,
+                  query_norm="none", swilu=False, value_grad="row_sparse")
+    mem.values.weight = nn.Parameter(table)
+    for mod in mem.modules():
+        for name, p in list(mod._parameters.items()):
+            if p is not None and p.is_meta:
+                mod._parameters[name] = nn.Parameter(torch.empty(p.shape, dtype=p.dtype), p.requires_grad)
+        for name, b in list(mod._buffers.items()):
+            if b is not None and b.is_meta:
+                mod._buffers[name] = torch.zeros(b.shape, dtype=b.dtype)
+    torch.manual_seed(0)
+    with torch.no_grad():
+        mem.query_proj.weight.normal_(0, 0.02)
+        mem.query_proj.bias.zero_()
+        mem.keys.normal_(0, (K_DIM // 2) ** -0.5)
+    return mem
+
+
+def _host_arm(ours):
+    """The host-table modules of one arm: this build's smlm_b200, or the reference's own smlm package as vendored,
+    unmodified, into baseline/_ref (None when it is absent)."""
+    if ours:
+        from smlm_b200 import host_optim, host_values, pkm, row_optim, sparse_values
+        return dict(PKM=pkm.ProductKeyMemory, hv=host_values, Adam=host_optim.HostLazyRowAdam,
+                    Row=row_optim.RowWiseOptimizer, clip=sparse_values.clip_row_sparse,
+                    row_store=sparse_values.row_store)
+    if not os.path.isfile(os.path.join(REF_PKG, "smlm", "host_values.py")):
+        return None
+    if REF_PKG not in sys.path:
+        sys.path.insert(0, REF_PKG)
+    from smlm import host_optim, host_values, pkm, row_optim, sparse_values
+    return dict(PKM=lambda **kw: pkm.ProductKeyMemory(impl="torch", **kw), hv=host_values,
+                Adam=host_optim.HostLazyRowAdam, Row=row_optim.RowWiseOptimizer, clip=sparse_values.clip_row_sparse,
+                row_store=sparse_values.row_store)
+
+
+def _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev, steps, warmup):
+    """One configuration of one arm: the layer step (bf16 autocast forward, backward, value clipping, the table
+    optimizer, fused AdamW on the dense parameters) with the table in host RAM; wall time per step with the device
+    synchronised on both sides (the host path is synchronous), median of `steps` after `warmup`, then one more
+    step with the staging phases timed (host_timings)."""
+    name, optim, gacc, hot = config
+    mem = _host_layer(arm["PKM"], n_keys, table)
+    arm["hv"].enable_host_values(mem)
+    mem.to(dev)
+    weight = mem.values.weight
+    if hot:
+        arm["hv"].enable_hot_rows(mem, reads, hot, dev)
+    if gacc:
+        arm["hv"].enable_step_rows(mem, capacity, dev)
+    dense = [p for p in mem.parameters() if p is not weight]
+    adamw = torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True)
+    topt = (arm["Adam"]([weight], lr=1e-3, betas=(0.9, 0.98), eps=1e-8) if optim == "adam"
+            else arm["Row"]([weight], lr=2.4e-3, kind="rowrms"))
+
+    def step(i):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = mem(xs[i % 2])
+        out.backward(gs[i % 2])
+        arm["clip"]([weight], 1.0)
+        torch.nn.utils.clip_grad_norm_([p for p in dense if p.grad is not None], 1.0, foreach=True)
+        adamw.step()
+        topt.step()
+        adamw.zero_grad(set_to_none=True)
+        topt.zero_grad(set_to_none=True)
+
+    for i in range(warmup):
+        step(i)
+    times = []
+    for i in range(steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        step(i)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    arm["hv"].host_timings(mem, reset=True)
+    mem.values.profile = True
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    step(steps)
+    torch.cuda.synchronize()
+    profiled = time.perf_counter() - t0
+    phases = arm["hv"].host_timings(mem, reset=True)
+    mem.values.profile = False
+    dt = statistics.median(times)
+    res = {"ms_per_step": round(dt * 1e3, 1), "tokens_per_s": round(xs[0].shape[0] / dt, 1),
+           "step_ms": [round(t * 1e3, 1) for t in times], "profiled_step_ms": round(profiled * 1e3, 1),
+           "phases_ms": {k: round(v * 1e3, 1) for k, v in phases.items()}}
+    if gacc:
+        res["gacc_peak_rows"] = int(mem.values.step_rows.peak)
+        res["gacc_spilled_steps"] = int(mem.values.step_rows.spilled_steps)
+    # drop everything this configuration allocated on the host before the next one (the shared table stays)
+    st = getattr(weight, "row_store", None)
+    if ours:
+        state = topt.state.get(weight, {})
+        arm["hv"].release(*[v for v in state.values() if torch.is_tensor(v)],
+                          getattr(st, "acc", None), getattr(st, "touched", None))
+    del mem, adamw, topt, weight, st, step
+    import gc
+    gc.collect()
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_host(args):
+    """BASELINE config 4's layer (--rows-per-half 4096: 16,777,216 x 384 fp32 table; 32,768 tokens per step, the
+    bench's default workload) with the value table in host RAM, one GPU: the reference's host-table configurations (Adam, rowrms,
+    rowrms + GACC, rowrms + HOT 5% + GACC) through this build's smlm_b200.host_values and, on the same box and
+    inputs, through the reference's own smlm.host_values (its C row loops on the host cores, stock PyTorch on the
+    GPU). HOT ranks rows by the read counts of the timed inputs (the best case, as the reference's own benchmark
+    of it). A configuration whose host RAM would not fit (with 16 GB to spare) is skipped.
+
+    `host_link` is this build's roofline: the table rows that must cross the host link per step, in each direction,
+    as multiples of the distinct rows U (Adam: in = gather + accumulator read by the add + the update's p, m, v,
+    accumulator = 6, out = add + p, m, v + accumulator cleared = 5, the clip norm from the rows' squared norms that
+    the add kept on the GPU; rowrms: 4 in, 3 out, plus the row state;
+    GACC: 1 in (the gather), 1 out (the updated rows); HOT rows never cross), over the measured pinned copy
+    bandwidths, taken one direction after the other; frac = that time / the measured step."""
+    from smlm_b200.pkm import ProductKeyMemory as OurPKM
+    dev = torch.device("cuda", 0)
+    n_keys, N = args.rows_per_half, args.tokens
+    rows = n_keys ** 2
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    table = torch.empty(rows, D_MODEL, dtype=torch.float32)
+    gen = torch.Generator(device=dev).manual_seed(11)
+    chunk = 1 << 20
+    for a in range(0, rows, chunk):                     # N(0, 384^-0.5), generated on the GPU in 1M-row chunks
+        table[a:a + chunk].copy_(torch.randn(min(chunk, rows - a), D_MODEL, device=dev, generator=gen)
+                                 * D_MODEL ** -0.5)
+    xs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(2)]
+    gs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(2)]
+    # read counts and distinct rows per step of the timed inputs, from the layer's own selection
+    # (the query projection and the selection of the same layer: same seed, so the rows the timed steps' first
+    # forwards read)
+    probe = _host_layer(OurPKM, n_keys, torch.empty(1, D_MODEL))
+    probe.query_proj.to(dev)
+    keys = probe.keys.detach().to(dev)
+    reads = torch.zeros(rows, dtype=torch.int64, device=dev)
+    distinct = []
+    from smlm_b200 import kernels as K
+    with torch.no_grad():
+        for x in xs:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                q = probe.query_proj.to(dev)(x).view(N, HEADS, K_DIM)
+            _, idx, _ = K.score_select(q.bfloat16(), keys.bfloat16(), KNN)
+            reads += torch.bincount(idx.reshape(-1), minlength=rows)
+            distinct.append(int(torch.unique(idx).numel()))
+    del probe, keys
+    capacity = int(max(distinct) * 1.05)
+    hot_rows = int(round(0.05 * rows))
+    hot_share = float(reads.sort(descending=True).values[:hot_rows].sum() / reads.sum())
+    reads = reads.cpu()
+    link = _host_link_gbs(dev)
+    out = {"case": "host", "workload": f"pkm-layer-{rows}-rows-host-table", "rows": rows, "v_dim": D_MODEL, "tokens": N,
+           "lookups_per_step": N * HEADS * KNN, "distinct_rows_per_step": distinct, "gacc_capacity": capacity,
+           "hot_read_share": round(hot_share, 4), "host_link_gbs": link,
+           "host": f"{_cpu_name()}, {threads} threads, {round(_mem_available() / 2**30)} GiB available",
+           "steps": args.steps, "warmup": args.warmup, "configs": {}}
+    table_gb = rows * D_MODEL * 4
+    for config in HOST_CONFIGS:
+        name, optim, gacc, hot = config
+        need = (0 if gacc else table_gb) + (2 * table_gb if optim == "adam" else 0) + (16 << 30)
+        entry = out["configs"][name] = {}
+        for label, ours in (("reference", False), ("this_build", True)):
+            arm = _host_arm(ours)
+            if arm is None:
+                entry[label] = {"unavailable": "the reference package is not in baseline/_ref"}
+                continue
+            if _mem_available() < need:
+                entry[label] = {"skipped": f"needs {need / 2**30:.0f} GiB of host RAM"}
+                continue
+            entry[label] = _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev,
+                                        args.steps, args.warmup)
+        ours = entry.get("this_build", {})
+        if "ms_per_step" in ours:
+            # the host-link roofline of this build's step: the rows' bytes that must cross the link each way
+            # (U distinct rows in host RAM per step, rows of 4 * v_dim bytes) over the measured copy bandwidths
+            u = ours.get("gacc_peak_rows", statistics.mean(distinct))
+            rb = D_MODEL * 4
+            rows_in, rows_out = {"adam": (6, 5), "rowrms": (4, 3)}.get(name, (1, 1))
+            per_row_state = 8 if optim == "rowrms" else 0           # v and n of the row-wise state, each way
+            gb_in, gb_out = u * (rows_in * rb + per_row_state) / 1e9, u * (rows_out * rb + per_row_state) / 1e9
+            bound = (gb_in / link["h2d"] + gb_out / link["d2h"]) * 1e3
+            ours["host_link"] = {"rows_in_per_row": rows_in, "rows_out_per_row": rows_out, "gb_in": round(gb_in, 2),
+                                 "gb_out": round(gb_out, 2), "bound_ms": round(bound, 1),
+                                 "frac": round(bound / ours["ms_per_step"], 3)}
+        if "ms_per_step" in entry.get("reference", {}) and "ms_per_step" in ours:
+            entry["speedup"] = round(entry["reference"]["ms_per_step"] / ours["ms_per_step"], 2)
+        print(json.dumps({"case": "host", "config": name, **entry}), flush=True)
+    return out
+
+
 # ------------------------------------------------------------------------------------------- inference
 def _event_ms(fn, reps):
     """Device time of `reps` calls of fn (CUDA events on the current stream, synchronised on both sides)."""
@@ -983,6 +1209,9 @@ def main():
         return
     if args.case == "model":
         print(json.dumps(run_model_case(args)), flush=True)
+        return
+    if args.case == "host":
+        print(json.dumps(run_host(args)), flush=True)
         return
     if args.case == "inference":
         print(json.dumps({"case": "inference", **run_inference(args, 0)}), flush=True)

@@ -414,21 +414,26 @@ SMLM_API int smlm_host_rows_gather(const float *table, int64_t table_rows, const
 
 /* acc[rows[i]] = acc[rows[i]] + grads[i] and touched[rows[i]] = 1 (acc / touched: mapped host tensors of
  * table_rows rows; grads device (n, d) fp32; rows device int64, distinct), skipping the rows whose skip[i] >= 0
- * (skip may be NULL; HOT rows keep their own accumulator on the device). Replaces HostEmbedding.accumulate's copy
- * to the host and C scatter-add (host_values.py:121-150, host_rows.c host_rows_add). */
-SMLM_API int smlm_host_rows_add(float *acc, uint8_t *touched, int64_t table_rows, const int64_t *rows,
-                                const float *grads, const int32_t *skip, int64_t n, int64_t d, int *status,
-                                void *stream);
+ * (skip may be NULL; HOT rows keep their own accumulator on the device). row_sqnorm: NULL, or a device fp32 array
+ * of table_rows entries that gets each added row's new squared L2 norm (the row_sqnorm input of
+ * smlm_touched_norm). Replaces HostEmbedding.accumulate's copy to the host and C scatter-add
+ * (host_values.py:121-150, host_rows.c host_rows_add) and HostRowStore.norm's pass over the accumulator rows
+ * (host_optim.py:95-107). */
+SMLM_API int smlm_host_rows_add(float *acc, uint8_t *touched, float *row_sqnorm, int64_t table_rows,
+                                const int64_t *rows, const float *grads, const int32_t *skip, int64_t n, int64_t d,
+                                int *status, void *stream);
 
 /* The row-wise step (kind SMLM_ROWRMS / SMLM_ROWADAGRAD; smlm_rowwise_step's formulas, order and rounding) of the
  * distinct rows rows[i] (device int64) with gradient grads[i] (device (n, d) fp32, e.g. a step's row sums kept on
  * the GPU), times the clip factor (*grad_scale_dev when given, else grad_scale); param, v and count may be mapped
- * host memory. Replaces RowWiseOptimizer._step_gacc's chunked copies to the host and C loop
- * (row_optim.py:73-135, host_rows.c host_rows_rowwise). */
+ * host memory. current: NULL, or the rows' current values (device (n, d) fp32, equal to param's rows, e.g. the
+ * rows the forward gathered), read instead of param, which is then only written. Replaces
+ * RowWiseOptimizer._step_gacc's chunked copies to the host and C loop (row_optim.py:73-135, host_rows.c
+ * host_rows_rowwise). */
 SMLM_API int smlm_rows_rowwise_step(float *param, int64_t table_rows, const int64_t *rows, const float *grads,
-                                    int64_t n, int64_t d, float *v, int32_t *count, int kind, float beta2, float eps,
-                                    float lr, const float *grad_scale_dev, float grad_scale, int *status,
-                                    void *stream);
+                                    const float *current, int64_t n, int64_t d, float *v, int32_t *count, int kind,
+                                    float beta2, float eps, float lr, const float *grad_scale_dev, float grad_scale,
+                                    int *status, void *stream);
 
 /* ------------------------------------------------------------------------------------- Engram n-gram rows
  * Row indices of an Engram module's lookups: for position t of sequence b and lookup (order o, head h), the XOR over

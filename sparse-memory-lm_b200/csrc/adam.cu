@@ -294,7 +294,7 @@ struct RowArgs {
 };
 
 // Formulas and rounding of the reference C loop (host_rows.c:84-117): q summed in double, row state in fp32.
-template <int VEC>
+template <int VEC, int NC>
 __global__ void __launch_bounds__(256) rowwise_kernel(RowArgs a) {
     const int lane = lane_id();
     const int n = *a.count;
@@ -303,24 +303,8 @@ __global__ void __launch_bounds__(256) rowwise_kernel(RowArgs a) {
     for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
         const int64_t r = a.list[i];
         const int64_t base = r * a.d;
-        double q = 0.0;
-        for (int c = lane * VEC; c < a.d; c += 32 * VEC) {
-#pragma unroll
-            for (int t = 0; t < VEC; t++) {
-                const float gk = __fmul_rn(a.acc[base + c + t], scale);
-                q = fma((double)gk, (double)gk, q);
-            }
-        }
-        q = warp_sum_d(q) / (double)a.d;
-        const float step = rowwise_state_step(a.kind, a.b2, a.eps, a.lr, a.v, a.count_state, r, q, lane);
-        for (int c = lane * VEC; c < a.d; c += 32 * VEC) {
-#pragma unroll
-            for (int t = 0; t < VEC; t++) {
-                const float gk = __fmul_rn(a.acc[base + c + t], scale);
-                a.p[base + c + t] = __fsub_rn(a.p[base + c + t], __fmul_rn(step, gk));
-                if (!a.keep_acc) a.acc[base + c + t] = 0.f;
-            }
-        }
+        rowwise_row<VEC, NC>(a.acc + base, !a.keep_acc, a.p + base, a.p + base, a.d, scale, a.kind, a.b2, a.eps,
+                             a.lr, a.v, a.count_state, r, lane);
         __syncwarp();
         if (lane == 0) a.touched[r] = 0;
     }
@@ -488,8 +472,16 @@ extern "C" int smlm_rowwise_step(float* param, float* acc, uint8_t* touched, flo
     RowArgs a{param,      acc,         v,     count, touched, b.list, b.count, grad_scale_dev, grad_scale, (int)d,
               kind,       b2,          eps,   lr,    (flags & SMLM_STEP_KEEP_ACC) ? 1 : 0};
     const int blocks = persistent_blocks(8, 8);
-    if (d % 4 == 0) rowwise_kernel<4><<<blocks, 256, 0, st>>>(a);
-    else rowwise_kernel<1><<<blocks, 256, 0, st>>>(a);
+    const bool vec = d % 4 == 0 && reinterpret_cast<uintptr_t>(param) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(acc) % 16 == 0;
+    switch (vec ? rowwise_groups(d) : -1) {
+        case 1: rowwise_kernel<4, 1><<<blocks, 256, 0, st>>>(a); break;
+        case 2: rowwise_kernel<4, 2><<<blocks, 256, 0, st>>>(a); break;
+        case 3: rowwise_kernel<4, 3><<<blocks, 256, 0, st>>>(a); break;
+        case 4: rowwise_kernel<4, 4><<<blocks, 256, 0, st>>>(a); break;
+        case 0: rowwise_kernel<4, 0><<<blocks, 256, 0, st>>>(a); break;
+        default: rowwise_kernel<1, 0><<<blocks, 256, 0, st>>>(a); break;
+    }
     SMLM_LAUNCHED("rowwise_kernel");
     return SMLM_OK;
 }

@@ -170,6 +170,79 @@ __device__ __forceinline__ float rowwise_state_step(int kind, float b2, float ep
     return __fdiv_rn(lr, denom);
 }
 
+// One row of the row-wise step, by one warp: q = mean of (g * sc)^2, summed in double over each lane's groups of VEC
+// consecutive columns (lane * VEC + 32 * VEC * k, in column order) and then across the warp; the state step; then
+// dst[c] = src[c] - step * (g[c] * sc), and g's row set to 0 when zero_g. VEC == 4 moves the rows with 16-byte
+// accesses (g, src, dst 16-byte aligned, d % 4 == 0), which matters most when a row lives in mapped host memory
+// (one request per 16 bytes instead of four); with NC > 0 (d <= 128 * NC) each lane keeps its NC float4 groups of g
+// in registers between the two passes, so g is read once. Same operations in the same order for every VEC / NC.
+template <int VEC, int NC>
+__device__ __forceinline__ void rowwise_row(const float* g, bool zero_g, const float* src, float* dst, int d, float sc,
+                                            int kind, float b2, float eps, float lr, float* v, int32_t* count,
+                                            int64_t r, int lane) {
+    double q = 0.0;
+    if constexpr (VEC == 4) {
+        float4 gc[NC > 0 ? NC : 1];
+        if constexpr (NC > 0) {
+#pragma unroll
+            for (int k = 0; k < NC; k++) {
+                const int c = lane * 4 + 128 * k;
+                if (c < d) gc[k] = *reinterpret_cast<const float4*>(g + c);
+            }
+        }
+        auto sq = [&](const float4 x) {
+            const float g0 = __fmul_rn(x.x, sc), g1 = __fmul_rn(x.y, sc), g2 = __fmul_rn(x.z, sc),
+                        g3 = __fmul_rn(x.w, sc);
+            q = fma((double)g0, (double)g0, q);
+            q = fma((double)g1, (double)g1, q);
+            q = fma((double)g2, (double)g2, q);
+            q = fma((double)g3, (double)g3, q);
+        };
+        if constexpr (NC > 0) {
+#pragma unroll
+            for (int k = 0; k < NC; k++)
+                if (lane * 4 + 128 * k < d) sq(gc[k]);
+        } else {
+            for (int c = lane * 4; c < d; c += 128) sq(*reinterpret_cast<const float4*>(g + c));
+        }
+        q = warp_sum_d(q) / (double)d;
+        const float step = rowwise_state_step(kind, b2, eps, lr, v, count, r, q, lane);
+        auto upd = [&](const int c, const float4 x) {
+            float4 p = *reinterpret_cast<const float4*>(src + c);
+            p.x = __fsub_rn(p.x, __fmul_rn(step, __fmul_rn(x.x, sc)));
+            p.y = __fsub_rn(p.y, __fmul_rn(step, __fmul_rn(x.y, sc)));
+            p.z = __fsub_rn(p.z, __fmul_rn(step, __fmul_rn(x.z, sc)));
+            p.w = __fsub_rn(p.w, __fmul_rn(step, __fmul_rn(x.w, sc)));
+            *reinterpret_cast<float4*>(dst + c) = p;
+            if (zero_g) *reinterpret_cast<float4*>(const_cast<float*>(g) + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+        };
+        if constexpr (NC > 0) {
+#pragma unroll
+            for (int k = 0; k < NC; k++) {
+                const int c = lane * 4 + 128 * k;
+                if (c < d) upd(c, gc[k]);
+            }
+        } else {
+            for (int c = lane * 4; c < d; c += 128) upd(c, *reinterpret_cast<const float4*>(g + c));
+        }
+    } else {
+        for (int c = lane; c < d; c += 32) {
+            const float gk = __fmul_rn(g[c], sc);
+            q = fma((double)gk, (double)gk, q);
+        }
+        q = warp_sum_d(q) / (double)d;
+        const float step = rowwise_state_step(kind, b2, eps, lr, v, count, r, q, lane);
+        for (int c = lane; c < d; c += 32) {
+            const float gk = __fmul_rn(g[c], sc);
+            dst[c] = __fsub_rn(src[c], __fmul_rn(step, gk));
+            if (zero_g) const_cast<float*>(g)[c] = 0.f;
+        }
+    }
+}
+
+// The register groups rowwise_row keeps per lane for width d (0: d > 512, g read twice).
+inline int rowwise_groups(int64_t d) { return d <= 128 ? 1 : d <= 256 ? 2 : d <= 384 ? 3 : d <= 512 ? 4 : 0; }
+
 // Vector loads of VEC elements (fp32 or bf16) widened to fp32 (16-byte / 8-byte loads for VEC == 4).
 template <typename T>
 struct Elt;

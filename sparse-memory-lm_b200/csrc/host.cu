@@ -6,9 +6,10 @@
 //   * smlm_host_rows_gather: the distinct rows a forward reads, from the mapped table (or, for HOT rows, from their
 //     device copies) into a device tensor that the bag kernels then read;
 //   * smlm_host_rows_add: a backward's per-row gradient sums (device) added into the mapped accumulator rows,
-//     touched marks set;
+//     touched marks set, and the rows' squared norms kept on the device for the clip norm;
 //   * smlm_rows_rowwise_step: the row-wise optimizer (rowrms / rowadagrad) over a list of rows with their gradients
-//     in a device tensor (GACC: the step's gradient sums kept on the GPU), table and state anywhere mapped.
+//     in a device tensor (GACC: the step's gradient sums kept on the GPU) and, optionally, their current values in
+//     another (the rows the forward gathered), table and state anywhere mapped: the table is then only written.
 // The per-row optimizer steps over the mapped accumulator reuse smlm_lazy_adam_step, smlm_lazy_adam_lowmem_step and
 // smlm_rowwise_step unchanged (their pointers may be mapped host memory).
 #include "common.cuh"
@@ -41,8 +42,10 @@ __global__ void __launch_bounds__(256) host_gather_kernel(const float* table, co
     }
 }
 
-// acc[rows[i]] = acc[rows[i]] + grads[i], touched[rows[i]] = 1, for the rows with skip[i] < 0 (rows distinct).
-__global__ void __launch_bounds__(256) host_add_kernel(float* acc, uint8_t* touched, const int64_t* rows,
+// acc[rows[i]] = acc[rows[i]] + grads[i], touched[rows[i]] = 1, for the rows with skip[i] < 0 (rows distinct); with
+// row_sq, also row_sq[rows[i]] = the new row's squared L2 norm (summed in double, stored fp32), so the clip norm
+// needs no second pass over the accumulator rows.
+__global__ void __launch_bounds__(256) host_add_kernel(float* acc, uint8_t* touched, float* row_sq, const int64_t* rows,
                                                        const float* grads, const int32_t* skip, int64_t n,
                                                        int64_t table_rows, int d, int* status) {
     const int lane = lane_id();
@@ -56,24 +59,34 @@ __global__ void __launch_bounds__(256) host_add_kernel(float* acc, uint8_t* touc
         }
         float* dst = acc + r * d;
         const float* src = grads + i * d;
+        double sq = 0.0;
         for (int c = lane * 4; c < d; c += 128) {
             float4 a = *reinterpret_cast<float4*>(dst + c);
             const float4 g = *reinterpret_cast<const float4*>(src + c);
             a.x = a.x + g.x; a.y = a.y + g.y; a.z = a.z + g.z; a.w = a.w + g.w;
             *reinterpret_cast<float4*>(dst + c) = a;
+            sq = fma((double)a.x, (double)a.x, sq);
+            sq = fma((double)a.y, (double)a.y, sq);
+            sq = fma((double)a.z, (double)a.z, sq);
+            sq = fma((double)a.w, (double)a.w, sq);
+        }
+        if (row_sq) {
+            sq = warp_sum_d(sq);
+            if (lane == 0) row_sq[r] = (float)sq;
         }
         if (lane == 0 && touched) touched[r] = 1;
     }
 }
 
 // The row-wise step of rows[i] with gradient grads[i] (a device tensor of the step's row sums): rowwise_kernel's
-// arithmetic in rowwise_kernel's order (q summed in double over each lane's VEC-column groups, then across the
-// warp; rowwise_state_step; p -= step * g * scale), one warp per row; rows distinct.
-template <int VEC>
+// arithmetic in rowwise_kernel's order (rowwise_row), one warp per row; rows distinct. The row's current values
+// come from current[i] when given (the copy the forward gathered onto the device, so the table is only written)
+// and from the table otherwise.
+template <int VEC, int NC>
 __global__ void __launch_bounds__(256) rows_rowwise_kernel(float* p, const int64_t* rows, const float* grads,
-                                                           int64_t n, int64_t table_rows, int d, float* row_v,
-                                                           int32_t* row_count, int kind, float b2, float eps,
-                                                           float lr, const float* scale_dev, float scale,
+                                                           const float* current, int64_t n, int64_t table_rows, int d,
+                                                           float* row_v, int32_t* row_count, int kind, float b2,
+                                                           float eps, float lr, const float* scale_dev, float scale,
                                                            int* status) {
     const int lane = lane_id();
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -84,23 +97,9 @@ __global__ void __launch_bounds__(256) rows_rowwise_kernel(float* p, const int64
             if (lane == 0) flag(status, SMLM_FLAG_INDEX_RANGE);
             continue;
         }
-        const float* g = grads + i * d;
-        double q = 0.0;
-        for (int c = lane * VEC; c < d; c += 32 * VEC) {
-#pragma unroll
-            for (int t = 0; t < VEC; t++) {
-                const float gk = __fmul_rn(g[c + t], sc);
-                q = fma((double)gk, (double)gk, q);
-            }
-        }
-        q = warp_sum_d(q) / (double)d;
-        const float step = rowwise_state_step(kind, b2, eps, lr, row_v, row_count, r, q, lane);
         float* pr = p + r * d;
-        for (int c = lane * VEC; c < d; c += 32 * VEC) {
-#pragma unroll
-            for (int t = 0; t < VEC; t++)
-                pr[c + t] = __fsub_rn(pr[c + t], __fmul_rn(step, __fmul_rn(g[c + t], sc)));
-        }
+        rowwise_row<VEC, NC>(grads + i * d, false, current ? current + i * d : pr, pr, d, sc, kind, b2, eps, lr, row_v,
+                             row_count, r, lane);
     }
 }
 
@@ -140,37 +139,46 @@ extern "C" int smlm_host_rows_gather(const float* table, int64_t table_rows, con
     return SMLM_OK;
 }
 
-extern "C" int smlm_host_rows_add(float* acc, uint8_t* touched, int64_t table_rows, const int64_t* rows,
-                                  const float* grads, const int32_t* skip, int64_t n, int64_t d, int* status,
-                                  void* stream) {
+extern "C" int smlm_host_rows_add(float* acc, uint8_t* touched, float* row_sqnorm, int64_t table_rows,
+                                  const int64_t* rows, const float* grads, const int32_t* skip, int64_t n, int64_t d,
+                                  int* status, void* stream) {
     SMLM_CHECK_ARG(n >= 0 && table_rows >= 0 && d > 0 && d % 4 == 0, "host_rows_add: bad sizes (d %% 4 == 0)");
     if (n == 0) return SMLM_OK;
     SMLM_CHECK_ARG(acc && rows && grads, "host_rows_add: null pointer");
     SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(acc) % 16 == 0 && reinterpret_cast<uintptr_t>(grads) % 16 == 0,
                    "host_rows_add: acc and grads must be 16-byte aligned");
-    host_add_kernel<<<host_rows_blocks(n), 256, 0, as_stream(stream)>>>(acc, touched, rows, grads, skip, n, table_rows,
-                                                                       (int)d, status);
+    host_add_kernel<<<host_rows_blocks(n), 256, 0, as_stream(stream)>>>(acc, touched, row_sqnorm, rows, grads, skip, n,
+                                                                       table_rows, (int)d, status);
     SMLM_LAUNCHED("host_add_kernel");
     return SMLM_OK;
 }
 
 extern "C" int smlm_rows_rowwise_step(float* param, int64_t table_rows, const int64_t* rows, const float* grads,
-                                      int64_t n, int64_t d, float* row_v, int32_t* row_count, int kind, float beta2,
-                                      float eps, float lr, const float* grad_scale_dev, float grad_scale, int* status,
-                                      void* stream) {
+                                      const float* current, int64_t n, int64_t d, float* row_v, int32_t* row_count,
+                                      int kind, float beta2, float eps, float lr, const float* grad_scale_dev,
+                                      float grad_scale, int* status, void* stream) {
     SMLM_CHECK_ARG(n >= 0 && table_rows >= 0 && d > 0, "rows_rowwise_step: bad sizes");
     SMLM_CHECK_ARG(kind == SMLM_ROWRMS || kind == SMLM_ROWADAGRAD, "rows_rowwise_step: unknown kind %d", kind);
     SMLM_CHECK_ARG(kind != SMLM_ROWRMS || row_count != nullptr, "rows_rowwise_step: rowrms needs the row counts");
     if (n == 0) return SMLM_OK;
     SMLM_CHECK_ARG(param && rows && grads && row_v, "rows_rowwise_step: null pointer");
-    if (d % 4 == 0)
-        rows_rowwise_kernel<4><<<host_rows_blocks(n), 256, 0, as_stream(stream)>>>(
-            param, rows, grads, n, table_rows, (int)d, row_v, row_count, kind, beta2, eps, lr, grad_scale_dev,
-            grad_scale, status);
-    else
-        rows_rowwise_kernel<1><<<host_rows_blocks(n), 256, 0, as_stream(stream)>>>(
-            param, rows, grads, n, table_rows, (int)d, row_v, row_count, kind, beta2, eps, lr, grad_scale_dev,
-            grad_scale, status);
+    auto aligned = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    const bool vec = d % 4 == 0 && aligned(param) && aligned(grads) && aligned(current);
+    const int blocks = host_rows_blocks(n);
+    cudaStream_t st = as_stream(stream);
+#define SMLM_ROWS_ROWWISE(V, G)                                                                                    \
+    rows_rowwise_kernel<V, G><<<blocks, 256, 0, st>>>(param, rows, grads, current, n, table_rows, (int)d, row_v,     \
+                                                     row_count, kind, beta2, eps, lr, grad_scale_dev, grad_scale,  \
+                                                     status)
+    switch (vec ? rowwise_groups(d) : -1) {
+        case 1: SMLM_ROWS_ROWWISE(4, 1); break;
+        case 2: SMLM_ROWS_ROWWISE(4, 2); break;
+        case 3: SMLM_ROWS_ROWWISE(4, 3); break;
+        case 4: SMLM_ROWS_ROWWISE(4, 4); break;
+        case 0: SMLM_ROWS_ROWWISE(4, 0); break;
+        default: SMLM_ROWS_ROWWISE(1, 0); break;
+    }
+#undef SMLM_ROWS_ROWWISE
     SMLM_LAUNCHED("rows_rowwise_kernel");
     return SMLM_OK;
 }

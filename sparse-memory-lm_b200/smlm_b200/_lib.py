@@ -93,8 +93,8 @@ SIGNATURES = {
     "smlm_host_register": (_i32, [_p, _sz, _p]),
     "smlm_host_unregister": (_i32, [_p]),
     "smlm_host_rows_gather": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _p, _p, _p]),
-    "smlm_host_rows_add": (_i32, [_p, _p, _i64, _p, _p, _p, _i64, _i64, _p, _p]),
-    "smlm_rows_rowwise_step": (_i32, [_p, _i64, _p, _p, _i64, _i64, _p, _p, _i32, _f32, _f32, _f32, _p, _f32, _p,
+    "smlm_host_rows_add": (_i32, [_p, _p, _p, _i64, _p, _p, _p, _i64, _i64, _p, _p]),
+    "smlm_rows_rowwise_step": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _p, _p, _i32, _f32, _f32, _f32, _p, _f32, _p,
                                       _p]),
 }
 

@@ -19,7 +19,9 @@ from .sparse_values import LazyRowAdam, row_store
 class HostRowStore:
     """The gradient store of a host table (reference: host_optim.py:78-107): `acc` (fp32, shaped like the table)
     and `touched` in host RAM, the deferred clip factor `grad_scale`, and `hot` (the table's HOT rows, which keep
-    their own accumulator on the GPU)."""
+    their own accumulator on the GPU). `row_sq` (no counterpart): the touched rows' squared norms on the GPU, written
+    by HostEmbedding.accumulate's add kernel, so norm() does not read the accumulator rows back over the host link;
+    code that writes `acc` by other means sets it to None (norm() then reads the rows)."""
 
     def __init__(self, table):
         if table.device.type != "cpu":
@@ -28,6 +30,13 @@ class HostRowStore:
         self.touched = torch.zeros(table.shape[0], dtype=torch.bool)
         self.grad_scale = 1.0
         self.hot = getattr(table, "hot_rows", None)
+        self.row_sq = None
+
+    def sq_buffer(self, device):
+        """The device array of per-row squared norms (created on first use)."""
+        if self.row_sq is None or self.row_sq.device != device:
+            self.row_sq = torch.empty(self.acc.shape[0], dtype=torch.float32, device=device)
+        return self.row_sq
 
     def sync(self):
         pass
@@ -44,15 +53,21 @@ class HostRowStore:
 
     def norm(self, device=None):
         """The accumulator's L2 norm over the touched rows (and the HOT rows'), as a device fp32 scalar, computed
-        by the touched-norm kernel over the mapped accumulator."""
+        by the touched-norm kernel from the rows' squared norms on the GPU (or over the mapped accumulator)."""
         if device is None:
-            device = self.hot.acc.device if self.hot is not None else torch.device("cuda", torch.cuda.current_device())
+            if self.row_sq is not None:
+                device = self.row_sq.device
+            elif self.hot is not None:
+                device = self.hot.acc.device
+            else:
+                device = torch.device("cuda", torch.cuda.current_device())
         rows, d = self.acc.shape
+        sq = self.row_sq if self.row_sq is not None and self.row_sq.device == device else None
         out = torch.empty((), dtype=torch.float32, device=device)
         ws = L.workspace(L.lib().smlm_touched_workspace(rows), device)
         with torch.cuda.device(device):
-            rc = L.lib().smlm_touched_norm(mapped(self.acc), None, mapped(self.touched), rows, d, L.ptr(out),
-                                           L.ptr(ws), ws.numel(), L.stream(device))
+            rc = L.lib().smlm_touched_norm(mapped(self.acc) if sq is None else None, L.ptr(sq), mapped(self.touched),
+                                           rows, d, L.ptr(out), L.ptr(ws), ws.numel(), L.stream(device))
         L.check(rc, "touched_norm")
         if self.hot is not None:
             out = torch.linalg.vector_norm(torch.stack([out, self.hot.acc.norm()]))

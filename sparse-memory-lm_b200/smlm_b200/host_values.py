@@ -16,12 +16,16 @@ the library's kernels move the rows over the host link themselves:
             sets their touched marks (HOT rows into their device accumulator; with GACC into the step's slots on
             the GPU instead of the host accumulator);
   step      the optimizers' kernels update the touched rows in place in the mapped table and state
-            (smlm_b200.host_optim.HostLazyRowAdam, RowWiseOptimizer); nothing is copied back.
+            (smlm_b200.host_optim.HostLazyRowAdam, RowWiseOptimizer); nothing is copied back. With GACC the step's
+            slots also keep the rows as the forward gathered them, so the row-wise step reads them on the GPU and
+            only writes the host table.
 
-So per step only the rows read cross the host link (once each way for the optimizer), and no CPU thread touches
-them. The calls that write host memory synchronise the stream before returning (CPU code may read that memory
-next), which also makes this path, like the reference's, not capturable in a CUDA graph. Rows need a width that is
-a multiple of 4 values. Host tensors stay registered (and alive) for the life of the process.
+So per step only the rows read cross the host link (in for the forward, then once each way for the optimizer,
+or only out with GACC), with 16-byte accesses, and no CPU thread touches them; the add kernel also keeps each
+row's squared norm on the GPU, so clipping reads no accumulator rows back. The calls that write host memory
+synchronise the stream before returning (CPU code may read that memory next), which also makes this path, like
+the reference's, not capturable in a CUDA graph. Rows need a width that is a multiple of 4 values. Host tensors
+stay registered (and alive) until release() unmaps them.
 """
 import ctypes
 import time
@@ -42,7 +46,7 @@ _MAPPED = {}        # host storage address -> (bytes, device address, storage ke
 
 def mapped(t):
     """The device address of a CPU tensor's data: its storage is page-locked and mapped into the device's address
-    space on first use (smlm_host_register) and stays so, and alive, for the rest of the process."""
+    space on first use (smlm_host_register) and stays so, and alive, until release() (or the end of the process)."""
     if t.device.type != "cpu":
         raise ValueError("mapped() takes host (CPU) tensors")
     storage = t.untyped_storage()
@@ -56,6 +60,18 @@ def mapped(t):
                 "host_register")
         hit = _MAPPED[base] = (nbytes, dev.value, storage)
     return ctypes.c_void_p(hit[1] + (t.data_ptr() - base))
+
+
+def release(*tensors):
+    """Unmaps the storages of host tensors mapped by mapped() and drops the references that kept them alive, so
+    that they are freed with their last owner. No kernel may still use them: call after the stream that last
+    touched them has been synchronised."""
+    for t in tensors:
+        if t is None or not torch.is_tensor(t) or t.device.type != "cpu":
+            continue
+        hit = _MAPPED.pop(t.untyped_storage().data_ptr(), None)
+        if hit is not None:
+            L.check(L.lib().smlm_host_unregister(ctypes.c_void_p(t.untyped_storage().data_ptr())), "host_unregister")
 
 
 def _sync(device):
@@ -118,9 +134,10 @@ class HostEmbedding(nn.Embedding):
             L.after(dev, "host_rows_gather")
         return rows, remapped.view_as(indices), values, slot
 
-    def accumulate(self, rows, gradient, slot=None):
+    def accumulate(self, rows, gradient, slot=None, values=None):
         """Adds each distinct row's gradient sum (device (U, d)) into its accumulator: the step's slots on the GPU
-        (GACC), the HOT accumulator on the GPU, or the mapped host accumulator."""
+        (GACC; `values`, the rows as the forward gathered them, go into the slots too), the HOT accumulator on the
+        GPU, or the mapped host accumulator."""
         dev = gradient.device
         hot = slot is not None
         if hot:
@@ -133,16 +150,17 @@ class HostEmbedding(nn.Embedding):
             with self.phase("scatter", dev):
                 if hot:
                     cold = (slot < 0).nonzero().squeeze(1)
-                    self.step_rows.add(rows.index_select(0, cold), gradient.index_select(0, cold))
+                    self.step_rows.add(rows.index_select(0, cold), gradient.index_select(0, cold),
+                                       values.index_select(0, cold) if values is not None else None)
                 else:
-                    self.step_rows.add(rows, gradient)
+                    self.step_rows.add(rows, gradient, values)
             return
         from .sparse_values import row_store
         st = row_store(self.weight)
         with self.phase("scatter", dev):
-            rc = L.lib().smlm_host_rows_add(mapped(st.acc), mapped(st.touched), st.acc.shape[0], L.ptr(rows),
-                                            L.ptr(gradient.contiguous()), L.ptr(slot), rows.numel(),
-                                            gradient.shape[1], L.status_ptr(dev), L.stream(dev))
+            rc = L.lib().smlm_host_rows_add(mapped(st.acc), mapped(st.touched), L.ptr(st.sq_buffer(dev)),
+                                            st.acc.shape[0], L.ptr(rows), L.ptr(gradient.contiguous()), L.ptr(slot),
+                                            rows.numel(), gradient.shape[1], L.status_ptr(dev), L.stream(dev))
             L.check(rc, "host_rows_add")
             _sync(dev)                     # the host accumulator is complete before CPU code reads it
         L.after(dev, "host_rows_add")
@@ -185,7 +203,7 @@ class _HostBag(torch.autograd.Function):
             acc = torch.zeros_like(values)
             touched = torch.zeros(values.shape[0], dtype=torch.bool, device=values.device)
             gw = K.bag_backward_rows(g, indices, w, values, acc, touched)
-            ctx.owner.accumulate(rows, acc, slot)
+            ctx.owner.accumulate(rows, acc, slot, values)
         else:
             gw = K.bag_backward_rows(g, indices, w, values, None, None)
         ctx.owner = None
@@ -242,20 +260,25 @@ class StepRows:
     """GACC: the gradient sums of the host-table rows read in the current step, on the GPU, in up to `capacity`
     slots (a row takes the next free slot when it is first read in the step; later reads add into it). Rows read
     after every slot is taken (overflow) keep their gradients on the host, summed per row before the step, so a
-    step that reads more rows than the capacity is slower, not wrong (reference: host_values.py:253-316)."""
+    step that reads more rows than the capacity is slower, not wrong (reference: host_values.py:253-316).
+    keep_values: each slot also keeps the row's values as the forward gathered them (the table does not change
+    within a step), so the optimizer step reads the rows from the GPU and only writes the host table."""
 
-    def __init__(self, num_rows, dim, capacity, device):
+    def __init__(self, num_rows, dim, capacity, device, keep_values=True):
         self.slot = torch.full((num_rows,), -1, dtype=torch.int32, device=device)
         self.rows = torch.empty(capacity, dtype=torch.int64, device=device)
         self.acc = torch.zeros(capacity, dim, dtype=torch.float32, device=device)
+        self.values = torch.empty(capacity, dim, dtype=torch.float32, device=device) if keep_values else None
+        self._values_ok = True
         self.n = 0
         self.peak = 0                      # most distinct rows read in one step so far, overflow included
         self.spilled_steps = 0             # steps with an overflow
         self._spill = []                   # (rows, gradients) on the host; a row may appear in several parts
         self._summed = None
 
-    def add(self, rows, gradient):
-        """rows: distinct row ids on the device, gradient: one row each."""
+    def add(self, rows, gradient, values=None):
+        """rows: distinct row ids on the device, gradient: one row each; values: the rows' current values (device),
+        or None (then the step reads the rows from the host table)."""
         slots = self.slot[rows]
         new = (slots < 0).nonzero().squeeze(1)
         free = self.rows.numel() - self.n
@@ -274,11 +297,20 @@ class StepRows:
             self.slot[fresh] = ids
             self.rows[self.n:self.n + k] = fresh
             slots[new] = ids
+            if self.values is not None:
+                if values is None:
+                    self._values_ok = False
+                else:
+                    self.values[self.n:self.n + k] = values.index_select(0, new)
             self.n += k
             self.peak = max(self.peak, self.n)
         if keep is not None:
             slots, gradient = slots[keep], gradient[keep]
         self.acc.index_add_(0, slots.long(), gradient)
+
+    def current(self):
+        """The slots' row values (device (n, d)) when every slot's values were given, else None."""
+        return self.values[:self.n] if self.values is not None and self._values_ok else None
 
     def spilled(self):
         """(rows, gradient sums) of the overflow on the host, each row once; None without an overflow."""
@@ -301,6 +333,7 @@ class StepRows:
         self.slot[self.rows[:self.n]] = -1
         self.acc[:self.n].zero_()
         self.n = 0
+        self._values_ok = True
 
 
 class StepStore:
@@ -330,13 +363,14 @@ class StepStore:
         pass
 
 
-def enable_step_rows(model, capacity, device):
+def enable_step_rows(model, capacity, device, keep_values=True):
     """GACC for every host table: sum each step's row gradients on `device` in up to `capacity` rows (rows read in
     one step, hot rows not counted). Needs a row-wise table optimizer. Call after enable_hot_rows, if both
-    (reference: host_values.py:343-350)."""
+    (reference: host_values.py:343-350). keep_values (no counterpart): the slots also keep the rows' values, so
+    the step only writes the host table (capacity x width x 4 more bytes on the device)."""
     for module in model.modules():
         if isinstance(module, HostEmbedding) and module.step_rows is None:
-            module.step_rows = StepRows(module.num_embeddings, module.embedding_dim, capacity, device)
+            module.step_rows = StepRows(module.num_embeddings, module.embedding_dim, capacity, device, keep_values)
             module.weight.row_store = StepStore(module.step_rows, module.hot)
     return model
 

@@ -101,16 +101,16 @@ class RowWiseOptimizer(torch.optim.Optimizer):
         with torch.cuda.device(dev):
             if sr is not None:
                 parts = []
-                if sr.n:
-                    parts.append((sr.rows[:sr.n], sr.acc[:sr.n]))
+                if sr.n:                  # with the rows' values from the forward's gather when the slots keep them
+                    parts.append((sr.rows[:sr.n], sr.acc[:sr.n], sr.current()))
                 spilled = sr.spilled()
                 if spilled is not None:   # rows read after every slot was taken: summed on the host, never in a slot
-                    parts.append((spilled[0].to(dev), spilled[1].to(dev)))
-                for rows, g in parts:
+                    parts.append((spilled[0].to(dev), spilled[1].to(dev), None))
+                for rows, g, cur in parts:
                     rc = L.lib().smlm_rows_rowwise_step(
-                        mapped(p.detach()), p.shape[0], L.ptr(rows), L.ptr(g.contiguous()), rows.numel(), p.shape[1],
-                        mapped(state["v"]), mapped(count) if count is not None else None, kind, group["beta2"],
-                        group["eps"], group["lr"], sp, sf, L.status_ptr(dev), L.stream(dev))
+                        mapped(p.detach()), p.shape[0], L.ptr(rows), L.ptr(g.contiguous()), L.ptr(cur), rows.numel(),
+                        p.shape[1], mapped(state["v"]), mapped(count) if count is not None else None, kind,
+                        group["beta2"], group["eps"], group["lr"], sp, sf, L.status_ptr(dev), L.stream(dev))
                     L.check(rc, "rows_rowwise_step")
                 torch.cuda.current_stream(dev).synchronize()
                 sr.reset()

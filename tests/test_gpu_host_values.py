@@ -184,7 +184,7 @@ def test_single_layer_host_table_bit_identical_to_gpu_table():
             m.zero_grad(set_to_none=True)
 
 
-def make_holder(initial, hot_frac=None, reads=None, capacity=None):
+def make_holder(initial, hot_frac=None, reads=None, capacity=None, keep_values=True, kind="rowrms"):
     emb = HostEmbedding(nn.Embedding(*initial.shape, _weight=initial.clone()))
     emb.weight.pk_value_param = True
     model = nn.Module()
@@ -193,8 +193,38 @@ def make_holder(initial, hot_frac=None, reads=None, capacity=None):
     if hot_frac:
         enable_hot_rows(model, reads, hot_frac, torch.device(DEV))
     if capacity:
-        enable_step_rows(model, capacity, torch.device(DEV))
-    return model, RowWiseOptimizer([emb.weight], lr=0.05, kind="rowrms")
+        enable_step_rows(model, capacity, torch.device(DEV), keep_values=keep_values)
+    return model, RowWiseOptimizer([emb.weight], lr=0.05, kind=kind)
+
+
+@pytest.mark.parametrize("width", [16, 384, 512])
+@pytest.mark.parametrize("kind", ["rowrms", "rowadagrad"])
+def test_gacc_step_from_gathered_rows_is_bit_identical(width, kind):
+    """Without clipping and with one backward per step, the row-wise step gives the same bits whether the rows'
+    gradients sit in the host accumulator, in GACC slots that read the rows from the host table, or in GACC slots
+    that keep the rows the forward gathered (the step then only writes the table); with a capacity below the rows
+    a step reads, the overflow rows take the host path in the same step. Widths 16 / 384 / 512: one, three and four
+    register groups per lane (the value bags take rows of up to 512 values)."""
+    gen = torch.Generator().manual_seed(width)
+    initial = torch.randn(300, width, generator=gen)
+    holders = [make_holder(initial, kind=kind), make_holder(initial, capacity=400, keep_values=False, kind=kind),
+               make_holder(initial, capacity=400, kind=kind), make_holder(initial, capacity=30, kind=kind)]
+    for _ in range(3):
+        idx = torch.randint(0, 300, (40, 6), generator=gen).to(DEV)
+        w = torch.rand(40, 6, generator=gen).to(DEV)
+        for model, opt in holders:
+            model.values.bag(idx, w).square().sum().backward()
+        assert row_store(holders[3][0].values.weight).steprows.spilled() is not None
+        assert row_store(holders[2][0].values.weight).steprows.current() is not None
+        for _, opt in holders:
+            opt.step()
+        ref, ref_state = holders[0][0].values.weight.detach(), holders[0][1].state_dict()["state"][0]
+        for model, opt in holders[1:]:
+            assert torch.equal(model.values.weight.detach(), ref)
+            st = opt.state_dict()["state"][0]
+            assert torch.equal(st["v"], ref_state["v"])
+            if kind == "rowrms":
+                assert torch.equal(st["n"], ref_state["n"])
 
 
 @pytest.mark.parametrize("hot_frac,capacity", [(0.3, None), (None, 40), (0.3, 25)])

@@ -116,8 +116,10 @@ def test_rowwise_golden_and_c_loop(kind):
 
 
 @pytest.mark.parametrize("kind", ["rowrms", "rowadagrad"])
-def test_rowwise_vs_oracle_large(kind):
-    rows, D = 20000, 384
+@pytest.mark.parametrize("D", [384, 128, 640, 23])
+def test_rowwise_vs_oracle_large(kind, D):
+    """Widths: 3 and 1 register groups per lane, rows read twice (640 > 512), scalar lanes (23 % 4 != 0)."""
+    rows = 20000
     p, _, _, acc, touched = random_state(rows, D, 3, frac=0.5)
     v = torch.rand(rows) * 1e-2
     n = torch.randint(0, 5, (rows,), dtype=torch.int32)

@@ -79,6 +79,10 @@ def parse():
                          "default Engram module (hash, one-lookup bags, backward, lazy Adam) per step; host: the "
                          "B-16M layer with its table in host RAM, this build against the reference's own host "
                          "path, per configuration (Adam, rowrms, rowrms + GACC, rowrms + HOT 5% + GACC)")
+    ap.add_argument("--host-arm", choices=["both", "this_build", "reference"], default="both",
+                    help="--case host: which implementations to time")
+    ap.add_argument("--host-configs", default="adam,rowrms,rowrms+gacc,rowrms+hot5%+gacc",
+                    help="--case host: comma-separated configurations to time")
     ap.add_argument("--no-inference", action="store_true", help="leave the inference measurement out of the line")
     ap.add_argument("--eager", action="store_true",
                     help="time the step as eager calls (default on one GPU: the step captured as one CUDA graph)")
@@ -817,8 +821,8 @@ def _host_arm(ours):
 def _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev, steps, warmup):
     """One configuration of one arm: the layer step (bf16 autocast forward, backward, value clipping, the table
     optimizer, fused AdamW on the dense parameters) with the table in host RAM; wall time per step with the device
-    synchronised on both sides (the host path is synchronous), median of `steps` after `warmup`, then one more
-    step with the staging phases timed (host_timings)."""
+    synchronised on both sides of `steps` consecutive steps after `warmup`, then one more step with the staging
+    phases timed (host_timings)."""
     name, optim, gacc, hot = config
     mem = _host_layer(arm["PKM"], n_keys, table)
     arm["hv"].enable_host_values(mem)
@@ -827,7 +831,8 @@ def _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev,
     if hot:
         arm["hv"].enable_hot_rows(mem, reads, hot, dev)
     if gacc:
-        arm["hv"].enable_step_rows(mem, capacity, dev)
+        # this build's step accumulator writes the updated rows back while the next step runs (overlap)
+        arm["hv"].enable_step_rows(mem, capacity, dev, **({"overlap": True} if ours else {}))
     dense = [p for p in mem.parameters() if p is not weight]
     adamw = torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True)
     topt = (arm["Adam"]([weight], lr=1e-3, betas=(0.9, 0.98), eps=1e-8) if optim == "adam"
@@ -846,13 +851,12 @@ def _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev,
 
     for i in range(warmup):
         step(i)
-    times = []
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
     for i in range(steps):
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
         step(i)
-        torch.cuda.synchronize()
-        times.append(time.perf_counter() - t0)
+    torch.cuda.synchronize()                       # every stream: the last write-back is inside the time
+    dt = (time.perf_counter() - t0) / steps
     arm["hv"].host_timings(mem, reset=True)
     mem.values.profile = True
     torch.cuda.synchronize()
@@ -862,9 +866,8 @@ def _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev,
     profiled = time.perf_counter() - t0
     phases = arm["hv"].host_timings(mem, reset=True)
     mem.values.profile = False
-    dt = statistics.median(times)
     res = {"ms_per_step": round(dt * 1e3, 1), "tokens_per_s": round(xs[0].shape[0] / dt, 1),
-           "step_ms": [round(t * 1e3, 1) for t in times], "profiled_step_ms": round(profiled * 1e3, 1),
+           "profiled_step_ms": round(profiled * 1e3, 1),
            "phases_ms": {k: round(v * 1e3, 1) for k, v in phases.items()}}
     if gacc:
         res["gacc_peak_rows"] = int(mem.values.step_rows.peak)
@@ -893,9 +896,11 @@ def run_host(args):
     `host_link` is this build's roofline: the table rows that must cross the host link per step, in each direction,
     as multiples of the distinct rows U (Adam: in = gather + accumulator read by the add + the update's p, m, v,
     accumulator = 6, out = add + p, m, v + accumulator cleared = 5, the clip norm from the rows' squared norms that
-    the add kept on the GPU; rowrms: 4 in, 3 out, plus the row state;
-    GACC: 1 in (the gather), 1 out (the updated rows); HOT rows never cross), over the measured pinned copy
-    bandwidths, taken one direction after the other; frac = that time / the measured step."""
+    the add kept on the GPU; rowrms: 4 in, 3 out, its row state on the GPU; GACC: in = the rows the previous step
+    did not read (the others come from the device cache), out = the updated rows; HOT rows never cross), over the
+    measured pinned copy bandwidths: serial_ms one direction after the other, duplex_ms both at once (this build's
+    GACC step overlaps its write-back with the next step); frac = serial_ms / the measured step (above 1 only
+    through overlap)."""
     from smlm_b200.pkm import ProductKeyMemory as OurPKM
     dev = torch.device("cuda", 0)
     n_keys, N = args.rows_per_half, args.tokens
@@ -917,7 +922,7 @@ def run_host(args):
     probe.query_proj.to(dev)
     keys = probe.keys.detach().to(dev)
     reads = torch.zeros(rows, dtype=torch.int64, device=dev)
-    distinct = []
+    distinct, read_sets = [], []
     from smlm_b200 import kernels as K
     with torch.no_grad():
         for x in xs:
@@ -926,10 +931,20 @@ def run_host(args):
             _, idx, _ = K.score_select(q.bfloat16(), keys.bfloat16(), KNN)
             reads += torch.bincount(idx.reshape(-1), minlength=rows)
             distinct.append(int(torch.unique(idx).numel()))
+            read_set = torch.zeros(rows, dtype=torch.bool, device=dev)
+            read_set[idx.reshape(-1)] = True
+            read_sets.append(read_set)
     del probe, keys
     capacity = int(max(distinct) * 1.05)
     hot_rows = int(round(0.05 * rows))
     hot_share = float(reads.sort(descending=True).values[:hot_rows].sum() / reads.sum())
+    is_hot = torch.zeros(rows, dtype=torch.bool, device=dev)
+    is_hot[torch.argsort(reads, descending=True, stable=True)[:hot_rows]] = True
+    # (rows in host RAM one step reads, of which the previous step read too): the timed steps alternate the inputs
+    both = read_sets[0] & read_sets[1]
+    plain_cold = (distinct[0], int(both.sum()))
+    hot_cold = (int((read_sets[0] & ~is_hot).sum()), int((both & ~is_hot).sum()))
+    del read_sets, both, is_hot
     reads = reads.cpu()
     link = _host_link_gbs(dev)
     out = {"case": "host", "workload": f"pkm-layer-{rows}-rows-host-table", "rows": rows, "v_dim": D_MODEL, "tokens": N,
@@ -938,11 +953,19 @@ def run_host(args):
            "host": f"{_cpu_name()}, {threads} threads, {round(_mem_available() / 2**30)} GiB available",
            "steps": args.steps, "warmup": args.warmup, "configs": {}}
     table_gb = rows * D_MODEL * 4
+    wanted = args.host_configs.split(",")
+    unknown = set(wanted) - {c[0] for c in HOST_CONFIGS}
+    if unknown:
+        raise ValueError(f"unknown host configurations: {sorted(unknown)}")
+    arms = [(label, ours) for label, ours in (("reference", False), ("this_build", True))
+            if args.host_arm in ("both", label)]
     for config in HOST_CONFIGS:
         name, optim, gacc, hot = config
+        if name not in wanted:
+            continue
         need = (0 if gacc else table_gb) + (2 * table_gb if optim == "adam" else 0) + (16 << 30)
         entry = out["configs"][name] = {}
-        for label, ours in (("reference", False), ("this_build", True)):
+        for label, ours in arms:
             arm = _host_arm(ours)
             if arm is None:
                 entry[label] = {"unavailable": "the reference package is not in baseline/_ref"}
@@ -956,15 +979,22 @@ def run_host(args):
         if "ms_per_step" in ours:
             # the host-link roofline of this build's step: the rows' bytes that must cross the link each way
             # (U distinct rows in host RAM per step, rows of 4 * v_dim bytes) over the measured copy bandwidths
-            u = ours.get("gacc_peak_rows", statistics.mean(distinct))
             rb = D_MODEL * 4
-            rows_in, rows_out = {"adam": (6, 5), "rowrms": (4, 3)}.get(name, (1, 1))
-            per_row_state = 8 if optim == "rowrms" else 0           # v and n of the row-wise state, each way
-            gb_in, gb_out = u * (rows_in * rb + per_row_state) / 1e9, u * (rows_out * rb + per_row_state) / 1e9
-            bound = (gb_in / link["h2d"] + gb_out / link["d2h"]) * 1e3
+            if gacc:
+                # rows in host RAM per step (HOT rows excluded); those the previous step also read come from the
+                # device cache, so only the others cross the link inwards
+                cold = hot_cold if hot else plain_cold
+                gb_in, gb_out = (cold[0] - cold[1]) * rb / 1e9, cold[0] * rb / 1e9
+                rows_in, rows_out = round(1 - cold[1] / cold[0], 3), 1
+            else:
+                u = statistics.mean(distinct)
+                rows_in, rows_out = {"adam": (6, 5), "rowrms": (4, 3)}[name]
+                gb_in, gb_out = u * rows_in * rb / 1e9, u * rows_out * rb / 1e9
+            serial = (gb_in / link["h2d"] + gb_out / link["d2h"]) * 1e3
+            duplex = max(gb_in / link["h2d"], gb_out / link["d2h"]) * 1e3
             ours["host_link"] = {"rows_in_per_row": rows_in, "rows_out_per_row": rows_out, "gb_in": round(gb_in, 2),
-                                 "gb_out": round(gb_out, 2), "bound_ms": round(bound, 1),
-                                 "frac": round(bound / ours["ms_per_step"], 3)}
+                                 "gb_out": round(gb_out, 2), "serial_ms": round(serial, 1),
+                                 "duplex_ms": round(duplex, 1), "frac": round(serial / ours["ms_per_step"], 3)}
         if "ms_per_step" in entry.get("reference", {}) and "ms_per_step" in ours:
             entry["speedup"] = round(entry["reference"]["ms_per_step"] / ours["ms_per_step"], 2)
         print(json.dumps({"case": "host", "config": name, **entry}), flush=True)

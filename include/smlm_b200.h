@@ -406,11 +406,20 @@ SMLM_API int smlm_host_register(void *ptr, size_t bytes, void **device_ptr);
 SMLM_API int smlm_host_unregister(void *ptr);
 
 /* out[i] (device, (n, d) fp32) = hot[slot[i]] when slot (device int32, may be NULL) has slot[i] >= 0 (the row's
- * HOT copy on the device), else table[rows[i]] (table: a mapped host table of table_rows rows; rows: device int64,
- * distinct). Out-of-range rows give zeros and SMLM_FLAG_INDEX_RANGE. Replaces HostEmbedding.gather's staging
- * (host_values.py:82-119: indices to the host, a C gather into pinned memory, a copy to the device). */
+ * HOT copy on the device), else cache[slot2[i]] when slot2 (device int32, may be NULL) has slot2[i] >= 0 (a device
+ * copy of the row, e.g. as the previous step updated it), else table[rows[i]] (table: a mapped host table of
+ * table_rows rows; rows: device int64, distinct). Out-of-range rows give zeros and SMLM_FLAG_INDEX_RANGE. Replaces
+ * HostEmbedding.gather's staging (host_values.py:82-119: indices to the host, a C gather into pinned memory, a
+ * copy to the device). */
 SMLM_API int smlm_host_rows_gather(const float *table, int64_t table_rows, const int64_t *rows, const int32_t *slot,
-                                   const float *hot, int64_t n, int64_t d, float *out, int *status, void *stream);
+                                   const float *hot, const int32_t *slot2, const float *cache, int64_t n, int64_t d,
+                                   float *out, int *status, void *stream);
+
+/* table[rows[i]] = values[i] (table: a mapped host table of table_rows rows; rows device int64, distinct; values
+ * device (n, d) fp32): the write-back of rows updated on the device. No counterpart in the reference (its row-wise
+ * step writes the rows with a C loop, row_optim.py:73-135). */
+SMLM_API int smlm_host_rows_scatter(float *table, int64_t table_rows, const int64_t *rows, const float *values,
+                                    int64_t n, int64_t d, int *status, void *stream);
 
 /* acc[rows[i]] = acc[rows[i]] + grads[i] and touched[rows[i]] = 1 (acc / touched: mapped host tensors of
  * table_rows rows; grads device (n, d) fp32; rows device int64, distinct), skipping the rows whose skip[i] >= 0
@@ -427,13 +436,15 @@ SMLM_API int smlm_host_rows_add(float *acc, uint8_t *touched, float *row_sqnorm,
  * distinct rows rows[i] (device int64) with gradient grads[i] (device (n, d) fp32, e.g. a step's row sums kept on
  * the GPU), times the clip factor (*grad_scale_dev when given, else grad_scale); param, v and count may be mapped
  * host memory. current: NULL, or the rows' current values (device (n, d) fp32, equal to param's rows, e.g. the
- * rows the forward gathered), read instead of param, which is then only written. Replaces
- * RowWiseOptimizer._step_gacc's chunked copies to the host and C loop (row_optim.py:73-135, host_rows.c
- * host_rows_rowwise). */
+ * rows the forward gathered), read instead of param, which is then only written. flags: SMLM_ROWS_TO_CURRENT
+ * writes the updated rows into current instead of param (param is not touched and may be NULL; the caller writes
+ * them back, smlm_host_rows_scatter). Replaces RowWiseOptimizer._step_gacc's chunked copies to the host and C loop
+ * (row_optim.py:73-135, host_rows.c host_rows_rowwise). */
+#define SMLM_ROWS_TO_CURRENT 1
 SMLM_API int smlm_rows_rowwise_step(float *param, int64_t table_rows, const int64_t *rows, const float *grads,
-                                    const float *current, int64_t n, int64_t d, float *v, int32_t *count, int kind,
+                                    float *current, int64_t n, int64_t d, float *v, int32_t *count, int kind,
                                     float beta2, float eps, float lr, const float *grad_scale_dev, float grad_scale,
-                                    int *status, void *stream);
+                                    int flags, int *status, void *stream);
 
 /* ------------------------------------------------------------------------------------- Engram n-gram rows
  * Row indices of an Engram module's lookups: for position t of sequence b and lookup (order o, head h), the XOR over

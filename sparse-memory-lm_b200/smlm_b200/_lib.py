@@ -27,6 +27,7 @@ ROWRMS, ROWADAGRAD = 0, 1
 BWD_FIRST_TOUCH_WRITES = 1
 BWD_DEFER_ROWS = 2
 STEP_KEEP_ACC = 1
+ROWS_TO_CURRENT = 1
 SCORE_F32_EXACT, SCORE_BF16 = 0, 1
 
 # Kernel launches behind one call, for the benchmark's launch count (checked against the ncu launch list):
@@ -92,10 +93,11 @@ SIGNATURES = {
     "smlm_ngram_rows": (_i32, [_p, _i64, _i64, _i32, _p, _p, _i32, _i32, _i32, _i64, _p, _p]),
     "smlm_host_register": (_i32, [_p, _sz, _p]),
     "smlm_host_unregister": (_i32, [_p]),
-    "smlm_host_rows_gather": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _p, _p, _p]),
+    "smlm_host_rows_gather": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p]),
+    "smlm_host_rows_scatter": (_i32, [_p, _i64, _p, _p, _i64, _i64, _p, _p]),
     "smlm_host_rows_add": (_i32, [_p, _p, _p, _i64, _p, _p, _p, _i64, _i64, _p, _p]),
-    "smlm_rows_rowwise_step": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _p, _p, _i32, _f32, _f32, _f32, _p, _f32, _p,
-                                      _p]),
+    "smlm_rows_rowwise_step": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _p, _p, _i32, _f32, _f32, _f32, _p, _f32,
+                                      _i32, _p, _p]),
 }
 
 _LIB = None

@@ -78,6 +78,18 @@ def _sync(device):
     torch.cuda.current_stream(device).synchronize()
 
 
+ROW_GRANULE = 1 << 16     # per-step row buffers are allocated in multiples of this many rows
+
+
+def _row_buffer(n, d, device, zero=False):
+    """An (n, d) fp32 device tensor whose allocation is rounded up to ROW_GRANULE rows: the distinct rows of a step
+    vary by a few thousand from step to step, and multi-GB requests of ever new sizes make the caching allocator
+    map new memory (a slow cudaMalloc) instead of reusing its blocks."""
+    cap = max(1, -(-n // ROW_GRANULE)) * ROW_GRANULE
+    t = torch.empty(cap, d, dtype=torch.float32, device=device)[:n]
+    return t.zero_() if zero else t
+
+
 class HostEmbedding(nn.Embedding):
     """A value table that stays fp32 in host RAM when its model moves to the GPU (reference:
     host_values.py:29-161); a normal parameter for checkpoints. `hot`: its HOT rows (enable_hot_rows), `step_rows`:
@@ -92,9 +104,13 @@ class HostEmbedding(nn.Embedding):
         self.hot = None
         self.step_rows = None
         self.register_state_dict_pre_hook(lambda module, *_: module.flush())
+        self._register_load_state_dict_pre_hook(lambda *_: self.flush())
 
     def flush(self):
-        """Write the GPU copies of the hot rows back into the host table."""
+        """Write the GPU copies of the hot rows back into the host table (after any write-back of a GACC step still
+        running, so the host table is complete for CPU code)."""
+        if self.step_rows is not None:
+            self.step_rows.sync()
         if self.hot is not None:
             _sync(self.hot.values.device)
             self.weight.detach().index_copy_(0, self.hot.rows.cpu(), self.hot.values.detach().cpu())
@@ -119,17 +135,21 @@ class HostEmbedding(nn.Embedding):
 
     def gather(self, indices):
         """(distinct rows (device int64, sorted), the lookups remapped onto them, their values gathered onto the
-        device (fp32), and their HOT slots (device int32, -1 for rows in host RAM) or None)."""
+        device (fp32; HOT rows and the previous GACC step's rows from their device copies), and their HOT slots
+        (device int32, -1 for rows in host RAM) or None)."""
         dev = indices.device
         with self.phase("unique", dev):
             rows, remapped = torch.unique(indices.reshape(-1), sorted=True, return_inverse=True)
         slot = self.hot.slot.index_select(0, rows) if self.hot is not None else None
-        values = torch.empty(rows.numel(), self.embedding_dim, dtype=torch.float32, device=dev)
+        prev_slot, cache = self.step_rows.cache() if self.step_rows is not None else (None, None)
+        slot2 = prev_slot.index_select(0, rows) if prev_slot is not None else None
+        values = _row_buffer(rows.numel(), self.embedding_dim, dev)
         with self.phase("gather", dev):
             t = self.weight.detach()
             rc = L.lib().smlm_host_rows_gather(mapped(t), t.shape[0], L.ptr(rows), L.ptr(slot),
-                                               L.ptr(self.hot.values) if slot is not None else None, rows.numel(),
-                                               t.shape[1], L.ptr(values), L.status_ptr(dev), L.stream(dev))
+                                               L.ptr(self.hot.values) if slot is not None else None, L.ptr(slot2),
+                                               L.ptr(cache), rows.numel(), t.shape[1], L.ptr(values),
+                                               L.status_ptr(dev), L.stream(dev))
             L.check(rc, "host_rows_gather")
             L.after(dev, "host_rows_gather")
         return rows, remapped.view_as(indices), values, slot
@@ -145,7 +165,7 @@ class HostEmbedding(nn.Embedding):
             if at_hot.numel():
                 s = slot.index_select(0, at_hot).long()
                 self.hot.acc.index_add_(0, s, gradient.index_select(0, at_hot))
-                self.hot.touched[s] = True
+                self.hot.touched.index_fill_(0, s, True)
         if self.step_rows is not None:
             with self.phase("scatter", dev):
                 if hot:
@@ -200,7 +220,7 @@ class _HostBag(torch.autograd.Function):
         if g.dtype not in (torch.float32, torch.bfloat16):
             g = g.float()
         if ctx.train_table:
-            acc = torch.zeros_like(values)
+            acc = _row_buffer(values.shape[0], values.shape[1], values.device, zero=True)
             touched = torch.zeros(values.shape[0], dtype=torch.bool, device=values.device)
             gw = K.bag_backward_rows(g, indices, w, values, acc, touched)
             ctx.owner.accumulate(rows, acc, slot, values)
@@ -261,10 +281,19 @@ class StepRows:
     slots (a row takes the next free slot when it is first read in the step; later reads add into it). Rows read
     after every slot is taken (overflow) keep their gradients on the host, summed per row before the step, so a
     step that reads more rows than the capacity is slower, not wrong (reference: host_values.py:253-316).
-    keep_values: each slot also keeps the row's values as the forward gathered them (the table does not change
-    within a step), so the optimizer step reads the rows from the GPU and only writes the host table."""
 
-    def __init__(self, num_rows, dim, capacity, device, keep_values=True):
+    keep_values (no counterpart; needs `table`): each slot also keeps the row's values as the forward gathered
+    them (the table does not change within a step). The row-wise step then updates the slots' rows on the GPU
+    (update(), the state too) and writes them back into the host table with one scatter kernel (finish()), and the
+    step's rows stay on the GPU as the previous step's cache: the next step's gather reads them there instead of
+    over the host link. overlap: that write-back runs on a side stream while the next step computes and gathers the
+    other rows (the two directions of the host link at once); it only has to end before the step after next
+    touches the host table, and CPU code reads the table after flush() (HostEmbedding.flush, state_dict)."""
+
+    def __init__(self, num_rows, dim, capacity, device, keep_values=True, table=None, overlap=False):
+        keep_values = keep_values and table is not None
+        if overlap and not keep_values:
+            raise ValueError("overlapped write-back needs keep_values and the table")
         self.slot = torch.full((num_rows,), -1, dtype=torch.int32, device=device)
         self.rows = torch.empty(capacity, dtype=torch.int64, device=device)
         self.acc = torch.zeros(capacity, dim, dtype=torch.float32, device=device)
@@ -275,6 +304,18 @@ class StepRows:
         self.spilled_steps = 0             # steps with an overflow
         self._spill = []                   # (rows, gradients) on the host; a row may appear in several parts
         self._summed = None
+        self.table = table
+        # the previous step's rows as its step left them: slot map, rows, values (keep_values only)
+        if keep_values:
+            self.prev_slot = torch.full((num_rows,), -1, dtype=torch.int32, device=device)
+            self.prev_rows = torch.empty(capacity, dtype=torch.int64, device=device)
+            self.prev_values = torch.empty(capacity, dim, dtype=torch.float32, device=device)
+        else:
+            self.prev_slot = self.prev_rows = self.prev_values = None
+        self.prev_n = 0
+        self._prev_version = None
+        self.stream = torch.cuda.Stream(device) if overlap else None
+        self._written = None               # event: the last write-back has ended (overlap)
 
     def add(self, rows, gradient, values=None):
         """rows: distinct row ids on the device, gradient: one row each; values: the rows' current values (device),
@@ -288,8 +329,7 @@ class StepRows:
             self._spill.append((rows.index_select(0, out).cpu(), gradient.index_select(0, out).cpu()))
             self._summed = None
             new = new[:free]
-            keep = torch.ones_like(slots, dtype=torch.bool)
-            keep[out] = False
+            keep = torch.ones_like(slots, dtype=torch.bool).index_fill_(0, out, False)
         k = new.numel()
         if k:
             ids = torch.arange(self.n, self.n + k, dtype=torch.int32, device=rows.device)
@@ -306,11 +346,44 @@ class StepRows:
             self.peak = max(self.peak, self.n)
         if keep is not None:
             slots, gradient = slots[keep], gradient[keep]
-        self.acc.index_add_(0, slots.long(), gradient)
+        if self.acc.is_cuda and self.acc.shape[1] % 4 == 0:
+            # the slots of one add are distinct: the host-add kernel (acc[slot] + g, 16-byte rows) on device memory
+            dev = self.acc.device
+            g, idx = gradient.contiguous(), slots.long()
+            rc = L.lib().smlm_host_rows_add(L.ptr(self.acc), None, None, self.acc.shape[0], L.ptr(idx), L.ptr(g),
+                                            None, idx.numel(), self.acc.shape[1], L.status_ptr(dev), L.stream(dev))
+            L.check(rc, "host_rows_add (step slots)")
+        else:
+            self.acc.index_add_(0, slots.long(), gradient)
 
     def current(self):
         """The slots' row values (device (n, d)) when every slot's values were given, else None."""
         return self.values[:self.n] if self.values is not None and self._values_ok else None
+
+    def cache(self):
+        """(slot map, values) of the previous step's rows for the gather, or (None, None). The cache is dropped
+        when the table was changed by anything but these steps (its version counter moved)."""
+        if not self.prev_n:
+            return None, None
+        if self.table._version != self._prev_version:
+            self._drop_cache()
+            return None, None
+        return self.prev_slot, self.prev_values
+
+    def _drop_cache(self):
+        self.wait_written()
+        self.prev_slot.index_fill_(0, self.prev_rows[:self.prev_n], -1)
+        self.prev_n = 0
+
+    def wait_written(self):
+        """Orders the current stream after the last write-back (overlap)."""
+        if self._written is not None:
+            torch.cuda.current_stream(self.acc.device).wait_event(self._written)
+
+    def sync(self):
+        """Waits on the host until the last write-back has reached the host table."""
+        if self._written is not None:
+            self._written.synchronize()
 
     def spilled(self):
         """(rows, gradient sums) of the overflow on the host, each row once; None without an overflow."""
@@ -326,14 +399,51 @@ class StepRows:
         return self._summed
 
     def reset(self):
+        """Drops the step's gradients (the table is unchanged; the previous step's cache stays)."""
         if self._spill:
             self.spilled()                 # counts the step's overflow rows in peak
             self.spilled_steps += 1
             self._spill, self._summed = [], None
-        self.slot[self.rows[:self.n]] = -1
+        self.slot.index_fill_(0, self.rows[:self.n], -1)
         self.acc[:self.n].zero_()
         self.n = 0
         self._values_ok = True
+
+    def finish(self):
+        """After update() wrote the step's rows into the slots: the slots become the previous step's cache, their
+        rows are written back into the host table (on the side stream with overlap, else here, synchronously),
+        and the gradients are dropped."""
+        dev = self.acc.device
+        self.wait_written()                # the older write-back read the buffers that are reused next
+        self.prev_slot.index_fill_(0, self.prev_rows[:self.prev_n], -1)
+        self.slot, self.prev_slot = self.prev_slot, self.slot
+        self.rows, self.prev_rows = self.prev_rows, self.rows
+        self.values, self.prev_values = self.prev_values, self.values
+        self.prev_n, n = self.n, self.n
+        self.n = 0
+        self.acc[:n].zero_()
+        self._values_ok = True
+        if self._spill:
+            self.spilled()
+            self.spilled_steps += 1
+            self._spill, self._summed = [], None
+        table = self.table.detach()
+        self._prev_version = self.table._version
+        main = torch.cuda.current_stream(dev)
+        if self.stream is not None:
+            self.stream.wait_stream(main)
+            ctx = torch.cuda.stream(self.stream)
+        else:
+            ctx = torch.cuda.stream(main)
+        with ctx:
+            rc = L.lib().smlm_host_rows_scatter(mapped(table), table.shape[0], L.ptr(self.prev_rows),
+                                                L.ptr(self.prev_values), n, table.shape[1], L.status_ptr(dev),
+                                                L.stream(dev))
+            L.check(rc, "host_rows_scatter")
+        if self.stream is not None:
+            self._written = self.stream.record_event()
+        else:
+            main.synchronize()             # the host table is complete before CPU code reads it
 
 
 class StepStore:
@@ -363,14 +473,16 @@ class StepStore:
         pass
 
 
-def enable_step_rows(model, capacity, device, keep_values=True):
+def enable_step_rows(model, capacity, device, keep_values=True, overlap=False):
     """GACC for every host table: sum each step's row gradients on `device` in up to `capacity` rows (rows read in
     one step, hot rows not counted). Needs a row-wise table optimizer. Call after enable_hot_rows, if both
-    (reference: host_values.py:343-350). keep_values (no counterpart): the slots also keep the rows' values, so
-    the step only writes the host table (capacity x width x 4 more bytes on the device)."""
+    (reference: host_values.py:343-350). keep_values and overlap (no counterpart; StepRows): the step's rows are
+    updated on the GPU and kept there as the next step's cache (2 x capacity x width x 4 more bytes on the device),
+    and with overlap written back to the host table while the next step runs."""
     for module in model.modules():
         if isinstance(module, HostEmbedding) and module.step_rows is None:
-            module.step_rows = StepRows(module.num_embeddings, module.embedding_dim, capacity, device, keep_values)
+            module.step_rows = StepRows(module.num_embeddings, module.embedding_dim, capacity, device, keep_values,
+                                        module.weight, overlap)
             module.weight.row_store = StepStore(module.step_rows, module.hot)
     return model
 

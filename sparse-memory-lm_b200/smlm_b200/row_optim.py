@@ -68,10 +68,11 @@ class RowWiseOptimizer(torch.optim.Optimizer):
 
     @torch.no_grad()
     def _step_host(self, group, p, st, state):
-        """A table in host RAM (smlm_b200.host_values; reference: row_optim.py:58-157): its HOT rows' state lives
-        on the GPU in slot order and they step there; the other rows step in place in host RAM through the mapped
-        table, accumulator and state (smlm_rowwise_step), or, with GACC, from the step's row sums on the GPU
-        (smlm_rows_rowwise_step), overflow rows included."""
+        """A table in host RAM (smlm_b200.host_values; reference: row_optim.py:58-157): the per-row state moves to
+        the GPU (8 bytes a row; the reference keeps it in RAM); the HOT rows' state is kept in slot order there and
+        they step there; the other rows step in place in host RAM through the mapped table and accumulator
+        (smlm_rowwise_step), or, with GACC, from the step's row sums on the GPU (smlm_rows_rowwise_step), overflow
+        rows included."""
         from . import _lib as L
         from .host_values import mapped
         hot = getattr(st, "hot", None)
@@ -84,11 +85,15 @@ class RowWiseOptimizer(torch.optim.Optimizer):
             dev = torch.device("cuda", torch.cuda.current_device())
         kind = L.ROWRMS if self.kind == "rowrms" else L.ROWADAGRAD
         scale = st.grad_scale
+        # the per-row state (8 bytes a row) lives on the GPU, so the steps read no state over the host link
+        for key in ("v", "n"):
+            if key in state and state[key].device != dev:
+                state[key] = state[key].to(dev)
         if hot is not None:
             if "hot_v" not in state:
-                state["hot_v"] = state["v"].index_select(0, hot.rows.cpu()).to(dev)
+                state["hot_v"] = state["v"].index_select(0, hot.rows)
                 if "n" in state:
-                    state["hot_n"] = state["n"].index_select(0, hot.rows.cpu()).to(dev)
+                    state["hot_n"] = state["n"].index_select(0, hot.rows)
             K.rowwise_step(hot.values, hot.acc, hot.touched, state["hot_v"], state.get("hot_n"), scale, group["lr"],
                            group["beta2"], group["eps"], self.kind)
         sp, sf, keep = None, 1.0, None
@@ -100,25 +105,33 @@ class RowWiseOptimizer(torch.optim.Optimizer):
         count = state.get("n")
         with torch.cuda.device(dev):
             if sr is not None:
+                cur = sr.current()
+                on_device = cur is not None and sr.prev_slot is not None
+                if not on_device and sr.prev_slot is not None:
+                    sr._drop_cache()      # rows are about to change in the host table only
                 parts = []
                 if sr.n:                  # with the rows' values from the forward's gather when the slots keep them
-                    parts.append((sr.rows[:sr.n], sr.acc[:sr.n], sr.current()))
+                    parts.append((sr.rows[:sr.n], sr.acc[:sr.n], cur, L.ROWS_TO_CURRENT if on_device else 0))
                 spilled = sr.spilled()
                 if spilled is not None:   # rows read after every slot was taken: summed on the host, never in a slot
-                    parts.append((spilled[0].to(dev), spilled[1].to(dev), None))
-                for rows, g, cur in parts:
+                    sr.wait_written()     # such a row may be in the write-back still running
+                    parts.append((spilled[0].to(dev), spilled[1].to(dev), None, 0))
+                for rows, g, c, flags in parts:
                     rc = L.lib().smlm_rows_rowwise_step(
-                        mapped(p.detach()), p.shape[0], L.ptr(rows), L.ptr(g.contiguous()), L.ptr(cur), rows.numel(),
-                        p.shape[1], mapped(state["v"]), mapped(count) if count is not None else None, kind,
-                        group["beta2"], group["eps"], group["lr"], sp, sf, L.status_ptr(dev), L.stream(dev))
+                        mapped(p.detach()), p.shape[0], L.ptr(rows), L.ptr(g.contiguous()), L.ptr(c), rows.numel(),
+                        p.shape[1], L.ptr(state["v"]), L.ptr(count), kind, group["beta2"], group["eps"],
+                        group["lr"], sp, sf, flags, L.status_ptr(dev), L.stream(dev))
                     L.check(rc, "rows_rowwise_step")
-                torch.cuda.current_stream(dev).synchronize()
-                sr.reset()
+                if on_device:
+                    sr.finish()           # the updated rows: back into the host table, kept as the next cache
+                else:
+                    torch.cuda.current_stream(dev).synchronize()
+                    sr.reset()
             elif bool(st.touched.any()):
                 ws = L.workspace(L.lib().smlm_touched_workspace(p.shape[0]), dev)
                 rc = L.lib().smlm_rowwise_step(
-                    mapped(p.detach()), mapped(st.acc), mapped(st.touched), mapped(state["v"]),
-                    mapped(count) if count is not None else None, sp, sf, p.shape[0], p.shape[1], kind,
+                    mapped(p.detach()), mapped(st.acc), mapped(st.touched), L.ptr(state["v"]), L.ptr(count), sp, sf,
+                    p.shape[0], p.shape[1], kind,
                     group["beta2"], group["eps"], group["lr"], 0, L.ptr(ws), ws.numel(), L.stream(dev))
                 L.check(rc, "rowwise_step (host table)")
                 torch.cuda.current_stream(dev).synchronize()
@@ -137,10 +150,10 @@ class RowWiseOptimizer(torch.optim.Optimizer):
         for p in self._params():
             state, hot = self.state[p], getattr(row_store(p), "hot", None)
             if hot is not None and "hot_v" in state:
-                rows = hot.rows.cpu()
-                state["v"].index_copy_(0, rows, state["hot_v"].cpu())
+                rows = hot.rows.to(state["v"].device)
+                state["v"].index_copy_(0, rows, state["hot_v"].to(state["v"].device))
                 if "hot_n" in state:
-                    state["n"].index_copy_(0, rows, state["hot_n"].cpu())
+                    state["n"].index_copy_(0, rows, state["hot_n"].to(state["n"].device))
 
     def state_dict(self):
         """Every row's state in table order (HOT rows written back first), so it loads with or without HOT."""

@@ -184,7 +184,7 @@ def test_single_layer_host_table_bit_identical_to_gpu_table():
             m.zero_grad(set_to_none=True)
 
 
-def make_holder(initial, hot_frac=None, reads=None, capacity=None, keep_values=True, kind="rowrms"):
+def make_holder(initial, hot_frac=None, reads=None, capacity=None, keep_values=True, kind="rowrms", overlap=False):
     emb = HostEmbedding(nn.Embedding(*initial.shape, _weight=initial.clone()))
     emb.weight.pk_value_param = True
     model = nn.Module()
@@ -193,7 +193,7 @@ def make_holder(initial, hot_frac=None, reads=None, capacity=None, keep_values=T
     if hot_frac:
         enable_hot_rows(model, reads, hot_frac, torch.device(DEV))
     if capacity:
-        enable_step_rows(model, capacity, torch.device(DEV), keep_values=keep_values)
+        enable_step_rows(model, capacity, torch.device(DEV), keep_values=keep_values, overlap=overlap)
     return model, RowWiseOptimizer([emb.weight], lr=0.05, kind=kind)
 
 
@@ -202,22 +202,34 @@ def make_holder(initial, hot_frac=None, reads=None, capacity=None, keep_values=T
 def test_gacc_step_from_gathered_rows_is_bit_identical(width, kind):
     """Without clipping and with one backward per step, the row-wise step gives the same bits whether the rows'
     gradients sit in the host accumulator, in GACC slots that read the rows from the host table, or in GACC slots
-    that keep the rows the forward gathered (the step then only writes the table); with a capacity below the rows
-    a step reads, the overflow rows take the host path in the same step. Widths 16 / 384 / 512: one, three and four
-    register groups per lane (the value bags take rows of up to 512 values)."""
+    that keep the rows the forward gathered (the step updates them on the GPU, writes them back, and the next step
+    reads them from that cache), with the write-back overlapped with the next step or not; with a capacity below
+    the rows a step reads, the overflow rows take the host path in the same step. Widths 16 / 384 / 512: one, three
+    and four register groups per lane (the value bags take rows of up to 512 values)."""
     gen = torch.Generator().manual_seed(width)
     initial = torch.randn(300, width, generator=gen)
     holders = [make_holder(initial, kind=kind), make_holder(initial, capacity=400, keep_values=False, kind=kind),
-               make_holder(initial, capacity=400, kind=kind), make_holder(initial, capacity=30, kind=kind)]
-    for _ in range(3):
+               make_holder(initial, capacity=400, kind=kind), make_holder(initial, capacity=30, kind=kind),
+               make_holder(initial, capacity=400, kind=kind, overlap=True),
+               make_holder(initial, capacity=30, kind=kind, overlap=True)]
+    outs = None
+    for step in range(4):
         idx = torch.randint(0, 300, (40, 6), generator=gen).to(DEV)
         w = torch.rand(40, 6, generator=gen).to(DEV)
+        outs = []
         for model, opt in holders:
-            model.values.bag(idx, w).square().sum().backward()
+            out = model.values.bag(idx, w)
+            out.square().sum().backward()
+            outs.append(out.detach())
+        assert all(torch.equal(o, outs[0]) for o in outs[1:])     # rows read from the cache: the same values
         assert row_store(holders[3][0].values.weight).steprows.spilled() is not None
         assert row_store(holders[2][0].values.weight).steprows.current() is not None
+        if step:
+            assert row_store(holders[2][0].values.weight).steprows.cache()[0] is not None
         for _, opt in holders:
             opt.step()
+        for model, _ in holders:
+            model.values.flush()                                   # the overlapped write-backs reach the table
         ref, ref_state = holders[0][0].values.weight.detach(), holders[0][1].state_dict()["state"][0]
         for model, opt in holders[1:]:
             assert torch.equal(model.values.weight.detach(), ref)
@@ -227,15 +239,17 @@ def test_gacc_step_from_gathered_rows_is_bit_identical(width, kind):
                 assert torch.equal(st["n"], ref_state["n"])
 
 
-@pytest.mark.parametrize("hot_frac,capacity", [(0.3, None), (None, 40), (0.3, 25)])
-def test_hot_rows_and_gacc_train_like_rows_in_ram(hot_frac, capacity):
+@pytest.mark.parametrize("hot_frac,capacity,overlap", [(0.3, None, False), (None, 40, False), (0.3, 25, False),
+                                                       (None, 40, True), (0.3, 25, True)])
+def test_hot_rows_and_gacc_train_like_rows_in_ram(hot_frac, capacity, overlap):
     """rowrms on a host table: HOT rows on the GPU and / or the GACC step accumulator (capacity 25 / 40 rows: steps
     read more rows, so the overflow path runs) give the same outputs, clip norms, rows and row state as all rows
     in RAM; state_dict writes the hot rows back (reference: tests/test_hot_rows.py)."""
     gen = torch.Generator().manual_seed(0)
     initial = torch.randn(200, 16, generator=gen)
     reads = torch.randint(0, 1000, (200,), generator=gen)
-    (plain, opt_a), (other, opt_b) = make_holder(initial), make_holder(initial, hot_frac, reads, capacity)
+    (plain, opt_a), (other, opt_b) = make_holder(initial), make_holder(initial, hot_frac, reads, capacity,
+                                                                      overlap=overlap)
     spilled = False
     for _ in range(4):
         idx = torch.randint(0, 200, (12, 5), generator=gen).to(DEV)

@@ -849,11 +849,13 @@ def _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev,
         adamw.zero_grad(set_to_none=True)
         topt.zero_grad(set_to_none=True)
 
+    # the steps alternate the two input batches throughout (warm-up, timed, profiled), so every timed step reads
+    # the rows of the other batch after its predecessor, as in training on fresh data
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for i in range(steps):
+    for i in range(warmup, warmup + steps):
         step(i)
     torch.cuda.synchronize()                       # every stream: the last write-back is inside the time
     dt = (time.perf_counter() - t0) / steps
@@ -861,7 +863,7 @@ def _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev,
     mem.values.profile = True
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    step(steps)
+    step(warmup + steps)
     torch.cuda.synchronize()
     profiled = time.perf_counter() - t0
     phases = arm["hv"].host_timings(mem, reset=True)

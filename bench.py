@@ -517,7 +517,9 @@ def run_configs(args):
     (the B-16M layer, 32 x 1024 tokens per GPU, its inputs embeddings of a uniform + Zipf(1.1) token mix: hot
     rows). Seeded synthetic inputs, upstream gradient ~ N(0, 1). fwd = the layer's forward; bwd = backward +
     value / dense clipping; opt = the table optimizer + fused AdamW on the dense parameters (with deferred row sums
-    the table's row sums run in opt, not in bwd)."""
+    the table's row sums run in opt, not in bwd). The fp32 lazy-Adam configurations are also timed as one CUDA
+    graph per step (GraphedStep, captured first; `graphed_step_ms`), which removes the host's launch time that
+    bounds the small configurations' eager steps."""
     from smlm_b200.pkm import ProductKeyMemory
     from smlm_b200.row_optim import RowWiseOptimizer
     from smlm_b200.sparse_values import LazyRowAdam, OptimizerSet, clip_row_sparse, row_store
@@ -534,18 +536,46 @@ def run_configs(args):
                     mem.keys.normal_(0, (K_DIM // 2) ** -0.5)
         table = mem.values.weight
         dense = [p for p in mem.parameters() if p is not table]
+        graphed = kind == "adam"            # fp32 lazy Adam: the whole step also as one CUDA graph
         if kind == "rowrms":
             topt = RowWiseOptimizer([table], lr=1e-3, kind="rowrms", beta2=0.98)
         else:
             topt = LazyRowAdam([table], lr=1e-3, betas=(0.9, 0.98), eps=1e-8,
                                state_dtype="bf16" if kind == "adam-bf16" else "fp32",
-                               value_copy_dtype=torch.bfloat16 if copy else None)
-        opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True), topt)
+                               value_copy_dtype=torch.bfloat16 if copy else None, capturable=graphed)
+        opt = OptimizerSet(torch.optim.AdamW(dense, lr=1e-3, betas=(0.9, 0.98), weight_decay=0.0, fused=True,
+                                             capturable=graphed), topt)
         gen = torch.Generator(device=dev).manual_seed(1)
         xs = [layer_inputs(inputs, N, gen, dev) for _ in range(2)]
         gs = [torch.randn(N, D_MODEL, device=dev, generator=gen) for _ in range(2)]
         ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
         uniq = []
+        graph_ms = None
+        if graphed:
+            # captured before any eager step (autograd's gradient streams), then replayed on alternating inputs
+            from smlm_b200.graph_step import GraphedStep
+
+            def whole(x, g):
+                with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+                    o = mem(x)
+                o.backward(g)
+                vnorm = clip_row_sparse([table], 1.0)
+                torch.nn.utils.clip_grad_norm_([p for p in dense if p.grad is not None], 1.0, foreach=True)
+                opt.step()
+                opt.zero_grad(set_to_none=True)
+                return vnorm
+            gstep = GraphedStep(whole, [xs[0], gs[0]], opt.opts, warmup=max(3, args.warmup))
+            for i in range(args.warmup):
+                gstep(xs[i % 2], gs[i % 2])
+            torch.cuda.synchronize()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record()
+            for i in range(args.steps):
+                gstep(xs[i % 2], gs[i % 2])
+            g1.record()
+            torch.cuda.synchronize()
+            graph_ms = g0.elapsed_time(g1) / args.steps
+            del gstep
 
         def step(i, e=None):
             if e:
@@ -577,6 +607,8 @@ def run_configs(args):
                  "values_read": "bf16 copy of the fp32 master" if copy else "fp32 table",
                  "fwd_ms": round(ph[0], 4), "bwd_ms": round(ph[1], 4), "opt_ms": round(ph[2], 4),
                  "tokens_per_s": round(N / (sum(ph) / 1e3), 1),
+                 "graphed_step_ms": round(graph_ms, 4) if graph_ms is not None else None,
+                 "graphed_tokens_per_s": round(N / (graph_ms / 1e3), 1) if graph_ms is not None else None,
                  "unique_rows_per_step": round(sum(uniq[1:]) / max(1, len(uniq) - 1))}
         if inputs == "zipf":
             with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):

@@ -911,7 +911,7 @@ def _host_config(arm, ours, config, table, n_keys, xs, gs, reads, capacity, dev,
     if ours:
         state = topt.state.get(weight, {})
         arm["hv"].release(*[v for v in state.values() if torch.is_tensor(v)],
-                          getattr(st, "acc", None), getattr(st, "touched", None))
+                          getattr(st, "_acc", None), getattr(st, "touched", None))
     del mem, adamw, topt, weight, st, step
     import gc
     gc.collect()
@@ -928,9 +928,9 @@ def run_host(args):
     of it). A configuration whose host RAM would not fit (with 16 GB to spare) is skipped.
 
     `host_link` is this build's roofline: the table rows that must cross the host link per step, in each direction,
-    as multiples of the distinct rows U (Adam: in = gather + accumulator read by the add + the update's p, m, v,
-    accumulator = 6, out = add + p, m, v + accumulator cleared = 5, the clip norm from the rows' squared norms that
-    the add kept on the GPU; rowrms: 4 in, 3 out, its row state on the GPU; GACC: in = the rows the previous step
+    as multiples of the distinct rows U (Adam: in = gather + the update's p, m, v, accumulator = 5, out = the add's
+    accumulator rows (a step's first add writes them without reading) + p, m, v = 4, the clip norm from the rows'
+    squared norms that the add kept on the GPU; rowrms: 3 in, 2 out, its row state on the GPU; GACC: in = the rows the previous step
     did not read (the others come from the device cache), out = the updated rows; HOT rows never cross), over the
     measured pinned copy bandwidths: serial_ms one direction after the other, duplex_ms both at once (this build's
     GACC step overlaps its write-back with the next step); frac = serial_ms / the measured step (above 1 only
@@ -1022,7 +1022,7 @@ def run_host(args):
                 rows_in, rows_out = round(1 - cold[1] / cold[0], 3), 1
             else:
                 u = statistics.mean(distinct)
-                rows_in, rows_out = {"adam": (6, 5), "rowrms": (4, 3)}[name]
+                rows_in, rows_out = {"adam": (5, 4), "rowrms": (3, 2)}[name]
                 gb_in, gb_out = u * rows_in * rb / 1e9, u * rows_out * rb / 1e9
             serial = (gb_in / link["h2d"] + gb_out / link["d2h"]) * 1e3
             duplex = max(gb_in / link["h2d"], gb_out / link["d2h"]) * 1e3

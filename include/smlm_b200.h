@@ -423,7 +423,9 @@ SMLM_API int smlm_host_rows_scatter(float *table, int64_t table_rows, const int6
 
 /* acc[rows[i]] = acc[rows[i]] + grads[i] and touched[rows[i]] = 1 (acc / touched: mapped host tensors of
  * table_rows rows; grads device (n, d) fp32; rows device int64, distinct), skipping the rows whose skip[i] >= 0
- * (skip may be NULL; HOT rows keep their own accumulator on the device). row_sqnorm: NULL, or a device fp32 array
+ * (skip may be NULL; HOT rows keep their own accumulator on the device). A row whose touched mark is 0 is written
+ * as 0 + grads[i] without reading it, so the optimizer steps may leave stepped rows' accumulators uncleared
+ * (SMLM_STEP_KEEP_ACC); touched may be NULL (every row accumulates). row_sqnorm: NULL, or a device fp32 array
  * of table_rows entries that gets each added row's new squared L2 norm (the row_sqnorm input of
  * smlm_touched_norm). Replaces HostEmbedding.accumulate's copy to the host and C scatter-add
  * (host_values.py:121-150, host_rows.c host_rows_add) and HostRowStore.norm's pass over the accumulator rows

@@ -68,9 +68,11 @@ __global__ void __launch_bounds__(256) host_scatter_kernel(float* table, const i
     }
 }
 
-// acc[rows[i]] = acc[rows[i]] + grads[i], touched[rows[i]] = 1, for the rows with skip[i] < 0 (rows distinct); with
-// row_sq, also row_sq[rows[i]] = the new row's squared L2 norm (summed in double, stored fp32), so the clip norm
-// needs no second pass over the accumulator rows.
+// acc[rows[i]] = acc[rows[i]] + grads[i], touched[rows[i]] = 1, for the rows with skip[i] < 0 (rows distinct); a row
+// whose touched mark is 0 gets 0 + grads[i] without its old value being read (the optimizer steps leave stepped
+// rows' accumulators as they are, so a step's first add writes them: one crossing of the host link instead of
+// three); with row_sq, also row_sq[rows[i]] = the new row's squared L2 norm (summed in double, stored fp32), so the
+// clip norm needs no second pass over the accumulator rows.
 __global__ void __launch_bounds__(256) host_add_kernel(float* acc, uint8_t* touched, float* row_sq, const int64_t* rows,
                                                        const float* grads, const int32_t* skip, int64_t n,
                                                        int64_t table_rows, int d, int* status) {
@@ -85,9 +87,10 @@ __global__ void __launch_bounds__(256) host_add_kernel(float* acc, uint8_t* touc
         }
         float* dst = acc + r * d;
         const float* src = grads + i * d;
+        const bool fresh = touched != nullptr && touched[r] == 0;
         double sq = 0.0;
         for (int c = lane * 4; c < d; c += 128) {
-            float4 a = *reinterpret_cast<float4*>(dst + c);
+            float4 a = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<float4*>(dst + c);
             const float4 g = *reinterpret_cast<const float4*>(src + c);
             a.x = a.x + g.x; a.y = a.y + g.y; a.z = a.z + g.z; a.w = a.w + g.w;
             *reinterpret_cast<float4*>(dst + c) = a;
@@ -100,6 +103,7 @@ __global__ void __launch_bounds__(256) host_add_kernel(float* acc, uint8_t* touc
             sq = warp_sum_d(sq);
             if (lane == 0) row_sq[r] = (float)sq;
         }
+        __syncwarp();                      // every lane has read the mark before lane 0 sets it
         if (lane == 0 && touched) touched[r] = 1;
     }
 }

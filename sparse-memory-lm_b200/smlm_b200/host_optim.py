@@ -19,36 +19,48 @@ from .sparse_values import LazyRowAdam, row_store
 class HostRowStore:
     """The gradient store of a host table (reference: host_optim.py:78-107): `acc` (fp32, shaped like the table)
     and `touched` in host RAM, the deferred clip factor `grad_scale`, and `hot` (the table's HOT rows, which keep
-    their own accumulator on the GPU). `row_sq` (no counterpart): the touched rows' squared norms on the GPU, written
-    by HostEmbedding.accumulate's add kernel, so norm() does not read the accumulator rows back over the host link;
-    code that writes `acc` by other means sets it to None (norm() then reads the rows)."""
+    their own accumulator on the GPU). The optimizer steps leave the stepped rows' accumulator values in place (a
+    step's first add overwrites them, `smlm_host_rows_add`), so the array itself (`_acc`) holds stale rows wherever
+    `touched` is 0; reading `acc` zeroes those first, as the reference's store always has them. `row_sq` (no
+    counterpart): the touched rows' squared norms on the GPU, written by HostEmbedding.accumulate's add kernel, so
+    norm() does not read the accumulator rows back over the host link; code that writes the accumulator by other
+    means sets it to None (norm() then reads the rows)."""
 
     def __init__(self, table):
         if table.device.type != "cpu":
             raise ValueError("host value tables must stay on the CPU")
-        self.acc = torch.zeros(table.shape, dtype=torch.float32)
+        self._acc = torch.zeros(table.shape, dtype=torch.float32)
         self.touched = torch.zeros(table.shape[0], dtype=torch.bool)
+        self.stale = False                 # rows with touched == 0 may hold old values in _acc
         self.grad_scale = 1.0
         self.hot = getattr(table, "hot_rows", None)
         self.row_sq = None
 
+    @property
+    def acc(self):
+        if self.stale:
+            self._acc[~self.touched] = 0.0
+            self.stale = False
+        return self._acc
+
     def sq_buffer(self, device):
         """The device array of per-row squared norms (created on first use)."""
         if self.row_sq is None or self.row_sq.device != device:
-            self.row_sq = torch.empty(self.acc.shape[0], dtype=torch.float32, device=device)
+            self.row_sq = torch.empty(self._acc.shape[0], dtype=torch.float32, device=device)
         return self.row_sq
 
     def sync(self):
         pass
 
     def reset(self, rows=None):
+        """Drops the touched rows' gradients (their values stay in `_acc`, stale)."""
         if rows is None:
             rows = self.touched.nonzero().squeeze(1)
             if self.hot is not None:
                 self.hot.acc.zero_()
                 self.hot.touched.zero_()
-        self.acc.index_fill_(0, rows, 0.0)
         self.touched.index_fill_(0, rows, False)
+        self.stale = True
         self.grad_scale = 1.0
 
     def norm(self, device=None):
@@ -61,12 +73,12 @@ class HostRowStore:
                 device = self.hot.acc.device
             else:
                 device = torch.device("cuda", torch.cuda.current_device())
-        rows, d = self.acc.shape
+        rows, d = self._acc.shape
         sq = self.row_sq if self.row_sq is not None and self.row_sq.device == device else None
         out = torch.empty((), dtype=torch.float32, device=device)
         ws = L.workspace(L.lib().smlm_touched_workspace(rows), device)
         with torch.cuda.device(device):
-            rc = L.lib().smlm_touched_norm(mapped(self.acc) if sq is None else None, L.ptr(sq), mapped(self.touched),
+            rc = L.lib().smlm_touched_norm(mapped(self._acc) if sq is None else None, L.ptr(sq), mapped(self.touched),
                                            rows, d, L.ptr(out), L.ptr(ws), ws.numel(), L.stream(device))
         L.check(rc, "touched_norm")
         if self.hot is not None:
@@ -132,22 +144,24 @@ class HostLazyRowAdam(LazyRowAdam):
                     if self.state_dtype == "fp32":
                         bc1 = 1 - b1 ** step
                         rc = L.lib().smlm_lazy_adam_step(
-                            mapped(p.detach()), mapped(state["exp_avg"]), mapped(state["exp_avg_sq"]), mapped(st.acc),
+                            mapped(p.detach()), mapped(state["exp_avg"]), mapped(state["exp_avg_sq"]), mapped(st._acc),
                             mapped(st.touched), sp, sf, rows, d, 1 - b1, b2, 1 - b2, math.sqrt(1 - b2 ** step),
-                            group["eps"], -(group["lr"] / bc1), None, L.F32, 0, L.ptr(ws), ws.numel(), L.stream(dev))
+                            group["eps"], -(group["lr"] / bc1), None, L.F32, L.STEP_KEEP_ACC, L.ptr(ws), ws.numel(),
+                            L.stream(dev))
                     else:
                         int8 = self.state_dtype == "int8"
                         rc = L.lib().smlm_lazy_adam_lowmem_step(
                             mapped(p.detach()), mapped(state["exp_avg"]), mapped(state["exp_avg_sq"]),
                             mapped(state["exp_avg_scale"]) if int8 else None,
                             mapped(state["exp_avg_sq_scale"]) if int8 else None, L.I8 if int8 else L.BF16,
-                            mapped(st.acc), mapped(st.touched), sp, sf, rows, d, b1, b2, 1 - b1, 1 - b2, group["eps"],
-                            group["lr"] / (1 - b1 ** step), math.sqrt(1 - b2 ** step), None, L.F32, 0, L.ptr(ws),
-                            ws.numel(), L.stream(dev))
+                            mapped(st._acc), mapped(st.touched), sp, sf, rows, d, b1, b2, 1 - b1, 1 - b2, group["eps"],
+                            group["lr"] / (1 - b1 ** step), math.sqrt(1 - b2 ** step), None, L.F32, L.STEP_KEEP_ACC,
+                            L.ptr(ws), ws.numel(), L.stream(dev))
                     L.check(rc, "host lazy Adam step")
                     torch.cuda.current_stream(dev).synchronize()
                 del keep
-                st.grad_scale = 1.0         # the kernel zeroed the accumulator rows and cleared the marks
+                st.grad_scale = 1.0         # the kernel cleared the marks and left the rows' values (stale now)
+                st.stale = True
 
 
 def value_table_memory_by_device(model, value_state="fp32", value_optim="adam"):

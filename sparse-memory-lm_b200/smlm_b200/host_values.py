@@ -178,8 +178,8 @@ class HostEmbedding(nn.Embedding):
         from .sparse_values import row_store
         st = row_store(self.weight)
         with self.phase("scatter", dev):
-            rc = L.lib().smlm_host_rows_add(mapped(st.acc), mapped(st.touched), L.ptr(st.sq_buffer(dev)),
-                                            st.acc.shape[0], L.ptr(rows), L.ptr(gradient.contiguous()), L.ptr(slot),
+            rc = L.lib().smlm_host_rows_add(mapped(st._acc), mapped(st.touched), L.ptr(st.sq_buffer(dev)),
+                                            st._acc.shape[0], L.ptr(rows), L.ptr(gradient.contiguous()), L.ptr(slot),
                                             rows.numel(), gradient.shape[1], L.status_ptr(dev), L.stream(dev))
             L.check(rc, "host_rows_add")
             _sync(dev)                     # the host accumulator is complete before CPU code reads it

@@ -130,11 +130,12 @@ class RowWiseOptimizer(torch.optim.Optimizer):
             elif bool(st.touched.any()):
                 ws = L.workspace(L.lib().smlm_touched_workspace(p.shape[0]), dev)
                 rc = L.lib().smlm_rowwise_step(
-                    mapped(p.detach()), mapped(st.acc), mapped(st.touched), L.ptr(state["v"]), L.ptr(count), sp, sf,
+                    mapped(p.detach()), mapped(st._acc), mapped(st.touched), L.ptr(state["v"]), L.ptr(count), sp, sf,
                     p.shape[0], p.shape[1], kind,
-                    group["beta2"], group["eps"], group["lr"], 0, L.ptr(ws), ws.numel(), L.stream(dev))
+                    group["beta2"], group["eps"], group["lr"], L.STEP_KEEP_ACC, L.ptr(ws), ws.numel(), L.stream(dev))
                 L.check(rc, "rowwise_step (host table)")
                 torch.cuda.current_stream(dev).synchronize()
+                st.stale = True           # the rows' accumulator values stay; the next add overwrites them
         del keep
         st.grad_scale = 1.0
 

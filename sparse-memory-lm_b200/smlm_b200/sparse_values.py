@@ -125,7 +125,7 @@ def row_store(table):
     (smlm_b200.host_values) gets a HostRowStore, or keeps the StepStore of its GACC step accumulator."""
     if getattr(table, "host_values", False):
         st = getattr(table, "row_store", None)
-        if st is None or (getattr(st, "steprows", None) is None and tuple(st.acc.shape) != tuple(table.shape)):
+        if st is None or (getattr(st, "steprows", None) is None and tuple(st._acc.shape) != tuple(table.shape)):
             from .host_optim import HostRowStore
             st = table.row_store = HostRowStore(table)
         return st

@@ -5,7 +5,7 @@ tests/test_host_values.py, tests/test_hot_rows.py)."""
 import pytest
 import torch
 
-from smlm_b200.host_optim import value_table_memory_by_device
+from smlm_b200.host_optim import HostRowStore, value_table_memory_by_device
 from smlm_b200.host_values import HostEmbedding, StepRows, enable_host_values, host_timings
 from smlm_b200.model import ModelConfig, Transformer
 
@@ -64,3 +64,17 @@ def test_step_rows_slots_overflow_and_reset():
     sr.reset()
     assert sr.n == 0 and sr.spilled() is None and sr.spilled_steps == 1
     assert int((sr.slot >= 0).sum()) == 0 and torch.count_nonzero(sr.acc) == 0
+
+
+def test_host_row_store_reads_zeros_where_rows_were_stepped():
+    """The optimizer steps leave stepped rows' accumulator values in place (the next add overwrites them); reading
+    `acc` shows zeros there, as the reference's store, and keeps the touched rows."""
+    st = HostRowStore(torch.zeros(6, 4))
+    st._acc[:] = torch.arange(24.0).view(6, 4)
+    st.touched[[1, 4]] = True
+    st.stale = True
+    acc = st.acc
+    assert torch.equal(acc[[1, 4]], torch.arange(24.0).view(6, 4)[[1, 4]])
+    assert torch.count_nonzero(acc[[0, 2, 3, 5]]) == 0 and not st.stale
+    st.reset()
+    assert st.stale and not st.touched.any() and torch.count_nonzero(st.acc) == 0

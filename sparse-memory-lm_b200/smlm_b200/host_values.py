@@ -105,6 +105,15 @@ class HostEmbedding(nn.Embedding):
         self.step_rows = None
         self.register_state_dict_pre_hook(lambda module, *_: module.flush())
         self._register_load_state_dict_pre_hook(lambda *_: self.flush())
+        self.register_load_state_dict_post_hook(lambda module, _keys: module.reload_hot())
+
+    def reload_hot(self):
+        """After the table was loaded: the HOT rows' device copies from the new table, their gradients dropped
+        (the row-wise optimizer takes their state from its own loaded state at the next step)."""
+        if self.hot is not None:
+            self.hot.values.copy_(self.weight.detach().index_select(0, self.hot.rows.cpu()))
+            self.hot.acc.zero_()
+            self.hot.touched.zero_()
 
     def flush(self):
         """Write the GPU copies of the hot rows back into the host table (after any write-back of a GACC step still

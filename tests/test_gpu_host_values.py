@@ -270,6 +270,13 @@ def test_hot_rows_and_gacc_train_like_rows_in_ram(hot_frac, capacity, overlap):
         assert spilled
     table = other.state_dict()["values.weight"]             # flushes the GPU rows into the table
     torch.testing.assert_close(table, plain.values.weight.detach(), rtol=1e-5, atol=1e-6)
+    if hot_frac:
+        # loading a table refreshes the HOT rows' device copies
+        saved = {k: v.clone() for k, v in other.state_dict().items()}
+        other.values.hot.values.add_(1.0)
+        other.load_state_dict(saved)
+        hot = other.values.hot
+        assert torch.equal(hot.values.cpu(), other.values.weight.detach()[hot.rows.cpu()])
     sa, sb = opt_a.state_dict()["state"][0], opt_b.state_dict()["state"][0]
     assert sa.keys() == sb.keys() == {"step", "v", "n"}
     torch.testing.assert_close(sb["v"], sa["v"], rtol=1e-5, atol=1e-9)

@@ -83,6 +83,13 @@ def parse():
                     help="--case host: which implementations to time")
     ap.add_argument("--host-configs", default="adam,rowrms,rowrms+gacc,rowrms+hot5%+gacc",
                     help="--case host: comma-separated configurations to time")
+    ap.add_argument("--model", choices=["b1m", "b16m"], default="b1m",
+                    help="--case model: b1m = BASELINE config 2 (the B-1M step, one CUDA graph); b16m = the "
+                         "reference's B-16M-sparse training step (12 layers, three memory layers sharing the "
+                         "16.8M-row table, 32 x 1024 tokens), eager, beside the reference's own run of it")
+    ap.add_argument("--micro-batch", type=int, default=0,
+                    help="--case model --model b16m: sequences per forward / backward, gradients accumulated over "
+                         "the step's 32 (0: all 32 at once; the reference's run used 4)")
     ap.add_argument("--no-inference", action="store_true", help="leave the inference measurement out of the line")
     ap.add_argument("--eager", action="store_true",
                     help="time the step as eager calls (default on one GPU: the step captured as one CUDA graph)")
@@ -719,6 +726,86 @@ def run_model_case(args):
             "unique_rows_per_step": uniq[0] if uniq else None, "clocks": clocks.summary()}
 
 
+# ------------------------------------------------------------------------------------------- B-16M model step
+def run_model_b16m(args):
+    """The reference's B-16M-sparse training step on one GPU (its `smlm/train.py` preset and its own long run's
+    settings: 12 layers, d_model 384, 6 heads, SwiGLU 1024, vocab 50,304 tied, memory layers 2 / 6 / 10 sharing one
+    4096^2 = 16,777,216 x 384 fp32 table with BatchNorm queries and swilu, row-sparse gradients, LazyRowAdam with
+    fp32 moments at value lr 2.4e-3 and fused AdamW (lr 6e-4, betas 0.9 / 0.95, weight decay 0.1) on the rest,
+    values and the rest clipped separately to 1.0, bf16 autocast, 32 sequences x 1024 tokens per step uniform over
+    the vocabulary, next-token cross entropy; random-init weights, seeded synthetic tokens). --impl cuda runs this
+    build's modules, --impl reference the reference's own `smlm` package (vendored unmodified in baseline/_ref)
+    with its Triton memory kernels, on the same GPU. --micro-batch sets the sequences per forward (the gradients of
+    the step's micro-batches accumulate, loss / accum each, as the reference's loop does; its long run used 4).
+    The step is eager (three backward passes into the shared table's row store per micro-batch are not
+    capturable): CUDA events around --steps consecutive steps after --warmup."""
+    dev = torch.device("cuda", 0)
+    B, T, vocab = 32, 1024, 50304
+    mb = args.micro_batch or B
+    if B % mb:
+        raise ValueError("--micro-batch must divide 32")
+    accum = B // mb
+    if args.impl == "reference":
+        if not os.path.isfile(os.path.join(REF_PKG, "smlm", "model.py")):
+            return {"case": "model", "impl": "reference", "unavailable": "the reference package is not in "
+                    "baseline/_ref (build it with __graft_entry__.build())"}
+        if REF_PKG not in sys.path:
+            sys.path.insert(0, REF_PKG)
+        from smlm.model import ModelConfig, Transformer
+        from smlm.optim import build_optimizer, clip_grads
+        extra = dict(mem_impl="triton")
+        what = "the reference's smlm package (baseline/_ref, unmodified), mem_impl=triton"
+    else:
+        from smlm_b200.model import ModelConfig, Transformer
+        from smlm_b200.optim import build_optimizer, clip_grads
+        extra = {}
+        what = "this build (smlm_b200)"
+    cfg = ModelConfig(vocab_size=vocab, d_model=D_MODEL, n_layers=12, n_heads=6, ffn_hidden=1024, max_seq_len=T,
+                      mem_layers=[2, 6, 10], mem_n_keys=4096, mem_share_values=True, mem_value_grad="row_sparse",
+                      **extra)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = Transformer(cfg)
+    model.train()
+    opt = build_optimizer(model, lr=6e-4, value_lr=2.4e-3, weight_decay=0.1, betas=(0.9, 0.95))
+    gen = torch.Generator(device=dev).manual_seed(2)
+    seqs = [torch.randint(0, vocab, (B, T + 1), device=dev, generator=gen) for _ in range(2)]
+
+    def step(i):
+        s_ = seqs[i % 2]
+        loss_sum = torch.zeros((), device=dev)
+        for a in range(accum):
+            x = s_[a * mb:(a + 1) * mb]
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                _, loss = model(x[:, :-1], x[:, 1:])
+            (loss / accum).backward()
+            loss_sum += loss.detach() / accum
+        clip_grads(model, 1.0)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss_sum
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(0) as clocks:
+        s.record()
+        for i in range(args.warmup, args.warmup + args.steps):
+            loss = step(i)
+        e.record()
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    return {"case": "model", "config": "b16m-model-train", "impl": args.impl, "what": what,
+            "model": "B-16M-sparse: 12 layers, d_model 384, 6 heads, SwiGLU 1024, vocab 50304 tied, PKM in layers "
+                     "2/6/10 sharing one 4096^2 x 384 fp32 table (BatchNorm query, swilu), LazyRowAdam fp32",
+            "tokens_per_step": B * T, "micro_batch": mb, "grad_accum": accum, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "tokens_per_s": round(B * T / (ms / 1e3), 1),
+            "loss": round(float(loss), 4), "peak_gib": round(torch.cuda.max_memory_allocated(dev) / 2**30, 1),
+            "clocks": clocks.summary(),
+            "reference_published": "138.0k tok/s on an H200 NVL (its long B-16M run, micro-batch 4, Triton kernels)"}
+
+
 # ------------------------------------------------------------------------------------------------ engram
 def run_engram(args):
     """The reference's default Engram n-gram memory module on one GPU (orders 2 and 3, 8 hash heads each, rows of
@@ -1272,7 +1359,8 @@ def main():
         print(json.dumps(run_engram(args)), flush=True)
         return
     if args.case == "model":
-        print(json.dumps(run_model_case(args)), flush=True)
+        line = run_model_case(args) if args.model == "b1m" and args.impl == "cuda" else run_model_b16m(args)
+        print(json.dumps(line), flush=True)
         return
     if args.case == "host":
         print(json.dumps(run_host(args)), flush=True)

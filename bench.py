@@ -737,8 +737,8 @@ def run_model_b16m(args):
     build's modules, --impl reference the reference's own `smlm` package (vendored unmodified in baseline/_ref)
     with its Triton memory kernels, on the same GPU. --micro-batch sets the sequences per forward (the gradients of
     the step's micro-batches accumulate, loss / accum each, as the reference's loop does; its long run used 4).
-    The step is eager (three backward passes into the shared table's row store per micro-batch are not
-    capturable): CUDA events around --steps consecutive steps after --warmup."""
+    This build's step is captured as one CUDA graph (GraphedStep; its eager time beside it), the reference's runs
+    eagerly: CUDA events around --steps consecutive steps after --warmup."""
     dev = torch.device("cuda", 0)
     B, T, vocab = 32, 1024, 50304
     mb = args.micro_batch or B
@@ -767,12 +767,13 @@ def run_model_b16m(args):
     with torch.device(dev):
         model = Transformer(cfg)
     model.train()
-    opt = build_optimizer(model, lr=6e-4, value_lr=2.4e-3, weight_decay=0.1, betas=(0.9, 0.95))
+    graphed = args.impl == "cuda"       # this build captures the whole step (LazyRowAdam(capturable=True))
+    opt = build_optimizer(model, lr=6e-4, value_lr=2.4e-3, weight_decay=0.1, betas=(0.9, 0.95),
+                          **({"capturable": True} if graphed else {}))
     gen = torch.Generator(device=dev).manual_seed(2)
     seqs = [torch.randint(0, vocab, (B, T + 1), device=dev, generator=gen) for _ in range(2)]
 
-    def step(i):
-        s_ = seqs[i % 2]
+    def train(s_):
         loss_sum = torch.zeros((), device=dev)
         for a in range(accum):
             x = s_[a * mb:(a + 1) * mb]
@@ -785,24 +786,38 @@ def run_model_b16m(args):
         opt.zero_grad(set_to_none=True)
         return loss_sum
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(0) as clocks:
-        s.record()
-        for i in range(args.warmup, args.warmup + args.steps):
-            loss = step(i)
-        e.record()
+    def timed(step):
+        for i in range(args.warmup):
+            step(seqs[i % 2])
         torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / args.steps
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(0) as clocks:
+            s.record()
+            for i in range(args.warmup, args.warmup + args.steps):
+                loss = step(seqs[i % 2])
+            e.record()
+            torch.cuda.synchronize()
+        return s.elapsed_time(e) / args.steps, float(loss), clocks.summary()
+
+    eager_ms = None
+    if graphed:
+        # captured first (autograd binds each parameter's gradient accumulation to the stream of its first backward)
+        from smlm_b200.graph_step import GraphedStep
+        gstep = GraphedStep(train, [seqs[0]], opt.opts, warmup=max(3, args.warmup))
+        ms, loss, clocks = timed(gstep)
+        del gstep
+        eager_ms, _, _ = timed(train)
+    else:
+        ms, loss, clocks = timed(train)
     return {"case": "model", "config": "b16m-model-train", "impl": args.impl, "what": what,
+            "step_mode": "one CUDA graph per step (GraphedStep)" if graphed else "eager",
+            "eager_ms_per_step": round(eager_ms, 3) if eager_ms is not None else None,
             "model": "B-16M-sparse: 12 layers, d_model 384, 6 heads, SwiGLU 1024, vocab 50304 tied, PKM in layers "
                      "2/6/10 sharing one 4096^2 x 384 fp32 table (BatchNorm query, swilu), LazyRowAdam fp32",
             "tokens_per_step": B * T, "micro_batch": mb, "grad_accum": accum, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "tokens_per_s": round(B * T / (ms / 1e3), 1),
-            "loss": round(float(loss), 4), "peak_gib": round(torch.cuda.max_memory_allocated(dev) / 2**30, 1),
-            "clocks": clocks.summary(),
+            "loss": round(loss, 4), "peak_gib": round(torch.cuda.max_memory_allocated(dev) / 2**30, 1),
+            "clocks": clocks,
             "reference_published": "138.0k tok/s on an H200 NVL (its long B-16M run, micro-batch 4, Triton kernels)"}
 
 

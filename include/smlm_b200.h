@@ -161,6 +161,15 @@ SMLM_API int smlm_lazy_adam_step(float *param, float *exp_avg, float *exp_avg_sq
                                  float neg_step_size, void *value_copy, int copy_dtype, int flags, void *workspace,
                                  size_t workspace_bytes, void *stream);
 
+/* smlm_lazy_adam_step with the six step scalars read from device memory when the kernel runs: scalars_dev[0..5] =
+ * one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step_size (fp32), so a training step with several backward
+ * passes into one table (the accumulator written, then stepped) can be captured in a CUDA graph; the caller writes
+ * each step's scalars before replaying. No counterpart in the reference. */
+SMLM_API int smlm_lazy_adam_step_dev(float *param, float *exp_avg, float *exp_avg_sq, float *acc, uint8_t *touched,
+                                     const float *grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
+                                     const float *scalars_dev, void *value_copy, int copy_dtype, int flags,
+                                     void *workspace, size_t workspace_bytes, void *stream);
+
 /* Lazy Adam with compact moments (state_dtype SMLM_BF16: bf16 exp_avg / exp_avg_sq; SMLM_I8: int8 exp_avg codes
  * c with m = sign(c) (c / 127)^2 exp_avg_scale[row], uint8 exp_avg_sq codes u with v = ((u / 255)
  * exp_avg_sq_scale[row])^4, the scales fp32 (rows,)). Per touched row, in fp32 with every operation rounded:

@@ -76,12 +76,13 @@ struct AdamArgs {
     float one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step;
     void* copy;
     int copy_dtype;
-    int keep_acc;  // leave the consumed accumulator rows as they are (they count as zero once untouched)
+    int keep_acc;        // leave the consumed accumulator rows as they are (they count as zero once untouched)
+    const float* s_dev;  // the six scalars above from device memory instead (a step captured in a CUDA graph)
 };
 
 // Element update in the reference C loop's order (host_rows.c:69-76), every operation rounded on its own.
-__device__ __forceinline__ void adam_elem(const AdamArgs& a, float scale, float& p, float& m, float& v, float g) {
-    adam_update(AdamScalars{a.one_minus_b1, a.b2, a.one_minus_b2, a.bc2_sqrt, a.eps, a.neg_step}, scale, p, m, v, g);
+__device__ __forceinline__ void adam_elem(const AdamScalars& sc, float scale, float& p, float& m, float& v, float g) {
+    adam_update(sc, scale, p, m, v, g);
 }
 
 template <int VEC>
@@ -89,6 +90,8 @@ __global__ void __launch_bounds__(256) lazy_adam_kernel(AdamArgs a) {
     const int lane = lane_id();
     const int n = *a.count;
     const float scale = a.scale_dev ? *a.scale_dev : a.scale;
+    const AdamScalars sc = a.s_dev ? AdamScalars{a.s_dev[0], a.s_dev[1], a.s_dev[2], a.s_dev[3], a.s_dev[4], a.s_dev[5]}
+                                   : AdamScalars{a.one_minus_b1, a.b2, a.one_minus_b2, a.bc2_sqrt, a.eps, a.neg_step};
     const int warps = gridDim.x * (blockDim.x >> 5);
     for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += warps) {
         const int64_t r = a.list[i];
@@ -100,10 +103,10 @@ __global__ void __launch_bounds__(256) lazy_adam_kernel(AdamArgs a) {
                 float4 m = *reinterpret_cast<float4*>(a.m + base + c);
                 float4 v = *reinterpret_cast<float4*>(a.v + base + c);
                 const float4 g = *reinterpret_cast<float4*>(a.acc + base + c);
-                adam_elem(a, scale, p.x, m.x, v.x, g.x);
-                adam_elem(a, scale, p.y, m.y, v.y, g.y);
-                adam_elem(a, scale, p.z, m.z, v.z, g.z);
-                adam_elem(a, scale, p.w, m.w, v.w, g.w);
+                adam_elem(sc, scale, p.x, m.x, v.x, g.x);
+                adam_elem(sc, scale, p.y, m.y, v.y, g.y);
+                adam_elem(sc, scale, p.z, m.z, v.z, g.z);
+                adam_elem(sc, scale, p.w, m.w, v.w, g.w);
                 *reinterpret_cast<float4*>(a.p + base + c) = p;
                 *reinterpret_cast<float4*>(a.m + base + c) = m;
                 *reinterpret_cast<float4*>(a.v + base + c) = v;
@@ -122,7 +125,7 @@ __global__ void __launch_bounds__(256) lazy_adam_kernel(AdamArgs a) {
         } else {
             for (int c = lane; c < a.d; c += 32) {
                 float p = a.p[base + c], m = a.m[base + c], v = a.v[base + c];
-                adam_elem(a, scale, p, m, v, a.acc[base + c]);
+                adam_elem(sc, scale, p, m, v, a.acc[base + c]);
                 a.p[base + c] = p;
                 a.m[base + c] = m;
                 a.v[base + c] = v;
@@ -384,11 +387,11 @@ extern "C" size_t smlm_touched_workspace(int64_t rows) {
     return layout_touched(std::max<int64_t>(rows, 0), nullptr, &b);
 }
 
-extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_sq, float* acc, uint8_t* touched,
-                                   const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
-                                   float one_minus_b1, float b2, float one_minus_b2, float bc2_sqrt, float eps,
-                                   float neg_step_size, void* value_copy, int copy_dtype, int flags, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
+static int lazy_adam_impl(float* param, float* exp_avg, float* exp_avg_sq, float* acc, uint8_t* touched,
+                          const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d, float one_minus_b1,
+                          float b2, float one_minus_b2, float bc2_sqrt, float eps, float neg_step_size,
+                          const float* scalars_dev, void* value_copy, int copy_dtype, int flags, void* workspace,
+                          size_t workspace_bytes, void* stream) {
     SMLM_CHECK_ARG(rows >= 0 && d >= 0, "lazy_adam_step: negative size");
     SMLM_CHECK_ARG(rows < (int64_t)0x7fffffff, "lazy_adam_step: rows must be below 2^31");
     SMLM_CHECK_ARG(d < (1 << 30), "lazy_adam_step: d too large");
@@ -403,7 +406,7 @@ extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_
     if (rc != SMLM_OK) return rc;
     AdamArgs a{param, exp_avg, exp_avg_sq, acc, touched, b.list, b.count, grad_scale_dev, grad_scale, (int)d,
                one_minus_b1, b2, one_minus_b2, bc2_sqrt, eps, neg_step_size, value_copy, copy_dtype,
-               (flags & SMLM_STEP_KEEP_ACC) ? 1 : 0};
+               (flags & SMLM_STEP_KEEP_ACC) ? 1 : 0, scalars_dev};
     const bool vec = d % 4 == 0 && reinterpret_cast<uintptr_t>(param) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(exp_avg) % 16 == 0 && reinterpret_cast<uintptr_t>(exp_avg_sq) % 16 == 0 &&
                      reinterpret_cast<uintptr_t>(acc) % 16 == 0 &&
@@ -413,6 +416,26 @@ extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_
     else lazy_adam_kernel<1><<<blocks, 256, 0, st>>>(a);
     SMLM_LAUNCHED("lazy_adam_kernel");
     return SMLM_OK;
+}
+
+extern "C" int smlm_lazy_adam_step(float* param, float* exp_avg, float* exp_avg_sq, float* acc, uint8_t* touched,
+                                   const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
+                                   float one_minus_b1, float b2, float one_minus_b2, float bc2_sqrt, float eps,
+                                   float neg_step_size, void* value_copy, int copy_dtype, int flags, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    return lazy_adam_impl(param, exp_avg, exp_avg_sq, acc, touched, grad_scale_dev, grad_scale, rows, d, one_minus_b1,
+                          b2, one_minus_b2, bc2_sqrt, eps, neg_step_size, nullptr, value_copy, copy_dtype, flags,
+                          workspace, workspace_bytes, stream);
+}
+
+extern "C" int smlm_lazy_adam_step_dev(float* param, float* exp_avg, float* exp_avg_sq, float* acc, uint8_t* touched,
+                                       const float* grad_scale_dev, float grad_scale, int64_t rows, int64_t d,
+                                       const float* scalars_dev, void* value_copy, int copy_dtype, int flags,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+    SMLM_CHECK_ARG(scalars_dev != nullptr, "lazy_adam_step_dev: null scalars");
+    return lazy_adam_impl(param, exp_avg, exp_avg_sq, acc, touched, grad_scale_dev, grad_scale, rows, d, 0.f, 0.f,
+                          0.f, 0.f, 0.f, 0.f, scalars_dev, value_copy, copy_dtype, flags, workspace, workspace_bytes,
+                          stream);
 }
 
 extern "C" int smlm_lazy_adam_lowmem_step(float* param, void* exp_avg, void* exp_avg_sq, float* exp_avg_scale,

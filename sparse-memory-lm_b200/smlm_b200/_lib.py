@@ -61,6 +61,7 @@ SIGNATURES = {
                                                 _p, _p, _i32, _p, _sz, _p]),
     "smlm_lazy_adam_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _f32,
                                    _p, _i32, _i32, _p, _sz, _p]),
+    "smlm_lazy_adam_step_dev": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _p, _p, _i32, _i32, _p, _sz, _p]),
     "smlm_lazy_adam_lowmem_step": (_i32, [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _f32, _i64, _i64, _f32, _f32, _f32,
                                           _f32, _f32, _f32, _f32, _p, _i32, _i32, _p, _sz, _p]),
     "smlm_rowwise_step": (_i32, [_p, _p, _p, _p, _p, _p, _f32, _i64, _i64, _i32, _f32, _f32, _f32, _i32, _p, _sz,

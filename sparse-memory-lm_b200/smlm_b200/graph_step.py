@@ -11,7 +11,8 @@ scalars; torch's capturable AdamW keeps its own step on the device) and launches
         out = step(x, g)                 # the step's outputs (static tensors, valid until the next call)
 
 Requirements: the same shapes every step, no host synchronisation inside the step, torch optimizers built with
-capturable=True, LazyRowAdam(capturable=True) with one backward per step (the fused deferred step). Build the
+capturable=True, LazyRowAdam(capturable=True) with fp32 moments (one backward per step takes the fused deferred step,
+several the plain step over the written accumulator; both read their scalars from device memory). Build the
 GraphedStep before running eager backward passes of the model on the legacy default stream: autograd ties each
 parameter's gradient accumulation to the stream of its first backward, and the legacy stream cannot join a
 capture (the warm-up steps here run on a side stream). Eager steps after the capture are fine.

@@ -542,12 +542,14 @@ def _scale_args(grad_scale, device):
 
 
 def lazy_adam_step(param, exp_avg, exp_avg_sq, acc, touched, grad_scale, step, lr, beta1, beta2, eps,
-                   value_copy=None, keep_acc=False, *, rows_per_program=None, block_d=None):
+                   value_copy=None, keep_acc=False, *, rows_per_program=None, block_d=None, scalars_dev=None):
     """In-place lazy Adam step over the touched rows (reference: kernels.py:417-433): torch's Adam formula, global
     step for the bias correction, no weight decay; the touched accumulator rows are zeroed and the mask cleared.
     grad_scale: 0-d tensor (clip factor) or float; step: the step number after this update (1 for the first).
     value_copy: optional (rows, D) bf16 / fp32 tensor that receives the updated rows too. keep_acc: leave the
-    consumed accumulator rows as they are (for accumulators whose untouched rows count as zero)."""
+    consumed accumulator rows as they are (for accumulators whose untouched rows count as zero). scalars_dev: a
+    device fp32 tensor of the six step scalars (LazyRowAdam(capturable=True)); step, lr, betas and eps are then not
+    used."""
     dev = L.require_cuda(param, exp_avg, exp_avg_sq, acc, touched, value_copy)
     for t in (param, exp_avg, exp_avg_sq, acc):
         if t.dtype != torch.float32 or not t.is_contiguous() or t.shape != param.shape:
@@ -557,12 +559,19 @@ def lazy_adam_step(param, exp_avg, exp_avg_sq, acc, touched, grad_scale, step, l
     bc1 = 1 - beta1 ** step
     bc2 = 1 - beta2 ** step
     ws = L.workspace(L.lib().smlm_touched_workspace(rows), dev)
+    copy_code = L.dtype_code(value_copy.dtype) if value_copy is not None else L.F32
+    flags = L.STEP_KEEP_ACC if keep_acc else 0
     with L.timed("lazy_adam_step", L.COMPACT_LAUNCHES + 1):
-        rc = L.lib().smlm_lazy_adam_step(L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(acc),
-                                         L.ptr(touched), sp, sf, rows, D, 1 - beta1, beta2, 1 - beta2,
-                                         math.sqrt(bc2), eps, -(lr / bc1), L.ptr(value_copy),
-                                         L.dtype_code(value_copy.dtype) if value_copy is not None else L.F32,
-                                         L.STEP_KEEP_ACC if keep_acc else 0, L.ptr(ws), ws.numel(), L.stream(dev))
+        if scalars_dev is not None:
+            rc = L.lib().smlm_lazy_adam_step_dev(L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(acc),
+                                                 L.ptr(touched), sp, sf, rows, D, L.ptr(scalars_dev),
+                                                 L.ptr(value_copy), copy_code, flags, L.ptr(ws), ws.numel(),
+                                                 L.stream(dev))
+        else:
+            rc = L.lib().smlm_lazy_adam_step(L.ptr(param), L.ptr(exp_avg), L.ptr(exp_avg_sq), L.ptr(acc),
+                                             L.ptr(touched), sp, sf, rows, D, 1 - beta1, beta2, 1 - beta2,
+                                             math.sqrt(bc2), eps, -(lr / bc1), L.ptr(value_copy), copy_code, flags,
+                                             L.ptr(ws), ws.numel(), L.stream(dev))
     L.check(rc, "lazy_adam_step")
     del keep
 

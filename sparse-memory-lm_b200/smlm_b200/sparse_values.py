@@ -261,7 +261,8 @@ class LazyRowAdam(torch.optim.Optimizer):
     capturable=True (no counterpart in the reference) lets a training step that ends in this optimizer be captured
     in a CUDA graph (smlm_b200.graph_step): the step's bias-correction scalars are read from a small device buffer,
     which prepare_replay() advances and fills (computed as the eager step computes them, so the same bits) before
-    every replay. Captured steps must take the fused deferred path (fp32 moments, one backward per step)."""
+    every replay. Captured steps need fp32 moments: one backward per step takes the fused deferred step, several
+    (memory layers sharing the table, accumulated micro-batches) the plain step over the written accumulator."""
 
     def __init__(self, params, lr, betas=(0.9, 0.95), eps=1e-8, name="memory_values", impl="cuda",
                  state_dtype="fp32", value_copy_dtype=None, capturable=False):
@@ -361,9 +362,22 @@ class LazyRowAdam(torch.optim.Optimizer):
                                               scalars_dev=self._scal[p])
                     st.stepped()
                     continue
+                if self.capturable and self.state_dtype == "fp32":
+                    # several backward passes wrote the accumulator: the plain step, scalars from the device buffer
+                    if not capturing:
+                        state["step"] += 1
+                        self._write_scalars(p, group)
+                    elif p not in self._scal:
+                        raise RuntimeError("LazyRowAdam(capturable=True): run one eager step before capturing")
+                    st.materialize()
+                    K.lazy_adam_step(p, state["exp_avg"], state["exp_avg_sq"], st._acc, st._touched,
+                                     st.grad_scale, 1, group["lr"], b1, b2, group["eps"],
+                                     value_copy=getattr(p, "value_copy", None), keep_acc=st.clean,
+                                     scalars_dev=self._scal[p])
+                    st.stepped()
+                    continue
                 if capturing:
-                    raise RuntimeError("LazyRowAdam: only the fused deferred step (one backward per step into an "
-                                       "empty row store) can be captured")
+                    raise RuntimeError("LazyRowAdam: a captured step needs capturable=True and fp32 moments")
                 state["step"] += 1
                 if self.state_dtype == "fp32" and st.pending is not None and not st.live:
                     # rows of one deferred backward: summed and stepped in one pass, acc never written

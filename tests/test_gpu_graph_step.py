@@ -1,10 +1,14 @@
 """A whole training step captured as one CUDA graph (smlm_b200.graph_step.GraphedStep) and the capturable lazy
-Adam it needs: replays give exactly the parameters, moments and outputs of the same steps run eagerly, and the
-device-buffer scalars give exactly the by-value step."""
+Adam it needs: replays give exactly the parameters, moments and outputs of the same steps run eagerly (one layer
+with the fused deferred step; a model whose three memory layers share one table, with two accumulated
+micro-batches, so several backward passes write the accumulator and the plain step runs), and the device-buffer
+scalars give exactly the by-value step."""
 import pytest
 import torch
 
 from smlm_b200.graph_step import GraphedStep
+from smlm_b200.model import ModelConfig, Transformer
+from smlm_b200.optim import build_optimizer, clip_grads
 from smlm_b200.pkm import ProductKeyMemory
 from smlm_b200.sparse_values import LazyRowAdam, OptimizerSet, clip_row_sparse
 
@@ -79,3 +83,49 @@ def test_device_scalars_equal_by_value_step():
     assert torch.equal(mems[0].values.weight, mems[1].values.weight)
     for k in ("exp_avg", "exp_avg_sq"):
         assert torch.equal(opts[0].state[mems[0].values.weight][k], opts[1].state[mems[1].values.weight][k])
+
+
+def test_graphed_model_step_with_shared_table_equals_eager():
+    """Three memory layers reading one shared table, two micro-batches per step (six backward passes into the
+    table's row store, the accumulator written, then the plain lazy Adam step with device scalars): the graphed
+    steps give the eager steps' losses, parameters and moments bit for bit."""
+    cfg = ModelConfig(vocab_size=256, d_model=64, n_layers=6, n_heads=4, ffn_hidden=128, max_seq_len=32,
+                      mem_layers=[1, 3, 5], mem_n_keys=32, mem_heads=2, mem_knn=8, mem_k_dim=64,
+                      mem_share_values=True, mem_value_grad="row_sparse")
+    models = []
+    for _ in range(2):
+        torch.manual_seed(7)
+        with torch.device(DEV):
+            models.append(Transformer(cfg))
+    opts = [build_optimizer(m, lr=1e-3, value_lr=3e-3, weight_decay=0.1, betas=(0.9, 0.95), capturable=True)
+            for m in models]
+    gen = torch.Generator().manual_seed(8)
+    data = [torch.randint(0, 256, (4, 17), generator=gen).to(DEV) for _ in range(5)]
+
+    def train(model, opt, seqs):
+        total = torch.zeros((), device=DEV)
+        for a in range(2):
+            x = seqs[2 * a:2 * a + 2]
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                _, loss = model(x[:, :-1], x[:, 1:])
+            (loss / 2).backward()
+            total += loss.detach() / 2
+        clip_grads(model, 1.0)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return total
+
+    gs = GraphedStep(lambda seqs: train(models[1], opts[1], seqs), [data[0]], opts[1].opts, warmup=1)
+    losses_b = [None] + [gs(seqs).clone() for seqs in data[1:]]
+    losses_a = [train(models[0], opts[0], seqs).clone() for seqs in data]
+    for a, b in zip(losses_a[1:], losses_b[1:]):
+        assert torch.equal(a, b)
+    for (n, pa), pb in zip(models[0].named_parameters(), models[1].parameters()):
+        assert torch.equal(pa, pb), n
+    table_a = models[0].memory_layers()[0].values.weight
+    table_b = models[1].memory_layers()[0].values.weight
+    lazy_a = next(o for o in opts[0].opts if table_a in o.state)
+    lazy_b = next(o for o in opts[1].opts if table_b in o.state)
+    for k in ("exp_avg", "exp_avg_sq"):
+        assert torch.equal(lazy_a.state[table_a][k], lazy_b.state[table_b][k])
+    assert int(lazy_a.state[table_a]["step"]) == int(lazy_b.state[table_b]["step"]) == 5

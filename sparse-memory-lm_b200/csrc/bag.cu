@@ -975,6 +975,192 @@ __global__ void __launch_bounds__(128) bb_rowsum_kernel(SegArgs a, RowAdam ad) {
     if (lane == 0) a.chunk_flags[c] = cflags;
 }
 
+// The backward's norm pass (MODE ROWS_NORM: per touched row the squared norm of its sum and the touched mark, the
+// sum itself not stored) with the rows that a single lookup reads taken 32 at a time. Most rows of a step are read
+// once; walking them one position per warp iteration, as bb_rowsum_kernel walks runs, spent most of the pass on
+// per-position control. Here each batch of 32 sorted positions first finds its singletons (key different from
+// both neighbours in the whole sorted list, so never a row that crosses a chunk border): the warp reads their
+// gradient rows one after the other, coalesced, AHEAD rows in flight, each lane keeping lane-partials of all 32
+// (the fmaf chain over its columns, in bb_rowsum_kernel's order), and a transposing butterfly leaves singleton j's
+// total on lane j, added in the same tree as warp_sum. The other positions go through bb_rowsum_kernel's run
+// walk. The same norms, bit for bit, as summing every row first (bb_rowsum_kernel's write path).
+template <typename GT, int NS, int AHEAD>
+__global__ void __launch_bounds__(128) bb_rownorm_kernel(SegArgs a) {
+    const int lane = lane_id();
+    const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (c >= a.chunks) return;
+    const GT* g = static_cast<const GT*>(a.g);
+    const int64_t start = c * a.P;
+    const int64_t end = min(start + (int64_t)a.P, a.m);
+    const uint32_t valid_lim = (uint32_t)a.rows;
+    const uint32_t first_row = a.keys[start];
+    if (first_row >= valid_lim) {
+        if (lane == 0) a.chunk_flags[c] = 0;
+        return;
+    }
+    const uint32_t last_row = a.keys[end - 1];
+    const uint32_t prev_row = start > 0 ? a.keys[start - 1] : NO_ROW;
+    const uint32_t next_row = end < a.m ? a.keys[end] : NO_ROW;
+    const bool head_cross = prev_row == first_row;
+    const bool tail_cross = last_row < valid_lim && next_row == last_row;
+    const bool mid = head_cross && tail_cross && first_row == last_row;
+    int cflags = 0;
+
+    uint32_t cur = NO_ROW;
+    float sum[NS][4];
+#pragma unroll
+    for (int s = 0; s < NS; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
+
+    auto flush = [&]() {
+        if (cur == NO_ROW) return;
+        float* dst = nullptr;
+        bool direct = false;
+        if (mid) {
+            dst = a.carry_head + c * a.d;
+            cflags |= FLAG_MID;
+        } else if (head_cross && cur == first_row) {
+            dst = a.carry_head + c * a.d;
+        } else if (tail_cross && cur == last_row) {
+            dst = a.carry_tail + c * a.d;
+            cflags |= FLAG_TAIL;
+        } else {
+            direct = true;
+        }
+        float sq = 0.f;
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = (lane + 32 * s) * 4;
+            if (col < a.d) {
+                if (!direct) {
+                    *reinterpret_cast<float4*>(dst + col) = make_float4(sum[s][0], sum[s][1], sum[s][2], sum[s][3]);
+                    continue;
+                }
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                x.x = x.x + sum[s][0]; x.y = x.y + sum[s][1]; x.z = x.z + sum[s][2]; x.w = x.w + sum[s][3];
+                sq = fmaf(x.x, x.x, sq); sq = fmaf(x.y, x.y, sq); sq = fmaf(x.z, x.z, sq); sq = fmaf(x.w, x.w, sq);
+            }
+        }
+        if (direct) {
+            if (a.sqnorm) {
+                sq = warp_sum(sq);
+                if (lane == 0) a.sqnorm[cur] = sq;
+            }
+            if (lane == 0 && a.touched) a.touched[cur] = 1;
+        }
+    };
+    auto load_g = [&](uint32_t tok, float (&v)[NS][4]) {
+        const GT* src = g + (size_t)tok * a.d;
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const int col = (lane + 32 * s) * 4;
+            if (col < a.d) Elt<GT>::template load<4>(src + col, v[s]);
+        }
+    };
+    auto step = [&](uint32_t row, float wv, const float (&gv)[NS][4]) {
+        if (row != cur) {
+            flush();
+            cur = row;
+#pragma unroll
+            for (int s = 0; s < NS; s++) sum[s][0] = sum[s][1] = sum[s][2] = sum[s][3] = 0.f;
+        }
+#pragma unroll
+        for (int s = 0; s < NS; s++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) sum[s][i] = fmaf(wv, gv[s][i], sum[s][i]);
+    };
+
+    for (int64_t b = start; b < end; b += 32) {
+        const int cnt = (int)min((int64_t)32, end - b);
+        uint32_t my_key = NO_ROW, my_tok = 0;
+        float my_w = 0.f;
+        if (lane < cnt) {
+            my_key = a.keys[b + lane];
+            if (my_key < valid_lim) {
+                const uint32_t p = a.pos[b + lane];
+                my_tok = p / (uint32_t)a.k;
+                my_w = load_weight(a.w, a.w_dtype, p);
+            }
+        }
+        const unsigned valid = __ballot_sync(FULL, my_key < valid_lim);  // in-range keys: a prefix
+        if (valid == 0) break;
+        // neighbours in the whole sorted list (across batch and chunk borders)
+        uint32_t before = __shfl_up_sync(FULL, my_key, 1), after = __shfl_down_sync(FULL, my_key, 1);
+        if (lane == 0) before = b > 0 ? a.keys[b - 1] : NO_ROW;
+        if (lane == cnt - 1) after = b + cnt < a.m ? a.keys[b + cnt] : NO_ROW;
+        const bool single = my_key < valid_lim && my_key != before && my_key != after;
+        const unsigned smask = __ballot_sync(FULL, single);
+        const unsigned wmask = valid & ~smask;  // positions for the run walk, in order
+        if (smask) {
+            // lane j takes the j-th singleton's row, token and weight
+            const int src = __fns(smask, 0, lane + 1);
+            const int ns1 = __popc(smask);
+            const uint32_t srow = __shfl_sync(FULL, my_key, src & 31);
+            const uint32_t stok = __shfl_sync(FULL, my_tok, src & 31);
+            const float sw = __shfl_sync(FULL, my_w, src & 31);
+            // gradient rows AHEAD singletons ahead, in a register ring (indices fixed at compile time)
+            float part[32];
+            float gbuf[AHEAD + 1][NS][4];
+#pragma unroll
+            for (int j = 0; j < AHEAD; j++)
+                if (j < ns1) load_g(__shfl_sync(FULL, stok, j), gbuf[j]);
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                part[j] = 0.f;
+                if (j < ns1) {  // warp-uniform
+                    if (j + AHEAD < ns1) load_g(__shfl_sync(FULL, stok, j + AHEAD), gbuf[(j + AHEAD) % (AHEAD + 1)]);
+                    const float wj = __shfl_sync(FULL, sw, j);
+                    float sq = 0.f;
+#pragma unroll
+                    for (int s = 0; s < NS; s++) {
+                        if ((lane + 32 * s) * 4 < a.d) {
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                const float x = fmaf(wj, gbuf[j % (AHEAD + 1)][s][i], 0.f);
+                                sq = fmaf(x, x, sq);
+                            }
+                        }
+                    }
+                    part[j] = sq;
+                }
+            }
+            // transposing butterfly: after the level with offset o, a lane holds the values of the singletons whose
+            // bit log2(o) equals its own, each the sum of its own and its partner's; finally singleton `lane`
+#pragma unroll
+            for (int o = 16, n = 16; o > 0; o >>= 1, n >>= 1) {
+                const bool upper = (lane & o) != 0;
+#pragma unroll
+                for (int j = 0; j < n; j++) {
+                    const float send = upper ? part[j] : part[j + n];
+                    const float keep = upper ? part[j + n] : part[j];
+                    part[j] = keep + __shfl_xor_sync(FULL, send, o);
+                }
+            }
+            if (lane < ns1) {
+                if (a.sqnorm) a.sqnorm[srow] = part[0];
+                if (a.touched) a.touched[srow] = 1;
+            }
+        }
+        if (wmask == 0) continue;
+        const int src = __fns(wmask, 0, lane + 1);
+        const int nw = __popc(wmask);
+        const uint32_t wkey = __shfl_sync(FULL, my_key, src & 31);
+        const uint32_t wtok = __shfl_sync(FULL, my_tok, src & 31);
+        const float wwt = __shfl_sync(FULL, my_w, src & 31);
+        float ga[NS][4], gb[NS][4];
+        load_g(__shfl_sync(FULL, wtok, 0), ga);
+        int t = 0;
+        for (; t + 1 < nw; t += 2) {
+            load_g(__shfl_sync(FULL, wtok, t + 1), gb);
+            step(__shfl_sync(FULL, wkey, t), __shfl_sync(FULL, wwt, t), ga);
+            if (t + 2 < nw) load_g(__shfl_sync(FULL, wtok, t + 2), ga);
+            step(__shfl_sync(FULL, wkey, t + 1), __shfl_sync(FULL, wwt, t + 1), gb);
+        }
+        if (t < nw) step(__shfl_sync(FULL, wkey, t), __shfl_sync(FULL, wwt, t), ga);
+    }
+    flush();
+    if (lane == 0) a.chunk_flags[c] = cflags;
+}
+
 // bb_rowsum_kernel with four chunks per warp, one per quarter-warp (8 lanes x 4 NSQ columns hold a row): the
 // quarters run the same instruction stream on different chunks, so the per-position control (shuffles, run
 // tests, loop) serves four positions, and a warp keeps four rows in flight. Same summation order and results.
@@ -1186,11 +1372,19 @@ template <typename GT, int MODE>
 static int launch_rows_mode(SegArgs a, RowAdam ad, cudaStream_t st) {
     const int ns = (a.d / 4 + 31) / 32;
     const int blocks = (int)((a.chunks + 3) / 4);
-    if (ns <= 1) bb_rowsum_kernel<GT, 1, MODE><<<blocks, 128, 0, st>>>(a, ad);
-    else if (ns == 2) bb_rowsum_kernel<GT, 2, MODE><<<blocks, 128, 0, st>>>(a, ad);
-    else if (ns == 3) bb_rowsum_kernel<GT, 3, MODE><<<blocks, 128, 0, st>>>(a, ad);
-    else bb_rowsum_kernel<GT, 4, MODE><<<blocks, 128, 0, st>>>(a, ad);
-    SMLM_LAUNCHED("bb_rowsum_kernel");
+    if constexpr (MODE == ROWS_NORM) {
+        if (ns <= 1) bb_rownorm_kernel<GT, 1, 2><<<blocks, 128, 0, st>>>(a);
+        else if (ns == 2) bb_rownorm_kernel<GT, 2, 2><<<blocks, 128, 0, st>>>(a);
+        else if (ns == 3) bb_rownorm_kernel<GT, 3, 2><<<blocks, 128, 0, st>>>(a);
+        else bb_rownorm_kernel<GT, 4, 2><<<blocks, 128, 0, st>>>(a);
+        SMLM_LAUNCHED("bb_rownorm_kernel");
+    } else {
+        if (ns <= 1) bb_rowsum_kernel<GT, 1, MODE><<<blocks, 128, 0, st>>>(a, ad);
+        else if (ns == 2) bb_rowsum_kernel<GT, 2, MODE><<<blocks, 128, 0, st>>>(a, ad);
+        else if (ns == 3) bb_rowsum_kernel<GT, 3, MODE><<<blocks, 128, 0, st>>>(a, ad);
+        else bb_rowsum_kernel<GT, 4, MODE><<<blocks, 128, 0, st>>>(a, ad);
+        SMLM_LAUNCHED("bb_rowsum_kernel");
+    }
     bb_fixup_kernel<4, MODE><<<(int)((a.chunks + 7) / 8), 256, 0, st>>>(a, ad);
     SMLM_LAUNCHED("bb_fixup_kernel");
     return SMLM_OK;

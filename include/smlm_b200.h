@@ -300,6 +300,10 @@ SMLM_API size_t smlm_score_select_workspace(int64_t n, int64_t h);
  * TMA-fed, accumulators in TMEM), rounded to bf16 as the reference's bf16 einsum output; their top-knn
  * (score desc, index asc) is kept in the GEMM epilogue, so the (n, h, nk) score tensors are never written.
  * Then the pairs / final top-knn / softmax of smlm_pk_select. Outputs as smlm_pk_select with bf16 scores.
+ * Calls of at most 16 tokens (decoding) with nk a multiple of 256 up to 8192 score on the SIMT cores instead
+ * (one fp32 fmaf chain per sub-key, rounded once to bf16) when the workspace holds their lists: the tensor-core
+ * pipeline has too little work there to hide its latency. Their scores equal the tensor-core path's up to the
+ * order of the fp32 additions (both are within one bf16 step of the reference's einsum).
  * s1_out / s2_out (optional, bf16 (n, h, nk)): the rounded sub-key scores, for checking only.
  * half in {64, 128}; nk % 8 == 0; 1 <= knn <= 32. A kernel-internal wait that gives up raises
  * SMLM_FLAG_TIMEOUT in *status (outputs then invalid); nothing traps.
@@ -316,10 +320,11 @@ SMLM_API int smlm_score_select(const void *q, const void *keys, int64_t n, int64
  * process exits); larger calls return SMLM_ERR_INVALID. The first call on a device looks up that array's device
  * address (cudaGetSymbolAddress) with the device current; make that first call before any stream capture (a
  * first call on a capturing stream returns SMLM_ERR_INVALID). All calls share the one array, so calls that
- * overlap on the GPU (other streams, other threads) race: serialise them. The key range is split over several
- * CTAs per (token tile, head) as the workspace entry point does, but only as far as the array holds the splits'
- * lists (n * h * splits <= SMLM_NOALLOC_MAX_ROWS): near the row limit the call runs unsplit, so a few hundred
- * tokens at most use fewer SMs than smlm_score_select would. The call allocates nothing: no cudaMalloc /
+ * overlap on the GPU (other streams, other threads) race: serialise them. Calls of at most 16 tokens take the
+ * same SIMT path as smlm_score_select. Otherwise the key range is split over several CTAs per (token tile, head)
+ * as the workspace entry point does, but only as far as the array holds the splits' lists (n * h * splits <=
+ * SMLM_NOALLOC_MAX_ROWS): near the row limit the call runs unsplit, so a few hundred tokens at most use fewer
+ * SMs than smlm_score_select would. The call allocates nothing: no cudaMalloc /
  * cudaFree, no allocating library routine. */
 #define SMLM_NOALLOC_MAX_ROWS 16384
 SMLM_API int smlm_score_select_noalloc(const void *q, const void *keys, int64_t n, int64_t h, int64_t nk,

@@ -616,6 +616,111 @@ int score_splits(int64_t n, int64_t h, int64_t ntiles) {
     return (int)std::max<int64_t>(1, std::min<int64_t>(s, 512));
 }
 
+// ------------------------------------------------------------------------------ few tokens: SIMT scoring
+// Decoding and other calls of a few tokens have too little GEMM work to fill the tensor-core pipeline: the
+// tcgen05 kernel then runs a few units split over the key range, each a chain of barrier set-up, TMEM allocation,
+// TMA loads, one MMA per key tile and the merges, and the chain's latency is the call's time. For such calls each
+// CTA instead scores SMALL_KEYS consecutive sub-keys of both halves of one (token, head) with plain FMAs (one
+// sub-key per thread: its row read with 16-byte loads, an fp32 fmaf chain over the half dimension against the
+// query half in shared memory, rounded once to bf16, as the reference's autocast einsum rounds its fp32
+// accumulation), keeps the top 32 of each half (a warp sort per 32 sub-keys, then bitonic merges), and writes one
+// list per half in the fused kernel's list format; the pair kernel merges the key ranges' lists as it merges the
+// fused kernel's splits. Scores equal the fused kernel's wherever the two fp32 sums round to the same bf16 value
+// (the order of fp32 additions differs; both are within one bf16 step of cuBLAS's einsum).
+constexpr int SMALL_KEYS = 256;       // sub-keys per half per CTA (one per thread)
+constexpr int SMALL_MAX_TOKENS = 16;  // calls of at most this many tokens take the SIMT path
+constexpr int SMALL_MAX_RANGES = 32;  // key ranges per (token, head), so n_keys <= 8192
+
+// Key ranges of the SIMT path for this call, 0 when the call takes the tensor-core kernel.
+int small_ranges(int64_t n, int64_t nk) {
+    if (n > SMALL_MAX_TOKENS || nk % SMALL_KEYS != 0 || nk / SMALL_KEYS > SMALL_MAX_RANGES) return 0;
+    return (int)(nk / SMALL_KEYS);
+}
+
+__device__ __forceinline__ uint32_t warp_sort32_desc_u32(uint32_t v, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+        const bool desc = (lane & k) == 0;
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const uint32_t x = __shfl_xor_sync(FULL, v, j);
+            v = (((lane & j) == 0) == desc) ? max(v, x) : min(v, x);
+        }
+    }
+    return v;
+}
+
+// grid: n * h * ranges CTAs of SMALL_KEYS threads; lists[((row * 2 + half) * ranges + range) * 32 + i], row = t * h + hd
+template <int HALF>
+__global__ void __launch_bounds__(SMALL_KEYS) score_small_kernel(const uint16_t* q, const uint16_t* keys, int h,
+                                                                 int nk, int ranges, uint32_t* lists, uint16_t* dbg1,
+                                                                 uint16_t* dbg2) {
+    constexpr int WARPS = SMALL_KEYS / 32;
+    constexpr int VECS = HALF / 8;  // 16-byte vectors of 8 bf16 per sub-key row
+    __shared__ float sq[2 * HALF];
+    __shared__ uint32_t swl[WARPS][32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int range = (int)(blockIdx.x % ranges);
+    const int64_t row = blockIdx.x / ranges;  // token * h + head
+    const int hd = (int)(row % h);
+    for (int i = tid; i < 2 * HALF; i += SMALL_KEYS) sq[i] = bf16_bits_to_f32(q[row * 2 * HALF + i]);
+    __syncthreads();
+    const int col = range * SMALL_KEYS + tid;
+#pragma unroll 1
+    for (int half = 0; half < 2; half++) {
+        const uint4* krow = reinterpret_cast<const uint4*>(keys + ((int64_t)(hd * 2 + half) * nk + col) * HALF);
+        uint4 kv[VECS];
+#pragma unroll
+        for (int i = 0; i < VECS; i++) kv[i] = __ldg(krow + i);
+        const float* qh = sq + half * HALF;
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < VECS; i++) {
+            const uint32_t w4[4] = {kv[i].x, kv[i].y, kv[i].z, kv[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                acc = fmaf(qh[8 * i + 2 * j], bf16_bits_to_f32(w4[j] & 0xffffu), acc);
+                acc = fmaf(qh[8 * i + 2 * j + 1], bf16_bits_to_f32(w4[j] >> 16), acc);
+            }
+        }
+        const uint32_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
+        uint16_t* dbg = half ? dbg2 : dbg1;
+        if (dbg) dbg[row * nk + col] = (uint16_t)bits;
+        const uint32_t key = score_key(bits, col);
+        swl[warp][lane] = warp_sort32_desc_u32(key, lane);
+        __syncthreads();
+        if (warp == 0) {
+            // sorted list + reversed next sorted list -> their elementwise maxima hold the top 32 of both as a
+            // bitonic sequence -> half-cleaners sort it
+            uint32_t k = swl[0][lane];
+#pragma unroll
+            for (int w = 1; w < WARPS; w++) {
+                k = max(k, swl[w][31 - lane]);
+#pragma unroll
+                for (int j = 16; j > 0; j >>= 1) {
+                    const uint32_t x = __shfl_xor_sync(FULL, k, j);
+                    k = (lane & j) ? min(k, x) : max(k, x);
+                }
+            }
+            lists[((row * 2 + half) * ranges + range) * 32 + lane] = k;
+        }
+        __syncthreads();
+    }
+}
+
+int launch_score_small(const void* q, const void* keys, int64_t n, int64_t h, int64_t nk, int64_t half, int ranges,
+                       uint32_t* lists, void* s1_out, void* s2_out, cudaStream_t st) {
+    const int64_t grid = n * h * ranges;
+    auto* qq = static_cast<const uint16_t*>(q);
+    auto* kk = static_cast<const uint16_t*>(keys);
+    auto* d1 = static_cast<uint16_t*>(s1_out);
+    auto* d2 = static_cast<uint16_t*>(s2_out);
+    if (half == 128) score_small_kernel<128><<<(unsigned)grid, SMALL_KEYS, 0, st>>>(qq, kk, (int)h, (int)nk, ranges, lists, d1, d2);
+    else score_small_kernel<64><<<(unsigned)grid, SMALL_KEYS, 0, st>>>(qq, kk, (int)h, (int)nk, ranges, lists, d1, d2);
+    SMLM_LAUNCHED("score_small_kernel");
+    return SMLM_OK;
+}
+
 }  // namespace tc
 }  // namespace smlm
 
@@ -641,6 +746,15 @@ extern "C" int smlm_score_select(const void* q, const void* keys, int64_t n, int
     SMLM_CHECK_ARG(q && keys && scores && indices && weights, "score_select: null pointer");
     SMLM_CHECK_ARG(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(keys) % 16 == 0,
                    "score_select: q and keys must be 16-byte aligned");
+    cudaStream_t st = as_stream(stream);
+    const int ranges = tc::small_ranges(n, nk);
+    if (ranges > 0 && workspace != nullptr &&
+        workspace_bytes >= (size_t)n * h * 2 * ranges * 32 * sizeof(uint32_t)) {
+        uint32_t* lists = static_cast<uint32_t*>(workspace);
+        const int rc = tc::launch_score_small(q, keys, n, h, nk, half, ranges, lists, s1_out, s2_out, st);
+        if (rc != SMLM_OK) return rc;
+        return launch_pk_pairs(lists, ranges, n * h, (int)nk, (int)knn, scores, indices, weights, st);
+    }
     const int splits = tc::score_splits(n, h, (nk + tc::BN - 1) / tc::BN);
     const size_t need = (size_t)n * h * 2 * splits * 2 * 32 * sizeof(uint32_t);
     if (workspace == nullptr || workspace_bytes < need) {
@@ -679,7 +793,6 @@ extern "C" int smlm_score_select(const void* q, const void* keys, int64_t n, int
             return SMLM_ERR_CUDA;
         }
     }
-    cudaStream_t st = as_stream(stream);
     uint32_t* lists = static_cast<uint32_t*>(workspace);
     const int atoms = (int)(half / tc::ATOM);
     const size_t smem = tc::smem_bytes(atoms);
@@ -756,6 +869,14 @@ extern "C" int smlm_score_select_noalloc(const void* q, const void* keys, int64_
     uint32_t* lists = nullptr;
     int rc = tc::noalloc_scratch(st, &lists);
     if (rc != SMLM_OK) return rc;
+    // the workspace entry point's few-token path, whose lists (n * h * 2 * ranges * 32) fit the static array
+    // whenever n is within its token limit
+    const int ranges = tc::small_ranges(n, nk);
+    if (ranges > 0 && n * h * ranges <= 2 * (int64_t)SMLM_NOALLOC_MAX_ROWS) {
+        rc = tc::launch_score_small(q, keys, n, h, nk, half, ranges, lists, nullptr, nullptr, st);
+        if (rc != SMLM_OK) return rc;
+        return launch_pk_pairs(lists, ranges, n * h, (int)nk, (int)knn, scores, indices, weights, st);
+    }
     auto encode = tc::encode_fn();
     if (!encode) {
         set_error("score_select_noalloc: cuTensorMapEncodeTiled is not available from the driver");

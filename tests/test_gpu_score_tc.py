@@ -126,7 +126,7 @@ def test_fused_scores_against_fp32_contraction():
         assert float((got == once).double().mean()) > 0.99
 
 
-@pytest.mark.parametrize("n_small", [1, 3, 64, 130, 600])
+@pytest.mark.parametrize("n_small", [64, 130, 600])
 def test_key_range_splits_match_full_sweep(n_small):
     """Few token tiles (decoding, short prompts) split each (tile, head)'s key tiles over several CTAs, each with
     its own top lists, merged by the pair kernel. A token's scores do not depend on the other tokens of its tile,
@@ -137,3 +137,32 @@ def test_key_range_splits_match_full_sweep(n_small):
     part = K.score_select(q[:n_small].contiguous(), keys, 32)
     for a, b in zip(part, full):
         assert torch.equal(a, b[:n_small])
+
+
+@pytest.mark.parametrize("n_small", [1, 3, 16])
+def test_few_token_path_against_tensor_core_sweep(n_small):
+    """Calls of at most 16 tokens (decoding) score on the SIMT cores (score_small_kernel: an fp32 fmaf chain per
+    sub-key, rounded once to bf16) instead of the tensor cores. Their scores are the tensor-core sweep's up to the
+    order of the fp32 additions: within one bf16 step, equal almost everywhere; on every (token, head) whose scores
+    agree the selection, weights and order are identical; and on its own scores the selection is the oracle's."""
+    q, keys = inputs(37 * 128, 4, 4096, 128, 11)
+    full = K.score_select(q, keys, 32, dump=True)
+    part = K.score_select(q[:n_small].contiguous(), keys, 32, dump=True)
+    fs1, fs2 = (x[:n_small].float() for x in full[3:])
+    ps1, ps2 = (x.float() for x in part[3:])
+    qs, kf = q[:n_small].float(), keys.float()
+    for c, (a, b) in enumerate(((ps1, fs1), (ps2, fs2))):
+        # one bf16 rounding of either sum, plus the fp32 accumulation error of a 128-term sum (which dominates
+        # where the terms cancel)
+        mag = torch.einsum("nhd,hkd->nhk", qs[..., c * 128:(c + 1) * 128].abs(), kf[:, c].abs())
+        bound = (a.abs() + b.abs()) * 2.0 ** -8 + mag * 2.0 ** -16 + 2.0 ** -133
+        assert bool(((a - b).abs() <= bound).all())
+        assert float((a == b).float().mean()) > 0.999
+    same = ((ps1 == fs1).all(-1) & (ps2 == fs2).all(-1))
+    assert int(same.sum()) > 0
+    for a, b in zip(part[:3], full[:3]):
+        assert torch.equal(a[same], b[:n_small][same])
+    osc, oidx, ow = O.select(bits_of_bf16(part[3]), bits_of_bf16(part[4]), 32, bf16=True)
+    assert np.array_equal(bits_of_bf16(part[0]), osc)
+    assert np.array_equal(part[1].cpu().numpy(), oidx)
+    np.testing.assert_allclose(part[2].cpu().numpy(), ow, rtol=0, atol=1e-6)

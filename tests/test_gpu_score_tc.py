@@ -107,11 +107,13 @@ def test_score_select_backward_matches_unfused():
     assert bool(((a - b).abs() <= bound).all()), f"dq differs on rows with the same selection ({n_cmp} rows)"
 
 
-def test_fused_scores_against_fp32_contraction():
-    """The fused kernel's bf16 sub-key scores against a float64 CPU contraction of the same bf16 operands: every
-    score lies within one bf16 rounding of the exact value plus fp32 accumulation error, and nearly all of them
-    are the exact value rounded once to bf16 (round to nearest even)."""
-    N, H, NK, half = 1024, 4, 1024, 128
+@pytest.mark.parametrize("N", [1024, 8])
+def test_fused_scores_against_fp32_contraction(N):
+    """The bf16 sub-key scores (N = 1024: the tensor-core kernel; N = 8: the few-token SIMT kernel) against a
+    float64 CPU contraction of the same bf16 operands: every score lies within one bf16 rounding of the exact value
+    plus fp32 accumulation error, and nearly all of them are the exact value rounded once to bf16 (round to
+    nearest even)."""
+    H, NK, half = 4, 1024, 128
     q, keys = inputs(N, H, NK, half, 17)
     _, _, _, s1, s2 = K.score_select(q, keys, 32, dump=True)
     qc, kc = q.double().cpu(), keys.double().cpu()
